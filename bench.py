@@ -1,0 +1,427 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 MoE FFN decode path (BASELINE configs 0/2 shape).
+
+Workload ("moe_decode"): one batch-1 decode token through the 46 MoE FFN
+layers of GLM-4.7-Flash (layers 1..46), each of BASELINE config-0 shape
+(D=2048, F=1536, 64 experts, top-4, shared expert, Q8 with gs=32), 46
+distinct seeded random layers resident in HBM (31.7 GB, far larger than L2).
+A step is one such token. The metric is BASELINE's "MoE-layer HBM GB/s":
+algorithmic bytes (53,633,280 per token per layer, q80_bytes composition of
+infer.c:1464-1542) over time.
+
+  value     device time (CUDA events) of K replays of a CUDA graph that holds
+            the 46 layer calls (138 kernels), inputs already in HBM.
+  e2e       the same work through the host-memory C-ABI entry point
+            glm_cuda_moe_layer (what glm.c's layer loop would call): per layer
+            an 8 KB H2D of x from pinned memory, the kernels, an 8 KB D2H.
+  roofline  the dominant kernel (gate/up + SwiGLU), its algorithmic bytes per
+            launch over its mean CUDA-event duration, measured right after the
+            timed region over the same 46 layers, against MEASURED_PEAKS.json.
+  cpu_baseline  glm.c's own apply_moe_shared_ffn_layer (compiled from its
+            sources, OpenMP on all host cores) on a bounded sample.
+
+--impl reference times only glm.c's CPU path (rank 0; other ranks exit 0).
+Multi-GPU (torchrun): decode does not shard, so every rank runs an
+independent replica ("scaling": "weak"); value is the sum over ranks of the
+bytes processed divided by the slowest rank's time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+D, F, E, K, GS = 2048, 1536, 64, 4, 32
+N_MOE_LAYERS = 46
+METRIC = "MoE-layer HBM GB/s (bs1 decode, 46 config-0 MoE layers per token)"
+UNIT = "GB/s"
+
+
+def layer_bytes() -> int:
+    from __graft_entry__ import load_package
+
+    return load_package().synth.moe_bytes(D, F, E, K, GS)
+
+
+def gate_up_bytes() -> int:
+    """Algorithmic bytes of one gate/up+SwiGLU launch: (K+1) experts x
+    (gate + up) Q8 [F x D], xn read, h written."""
+    q8 = F * D + F * (D // GS) * 4
+    return (K + 1) * 2 * q8 + D * 4 + (K + 1) * F * 4
+
+
+def down_bytes() -> int:
+    q8 = D * F + D * (F // GS) * 4
+    return (K + 1) * q8 + (K + 1) * F * 4 + 2 * D * 4
+
+
+def route_bytes() -> int:
+    return E * D * 4 + E * 4 + 3 * D * 4
+
+
+def measured_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def ncu_traffic() -> dict:
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return {}
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons with NVML during the timed region."""
+
+    REASONS = {
+        "hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+        "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, pci_bus_id: str, period_s: float = 0.01):
+        self.pci, self.period = pci_bus_id, period_s
+        self.samples: list[int] = []
+        self.reasons: int = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+
+    def __enter__(self):
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByPciBusId(self.pci.encode())
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._reasons_fn = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                getattr(pynvml, "nvmlDeviceGetCurrentClocksThrottleReasons")
+        except Exception:  # noqa: BLE001 - clocks are reported as unavailable
+            self._nv = None
+            return self
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                self.reasons |= self._reasons_fn(self._h)
+            except Exception:  # noqa: BLE001
+                pass
+            self._stop.wait(self.period)
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+        return False
+
+    def report(self) -> dict:
+        if not self._nv:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        reasons = [k for k, bit in self.REASONS.items() if self.reasons & bit]
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(self.samples)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def make_device_layers(torch, n_layers: int, seed: int, device):
+    """46 distinct seeded layers with config-0 distributions, generated on the
+    device (int8 uniform [-127,127]; scales |N(0,0.02)|/127; router N(0,0.02);
+    bias N(0,0.01); ffn_norm 1)."""
+    layers = []
+    g = torch.Generator(device=device)
+    for li in range(n_layers):
+        g.manual_seed(seed * 1000 + li)
+
+        def q8(lead, rows, cols):
+            q = torch.randint(-127, 128, lead + (rows, cols), generator=g, device=device, dtype=torch.int8)
+            s = torch.randn(lead + (rows, cols // GS), generator=g, device=device).abs_().mul_(0.02 / 127.0)
+            return q, s
+
+        L = {"ffn_norm": torch.ones(D, device=device),
+             "router": torch.randn(E, D, generator=g, device=device).mul_(0.02),
+             "router_bias": torch.randn(E, generator=g, device=device).mul_(0.01)}
+        L["gate_sh_q"], L["gate_sh_s"] = q8((), F, D)
+        L["up_sh_q"], L["up_sh_s"] = q8((), F, D)
+        L["down_sh_q"], L["down_sh_s"] = q8((), D, F)
+        L["gate_q"], L["gate_s"] = q8((E,), F, D)
+        L["up_q"], L["up_s"] = q8((E,), F, D)
+        L["down_q"], L["down_s"] = q8((E,), D, F)
+        layers.append(L)
+    return layers
+
+
+def cpu_baseline(layer_host: dict, x_host, budget_s: float) -> dict:
+    """glm.c's own apply_moe_shared_ffn_layer on the host cores, bounded sample."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    ncores = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(ncores))
+    os.environ.setdefault("OMP_PROC_BIND", "true")
+    os.environ.setdefault("OMP_PLACES", "cores")
+    import oracle
+
+    kind = "reference" if oracle.ref_available() else "port"
+    if kind == "port":
+        return {"value": None, "unit": UNIT, "cores": 1, "kind": "port",
+                "sample": "oracle/_ref missing; no CPU baseline measured"}
+    probe = oracle.time_moe_layer(layer_host, x_host, 2, 5) / 5.0
+    iters = max(5, int(budget_s * 1000.0 / max(probe, 1e-3)))
+    ms = oracle.time_moe_layer(layer_host, x_host, 2, iters)
+    gbps = iters * layer_bytes() / (ms / 1e3) / 1e9
+    return {"value": round(gbps, 3), "unit": UNIT, "cores": oracle.omp_threads(), "kind": kind,
+            "sample": f"{iters} calls of apply_moe_shared_ffn_layer (one config-0 layer, {x_host.shape[0]} "
+                      f"rotating tokens), {ms / iters:.3f} ms/call, OMP_NUM_THREADS={os.environ['OMP_NUM_THREADS']}"}
+
+
+def run_reference(args) -> None:
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return
+    from __graft_entry__ import load_package
+
+    synth = load_package().synth
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    ncores = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(ncores))
+    os.environ.setdefault("OMP_PROC_BIND", "true")
+    os.environ.setdefault("OMP_PLACES", "cores")
+    import oracle
+
+    if not oracle.ref_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libglmref.so was not built "
+                          "(reference sources absent where build() ran)"}))
+        return
+    L = synth.moe_layer(seed=42, **synth.CONFIG0)
+    x = synth.tokens(42, 64, D)
+    probe = oracle.time_moe_layer(L, x, 1, 3) / 3.0
+    step_s = args.ref_budget_s / max(1, args.steps + args.warmup)
+    calls = max(2, int(step_s * 1000.0 / max(probe, 1e-3)))
+    for _ in range(args.warmup):
+        oracle.time_moe_layer(L, x, 0, calls)
+    total_ms = 0.0
+    for _ in range(args.steps):
+        total_ms += oracle.time_moe_layer(L, x, 0, calls)
+    gbps = args.steps * calls * layer_bytes() / (total_ms / 1e3) / 1e9
+    sample = (f"each step = {calls} calls of glm.c apply_moe_shared_ffn_layer on one config-0 layer with 64 "
+              f"rotating tokens ({total_ms / (args.steps * calls):.3f} ms/call)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbps, 3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32/int8",
+        "data": "synthetic (seeded; BASELINE config-0 distributions)",
+        "config": {"workload": "moe_decode", "layer": "config-0 MoE FFN", "batch": 1, "group_size": GS},
+        "cpu_baseline": {"value": round(gbps, 3), "unit": UNIT, "cores": oracle.omp_threads(),
+                         "kind": "reference", "sample": sample},
+        "e2e": {"value": round(gbps, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
+def run_ours(args) -> None:
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    from __graft_entry__ import load_package
+
+    pkg = load_package()
+    lib = pkg.glm_cuda.GlmCuda()
+    lib.init(local, D, F, E, K, GS, N_MOE_LAYERS)
+    layers = make_device_layers(torch, N_MOE_LAYERS, args.seed + rank, dev)
+    for li, L in enumerate(layers):
+        lib.bind_moe_layer_device(li, L)
+    torch.cuda.synchronize()
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(args.seed * 7 + rank)
+    n_tok = 8
+    tokens = torch.randn(n_tok, D, generator=gen, device=dev)
+    x_work = torch.empty(D, device=dev)
+
+    # Warm the launch path (sets kernel attributes) before capture.
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        x_work.copy_(tokens[0])
+        for li in range(N_MOE_LAYERS):
+            lib.moe_layer_async(li, x_work, 1, stream=stream.cuda_stream)
+    torch.cuda.synchronize()
+
+    graphs = []
+    for t in range(n_tok):
+        gph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gph, stream=stream):
+            x_work.copy_(tokens[t])
+            for li in range(N_MOE_LAYERS):
+                lib.moe_layer_async(li, x_work, 1, stream=torch.cuda.current_stream().cuda_stream)
+        graphs.append(gph)
+    torch.cuda.synchronize()
+
+    for i in range(args.warmup):
+        graphs[i % n_tok].replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    props = torch.cuda.get_device_properties(dev)
+    pci = "%08x:%02x:%02x.0" % (props.pci_domain_id, props.pci_bus_id, props.pci_device_id)
+    with ClockSampler(pci) as clocks:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for i in range(args.steps):
+                graphs[i % n_tok].replay()
+            stop.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(stop)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    lb = layer_bytes()
+    value = world * args.steps * N_MOE_LAYERS * lb / (ms / 1e3) / 1e9
+
+    # Per-kernel durations (CUDA events between the three kernels) over the
+    # same 46 layers, for the roofline of the dominant kernel.
+    prof = np.zeros(3)
+    n_prof = 0
+    for rep in range(args.profile_tokens):
+        x_work.copy_(tokens[rep % n_tok])
+        torch.cuda.synchronize()
+        for li in range(N_MOE_LAYERS):
+            prof += np.array(lib.moe_layer_profile(li, x_work))
+            n_prof += 1
+    prof /= max(n_prof, 1)
+    kernel_bytes = [route_bytes(), gate_up_bytes(), down_bytes()]
+    names = ["moe_route_kernel", "moe_gate_up_kernel", "moe_down_kernel"]
+    dom = int(np.argmax(prof))
+    peaks = measured_peaks()
+    achieved = kernel_bytes[dom] / (prof[dom] / 1e3) / 1e9
+    traffic = ncu_traffic().get(names[dom])
+
+    # End to end through the host-memory C-ABI (pinned x, sync per layer).
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    x_pin = torch.empty(D, dtype=torch.float32, pin_memory=True)
+    x_np = x_pin.numpy()
+    tok_host = tokens.cpu().numpy()
+    for i in range(2):
+        x_np[:] = tok_host[i % n_tok]
+        for li in range(N_MOE_LAYERS):
+            lib.moe_layer_host_inplace(li, x_np)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        x_np[:] = tok_host[i % n_tok]
+        for li in range(N_MOE_LAYERS):
+            lib.moe_layer_host_inplace(li, x_np)
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_value = world * e2e_steps * N_MOE_LAYERS * lb / e2e_s / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        host_layer = {k: v.cpu().numpy() for k, v in layers[0].items()}
+        host_layer.update(dim=D, ffn=F, n_experts=E, k_used=K, gs=GS)
+        cpu = cpu_baseline(host_layer, tok_host, args.cpu_budget_s)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8 weights x int8-digit activations -> int32; fp32 scales/accum",
+            "data": "synthetic (seeded, BASELINE config-0 distributions, generated on device)",
+            "config": {"workload": "moe_decode: 1 token x 46 distinct GLM-4.7-Flash MoE FFN layers per step",
+                       "dim": D, "moe_ffn_dim": F, "experts": E, "top_k": K, "group_size": GS,
+                       "layers_per_step": N_MOE_LAYERS, "global_batch": world,
+                       "parallelism": f"replicas x{world}",
+                       "l2": "inputs larger than L2: 46 distinct layers = %.1f GB per GPU" %
+                             (N_MOE_LAYERS * 690.1e6 / 1e9),
+                       "timing": "CUDA-graph replays, CUDA events, max over ranks"},
+            "layer_us": round(ms / args.steps / N_MOE_LAYERS * 1e3, 3),
+            "roofline": {"bound": "hbm", "kernel": names[dom], "achieved": round(achieved, 1),
+                         "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                         "traffic": traffic, "peak_source": peaks["source"],
+                         "algorithmic_bytes_per_launch": kernel_bytes[dom],
+                         "kernel_us": {n: round(v * 1e3, 3) for n, v in zip(names, prof)}},
+            "roofline_layer": {"achieved": round(lb / (prof.sum() / 1e3) / 1e9, 1),
+                               "frac": round(lb / (prof.sum() / 1e3) / 1e9 / peaks["hbm_gbs"], 4)},
+            "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": N_MOE_LAYERS * D * 4,
+                    "d2h_bytes_per_step": N_MOE_LAYERS * D * 4, "steps": e2e_steps,
+                    "api": "glm_cuda_moe_layer (host pointers, synchronous per layer)"},
+            "gpu_launches": args.steps * N_MOE_LAYERS * 3,
+            "clocks": clocks.report(),
+            "route_stats": lib.route_stats(),
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line))
+    lib.free()
+    del graphs
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seed", type=int, default=42)
+    ap.add_argument("--e2e-steps", type=int, default=50)
+    ap.add_argument("--profile-tokens", type=int, default=4)
+    ap.add_argument("--cpu-budget-s", type=float, default=8.0)
+    ap.add_argument("--ref-budget-s", type=float, default=90.0,
+                    help="total CPU seconds of the reference arm; each step is an equal bounded sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

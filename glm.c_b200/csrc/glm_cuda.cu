@@ -1,0 +1,433 @@
+// C-ABI layer of the B200 backend (declarations and citations in
+// include/glm_cuda.h). Owns the per-process device context: weights in HBM
+// (planar Q8, unchanged layout), decode scratch, a private stream, and the
+// host-pointer-keyed weight cache of the matvec hook.
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "glm_cuda.h"
+#include "glm_internal.h"
+
+namespace {
+
+struct LayerSlot {
+    glmq::MoeLayerDev w;
+    std::vector<void*> owned;  // device buffers this library allocated
+    bool ready = false;
+};
+
+struct MatvecEntry {
+    int8_t* q = nullptr;
+    float* s = nullptr;
+    int rows = 0, dim = 0, gs = 0;
+};
+
+struct State {
+    bool inited = false;
+    int device = 0;
+    int num_sms = 0;
+    glmq::MoeDims dims{};
+    std::vector<LayerSlot> layers;
+    glmq::MoeScratch scratch{};
+    cudaStream_t stream = nullptr;
+    // staging for the host-pointer entry points
+    float* x_dev = nullptr;
+    int32_t* idx_dev = nullptr;
+    float* w_dev = nullptr;
+    int stage_tokens = 0;
+    float* mv_x = nullptr;
+    float* mv_y = nullptr;
+    size_t mv_x_cap = 0, mv_y_cap = 0;
+    std::unordered_map<const void*, MatvecEntry> mv_cache;
+    unsigned long long launches = 0;
+};
+
+State g;
+std::mutex g_mu;
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    fprintf(stderr, "[glm-cuda] %s\n", buf);
+    return code;
+}
+
+#define CUDA_TRY(call)                                                                          \
+    do {                                                                                        \
+        cudaError_t e_ = (call);                                                                \
+        if (e_ != cudaSuccess)                                                                  \
+            return fail(e_ == cudaErrorMemoryAllocation ? GLM_CUDA_ERR_NOMEM : GLM_CUDA_ERR_CUDA, \
+                        "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, __LINE__); \
+    } while (0)
+
+template <typename T>
+int dev_alloc(T** p, size_t count) {
+    *p = nullptr;
+    if (count == 0) return 0;
+    CUDA_TRY(cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T)));
+    return 0;
+}
+
+void release_layer(LayerSlot& L) {
+    for (void* p : L.owned) cudaFree(p);
+    L.owned.clear();
+    L.w = glmq::MoeLayerDev{};
+    L.ready = false;
+}
+
+void release_all() {
+    for (auto& L : g.layers) release_layer(L);
+    g.layers.clear();
+    for (auto& kv : g.mv_cache) {
+        cudaFree(kv.second.q);
+        cudaFree(kv.second.s);
+    }
+    g.mv_cache.clear();
+    void* bufs[] = {g.scratch.xn, g.scratch.h, g.scratch.center, g.scratch.bound, g.scratch.topk_idx,
+                    g.scratch.topk_w, g.scratch.counter, g.scratch.stats, g.x_dev, g.idx_dev,
+                    g.w_dev, g.mv_x, g.mv_y};
+    for (void* p : bufs)
+        if (p) cudaFree(p);
+    g.scratch = glmq::MoeScratch{};
+    g.x_dev = nullptr;
+    g.idx_dev = nullptr;
+    g.w_dev = nullptr;
+    g.mv_x = g.mv_y = nullptr;
+    g.mv_x_cap = g.mv_y_cap = 0;
+    g.stage_tokens = 0;
+    if (g.stream) cudaStreamDestroy(g.stream);
+    g.stream = nullptr;
+    g.inited = false;
+}
+
+bool routed_disabled_by_env() {
+    // infer.c:1161-1165: set, non-empty and not starting with '0'.
+    const char* v = getenv("GLM_DISABLE_MOE_ROUTED");
+    return v && v[0] && v[0] != '0';
+}
+
+int check_layer(int layer) {
+    if (!g.inited) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_init has not been called");
+    if (layer < 0 || layer >= (int)g.layers.size())
+        return fail(GLM_CUDA_ERR_ARG, "layer %d out of range [0,%zu)", layer, g.layers.size());
+    if (!g.layers[layer].ready) return fail(GLM_CUDA_ERR_STATE, "layer %d has no weights", layer);
+    return 0;
+}
+
+template <typename T>
+int upload(LayerSlot& L, const T* host, size_t count, const T** out) {
+    *out = nullptr;
+    if (!host) return 0;
+    T* d = nullptr;
+    if (int rc = dev_alloc(&d, count)) return rc;
+    L.owned.push_back(d);
+    CUDA_TRY(cudaMemcpyAsync(d, host, count * sizeof(T), cudaMemcpyHostToDevice, g.stream));
+    *out = d;
+    return 0;
+}
+
+int ensure_stage(int n_tokens) {
+    if (n_tokens <= g.stage_tokens) return 0;
+    if (g.x_dev) cudaFree(g.x_dev);
+    if (g.idx_dev) cudaFree(g.idx_dev);
+    if (g.w_dev) cudaFree(g.w_dev);
+    g.x_dev = nullptr;
+    g.idx_dev = nullptr;
+    g.w_dev = nullptr;
+    g.stage_tokens = 0;
+    if (int rc = dev_alloc(&g.x_dev, (size_t)n_tokens * g.dims.D)) return rc;
+    if (int rc = dev_alloc(&g.idx_dev, (size_t)n_tokens * g.dims.K)) return rc;
+    if (int rc = dev_alloc(&g.w_dev, (size_t)n_tokens * g.dims.K)) return rc;
+    g.stage_tokens = n_tokens;
+    return 0;
+}
+
+int moe_enqueue(int layer, float* x_dev, int n_tokens, int32_t* idx_dev, float* w_dev, cudaStream_t st) {
+    const LayerSlot& L = g.layers[layer];
+    const int routed = routed_disabled_by_env() ? 0 : 1;
+    const auto& d = g.dims;
+    for (int t = 0; t < n_tokens; ++t) {
+        float* xt = x_dev + (size_t)t * d.D;
+        cudaError_t e = glmq::launch_moe_decode(L.w, d, g.scratch, xt, xt, routed, g.num_sms, st);
+        g.launches += 3;
+        if (e != cudaSuccess) return fail(GLM_CUDA_ERR_CUDA, "moe decode launch: %s", cudaGetErrorString(e));
+        if (idx_dev)
+            CUDA_TRY(cudaMemcpyAsync(idx_dev + (size_t)t * d.K, g.scratch.topk_idx, sizeof(int32_t) * d.K,
+                                     cudaMemcpyDeviceToDevice, st));
+        if (w_dev)
+            CUDA_TRY(cudaMemcpyAsync(w_dev + (size_t)t * d.K, g.scratch.topk_w, sizeof(float) * d.K,
+                                     cudaMemcpyDeviceToDevice, st));
+    }
+    return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int glm_cuda_init(int device, int dim, int moe_ffn_dim, int n_routed_experts, int n_experts_used, int group_size,
+                  int n_layers) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g.inited) release_all();
+    if (dim <= 0 || dim % 128 || moe_ffn_dim <= 0 || moe_ffn_dim % 64)
+        return fail(GLM_CUDA_ERR_ARG, "unsupported dims dim=%d moe_ffn_dim=%d (need dim%%128==0, ffn%%64==0)", dim,
+                    moe_ffn_dim);
+    if (group_size != 32) return fail(GLM_CUDA_ERR_ARG, "unsupported group size %d (supported: 32)", group_size);
+    if (n_experts_used < 1 || n_experts_used > 8 || n_experts_used > n_routed_experts || n_routed_experts > 1024)
+        return fail(GLM_CUDA_ERR_ARG, "unsupported expert counts E=%d K=%d", n_routed_experts, n_experts_used);
+    if (n_layers <= 0) return fail(GLM_CUDA_ERR_ARG, "n_layers must be positive");
+    int ndev = 0;
+    CUDA_TRY(cudaGetDeviceCount(&ndev));
+    if (device < 0 || device >= ndev) return fail(GLM_CUDA_ERR_ARG, "device %d not present (%d devices)", device, ndev);
+    CUDA_TRY(cudaSetDevice(device));
+    cudaDeviceProp prop{};
+    CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+    if (prop.major < 10)
+        return fail(GLM_CUDA_ERR_CUDA, "device %d is sm_%d%d; this library is built for sm_100a", device,
+                    prop.major, prop.minor);
+    g.device = device;
+    g.num_sms = prop.multiProcessorCount;
+    g.dims = glmq::MoeDims{dim, moe_ffn_dim, n_routed_experts, n_experts_used, group_size};
+    CUDA_TRY(cudaStreamCreateWithFlags(&g.stream, cudaStreamNonBlocking));
+    auto& s = g.scratch;
+    int rc = 0;
+    if ((rc = dev_alloc(&s.xn, dim)) || (rc = dev_alloc(&s.h, (size_t)(n_experts_used + 1) * moe_ffn_dim)) ||
+        (rc = dev_alloc(&s.center, n_routed_experts)) || (rc = dev_alloc(&s.bound, n_routed_experts)) ||
+        (rc = dev_alloc(&s.topk_idx, n_experts_used)) || (rc = dev_alloc(&s.topk_w, n_experts_used)) ||
+        (rc = dev_alloc(&s.counter, 1)) || (rc = dev_alloc(&s.stats, 4))) {
+        release_all();
+        return rc;
+    }
+    CUDA_TRY(cudaMemset(s.counter, 0, sizeof(unsigned int)));
+    CUDA_TRY(cudaMemset(s.stats, 0, 4 * sizeof(unsigned long long)));
+    g.layers.assign(n_layers, LayerSlot{});
+    g.launches = 0;
+    g.inited = true;
+    g_err.clear();
+    return 0;
+}
+
+int glm_cuda_upload_moe_layer(int layer, const float* ffn_norm, const float* gate_inp, const float* exp_probs_b,
+                              const int8_t* gate_sh_q, const float* gate_sh_s, const int8_t* up_sh_q,
+                              const float* up_sh_s, const int8_t* down_sh_q, const float* down_sh_s,
+                              const int8_t* gate_q, const float* gate_s, const int8_t* up_q, const float* up_s,
+                              const int8_t* down_q, const float* down_s) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_init has not been called");
+    if (layer < 0 || layer >= (int)g.layers.size()) return fail(GLM_CUDA_ERR_ARG, "layer %d out of range", layer);
+    if (!ffn_norm || !gate_inp || !exp_probs_b || !gate_sh_q || !gate_sh_s || !up_sh_q || !up_sh_s || !down_sh_q ||
+        !down_sh_s)
+        return fail(GLM_CUDA_ERR_ARG, "layer %d: shared-expert/router pointers must be non-NULL", layer);
+    const bool routed = gate_q != nullptr;
+    if (routed && (!gate_s || !up_q || !up_s || !down_q || !down_s))
+        return fail(GLM_CUDA_ERR_ARG, "layer %d: routed block is incomplete", layer);
+    const auto& d = g.dims;
+    const size_t D = d.D, F = d.F, E = d.E, gD = D / d.gs, gF = F / d.gs;
+    LayerSlot& L = g.layers[layer];
+    release_layer(L);
+    auto& w = L.w;
+    int rc = 0;
+    if ((rc = upload(L, ffn_norm, D, &w.ffn_norm)) || (rc = upload(L, gate_inp, E * D, &w.router)) ||
+        (rc = upload(L, exp_probs_b, E, &w.router_bias)) || (rc = upload(L, gate_sh_q, F * D, &w.gate_sh_q)) ||
+        (rc = upload(L, gate_sh_s, F * gD, &w.gate_sh_s)) || (rc = upload(L, up_sh_q, F * D, &w.up_sh_q)) ||
+        (rc = upload(L, up_sh_s, F * gD, &w.up_sh_s)) || (rc = upload(L, down_sh_q, D * F, &w.down_sh_q)) ||
+        (rc = upload(L, down_sh_s, D * gF, &w.down_sh_s))) {
+        release_layer(L);
+        return rc;
+    }
+    if (routed) {
+        if ((rc = upload(L, gate_q, E * F * D, &w.gate_q)) || (rc = upload(L, gate_s, E * F * gD, &w.gate_s)) ||
+            (rc = upload(L, up_q, E * F * D, &w.up_q)) || (rc = upload(L, up_s, E * F * gD, &w.up_s)) ||
+            (rc = upload(L, down_q, E * D * F, &w.down_q)) || (rc = upload(L, down_s, E * D * gF, &w.down_s))) {
+            release_layer(L);
+            return rc;
+        }
+    }
+    CUDA_TRY(cudaStreamSynchronize(g.stream));
+    L.ready = true;
+    return 0;
+}
+
+int glm_cuda_bind_moe_layer_device(int layer, const float* ffn_norm, const float* gate_inp,
+                                   const float* exp_probs_b, const int8_t* gate_sh_q, const float* gate_sh_s,
+                                   const int8_t* up_sh_q, const float* up_sh_s, const int8_t* down_sh_q,
+                                   const float* down_sh_s, const int8_t* gate_q, const float* gate_s,
+                                   const int8_t* up_q, const float* up_s, const int8_t* down_q,
+                                   const float* down_s) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_init has not been called");
+    if (layer < 0 || layer >= (int)g.layers.size()) return fail(GLM_CUDA_ERR_ARG, "layer %d out of range", layer);
+    if (!ffn_norm || !gate_inp || !exp_probs_b || !gate_sh_q || !gate_sh_s || !up_sh_q || !up_sh_s || !down_sh_q ||
+        !down_sh_s)
+        return fail(GLM_CUDA_ERR_ARG, "layer %d: shared-expert/router pointers must be non-NULL", layer);
+    if (gate_q && (!gate_s || !up_q || !up_s || !down_q || !down_s))
+        return fail(GLM_CUDA_ERR_ARG, "layer %d: routed block is incomplete", layer);
+    LayerSlot& L = g.layers[layer];
+    release_layer(L);
+    L.w = glmq::MoeLayerDev{ffn_norm, gate_inp, exp_probs_b, gate_sh_q, gate_sh_s, up_sh_q, up_sh_s, down_sh_q,
+                            down_sh_s, gate_q, gate_s, up_q, up_s, down_q, down_s};
+    L.ready = true;
+    return 0;
+}
+
+int glm_cuda_moe_layer(int layer, float* x, int n_tokens, int32_t* topk_idx, float* topk_w) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (int rc = check_layer(layer)) return rc;
+    if (!x || n_tokens < 0) return fail(GLM_CUDA_ERR_ARG, "x must be non-NULL and n_tokens >= 0");
+    if (n_tokens == 0) return 0;
+    if (int rc = ensure_stage(n_tokens)) return rc;
+    const auto& d = g.dims;
+    CUDA_TRY(cudaMemcpyAsync(g.x_dev, x, sizeof(float) * (size_t)n_tokens * d.D, cudaMemcpyHostToDevice, g.stream));
+    if (int rc = moe_enqueue(layer, g.x_dev, n_tokens, topk_idx ? g.idx_dev : nullptr, topk_w ? g.w_dev : nullptr,
+                             g.stream))
+        return rc;
+    CUDA_TRY(cudaMemcpyAsync(x, g.x_dev, sizeof(float) * (size_t)n_tokens * d.D, cudaMemcpyDeviceToHost, g.stream));
+    if (topk_idx)
+        CUDA_TRY(cudaMemcpyAsync(topk_idx, g.idx_dev, sizeof(int32_t) * (size_t)n_tokens * d.K,
+                                 cudaMemcpyDeviceToHost, g.stream));
+    if (topk_w)
+        CUDA_TRY(cudaMemcpyAsync(topk_w, g.w_dev, sizeof(float) * (size_t)n_tokens * d.K, cudaMemcpyDeviceToHost,
+                                 g.stream));
+    CUDA_TRY(cudaStreamSynchronize(g.stream));
+    return 0;
+}
+
+int glm_cuda_moe_layer_async(int layer, float* x_dev, int n_tokens, int32_t* topk_idx_dev, float* topk_w_dev,
+                             void* stream) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (int rc = check_layer(layer)) return rc;
+    if (!x_dev || n_tokens < 0) return fail(GLM_CUDA_ERR_ARG, "x_dev must be non-NULL and n_tokens >= 0");
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : g.stream;
+    return moe_enqueue(layer, x_dev, n_tokens, topk_idx_dev, topk_w_dev, st);
+}
+
+int glm_cuda_moe_layer_profile(int layer, float* x_dev, float ms_out[3]) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (int rc = check_layer(layer)) return rc;
+    if (!x_dev || !ms_out) return fail(GLM_CUDA_ERR_ARG, "x_dev and ms_out must be non-NULL");
+    cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+    for (auto& e : ev) CUDA_TRY(cudaEventCreate(&e));
+    const int routed = routed_disabled_by_env() ? 0 : 1;
+    cudaError_t err = glmq::launch_moe_decode(g.layers[layer].w, g.dims, g.scratch, x_dev, x_dev, routed,
+                                              g.num_sms, g.stream, ev);
+    g.launches += 3;
+    if (err == cudaSuccess) err = cudaEventSynchronize(ev[3]);
+    for (int i = 0; err == cudaSuccess && i < 3; ++i) err = cudaEventElapsedTime(&ms_out[i], ev[i], ev[i + 1]);
+    for (auto& e : ev) cudaEventDestroy(e);
+    if (err != cudaSuccess) return fail(GLM_CUDA_ERR_CUDA, "moe profile: %s", cudaGetErrorString(err));
+    return 0;
+}
+
+int glm_cuda_matvec_q80(const int8_t* qmat, const float* smat, const float* x, float* y, int rows, int dim, int gs) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_init has not been called");
+    if (!qmat || !smat || !x || !y || rows <= 0 || dim <= 0) return fail(GLM_CUDA_ERR_ARG, "bad matvec arguments");
+    if (gs != 32 || dim % 64) return fail(GLM_CUDA_ERR_ARG, "matvec: unsupported gs=%d dim=%d", gs, dim);
+    auto it = g.mv_cache.find(qmat);
+    if (it != g.mv_cache.end() && (it->second.rows != rows || it->second.dim != dim || it->second.gs != gs)) {
+        cudaFree(it->second.q);
+        cudaFree(it->second.s);
+        g.mv_cache.erase(it);
+        it = g.mv_cache.end();
+    }
+    if (it == g.mv_cache.end()) {
+        MatvecEntry m;
+        m.rows = rows;
+        m.dim = dim;
+        m.gs = gs;
+        if (int rc = dev_alloc(&m.q, (size_t)rows * dim)) return rc;
+        if (int rc = dev_alloc(&m.s, (size_t)rows * (dim / gs))) {
+            cudaFree(m.q);
+            return rc;
+        }
+        CUDA_TRY(cudaMemcpyAsync(m.q, qmat, (size_t)rows * dim, cudaMemcpyHostToDevice, g.stream));
+        CUDA_TRY(cudaMemcpyAsync(m.s, smat, sizeof(float) * (size_t)rows * (dim / gs), cudaMemcpyHostToDevice,
+                                 g.stream));
+        it = g.mv_cache.emplace(qmat, m).first;
+    }
+    if ((size_t)dim > g.mv_x_cap) {
+        if (g.mv_x) cudaFree(g.mv_x);
+        g.mv_x = nullptr;
+        g.mv_x_cap = 0;
+        if (int rc = dev_alloc(&g.mv_x, (size_t)dim)) return rc;
+        g.mv_x_cap = dim;
+    }
+    if ((size_t)rows > g.mv_y_cap) {
+        if (g.mv_y) cudaFree(g.mv_y);
+        g.mv_y = nullptr;
+        g.mv_y_cap = 0;
+        if (int rc = dev_alloc(&g.mv_y, (size_t)rows)) return rc;
+        g.mv_y_cap = rows;
+    }
+    CUDA_TRY(cudaMemcpyAsync(g.mv_x, x, sizeof(float) * dim, cudaMemcpyHostToDevice, g.stream));
+    cudaError_t e = glmq::launch_q80_matvec(it->second.q, it->second.s, g.mv_x, g.mv_y, rows, dim, gs, g.num_sms,
+                                            g.stream);
+    g.launches += 1;
+    if (e != cudaSuccess) return fail(GLM_CUDA_ERR_CUDA, "matvec launch: %s", cudaGetErrorString(e));
+    CUDA_TRY(cudaMemcpyAsync(y, g.mv_y, sizeof(float) * rows, cudaMemcpyDeviceToHost, g.stream));
+    CUDA_TRY(cudaStreamSynchronize(g.stream));
+    return 0;
+}
+
+int glm_cuda_matvec_q80_async(const int8_t* q_dev, const float* s_dev, const float* x_dev, float* y_dev, int rows,
+                              int dim, int gs, void* stream) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_init has not been called");
+    if (!q_dev || !s_dev || !x_dev || !y_dev || rows <= 0 || dim <= 0)
+        return fail(GLM_CUDA_ERR_ARG, "bad matvec arguments");
+    if (gs != 32 || dim % 64) return fail(GLM_CUDA_ERR_ARG, "matvec: unsupported gs=%d dim=%d", gs, dim);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : g.stream;
+    cudaError_t e = glmq::launch_q80_matvec(q_dev, s_dev, x_dev, y_dev, rows, dim, gs, g.num_sms, st);
+    g.launches += 1;
+    if (e != cudaSuccess) return fail(GLM_CUDA_ERR_CUDA, "matvec launch: %s", cudaGetErrorString(e));
+    return 0;
+}
+
+int glm_cuda_synchronize(void) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_init has not been called");
+    CUDA_TRY(cudaStreamSynchronize(g.stream));
+    CUDA_TRY(cudaGetLastError());
+    return 0;
+}
+
+int glm_cuda_route_stats(uint64_t out[4]) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_init has not been called");
+    if (!out) return fail(GLM_CUDA_ERR_ARG, "out must be non-NULL");
+    unsigned long long h[4] = {0, 0, 0, 0};
+    CUDA_TRY(cudaDeviceSynchronize());
+    CUDA_TRY(cudaMemcpy(h, g.scratch.stats, sizeof h, cudaMemcpyDeviceToHost));
+    for (int i = 0; i < 4; ++i) out[i] = h[i];
+    return 0;
+}
+
+uint64_t glm_cuda_launch_count(void) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    return g.launches;
+}
+
+const char* glm_cuda_last_error(void) { return g_err.c_str(); }
+
+void glm_cuda_free(void) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g.inited) {
+        cudaStreamSynchronize(g.stream);
+        release_all();
+    }
+}
+
+}  // extern "C"

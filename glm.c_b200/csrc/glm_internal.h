@@ -1,0 +1,60 @@
+// Internal (non-exported) interfaces between the C-ABI layer (glm_cuda.cu)
+// and the kernel translation units.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace glmq {
+
+// Device-resident weights of one MoE FFN layer, planar Q8 as in glm.c
+// (LayerMoeShared model.h:65-74, LayerMoeRouted model.h:76-83).
+struct MoeLayerDev {
+    const float* ffn_norm = nullptr;     // [D]
+    const float* router = nullptr;       // [E][D]   gate_inp
+    const float* router_bias = nullptr;  // [E]      exp_probs_b
+    const int8_t* gate_sh_q = nullptr;   // [F][D]
+    const float* gate_sh_s = nullptr;    // [F][D/gs]
+    const int8_t* up_sh_q = nullptr;
+    const float* up_sh_s = nullptr;
+    const int8_t* down_sh_q = nullptr;   // [D][F]
+    const float* down_sh_s = nullptr;    // [D][F/gs]
+    const int8_t* gate_q = nullptr;      // [E][F][D]
+    const float* gate_s = nullptr;       // [E][F][D/gs]
+    const int8_t* up_q = nullptr;
+    const float* up_s = nullptr;
+    const int8_t* down_q = nullptr;      // [E][D][F]
+    const float* down_s = nullptr;       // [E][D][F/gs]
+};
+
+struct MoeDims {
+    int D, F, E, K, gs;
+};
+
+// Per-device scratch of the decode path (all device pointers).
+struct MoeScratch {
+    float* xn;              // [D]
+    float* h;               // [(K+1)][F]  SwiGLU activations, routed slots by rank, shared last
+    double* center;         // [E] router logit estimates
+    double* bound;          // [E] rigorous error bound of the reference's serial fp32 sum
+    int32_t* topk_idx;      // [K]
+    float* topk_w;          // [K]
+    unsigned int* counter;  // [1] last-CTA election; kept at 0 between launches
+    unsigned long long* stats;  // [4] calls, interval fallbacks, unresolved near-ties, mean fallbacks
+};
+
+// One decode token through one MoE layer: x_out = x_in + FFN(x_in).
+// x_in may equal x_out. Returns a cudaError_t from the launches.
+// `events` (optional, 4 entries) are recorded before K1, after K1, after K2
+// and after K3 on `stream`, for per-kernel timing.
+cudaError_t launch_moe_decode(const MoeLayerDev& w, const MoeDims& d, const MoeScratch& s, const float* x_in,
+                              float* x_out, int routed_enabled, int num_sms, cudaStream_t stream,
+                              cudaEvent_t* events = nullptr);
+
+// y = Q8(q, s) . x for a rows x cols planar Q8 matrix (gs = 32, cols % 64 == 0).
+cudaError_t launch_q80_matvec(const int8_t* q, const float* s, const float* x, float* y, int rows, int cols,
+                              int gs, int num_sms, cudaStream_t stream);
+
+size_t q80_matvec_smem_bytes(int cols);
+
+}  // namespace glmq

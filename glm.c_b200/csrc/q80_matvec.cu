@@ -1,0 +1,136 @@
+// Batch-1 planar Q8 matvec on sm_100a: y[r] = sum_g s[r,g] * sum_k q[r,gs*g+k] x[gs*g+k]
+// Replaces matvec_q80_rows (infer.c:765-786) behind matvec_rows (infer.c:792-797).
+//
+// One persistent CTA per SM owns an equal contiguous slice of the rows; its
+// 16 warps split the slice into 16-row tiles and, when the slice has fewer
+// tiles than warps, also split the columns (k-split) and reduce through shared
+// memory. The dot products run on the integer tensor core (see
+// q80_common.cuh); the activation vector is quantised once per CTA into
+// shared-memory digit planes.
+#include <cstdint>
+
+#include "glm_internal.h"
+#include "q80_common.cuh"
+
+namespace glmq {
+
+constexpr int kMvWarps = 16;
+constexpr int kMvThreads = kMvWarps * 32;
+constexpr int kMvUnroll = 4;
+
+struct MatvecArgs {
+    const int8_t* q;
+    const float* s;
+    const float* x;
+    float* y;
+    int rows, cols;
+};
+
+__global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a) {
+    extern __shared__ __align__(16) unsigned char sm[];
+    const int nch = a.cols >> 6;
+    int8_t* planes = reinterpret_cast<int8_t*>(sm);
+    float* sxg = reinterpret_cast<float*>(sm + (size_t)nch * kChunkBytes);
+    float* sxtab = sxg + (a.cols >> 5);
+    float* part = sxtab + (size_t)nch * kChunkTab;  // [kMvWarps][16]
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, t = lane & 3;
+    const int rb = (int)((long long)blockIdx.x * a.rows / gridDim.x);
+    const int re = (int)((long long)(blockIdx.x + 1) * a.rows / gridDim.x);
+    const int ntiles = (re - rb + 15) >> 4;
+    int ks = kMvWarps / (ntiles > 0 ? ntiles : 1);
+    ks = ks < 1 ? 1 : (ks > nch ? nch : ks);
+    const int tiles_per_pass = kMvWarps / ks;
+
+    quantize_to_planes(a.x, a.cols, planes, sxg, sxtab);
+
+    const int boff = b_frag_offset(lane);
+    const int kq = warp % ks, tw = warp / ks;
+    const int jb = kq * nch / ks, je = (kq + 1) * nch / ks;
+    const size_t sgrp = (size_t)(a.cols >> 5);
+
+    for (int tile0 = 0; tile0 < ntiles; tile0 += tiles_per_pass) {
+        const int tile = tile0 + tw;
+        float acc0 = 0.f, acc1 = 0.f;
+        if (tw < tiles_per_pass && tile < ntiles) {
+            const int r0 = rb + tile * 16 + gid, r1 = r0 + 8;
+            const int8_t* q0 = r0 < re ? a.q + (size_t)r0 * a.cols : nullptr;
+            const int8_t* q1 = r1 < re ? a.q + (size_t)r1 * a.cols : nullptr;
+            const float* s0 = r0 < re ? a.s + (size_t)r0 * sgrp : nullptr;
+            const float* s1 = r1 < re ? a.s + (size_t)r1 * sgrp : nullptr;
+            for (int j = jb; j < je; j += kMvUnroll) {
+                int4 qa[kMvUnroll], qb[kMvUnroll];
+                float2 sa[kMvUnroll], sb[kMvUnroll];
+#pragma unroll
+                for (int u = 0; u < kMvUnroll; ++u) {
+                    const int jj = j + u;
+                    const bool in = jj < je;
+                    const int off = jj * kChunkCols + 16 * t;
+                    qa[u] = (in && q0) ? ld_weights16(q0 + off) : make_int4(0, 0, 0, 0);
+                    qb[u] = (in && q1) ? ld_weights16(q1 + off) : make_int4(0, 0, 0, 0);
+                    sa[u] = (in && s0) ? ld_scales2(s0 + 2 * jj) : make_float2(0.f, 0.f);
+                    sb[u] = (in && s1) ? ld_scales2(s1 + 2 * jj) : make_float2(0.f, 0.f);
+                }
+#pragma unroll
+                for (int u = 0; u < kMvUnroll; ++u) {
+                    const int jj = j + u;
+                    if (jj < je) {
+                        const int4 b = boff >= 0 ? *reinterpret_cast<const int4*>(planes + jj * kChunkBytes + boff)
+                                                 : make_int4(0, 0, 0, 0);
+                        const float2 tab = *reinterpret_cast<const float2*>(sxtab + jj * kChunkTab + 2 * t);
+                        chunk_mma_accumulate(qa[u], qb[u], sa[u], sb[u], b, tab, t, acc0, acc1);
+                    }
+                }
+            }
+        }
+        acc0 = quad_sum(acc0);
+        acc1 = quad_sum(acc1);
+        if (ks == 1) {
+            if (t == 0 && tw < tiles_per_pass && tile < ntiles) {
+                const int r0 = rb + tile * 16 + gid;
+                if (r0 < re) a.y[r0] = acc0;
+                if (r0 + 8 < re) a.y[r0 + 8] = acc1;
+            }
+            continue;  // uniform across the CTA: ks is
+        }
+        if (t == 0 && tw < tiles_per_pass) {
+            part[warp * 16 + gid] = acc0;
+            part[warp * 16 + gid + 8] = acc1;
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < tiles_per_pass * 16; i += kMvThreads) {
+            const int tl = i >> 4, rr = i & 15;
+            const int r = rb + (tile0 + tl) * 16 + rr;
+            if (tile0 + tl < ntiles && r < re) {
+                float sum = 0.f;
+                for (int k = 0; k < ks; ++k) sum += part[(tl * ks + k) * 16 + rr];
+                a.y[r] = sum;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+size_t q80_matvec_smem_bytes(int cols) {
+    const int nch = cols >> 6;
+    return (size_t)nch * kChunkBytes + (size_t)(cols >> 5) * 4 + (size_t)nch * kChunkTab * 4 + kMvWarps * 16 * 4;
+}
+
+cudaError_t launch_q80_matvec(const int8_t* q, const float* s, const float* x, float* y, int rows, int cols,
+                              int gs, int num_sms, cudaStream_t stream) {
+    if (gs != 32 || cols % 64 || rows <= 0) return cudaErrorInvalidValue;
+    const size_t smem = q80_matvec_smem_bytes(cols);
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaFuncSetAttribute(q80_matvec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        attr_set = true;
+    }
+    int grid = num_sms;
+    if (grid > (rows + 15) / 16) grid = (rows + 15) / 16;
+    MatvecArgs a{q, s, x, y, rows, cols};
+    q80_matvec_kernel<<<grid, kMvThreads, smem, stream>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace glmq

@@ -1,0 +1,169 @@
+"""ctypes binding of include/glm_cuda.h (the library's C-ABI).
+
+This is how tests, the benchmark and Python callers reach the CUDA path; it
+mirrors the C entry points one to one and raises GlmCudaError on any nonzero
+return, carrying glm_cuda_last_error(). Loading fails loudly when the built
+library is missing: there is no fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import numpy as np
+
+from . import build as _build
+
+LIB_PATH = _build.LIB
+HEADER = os.path.join(_build.INCLUDE, "glm_cuda.h")
+
+MOE_FIELDS = (
+    "ffn_norm", "router", "router_bias",
+    "gate_sh_q", "gate_sh_s", "up_sh_q", "up_sh_s", "down_sh_q", "down_sh_s",
+    "gate_q", "gate_s", "up_q", "up_s", "down_q", "down_s",
+)
+
+
+class GlmCudaError(RuntimeError):
+    def __init__(self, fn: str, rc: int, msg: str):
+        super().__init__(f"{fn} returned {rc}: {msg}")
+        self.rc = rc
+
+
+def declared_functions(header: str = HEADER) -> list[str]:
+    """Names of the functions include/glm_cuda.h declares."""
+    src = open(header).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(glm_cuda_\w+)\s*\(", src)))
+
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+
+
+def _signatures(L: ctypes.CDLL) -> None:
+    L.glm_cuda_init.argtypes = [_I] * 7
+    L.glm_cuda_upload_moe_layer.argtypes = [_I] + [_P] * 15
+    L.glm_cuda_bind_moe_layer_device.argtypes = [_I] + [_P] * 15
+    L.glm_cuda_moe_layer.argtypes = [_I, _P, _I, _P, _P]
+    L.glm_cuda_moe_layer_async.argtypes = [_I, _P, _I, _P, _P, _P]
+    L.glm_cuda_moe_layer_profile.argtypes = [_I, _P, _P]
+    L.glm_cuda_matvec_q80.argtypes = [_P, _P, _P, _P, _I, _I, _I]
+    L.glm_cuda_matvec_q80_async.argtypes = [_P, _P, _P, _P, _I, _I, _I, _P]
+    L.glm_cuda_synchronize.argtypes = []
+    L.glm_cuda_route_stats.argtypes = [_P]
+    L.glm_cuda_launch_count.argtypes = []
+    L.glm_cuda_launch_count.restype = ctypes.c_uint64
+    L.glm_cuda_last_error.argtypes = []
+    L.glm_cuda_last_error.restype = ctypes.c_char_p
+    L.glm_cuda_free.argtypes = []
+    L.glm_cuda_free.restype = None
+    for name in ("glm_cuda_init", "glm_cuda_upload_moe_layer", "glm_cuda_bind_moe_layer_device",
+                 "glm_cuda_moe_layer", "glm_cuda_moe_layer_async", "glm_cuda_moe_layer_profile",
+                 "glm_cuda_matvec_q80",
+                 "glm_cuda_matvec_q80_async", "glm_cuda_synchronize", "glm_cuda_route_stats"):
+        getattr(L, name).restype = _I
+
+
+_lib = None
+
+
+def load(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Load libglm_cuda.so (RTLD_GLOBAL so the process records it as loaded)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise FileNotFoundError(f"{path} is missing: run __graft_entry__.build() (no CPU fallback exists)")
+    L = ctypes.CDLL(path, mode=ctypes.RTLD_GLOBAL)
+    _signatures(L)
+    _lib = L
+    return L
+
+
+def _ptr(a) -> int | None:
+    if a is None:
+        return None
+    if isinstance(a, int):
+        return a
+    if isinstance(a, np.ndarray):
+        return a.ctypes.data
+    return a.data_ptr()  # torch tensor
+
+
+class GlmCuda:
+    """One-to-one wrapper of the C entry points."""
+
+    def __init__(self, path: str = LIB_PATH):
+        self.L = load(path)
+
+    def _check(self, fn: str, rc: int) -> None:
+        if rc != 0:
+            raise GlmCudaError(fn, rc, self.last_error())
+
+    def last_error(self) -> str:
+        return (self.L.glm_cuda_last_error() or b"").decode()
+
+    def init(self, device: int, dim: int, ffn: int, n_experts: int, k_used: int, gs: int, n_layers: int) -> None:
+        self._check("glm_cuda_init", self.L.glm_cuda_init(device, dim, ffn, n_experts, k_used, gs, n_layers))
+
+    def upload_moe_layer(self, layer: int, L: dict) -> None:
+        arrs = [None if L.get(k) is None else np.ascontiguousarray(L[k]) for k in MOE_FIELDS]
+        self._check("glm_cuda_upload_moe_layer",
+                    self.L.glm_cuda_upload_moe_layer(layer, *[_ptr(a) for a in arrs]))
+
+    def bind_moe_layer_device(self, layer: int, ptrs: dict) -> None:
+        """ptrs: field name -> device pointer (int or torch tensor)."""
+        self._check("glm_cuda_bind_moe_layer_device",
+                    self.L.glm_cuda_bind_moe_layer_device(layer, *[_ptr(ptrs.get(k)) for k in MOE_FIELDS]))
+
+    def moe_layer(self, layer: int, x: np.ndarray, k_used: int):
+        x2 = np.array(x, dtype=np.float32, copy=True, order="C")
+        T = x2.shape[0] if x2.ndim == 2 else 1
+        idx = np.zeros((T, k_used), dtype=np.int32)
+        w = np.zeros((T, k_used), dtype=np.float32)
+        self._check("glm_cuda_moe_layer", self.L.glm_cuda_moe_layer(layer, _ptr(x2), T, _ptr(idx), _ptr(w)))
+        return x2, idx, w
+
+    def moe_layer_host_inplace(self, layer: int, x: np.ndarray, idx=None, w=None) -> None:
+        T = x.shape[0] if x.ndim == 2 else 1
+        self._check("glm_cuda_moe_layer", self.L.glm_cuda_moe_layer(layer, _ptr(x), T, _ptr(idx), _ptr(w)))
+
+    def moe_layer_async(self, layer: int, x_dev, n_tokens: int, idx_dev=None, w_dev=None, stream=None) -> None:
+        self._check("glm_cuda_moe_layer_async",
+                    self.L.glm_cuda_moe_layer_async(layer, _ptr(x_dev), n_tokens, _ptr(idx_dev), _ptr(w_dev),
+                                                    stream))
+
+    def moe_layer_profile(self, layer: int, x_dev) -> tuple[float, float, float]:
+        """(route, gate_up, down) kernel milliseconds for one token, x_dev in place."""
+        out = (ctypes.c_float * 3)()
+        self._check("glm_cuda_moe_layer_profile",
+                    self.L.glm_cuda_moe_layer_profile(layer, _ptr(x_dev), ctypes.addressof(out)))
+        return float(out[0]), float(out[1]), float(out[2])
+
+    def matvec(self, q: np.ndarray, s: np.ndarray, x: np.ndarray, gs: int) -> np.ndarray:
+        rows, cols = q.shape
+        y = np.zeros(rows, dtype=np.float32)
+        self._check("glm_cuda_matvec_q80", self.L.glm_cuda_matvec_q80(_ptr(q), _ptr(s), _ptr(x), _ptr(y),
+                                                                       rows, cols, gs))
+        return y
+
+    def matvec_async(self, q_dev, s_dev, x_dev, y_dev, rows: int, cols: int, gs: int, stream=None) -> None:
+        self._check("glm_cuda_matvec_q80_async",
+                    self.L.glm_cuda_matvec_q80_async(_ptr(q_dev), _ptr(s_dev), _ptr(x_dev), _ptr(y_dev), rows,
+                                                     cols, gs, stream))
+
+    def synchronize(self) -> None:
+        self._check("glm_cuda_synchronize", self.L.glm_cuda_synchronize())
+
+    def route_stats(self) -> list[int]:
+        out = (ctypes.c_uint64 * 4)()
+        self._check("glm_cuda_route_stats", self.L.glm_cuda_route_stats(ctypes.addressof(out)))
+        return list(out)
+
+    def launch_count(self) -> int:
+        return int(self.L.glm_cuda_launch_count())
+
+    def free(self) -> None:
+        self.L.glm_cuda_free()

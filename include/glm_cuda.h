@@ -1,0 +1,120 @@
+/*
+ * glm_cuda.h -- C-ABI of the B200 (sm_100a) backend for glm.c's
+ * mixture-of-experts FFN hot path (GLM-4.7-Flash).
+ *
+ * Plain pointers and sizes only; no CUDA or C++ types cross this boundary
+ * (streams are passed as void*). Every entry point returns 0 on success and a
+ * negative GLM_CUDA_ERR_* code on failure; glm_cuda_last_error() returns the
+ * message. There is no CPU fallback behind any of these calls: if the device
+ * path cannot run, the call fails.
+ *
+ * Weight layout is glm.c's planar Q8 format, unchanged: int8 q[rows][cols]
+ * row-major plus fp32 s[rows][cols/gs] row-major (infer.c:765-786), routed
+ * experts stored expert-major (infer.c:697-742). Supported now: gs == 32,
+ * dim % 128 == 0, moe_ffn_dim % 64 == 0, 1 <= n_experts_used <= 8.
+ *
+ * Threading: like glm.c's backends (one instance per process, infer.m:18-37)
+ * the library keeps one global device context; calls are serialised by an
+ * internal mutex.
+ */
+#ifndef GLM_CUDA_H
+#define GLM_CUDA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GLM_CUDA_OK 0
+#define GLM_CUDA_ERR_ARG (-1)      /* bad argument or unsupported shape */
+#define GLM_CUDA_ERR_STATE (-2)    /* not initialised / layer not uploaded */
+#define GLM_CUDA_ERR_CUDA (-3)     /* a CUDA call failed */
+#define GLM_CUDA_ERR_NOMEM (-4)    /* device allocation failed */
+
+/* Device bring-up and per-process state for `n_layers` layer slots.
+ * Replaces the device part of glm_backend_init (backend.h:7, backend.c:88-101;
+ * Metal counterpart glm_metal_init, infer.m:847-929). The glm.c glue treats a
+ * nonzero return the way backend.c:94-97 treats a Metal init failure. */
+int glm_cuda_init(int device, int dim, int moe_ffn_dim, int n_routed_experts, int n_experts_used,
+                  int group_size, int n_layers);
+
+/* Copy one MoE layer's weights to HBM, preserving the planar Q8 layout.
+ * Arguments are the fields of LayerMoeShared (model.h:65-74) followed by
+ * LayerMoeRouted (model.h:76-83) for layer `layer` as runtime_open leaves
+ * them (infer.c:640-743); host pointers. gate_q == NULL uploads no routed
+ * block (has_moe_routed == 0). Replaces the weight-upload step of
+ * glm_metal_prepare (infer.m:932-1010), which never uploaded routed experts. */
+int glm_cuda_upload_moe_layer(int layer, const float *ffn_norm, const float *gate_inp, const float *exp_probs_b,
+                              const int8_t *gate_sh_q, const float *gate_sh_s, const int8_t *up_sh_q,
+                              const float *up_sh_s, const int8_t *down_sh_q, const float *down_sh_s,
+                              const int8_t *gate_q, const float *gate_s, const int8_t *up_q, const float *up_s,
+                              const int8_t *down_q, const float *down_s);
+
+/* As glm_cuda_upload_moe_layer, but the pointers are device memory that the
+ * caller owns and keeps alive; nothing is copied. */
+int glm_cuda_bind_moe_layer_device(int layer, const float *ffn_norm, const float *gate_inp,
+                                   const float *exp_probs_b, const int8_t *gate_sh_q, const float *gate_sh_s,
+                                   const int8_t *up_sh_q, const float *up_sh_s, const int8_t *down_sh_q,
+                                   const float *down_sh_s, const int8_t *gate_q, const float *gate_s,
+                                   const int8_t *up_q, const float *up_s, const int8_t *down_q,
+                                   const float *down_s);
+
+/* The MoE FFN of layer `layer` applied in place to x[n_tokens][dim] (host
+ * memory): rmsnorm, sigmoid router with biased top-k, K routed SwiGLU experts
+ * weighted by 1.8 * normalised probability, shared expert, residual add.
+ * Replaces apply_moe_shared_ffn_layer (infer.c:1087-1216), called from the
+ * layer loop at infer.c:1845. topk_idx / topk_w (may be NULL) receive
+ * [n_tokens][n_experts_used] as RunState.moe_topk_idx / moe_topk_w hold them
+ * (model.h:157-158). GLM_DISABLE_MOE_ROUTED is honoured per call as at
+ * infer.c:1161-1165. Synchronous: returns after x is back in host memory. */
+int glm_cuda_moe_layer(int layer, float *x, int n_tokens, int32_t *topk_idx, float *topk_w);
+
+/* Stream-ordered variant on device memory (x_dev in place, topk outputs
+ * optional device arrays); `stream` is a cudaStream_t or NULL for the
+ * library's own stream. Returns after enqueueing. */
+int glm_cuda_moe_layer_async(int layer, float *x_dev, int n_tokens, int32_t *topk_idx_dev, float *topk_w_dev,
+                             void *stream);
+
+/* Instrumented single-token run of glm_cuda_moe_layer_async on device
+ * memory: CUDA events are recorded between the three decode kernels (router,
+ * gate/up+SwiGLU, down+combine) and ms_out[0..2] receive their durations.
+ * Synchronises the library stream. For profiling; no counterpart in glm.c
+ * beyond its per-token bench timing (infer.c:2194-2196). */
+int glm_cuda_moe_layer_profile(int layer, float *x_dev, float ms_out[3]);
+
+/* y[rows] = Q8(qmat, smat) . x[dim], host pointers. Same signature and
+ * return convention as glm_backend_try_metal_matvec (backend.h:13,
+ * backend.c:82-86; called by matvec_rows at infer.c:793): 0 = handled,
+ * nonzero = not handled. The weight matrix is copied to HBM on first use and
+ * cached by its host address, as infer.m:307-322 caches Metal buffers. */
+int glm_cuda_matvec_q80(const int8_t *qmat, const float *smat, const float *x, float *y, int rows, int dim, int gs);
+
+/* Stream-ordered matvec on device pointers. */
+int glm_cuda_matvec_q80_async(const int8_t *q_dev, const float *s_dev, const float *x_dev, float *y_dev, int rows,
+                              int dim, int gs, void *stream);
+
+/* Wait for all work the library enqueued on its own stream. */
+int glm_cuda_synchronize(void);
+
+/* Router statistics since init: out[0] routed tokens, out[1] tokens whose
+ * fast interval certification failed and took the exact recomputation,
+ * out[2] ties that only libm's last bit of expf could decide (resolved with a
+ * correctly rounded exp), out[3] rmsnorm means recomputed serially. */
+int glm_cuda_route_stats(uint64_t out[4]);
+
+/* Number of kernel launches the library has issued since init. */
+uint64_t glm_cuda_launch_count(void);
+
+/* Message of the most recent failure ("" if none). */
+const char *glm_cuda_last_error(void);
+
+/* Release all device memory and state. Replaces glm_backend_free's device
+ * part (backend.c:108-110, glm_metal_free). Safe to call twice. */
+void glm_cuda_free(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GLM_CUDA_H */

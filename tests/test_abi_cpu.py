@@ -1,0 +1,72 @@
+"""Host-side checks that need no GPU: the C-ABI library loads, exports every
+entry point include/glm_cuda.h declares, and rejects calls cleanly before
+initialisation; the algorithmic-byte formulas match glm.c's q80_bytes."""
+import subprocess
+
+import pytest
+
+
+def test_header_declares_entry_points(pkg):
+    names = pkg.glm_cuda.declared_functions()
+    for must in ("glm_cuda_init", "glm_cuda_upload_moe_layer", "glm_cuda_moe_layer", "glm_cuda_matvec_q80",
+                 "glm_cuda_free", "glm_cuda_last_error"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    pkg.build.build()
+    out = subprocess.run(["nm", "-D", "--defined-only", pkg.build.LIB], capture_output=True, text=True,
+                         check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    missing = [n for n in pkg.glm_cuda.declared_functions() if n not in exported]
+    assert not missing, f"declared but not exported: {missing}"
+    L = pkg.glm_cuda.load()
+    for n in pkg.glm_cuda.declared_functions():
+        assert getattr(L, n) is not None
+
+
+def test_calls_before_init_fail_cleanly(pkg):
+    import numpy as np
+
+    lib = pkg.glm_cuda.GlmCuda()
+    lib.free()
+    x = np.zeros((1, 256), dtype=np.float32)
+    with pytest.raises(pkg.glm_cuda.GlmCudaError) as e:
+        lib.moe_layer(0, x, 4)
+    assert e.value.rc == -2 and "glm_cuda_init" in str(e.value)
+    with pytest.raises(pkg.glm_cuda.GlmCudaError) as e:
+        lib.matvec(np.zeros((2, 64), np.int8), np.zeros((2, 2), np.float32), np.zeros(64, np.float32), 32)
+    assert e.value.rc == -2
+    lib.free()  # idempotent
+
+
+def test_init_rejects_unsupported_shapes(pkg):
+    lib = pkg.glm_cuda.GlmCuda()
+    for args in ((0, 2048, 1536, 64, 4, 16, 1),   # gs=16 not built yet
+                 (0, 2000, 1536, 64, 4, 32, 1),   # dim % 128
+                 (0, 2048, 1536, 64, 9, 32, 1),   # K > 8
+                 (0, 2048, 1536, 64, 4, 32, 0)):  # no layers
+        with pytest.raises(pkg.glm_cuda.GlmCudaError) as e:
+            lib.init(*args)
+        assert e.value.rc == -1
+
+
+def test_init_without_gpu_reports_cuda_error(pkg):
+    torch = pytest.importorskip("torch")
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    lib = pkg.glm_cuda.GlmCuda()
+    with pytest.raises(pkg.glm_cuda.GlmCudaError) as e:
+        lib.init(0, 2048, 1536, 64, 4, 32, 1)
+    assert e.value.rc in (-3, -1)
+    assert lib.last_error()
+
+
+def test_algorithmic_bytes_match_reference_formula(pkg):
+    s = pkg.synth
+    # q80_bytes (infer.c:1464-1470) composition used for config 0 / config 1
+    assert s.moe_bytes(2048, 1536, 64, 4, 32) == 53_633_280
+    assert s.q8_matvec_bytes(1536, 2048, 32) == 3_553_280
+    assert s.q8_matvec_bytes(2048, 1536, 32) == 3_553_280
+    assert s.q8_matvec_bytes(4608, 2048, 32) == 10_643_456
+    assert s.q8_matvec_bytes(154880, 2048, 32) == 357_471_232
