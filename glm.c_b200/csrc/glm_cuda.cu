@@ -176,6 +176,8 @@ int moe_enqueue(int layer, float* x_dev, int n_tokens, int32_t* idx_dev, float* 
 
 }  // namespace
 
+void glmq::set_last_error(const char* msg) { g_err = msg ? msg : ""; }
+
 extern "C" {
 
 int glm_cuda_init(int device, int dim, int moe_ffn_dim, int n_routed_experts, int n_experts_used, int group_size,

@@ -57,4 +57,7 @@ cudaError_t launch_q80_matvec(const int8_t* q, const float* s, const float* x, f
 
 size_t q80_matvec_smem_bytes(int cols);
 
+// Record the message glm_cuda_last_error() returns for this thread.
+void set_last_error(const char* msg);
+
 }  // namespace glmq

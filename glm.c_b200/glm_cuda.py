@@ -49,6 +49,8 @@ def _signatures(L: ctypes.CDLL) -> None:
     L.glm_cuda_moe_layer.argtypes = [_I, _P, _I, _P, _P]
     L.glm_cuda_moe_layer_async.argtypes = [_I, _P, _I, _P, _P, _P]
     L.glm_cuda_moe_layer_profile.argtypes = [_I, _P, _P]
+    L.glm_cuda_moe_layer_noalloc.argtypes = [_P] * 15 + [_I] * 5 + [_P, _I, _P, _P, _P]
+    L.glm_cuda_moe_layer_noalloc.restype = _I
     L.glm_cuda_matvec_q80.argtypes = [_P, _P, _P, _P, _I, _I, _I]
     L.glm_cuda_matvec_q80_async.argtypes = [_P, _P, _P, _P, _I, _I, _I, _P]
     L.glm_cuda_synchronize.argtypes = []
@@ -141,6 +143,15 @@ class GlmCuda:
         self._check("glm_cuda_moe_layer_profile",
                     self.L.glm_cuda_moe_layer_profile(layer, _ptr(x_dev), ctypes.addressof(out)))
         return float(out[0]), float(out[1]), float(out[2])
+
+    def moe_layer_noalloc(self, ptrs: dict, dim: int, ffn: int, n_experts: int, k_used: int, gs: int, x_dev,
+                          n_tokens: int, idx_dev=None, w_dev=None, stream=None) -> None:
+        """glm_cuda_moe_layer_noalloc: device weights in `ptrs` (field -> pointer
+        or tensor), x_dev updated in place; needs no glm_cuda_init."""
+        self._check("glm_cuda_moe_layer_noalloc",
+                    self.L.glm_cuda_moe_layer_noalloc(*[_ptr(ptrs.get(k)) for k in MOE_FIELDS], dim, ffn,
+                                                      n_experts, k_used, gs, _ptr(x_dev), n_tokens,
+                                                      _ptr(idx_dev), _ptr(w_dev), stream))
 
     def matvec(self, q: np.ndarray, s: np.ndarray, x: np.ndarray, gs: int) -> np.ndarray:
         rows, cols = q.shape

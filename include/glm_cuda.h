@@ -83,6 +83,29 @@ int glm_cuda_moe_layer_async(int layer, float *x_dev, int n_tokens, int32_t *top
  * beyond its per-token bench timing (infer.c:2194-2196). */
 int glm_cuda_moe_layer_profile(int layer, float *x_dev, float ms_out[3]);
 
+/* No counterpart in glm.c: an addition for callers that must not allocate
+ * device memory at call time (e.g. a server that plans all GPU memory at
+ * start-up and forbids cudaMalloc on the request path, or an embedder that
+ * only hands over pointers it already owns), and so cannot call
+ * glm_cuda_init. Same computation as glm_cuda_moe_layer_async, on device
+ * memory the caller owns: the 15 weight pointers in the order of
+ * glm_cuda_upload_moe_layer, the shape, x_dev[n_tokens][dim] updated in place
+ * and optional topk outputs. Allocates nothing: its scratch is a fixed
+ * ~170 KB static device array per GPU (held until the process exits), so
+ * dim <= 4096, moe_ffn_dim <= 4096, n_routed_experts <= 256 and
+ * n_experts_used <= 8 (else GLM_CUDA_ERR_ARG), with gs == 32. The first call
+ * on a device resolves that array's address; make it before any stream
+ * capture. All calls share the array: calls that overlap on the GPU race and
+ * must be ordered by the caller. Uses the current device; `stream` may be
+ * NULL (legacy default stream). */
+int glm_cuda_moe_layer_noalloc(const float *ffn_norm, const float *gate_inp, const float *exp_probs_b,
+                               const int8_t *gate_sh_q, const float *gate_sh_s, const int8_t *up_sh_q,
+                               const float *up_sh_s, const int8_t *down_sh_q, const float *down_sh_s,
+                               const int8_t *gate_q, const float *gate_s, const int8_t *up_q, const float *up_s,
+                               const int8_t *down_q, const float *down_s, int dim, int moe_ffn_dim,
+                               int n_routed_experts, int n_experts_used, int group_size, float *x_dev,
+                               int n_tokens, int32_t *topk_idx_dev, float *topk_w_dev, void *stream);
+
 /* y[rows] = Q8(qmat, smat) . x[dim], host pointers. Same signature and
  * return convention as glm_backend_try_metal_matvec (backend.h:13,
  * backend.c:82-86; called by matvec_rows at infer.c:793): 0 = handled,
