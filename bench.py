@@ -247,6 +247,7 @@ def run_ours(args) -> None:
     import torch.distributed as dist
 
     world, rank, local = dist_setup()
+    N_MOE_LAYERS = args.layers  # noqa: N806 - 46 for the headline; fewer only for small profiler captures
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
@@ -408,6 +409,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seed", type=int, default=42)
+    ap.add_argument("--layers", type=int, default=N_MOE_LAYERS,
+                    help="distinct MoE layers per step (46 = GLM-4.7-Flash; fewer only for profiler captures)")
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--profile-tokens", type=int, default=4)
     ap.add_argument("--cpu-budget-s", type=float, default=8.0)
