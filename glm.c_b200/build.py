@@ -17,8 +17,8 @@ CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libglm_cuda.so")
 
-SOURCES = ["glm_cuda.cu", "moe_decode.cu", "q80_matvec.cu", "moe_noalloc.cu"]
-HEADERS = ["glm_internal.h", "q80_common.cuh"]
+SOURCES = ["glm_cuda.cu", "moe_decode.cu", "moe_persistent.cu", "q80_matvec.cu", "moe_noalloc.cu"]
+HEADERS = ["glm_internal.h", "q80_common.cuh", "route_common.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

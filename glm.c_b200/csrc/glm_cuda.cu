@@ -48,6 +48,10 @@ struct State {
     size_t mv_x_cap = 0, mv_y_cap = 0;
     std::unordered_map<const void*, MatvecEntry> mv_cache;
     unsigned long long launches = 0;
+    unsigned int* status_host = nullptr;      // pinned copy of scratch.status
+    glmq::MoeLayerDev* layers_dev = nullptr;  // device copy of every slot's pointers (persistent kernel)
+    bool persistent_ok = false;               // sizes fit the persistent kernel on this device
+    int decode_path = GLM_CUDA_PATH_AUTO;
 };
 
 State g;
@@ -96,9 +100,10 @@ void release_all() {
         cudaFree(kv.second.s);
     }
     g.mv_cache.clear();
-    void* bufs[] = {g.scratch.xn, g.scratch.h, g.scratch.center, g.scratch.bound, g.scratch.topk_idx,
-                    g.scratch.topk_w, g.scratch.counter, g.scratch.stats, g.x_dev, g.idx_dev,
-                    g.w_dev, g.mv_x, g.mv_y};
+    void* bufs[] = {g.scratch.xn,     g.scratch.h,     g.scratch.center, g.scratch.bound,  g.scratch.topk_idx,
+                    g.scratch.topk_w, g.scratch.counter, g.scratch.stats, g.scratch.status, g.scratch.grid_bar,
+                    g.x_dev,          g.idx_dev,       g.w_dev,          g.mv_x,           g.mv_y,
+                    g.layers_dev};
     for (void* p : bufs)
         if (p) cudaFree(p);
     g.scratch = glmq::MoeScratch{};
@@ -108,10 +113,38 @@ void release_all() {
     g.mv_x = g.mv_y = nullptr;
     g.mv_x_cap = g.mv_y_cap = 0;
     g.stage_tokens = 0;
+    g.layers_dev = nullptr;
+    g.persistent_ok = false;
+    g.decode_path = GLM_CUDA_PATH_AUTO;
     if (g.stream) cudaStreamDestroy(g.stream);
     g.stream = nullptr;
+    if (g.status_host) cudaFreeHost(g.status_host);
+    g.status_host = nullptr;
     g.inited = false;
 }
+
+// After a synchronisation that copied scratch.status into status_host: a
+// nonzero word means one of the persistent kernel's bounded waits gave up
+// (bit 2 grid barrier, 3 weight tile, 4 ring slot, 5 routing hand-off).
+int take_device_status() {
+    const unsigned int st = g.status_host ? *g.status_host : 0u;
+    if (st == 0) return 0;
+    *g.status_host = 0;
+    cudaMemsetAsync(g.scratch.status, 0, sizeof(unsigned int), g.stream);
+    return fail(GLM_CUDA_ERR_CUDA, "the decode kernel gave up waiting (status 0x%x)", st);
+}
+
+// Mirror slot `layer`'s pointers into the device table the persistent kernel reads.
+int publish_layer(int layer) {
+    CUDA_TRY(cudaMemcpyAsync(g.layers_dev + layer, &g.layers[layer].w, sizeof(glmq::MoeLayerDev),
+                             cudaMemcpyHostToDevice, g.stream));
+    CUDA_TRY(cudaStreamSynchronize(g.stream));
+    return 0;
+}
+
+bool use_persistent() { return g.persistent_ok && g.decode_path != GLM_CUDA_PATH_CHAIN; }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 bool routed_disabled_by_env() {
     // infer.c:1161-1165: set, non-empty and not starting with '0'.
@@ -159,6 +192,18 @@ int moe_enqueue(int layer, float* x_dev, int n_tokens, int32_t* idx_dev, float* 
     const LayerSlot& L = g.layers[layer];
     const int routed = routed_disabled_by_env() ? 0 : 1;
     const auto& d = g.dims;
+    if (use_persistent()) {
+        for (int t = 0; t < n_tokens; ++t) {
+            cudaError_t e = glmq::launch_moe_persistent(g.layers_dev, layer, 1, d, g.scratch, x_dev + (size_t)t * d.D,
+                                                        idx_dev ? idx_dev + (size_t)t * d.K : nullptr,
+                                                        w_dev ? w_dev + (size_t)t * d.K : nullptr, routed,
+                                                        g.num_sms, st);
+            g.launches += 1;
+            if (e != cudaSuccess)
+                return fail(GLM_CUDA_ERR_CUDA, "moe persistent launch: %s", cudaGetErrorString(e));
+        }
+        return 0;
+    }
     for (int t = 0; t < n_tokens; ++t) {
         float* xt = x_dev + (size_t)t * d.D;
         cudaError_t e = glmq::launch_moe_decode(L.w, d, g.scratch, xt, xt, routed, g.num_sms, st);
@@ -209,12 +254,18 @@ int glm_cuda_init(int device, int dim, int moe_ffn_dim, int n_routed_experts, in
     if ((rc = dev_alloc(&s.xn, dim)) || (rc = dev_alloc(&s.h, (size_t)(n_experts_used + 1) * moe_ffn_dim)) ||
         (rc = dev_alloc(&s.center, n_routed_experts)) || (rc = dev_alloc(&s.bound, n_routed_experts)) ||
         (rc = dev_alloc(&s.topk_idx, n_experts_used)) || (rc = dev_alloc(&s.topk_w, n_experts_used)) ||
-        (rc = dev_alloc(&s.counter, 1)) || (rc = dev_alloc(&s.stats, 4))) {
+        (rc = dev_alloc(&s.counter, 1)) || (rc = dev_alloc(&s.stats, 4)) || (rc = dev_alloc(&s.status, 1)) ||
+        (rc = dev_alloc(&s.grid_bar, 1)) || (rc = dev_alloc(&g.layers_dev, n_layers))) {
         release_all();
         return rc;
     }
     CUDA_TRY(cudaMemset(s.counter, 0, sizeof(unsigned int)));
     CUDA_TRY(cudaMemset(s.stats, 0, 4 * sizeof(unsigned long long)));
+    CUDA_TRY(cudaMemset(s.status, 0, sizeof(unsigned int)));
+    CUDA_TRY(cudaMemset(g.layers_dev, 0, sizeof(glmq::MoeLayerDev) * n_layers));
+    CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&g.status_host), sizeof(unsigned int), cudaHostAllocDefault));
+    *g.status_host = 0;
+    g.persistent_ok = glmq::persistent_check(g.dims, g.num_sms, nullptr) == cudaSuccess;
     g.layers.assign(n_layers, LayerSlot{});
     g.launches = 0;
     g.inited = true;
@@ -260,7 +311,7 @@ int glm_cuda_upload_moe_layer(int layer, const float* ffn_norm, const float* gat
     }
     CUDA_TRY(cudaStreamSynchronize(g.stream));
     L.ready = true;
-    return 0;
+    return publish_layer(layer);
 }
 
 int glm_cuda_bind_moe_layer_device(int layer, const float* ffn_norm, const float* gate_inp,
@@ -277,12 +328,16 @@ int glm_cuda_bind_moe_layer_device(int layer, const float* ffn_norm, const float
         return fail(GLM_CUDA_ERR_ARG, "layer %d: shared-expert/router pointers must be non-NULL", layer);
     if (gate_q && (!gate_s || !up_q || !up_s || !down_q || !down_s))
         return fail(GLM_CUDA_ERR_ARG, "layer %d: routed block is incomplete", layer);
+    const void* ptrs[] = {ffn_norm, gate_inp, exp_probs_b, gate_sh_q, gate_sh_s, up_sh_q, up_sh_s, down_sh_q,
+                          down_sh_s, gate_q, gate_s, up_q, up_s, down_q, down_s};
+    for (const void* p : ptrs)
+        if (!aligned16(p)) return fail(GLM_CUDA_ERR_ARG, "layer %d: device weights must be 16-byte aligned", layer);
     LayerSlot& L = g.layers[layer];
     release_layer(L);
     L.w = glmq::MoeLayerDev{ffn_norm, gate_inp, exp_probs_b, gate_sh_q, gate_sh_s, up_sh_q, up_sh_s, down_sh_q,
                             down_sh_s, gate_q, gate_s, up_q, up_s, down_q, down_s};
     L.ready = true;
-    return 0;
+    return publish_layer(layer);
 }
 
 int glm_cuda_moe_layer(int layer, float* x, int n_tokens, int32_t* topk_idx, float* topk_w) {
@@ -303,8 +358,10 @@ int glm_cuda_moe_layer(int layer, float* x, int n_tokens, int32_t* topk_idx, flo
     if (topk_w)
         CUDA_TRY(cudaMemcpyAsync(topk_w, g.w_dev, sizeof(float) * (size_t)n_tokens * d.K, cudaMemcpyDeviceToHost,
                                  g.stream));
+    CUDA_TRY(cudaMemcpyAsync(g.status_host, g.scratch.status, sizeof(unsigned int), cudaMemcpyDeviceToHost,
+                             g.stream));
     CUDA_TRY(cudaStreamSynchronize(g.stream));
-    return 0;
+    return take_device_status();
 }
 
 int glm_cuda_moe_layer_async(int layer, float* x_dev, int n_tokens, int32_t* topk_idx_dev, float* topk_w_dev,
@@ -314,6 +371,44 @@ int glm_cuda_moe_layer_async(int layer, float* x_dev, int n_tokens, int32_t* top
     if (!x_dev || n_tokens < 0) return fail(GLM_CUDA_ERR_ARG, "x_dev must be non-NULL and n_tokens >= 0");
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : g.stream;
     return moe_enqueue(layer, x_dev, n_tokens, topk_idx_dev, topk_w_dev, st);
+}
+
+int glm_cuda_moe_layers_async(int first_layer, int n_layers, float* x_dev, int32_t* topk_idx_dev,
+                              float* topk_w_dev, void* stream) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_init has not been called");
+    if (n_layers <= 0 || first_layer < 0 || first_layer + n_layers > (int)g.layers.size())
+        return fail(GLM_CUDA_ERR_ARG, "layers [%d,%d) out of range [0,%zu)", first_layer, first_layer + n_layers,
+                    g.layers.size());
+    for (int l = first_layer; l < first_layer + n_layers; ++l)
+        if (int rc = check_layer(l)) return rc;
+    if (!x_dev) return fail(GLM_CUDA_ERR_ARG, "x_dev must be non-NULL");
+    if (!g.persistent_ok)
+        return fail(GLM_CUDA_ERR_ARG, "these model sizes do not fit the multi-layer decode kernel on this device");
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : g.stream;
+    const int routed = routed_disabled_by_env() ? 0 : 1;
+    cudaError_t e = glmq::launch_moe_persistent(g.layers_dev, first_layer, n_layers, g.dims, g.scratch, x_dev,
+                                                topk_idx_dev, topk_w_dev, routed, g.num_sms, st);
+    g.launches += 1;
+    if (e != cudaSuccess) return fail(GLM_CUDA_ERR_CUDA, "moe persistent launch: %s", cudaGetErrorString(e));
+    return 0;
+}
+
+int glm_cuda_set_decode_path(int path) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_init has not been called");
+    if (path != GLM_CUDA_PATH_AUTO && path != GLM_CUDA_PATH_PERSISTENT && path != GLM_CUDA_PATH_CHAIN)
+        return fail(GLM_CUDA_ERR_ARG, "unknown decode path %d", path);
+    if (path == GLM_CUDA_PATH_PERSISTENT && !g.persistent_ok)
+        return fail(GLM_CUDA_ERR_ARG, "these model sizes do not fit the persistent decode kernel on this device");
+    g.decode_path = path;
+    return 0;
+}
+
+int glm_cuda_decode_path(void) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_init has not been called");
+    return use_persistent() ? GLM_CUDA_PATH_PERSISTENT : GLM_CUDA_PATH_CHAIN;
 }
 
 int glm_cuda_moe_layer_profile(int layer, float* x_dev, float ms_out[3]) {
@@ -401,9 +496,10 @@ int glm_cuda_matvec_q80_async(const int8_t* q_dev, const float* s_dev, const flo
 int glm_cuda_synchronize(void) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (!g.inited) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_init has not been called");
-    CUDA_TRY(cudaStreamSynchronize(g.stream));
+    CUDA_TRY(cudaDeviceSynchronize());
     CUDA_TRY(cudaGetLastError());
-    return 0;
+    CUDA_TRY(cudaMemcpy(g.status_host, g.scratch.status, sizeof(unsigned int), cudaMemcpyDeviceToHost));
+    return take_device_status();
 }
 
 int glm_cuda_route_stats(uint64_t out[4]) {

@@ -41,6 +41,9 @@ struct MoeScratch {
     float* topk_w;          // [K]
     unsigned int* counter;  // [1] last-CTA election; kept at 0 between launches
     unsigned long long* stats;  // [4] calls, interval fallbacks, unresolved near-ties, mean fallbacks
+    // Persistent kernel only:
+    unsigned int* status = nullptr;    // [1] nonzero after one of its bounded waits gave up
+    unsigned int* grid_bar = nullptr;  // [1] grid-barrier arrivals (zeroed at each launch)
 };
 
 // One decode token through one MoE layer: x_out = x_in + FFN(x_in).
@@ -50,6 +53,18 @@ struct MoeScratch {
 cudaError_t launch_moe_decode(const MoeLayerDev& w, const MoeDims& d, const MoeScratch& s, const float* x_in,
                               float* x_out, int routed_enabled, int num_sms, cudaStream_t stream,
                               cudaEvent_t* events = nullptr);
+
+// Whether the persistent decode kernel supports these sizes on a device with
+// `num_sms` SMs (and its dynamic shared memory size).
+cudaError_t persistent_check(const MoeDims& d, int num_sms, size_t* smem_out);
+
+// One token through the MoE FFN of layers [first, first + n_layers) of the
+// device table `layers_dev`, in one cooperative launch of one CTA per SM:
+// x <- x + FFN_l(x) for each layer in turn. topk_out / topkw_out (optional,
+// [n_layers][K]) receive each layer's expert ids and weights.
+cudaError_t launch_moe_persistent(const MoeLayerDev* layers_dev, int first, int n_layers, const MoeDims& d,
+                                  const MoeScratch& s, float* x, int32_t* topk_out, float* topkw_out,
+                                  int routed_enabled, int num_sms, cudaStream_t stream);
 
 // y = Q8(q, s) . x for a rows x cols planar Q8 matrix (gs = 32, cols % 64 == 0).
 cudaError_t launch_q80_matvec(const int8_t* q, const float* s, const float* x, float* y, int rows, int cols,

@@ -1,0 +1,698 @@
+// Persistent batch-1 MoE decode: one cooperative launch runs the MoE FFN of
+// one or more consecutive layers for one token (apply_moe_shared_ffn_layer,
+// infer.c:1087-1216, once per layer).
+//
+// Why persistent. Each MoE layer moves ~53.6 MB but only ~360 KB per SM; a
+// kernel launch costs microseconds of start-up and tail, and a chain of
+// small dependent kernels per layer spends most of its time there. Here one
+// CTA per SM stays resident for all layers:
+//
+//   warp 15 (producer)  walks a fixed per-CTA schedule of weight tiles and
+//                       streams each into a 5-slot shared-memory ring with
+//                       TMA bulk copies (one copy per contiguous run of rows,
+//                       completion counted on the slot's mbarrier). It runs
+//                       ahead across phases and layers and stops only where
+//                       data depends on routing: the routed gate/up and down
+//                       rows of layer l wait for that layer's expert ids.
+//   warps 0-14          consume the tiles phase by phase:
+//     P0  rmsnorm of x (every CTA), xn quantised to int8 digit planes
+//     P1  CTA c < E: router logit centre/bound of expert c; all CTAs: their
+//         slice of the shared expert's gate/up rows -> h
+//     --  grid barrier A
+//     P2  every CTA ranks the experts itself (identical, certified result)
+//         and hands the ids to its producer; the shared expert's h is
+//         complete, so this CTA's output rows of the shared down matrix are
+//         computed while the routed rows stream in; then its routed gate/up
+//         rows -> h
+//     --  grid barrier B
+//     P3  routed h quantised; this CTA's output rows of the K routed down
+//         matrices; weighted combine in rank order + residual -> x
+//     --  grid barrier C (between layers)
+//
+// Grid barriers are a global arrival counter polled with acquire loads. Every
+// wait in this kernel (barriers, ring slots, routing hand-off) gives up after
+// a bounded number of polls, records the reason in `status`, raises an abort
+// flag, and the kernel leaves at its next grid barrier, so a fault cannot
+// hang the GPU. Cooperative launch guarantees all CTAs are co-resident.
+#include <cstdint>
+
+#include <cuda_runtime.h>
+
+#include "glm_internal.h"
+#include "q80_common.cuh"
+#include "route_common.cuh"
+
+namespace glmq {
+
+constexpr int kPCons = 15;                     // consumer warps (+1 producer: 512 threads, 128 regs)
+constexpr int kPConsThreads = kPCons * 32;
+constexpr int kPThreads = kPConsThreads + 32;
+constexpr int kPSlots = 5;
+#ifndef GLM_P_INFLIGHT
+#define GLM_P_INFLIGHT 3
+#endif
+// At most this many ring items in flight (issued, not landed): the ring holds
+// up to kPSlots landed tiles, but fewer bytes in flight keep the queueing
+// delay of the kernel's small critical-path loads short.
+constexpr int kPInflight = GLM_P_INFLIGHT;
+constexpr int kPTile = 16;                     // rows per ring item
+constexpr int kPHsh = 2;                       // 4-group steps of the shared h per consumer warp
+constexpr uint32_t kPollLimit = 1u << 22;
+constexpr unsigned kStatBarrier = 4u, kStatFull = 8u, kStatEmpty = 16u, kStatRoute = 32u;
+constexpr unsigned kStatAbort = kStatBarrier | kStatFull | kStatEmpty | kStatRoute;
+
+struct PersistArgs {
+    const MoeLayerDev* layers;  // device table
+    int first, n_layers;
+    float* x;
+    float* h;
+    double* center;
+    double* bound;
+    int32_t* topk_out;  // [n_layers][K] or null
+    float* topkw_out;
+    unsigned* bar;      // zero at launch
+    unsigned* status;
+    unsigned long long* stats;
+    int D, F, E, K, routed_enabled, slot_bytes;
+};
+
+__host__ __device__ inline size_t p_take(size_t& o, size_t n) {
+    const size_t r = o;
+    o = (o + n + 127) & ~(size_t)127;
+    return r;
+}
+
+// Dynamic shared memory layout (offsets in bytes).
+struct PSmem {
+    size_t bars, ring, xs, ph, px, tx, gx, th, gh, part, ys, bias, cen, bnd, sel, rscr, misc, total;
+    __host__ __device__ PSmem(int D, int F, int E, int K, int slot_bytes) {
+        size_t o = 0;
+        const int NS = K + 1, nchD = D >> 6, nchF = F >> 6;
+        bars = p_take(o, 128);
+        ring = p_take(o, (size_t)kPSlots * slot_bytes);
+        // xn (until routing is decided) and the h digit planes (after that)
+        // are never live together.
+        const size_t hpl = (size_t)NS * nchF * kChunkBytes;
+        xs = p_take(o, hpl > (size_t)D * 4 ? hpl : (size_t)D * 4);
+        ph = xs;
+        px = p_take(o, (size_t)nchD * kChunkBytes);
+        tx = p_take(o, (size_t)nchD * kChunkTab * 4);
+        gx = p_take(o, (size_t)(D >> 5) * 4);
+        th = p_take(o, (size_t)NS * nchF * kChunkTab * 4);
+        gh = p_take(o, (size_t)NS * (F >> 5) * 4);
+        part = p_take(o, (size_t)(K > 4 ? 8 : 4) * kPCons * kPTile * 4);
+        ys = p_take(o, (size_t)NS * kPTile * 4);
+        bias = p_take(o, (size_t)E * 4);
+        cen = p_take(o, (size_t)E * 8);
+        bnd = p_take(o, (size_t)E * 8);
+        sel = p_take(o, (size_t)E * 20);
+        rscr = p_take(o, (size_t)(64 + 5 * kPCons) * 4);
+        misc = p_take(o, 512);
+        total = o;
+    }
+};
+
+// Ring slot: the largest of a gate/up tile (16 rows of D), a down tile (16
+// rows of F) and the layer constants (norm + bias).
+__host__ __device__ inline int p_slot_bytes(int D, int F, int E) {
+    int b = kPTile * (D + D / 8);
+    const int bf = kPTile * (F + F / 8);
+    if (bf > b) b = bf;
+    if (D * 4 + E * 4 > b) b = D * 4 + E * 4;
+    return (b + 127) & ~127;
+}
+
+// ------------------------------------------------------------ primitives
+
+__device__ __forceinline__ void cons_sync() { asm volatile("bar.sync 1, %0;\n" ::"n"(kPConsThreads) : "memory"); }
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ unsigned ld_relaxed_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// ------------------------------------------------------------ row mapping
+
+// This CTA's rows: shared gate/up rows [sh0, sh0+nsh), routed gate/up rows
+// [rt0, rt0+nrt) of the slot-major K*F routed h, output rows [rb, re).
+struct PRows {
+    int sh0, nsh, rt0, nrt, rb, re;
+    __device__ PRows(int c, int G, int D, int F, int K) {
+        sh0 = (int)((long long)c * F / G);
+        nsh = (int)((long long)(c + 1) * F / G) - sh0;
+        rt0 = (int)((long long)c * K * F / G);
+        nrt = (int)((long long)(c + 1) * K * F / G) - rt0;
+        rb = (int)((long long)c * D / G);
+        re = (int)((long long)(c + 1) * D / G);
+    }
+    __device__ int n_sh_tiles() const { return (nsh + kPTile - 1) / kPTile; }
+    __device__ int n_rt_tiles() const { return (nrt + kPTile - 1) / kPTile; }
+};
+
+struct GRow {
+    const int8_t* q = nullptr;  // null: row absent (zero contribution)
+    const float* s = nullptr;
+    int hidx = -1;              // index into h, -1 past the end of the tile
+};
+
+// Row j of gate/up tile t, matrix mat (0 gate, 1 up): shared rows, or routed
+// rows once `topk` is known.
+__device__ __forceinline__ GRow gate_row(const MoeLayerDev& W, const PersistArgs& a, const PRows& m, bool routed,
+                                         int t, int j, int mat, const int* topk) {
+    GRow r;
+    const size_t D = (size_t)a.D, sgrp = D >> 5;
+    const int i = t * kPTile + j;
+    if (!routed) {
+        if (i >= m.nsh) return r;
+        const int rr = m.sh0 + i;
+        r.hidx = a.K * a.F + rr;
+        r.q = (mat ? W.up_sh_q : W.gate_sh_q) + (size_t)rr * D;
+        r.s = (mat ? W.up_sh_s : W.gate_sh_s) + (size_t)rr * sgrp;
+        return r;
+    }
+    if (i >= m.nrt) return r;
+    const int flat = m.rt0 + i, slot = flat / a.F, rr = flat - slot * a.F;
+    r.hidx = flat;
+    if (!a.routed_enabled || !W.gate_q || !topk) return r;
+    const int e = topk[slot];
+    if (e < 0) return r;
+    const size_t row = (size_t)e * a.F + rr;
+    r.q = (mat ? W.up_q : W.gate_q) + row * D;
+    r.s = (mat ? W.up_s : W.gate_s) + row * sgrp;
+    return r;
+}
+
+// ------------------------------------------------------------ producer
+
+// Producer lanes: gate/up tile t (one matrix) into `buf`: each maximal run of
+// rows with contiguous sources is one q copy and one s copy.
+__device__ void produce_gate_tile(const MoeLayerDev& W, const PersistArgs& a, const PRows& m, bool routed, int t,
+                                  int mat, const int* topk, unsigned char* buf, uint64_t* bar) {
+    const unsigned full = 0xffffffffu;
+    const int lane = threadIdx.x & 31;
+    const size_t D = (size_t)a.D, sgrp = D >> 5;
+    GRow r;
+    if (lane < kPTile) r = gate_row(W, a, m, routed, t, lane, mat, topk);
+    const bool take = lane < kPTile && r.q != nullptr;
+    const unsigned tmask = __ballot_sync(full, take);
+    const auto pq = reinterpret_cast<const int8_t*>(__shfl_up_sync(full, reinterpret_cast<unsigned long long>(r.q), 1));
+    const auto ps = reinterpret_cast<const float*>(__shfl_up_sync(full, reinterpret_cast<unsigned long long>(r.s), 1));
+    const bool cont = take && lane > 0 && ((tmask >> (lane - 1)) & 1u) && pq + D == r.q && ps + sgrp == r.s;
+    const unsigned cmask = __ballot_sync(full, cont);
+    const uint32_t bytes = (uint32_t)__popc(tmask) * (uint32_t)(D + (D >> 3));
+    if (lane == 0) {
+        if (bytes)
+            mbar_arrive_expect_tx(bar, bytes);
+        else
+            mbar_arrive(bar);
+    }
+    __syncwarp();
+    if (take && !cont) {
+        // run length: this lane plus the following lanes that continue it
+        const int n = __ffs(~(cmask >> (lane + 1)));
+        bulk_copy_g2s(buf + (size_t)lane * D, r.q, (uint32_t)(n * D), bar);
+        bulk_copy_g2s(buf + kPTile * D + (size_t)lane * (D >> 3), r.s, (uint32_t)(n * (D >> 3)), bar);
+    }
+}
+
+// Producer lanes: this CTA's output rows of down matrix `slot` (K = shared).
+__device__ void produce_down(const MoeLayerDev& W, const PersistArgs& a, const PRows& m, int slot, const int* topk,
+                             unsigned char* buf, uint64_t* bar) {
+    const int lane = threadIdx.x & 31;
+    const int n = m.re - m.rb;
+    const size_t F = (size_t)a.F, fgrp = F >> 5;
+    const int8_t* q = nullptr;
+    const float* s = nullptr;
+    if (n > 0) {
+        if (slot == a.K) {
+            q = W.down_sh_q + (size_t)m.rb * F;
+            s = W.down_sh_s + (size_t)m.rb * fgrp;
+        } else if (a.routed_enabled && W.down_q && topk[slot] >= 0) {
+            const size_t row = (size_t)topk[slot] * a.D + m.rb;
+            q = W.down_q + row * F;
+            s = W.down_s + row * fgrp;
+        }
+    }
+    if (lane == 0) {
+        if (q) {
+            mbar_arrive_expect_tx(bar, (uint32_t)(n * (F + (F >> 3))));
+            bulk_copy_g2s(buf, q, (uint32_t)(n * F), bar);
+            bulk_copy_g2s(buf + kPTile * F, s, (uint32_t)(n * (F >> 3)), bar);
+        } else {
+            mbar_arrive(bar);
+        }
+    }
+    __syncwarp();
+}
+
+// ------------------------------------------------------------ consumers
+
+struct PCtx {
+    unsigned char* ring;
+    uint64_t* full;
+    uint64_t* empty;
+    int slot_bytes;
+    volatile int* abort_flag;
+    unsigned* status;
+};
+
+__device__ __forceinline__ unsigned char* slot_buf(const PCtx& P, uint32_t it) {
+    return P.ring + (size_t)(it % kPSlots) * P.slot_bytes;
+}
+
+// Every consumer thread waits for ring item `it` itself. A wait that gives up
+// records why and raises the CTA's abort flag; the thread then carries on
+// with whatever the slot holds (no block-wide agreement per item), and the
+// CTA leaves at its next grid barrier, which checks the flag.
+__device__ __forceinline__ void cons_wait(const PCtx& P, uint32_t it) {
+    if (!mbar_wait_bounded(&P.full[it % kPSlots], (it / kPSlots) & 1u)) {
+        atomicOr(P.status, kStatFull);
+        *P.abort_flag = 1;
+    }
+}
+
+// A consumer warp is done reading item `it`: one arrival per warp hands the
+// slot back once all kPCons warps are done.
+__device__ __forceinline__ void cons_release(const PCtx& P, uint32_t it) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&P.empty[it % kPSlots]);
+}
+
+// Grid-wide barrier among the consumer warps of all CTAs; false when this
+// CTA or another one has given up (every CTA then leaves).
+__device__ bool grid_sync(const PersistArgs& a, const PCtx& P, unsigned& nbar, int tid, volatile int* s_ok) {
+    cons_sync();
+    ++nbar;
+    if (tid == 0) {
+        int ok = 0;
+        __threadfence();
+        if (!*P.abort_flag) atomicAdd(a.bar, 1u);
+        const unsigned target = nbar * gridDim.x;
+        for (uint32_t i = 0; i < kPollLimit && !*P.abort_flag; ++i) {
+            if (ld_acquire_gpu(a.bar) >= target) {
+                ok = 1;
+                break;
+            }
+            if ((i & 255u) == 255u && (ld_relaxed_gpu(a.status) & kStatAbort)) break;
+        }
+        if (!ok) {
+            atomicOr(a.status, kStatBarrier);
+            *P.abort_flag = 1;
+        }
+        __threadfence();
+        *s_ok = ok;
+    }
+    cons_sync();
+    return *s_ok != 0;
+}
+
+__device__ __forceinline__ float silu_p(float v) { return v / (1.0f + expf(-v)); }
+
+__global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArgs a) {
+    extern __shared__ __align__(128) unsigned char sm[];
+    const int D = a.D, F = a.F, E = a.E, K = a.K;
+    const int nchF = F >> 6;
+    const PSmem L(D, F, E, K, a.slot_bytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + L.bars);
+    uint64_t* empty = full + kPSlots;
+    uint64_t* route_ready = empty + kPSlots;
+    float* xs = reinterpret_cast<float*>(sm + L.xs);
+    int8_t* ph = reinterpret_cast<int8_t*>(sm + L.ph);
+    int8_t* px = reinterpret_cast<int8_t*>(sm + L.px);
+    float* tx = reinterpret_cast<float*>(sm + L.tx);
+    float* gx = reinterpret_cast<float*>(sm + L.gx);
+    float* th = reinterpret_cast<float*>(sm + L.th);
+    float* gh = reinterpret_cast<float*>(sm + L.gh);
+    float* part = reinterpret_cast<float*>(sm + L.part);
+    float* ys = reinterpret_cast<float*>(sm + L.ys);
+    float* s_bias = reinterpret_cast<float*>(sm + L.bias);
+    double* s_cen = reinterpret_cast<double*>(sm + L.cen);
+    double* s_bnd = reinterpret_cast<double*>(sm + L.bnd);
+    float* rscr = reinterpret_cast<float*>(sm + L.rscr);
+    int* misc = reinterpret_cast<int*>(sm + L.misc);
+    int* s_rank = misc;                                   // [kMaxTopK + 1]
+    int* s_cert = misc + 16;
+    int* s_topk = misc + 32;                              // [kMaxTopK]
+    float* s_topw = reinterpret_cast<float*>(misc + 48);  // [kMaxTopK]
+    float* s_inv = reinterpret_cast<float*>(misc + 64);
+    volatile int* s_ok = misc + 65;
+    volatile int* s_abort = misc + 66;
+    double* red = reinterpret_cast<double*>(misc + 72);   // [kPCons]
+    SelectScratch S;
+    S.sel_c = reinterpret_cast<float*>(sm + L.sel);
+    S.sel_lo = S.sel_c + E;
+    S.sel_hi = S.sel_lo + E;
+    S.p_c = S.sel_hi + E;
+    S.taken = reinterpret_cast<int*>(S.p_c + E);
+    S.rank = s_rank;
+    S.cert = s_cert;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int c = blockIdx.x, G = gridDim.x;
+    const PRows m(c, G, D, F, K);
+    const PCtx P{sm + L.ring, full, empty, a.slot_bytes, s_abort, a.status};
+
+    if (tid == 0) {
+        for (int i = 0; i < kPSlots; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kPCons);
+        }
+        mbar_init(route_ready, 1);
+        *s_abort = 0;
+        mbar_init_fence();
+    }
+    __syncthreads();
+
+    // ------------------------------------------------------------- producer
+    if (warp == kPCons) {
+        uint32_t it = 0;
+        // Ring slot of item i is free (its previous item was released) and
+        // at most kPInflight items are in flight.
+        auto acquire = [&](uint32_t i) -> bool {
+            if (i >= (uint32_t)kPSlots) {
+                const uint32_t slot = i % kPSlots, par = ((i / kPSlots) - 1) & 1u;
+                bool ok = false;
+                for (uint32_t k = 0; k < kPollLimit && !ok; ++k) {
+                    ok = mbar_try_wait(&empty[slot], par);
+                    if (*s_abort) return false;
+                }
+                if (!ok) return false;
+            }
+            if (kPInflight < kPSlots && i >= (uint32_t)kPInflight) {
+                const uint32_t j = i - kPInflight;
+                bool ok = false;
+                for (uint32_t k = 0; k < kPollLimit && !ok; ++k) {
+                    ok = mbar_try_wait(&full[j % kPSlots], (j / kPSlots) & 1u);
+                    if (*s_abort) return false;
+                }
+                if (!ok) return false;
+            }
+            return true;
+        };
+        bool alive = true;
+        for (int li = 0; li < a.n_layers && alive; ++li) {
+            const MoeLayerDev W = a.layers[a.first + li];
+            // layer constants: ffn_norm and the router bias
+            if (!(alive = __all_sync(0xffffffffu, acquire(it)))) break;
+            if (lane == 0) {
+                uint64_t* bar = &full[it % kPSlots];
+                unsigned char* buf = slot_buf(P, it);
+                mbar_arrive_expect_tx(bar, (uint32_t)(D * 4 + E * 4));
+                bulk_copy_g2s(buf, W.ffn_norm, (uint32_t)(D * 4), bar);
+                bulk_copy_g2s(buf + D * 4, W.router_bias, (uint32_t)(E * 4), bar);
+            }
+            __syncwarp();
+            ++it;
+            if (c < E) {  // this CTA's router row
+                if (!(alive = __all_sync(0xffffffffu, acquire(it)))) break;
+                if (lane == 0) {
+                    uint64_t* bar = &full[it % kPSlots];
+                    mbar_arrive_expect_tx(bar, (uint32_t)(D * 4));
+                    bulk_copy_g2s(slot_buf(P, it), W.router + (size_t)c * D, (uint32_t)(D * 4), bar);
+                }
+                __syncwarp();
+                ++it;
+            }
+            for (int t = 0; t < m.n_sh_tiles() && alive; ++t)
+                for (int mat = 0; mat < 2; ++mat) {
+                    if (!(alive = __all_sync(0xffffffffu, acquire(it)))) break;
+                    produce_gate_tile(W, a, m, false, t, mat, nullptr, slot_buf(P, it), &full[it % kPSlots]);
+                    ++it;
+                }
+            if (!alive) break;
+            // the shared down rows do not depend on routing either
+            if (!(alive = __all_sync(0xffffffffu, acquire(it)))) break;
+            produce_down(W, a, m, K, s_topk, slot_buf(P, it), &full[it % kPSlots]);
+            ++it;
+            // routed rows need this layer's expert ids
+            bool got = false;
+            for (uint32_t k = 0; k < kPollLimit && !got; ++k) {
+                got = mbar_try_wait(route_ready, (uint32_t)li & 1u);
+                if (*s_abort) break;
+            }
+            if (!(alive = __all_sync(0xffffffffu, got))) {
+                if (lane == 0) atomicOr(a.status, kStatRoute);
+                break;
+            }
+            for (int t = 0; t < m.n_rt_tiles() && alive; ++t)
+                for (int mat = 0; mat < 2; ++mat) {
+                    if (!(alive = __all_sync(0xffffffffu, acquire(it)))) break;
+                    produce_gate_tile(W, a, m, true, t, mat, s_topk, slot_buf(P, it), &full[it % kPSlots]);
+                    ++it;
+                }
+            for (int slot = 0; slot < K && alive; ++slot) {
+                if (!(alive = __all_sync(0xffffffffu, acquire(it)))) break;
+                produce_down(W, a, m, slot, s_topk, slot_buf(P, it), &full[it % kPSlots]);
+                ++it;
+            }
+        }
+        if (!alive) {
+            if (lane == 0) {
+                atomicOr(a.status, kStatEmpty);
+                *s_abort = 1;
+            }
+            // let copies still in flight land before the CTA can exit
+            for (uint32_t j = (it > (uint32_t)kPSlots ? it - kPSlots : 0u); j < it; ++j)
+                mbar_wait_bounded(&full[j % kPSlots], (j / kPSlots) & 1u);
+        }
+        return;
+    }
+
+    // ------------------------------------------------------------ consumers
+    const int gid = lane >> 2, t4 = lane & 3;
+    const int boff = b_frag_offset(lane);
+    const int4 z4 = make_int4(0, 0, 0, 0);
+    const float2 z2 = make_float2(0.f, 0.f);
+    constexpr int kPart = kPCons * kPTile;
+    uint32_t it = 0;
+    unsigned nbar = 0;
+    auto sync = []() { cons_sync(); };
+
+    // A ring item holds 16 rows (q, then scales). Every consumer warp dots
+    // its share of the 64-column chunks of the rows with the activation
+    // planes, hands the slot back, and leaves its row partials in a `part`
+    // buffer; after one block barrier threads 0-15 add the warps' partials of
+    // their row. Items that belong together (gate and up of a tile, the K
+    // routed down matrices) are waited for and computed in one pass, so a
+    // warp has several independent MMA chains and the group one barrier.
+    auto item_rows = [&](uint32_t item, const int8_t* planes, const float* tab, int cols, bool v0, bool v1,
+                         float* pt) {
+        const int nch = cols >> 6;
+        const int8_t* qb = reinterpret_cast<const int8_t*>(slot_buf(P, item));
+        const unsigned char* sb = slot_buf(P, item) + kPTile * cols;
+        float acc0 = 0.f, acc1 = 0.f;
+        for (int j = warp * nch / kPCons; j < (warp + 1) * nch / kPCons; ++j) {
+            const int off = j * kChunkCols + 16 * t4;
+            const int4 b4 = boff >= 0 ? lds16(planes + j * kChunkBytes + boff) : z4;
+            const float2 tb = *reinterpret_cast<const float2*>(tab + j * kChunkTab + 2 * t4);
+            const int4 q0 = v0 ? lds16(qb + gid * cols + off) : z4;
+            const int4 q1 = v1 ? lds16(qb + (gid + 8) * cols + off) : z4;
+            const float2 s0 = v0 ? *reinterpret_cast<const float2*>(sb + gid * (cols >> 3) + 8 * j) : z2;
+            const float2 s1 = v1 ? *reinterpret_cast<const float2*>(sb + (gid + 8) * (cols >> 3) + 8 * j) : z2;
+            chunk_mma_accumulate(q0, q1, s0, s1, b4, tb, t4, acc0, acc1);
+        }
+        cons_release(P, item);
+        acc0 = quad_sum(acc0);
+        acc1 = quad_sum(acc1);
+        if (t4 == 0) {
+            pt[warp * kPTile + gid] = acc0;
+            pt[warp * kPTile + gid + 8] = acc1;
+        }
+    };
+    auto row_total = [&](const float* pt) {
+        float tot = 0.f;
+#pragma unroll
+        for (int w = 0; w < kPCons; ++w) tot += pt[w * kPTile + tid];
+        return tot;
+    };
+
+    // Gate/up tile t (its gate item, then its up item) -> 16 entries of h,
+    // h = silu(gate) * up (infer.c:1184-1188, 1197-1201). part buffers
+    // 2(t&1) and 2(t&1)+1: the next tile writes the other pair.
+    auto gate_tile = [&](const MoeLayerDev& W, bool routed, int t) {
+        const int* tk = routed ? s_topk : nullptr;
+        float* pg = part + (size_t)(2 * (t & 1)) * kPart;
+        float* pu = pg + kPart;
+        cons_wait(P, it);
+        cons_wait(P, it + 1);
+        item_rows(it, px, tx, D, gate_row(W, a, m, routed, t, gid, 0, tk).q != nullptr,
+                  gate_row(W, a, m, routed, t, gid + 8, 0, tk).q != nullptr, pg);
+        item_rows(it + 1, px, tx, D, gate_row(W, a, m, routed, t, gid, 1, tk).q != nullptr,
+                  gate_row(W, a, m, routed, t, gid + 8, 1, tk).q != nullptr, pu);
+        it += 2;
+        cons_sync();
+        if (tid < kPTile) {
+            const int hidx = gate_row(W, a, m, routed, t, tid, 0, tk).hidx;
+            if (hidx >= 0) a.h[hidx] = silu_p(row_total(pg)) * row_total(pu);
+        }
+    };
+
+    // This CTA's output rows of the down matrices of slots [s0, s0 + ns)
+    // (slot K = shared) -> ys[slot]; part buffer b0 + i for the i-th.
+    auto down_items = [&](const MoeLayerDev& W, int s0, int ns, int b0) {
+        const int n = m.re - m.rb;
+        for (int i = 0; i < ns; ++i) cons_wait(P, it + i);
+        for (int i = 0; i < ns; ++i) {
+            const int slot = s0 + i;
+            const bool live = slot == K || (a.routed_enabled && W.down_q && s_topk[slot] >= 0);
+            item_rows(it + i, ph + (size_t)slot * nchF * kChunkBytes, th + (size_t)slot * nchF * kChunkTab, F,
+                      live && gid < n, live && gid + 8 < n, part + (size_t)(b0 + i) * kPart);
+        }
+        it += ns;
+        cons_sync();
+        if (tid < kPTile)
+            for (int i = 0; i < ns; ++i) ys[(s0 + i) * kPTile + tid] = row_total(part + (size_t)(b0 + i) * kPart);
+    };
+
+    for (int li = 0; li < a.n_layers; ++li) {
+        const MoeLayerDev W = a.layers[a.first + li];
+
+        // ---- P0: rmsnorm (infer.c:746-752, 1098), every CTA; xn -> planes
+        cons_wait(P, it);
+        {
+            const float* norm = reinterpret_cast<const float*>(slot_buf(P, it));
+            for (int i = tid; i < E; i += kPConsThreads) s_bias[i] = norm[D + i];
+            constexpr int kXPer = (2048 + kPConsThreads - 1) / kPConsThreads;  // D <= 2048
+            float xr[kXPer];
+#pragma unroll
+            for (int u = 0; u < kXPer; ++u)
+                xr[u] = tid + u * kPConsThreads < D ? ldcg_f32(a.x + tid + u * kPConsThreads) : 0.0f;
+            double ss = 0.0;
+#pragma unroll
+            for (int u = 0; u < kXPer; ++u) {
+                const double v = (double)xr[u];
+                ss = __dadd_rn(ss, __dmul_rn(v, v));
+            }
+            ss = warp_sum_d(ss);
+            if (lane == 0) red[warp] = ss;
+            cons_sync();
+            if (tid == 0) {
+                double tot = 0.0;
+                for (int w = 0; w < kPCons; ++w) tot += red[w];
+                *s_inv = rms_inv_certified(tot, a.x, D, c == 0 ? &a.stats[3] : nullptr);
+            }
+            cons_sync();
+            const float inv = *s_inv;
+#pragma unroll
+            for (int u = 0; u < kXPer; ++u) {
+                const int i = tid + u * kPConsThreads;
+                if (i < D) xs[i] = __fmul_rn(__fmul_rn(xr[u], inv), norm[i]);
+            }
+            cons_release(P, it);
+            ++it;
+        }
+        quantize_planes_part<false>(xs, D, px, gx, tx, tid, kPConsThreads, sync);
+
+        // ---- P1: router logit of expert c; shared-expert gate/up rows
+        if (c < E) {
+            cons_wait(P, it);
+            double C = 0.0, B = 0.0;
+            block_logit_bound_rows(reinterpret_cast<const float*>(slot_buf(P, it)), xs, D, tid, kPConsThreads, rscr,
+                                   sync, C, B);
+            cons_release(P, it);
+            ++it;
+            if (tid == 0) {
+                __stcg(a.center + c, C);
+                __stcg(a.bound + c, B);
+            }
+        }
+        for (int t = 0; t < m.n_sh_tiles(); ++t) gate_tile(W, false, t);
+        if (!grid_sync(a, P, nbar, tid, s_ok)) return;
+
+        // ---- P2: routing (every CTA, identical); shared down; routed gate/up
+        // The shared expert's h is complete: load this warp's groups of it
+        // now, ahead of the routed weight stream the selection releases.
+        float4 hv[kPHsh];
+        q4_load<true, kPHsh>(a.h + (size_t)K * F, F >> 5, warp, kPCons, lane, hv);
+        for (int i = tid; i < E; i += kPConsThreads) {
+            s_cen[i] = ldcg_f64(a.center + i);
+            s_bnd[i] = ldcg_f64(a.bound + i);
+        }
+        cons_sync();
+        block_select(s_cen, s_bnd, s_bias, E, K, W.router, xs, D, tid, kPConsThreads, S, s_topk, s_topw,
+                     c == 0 ? a.stats : nullptr, sync);
+        if (tid == 0) mbar_arrive(route_ready);  // the producer may fetch routed rows now
+        if (c == 0 && tid < K) {
+            if (a.topk_out) a.topk_out[li * K + tid] = s_topk[tid];
+            if (a.topkw_out) a.topkw_out[li * K + tid] = s_topw[tid];
+        }
+        // xs is dead from here on; its space holds the h digit planes.
+        q4_store<kPHsh>(hv, F >> 5, warp, kPCons, lane, ph + (size_t)K * nchF * kChunkBytes, gh + (size_t)K * (F >> 5));
+        cons_sync();
+        fill_sxtab(gh + (size_t)K * (F >> 5), th + (size_t)K * nchF * kChunkTab, nchF, tid, kPConsThreads);
+        cons_sync();
+        down_items(W, K, 1, 2);  // part buffer 2: routed tile 0 uses 0 and 1
+        for (int t = 0; t < m.n_rt_tiles(); ++t) gate_tile(W, true, t);
+        if (!grid_sync(a, P, nbar, tid, s_ok)) return;
+
+        // ---- P3: routed h -> digit planes; routed down rows; combine
+        quantize_planes_part<true>(a.h, K * F, ph, gh, th, tid, kPConsThreads, sync);
+        // at most 4 items waited for at once (the ring holds kPSlots = 5);
+        // consecutive batches alternate part buffers 0-3 and 4-7
+        for (int s0 = 0, b = 0; s0 < K; s0 += 4, b ^= 4) down_items(W, s0, K - s0 < 4 ? K - s0 : 4, b);
+        const int n = m.re - m.rb;
+        if (tid < n) {
+            // infer.c:1175,1192 then 1212-1214: acc += (1.8 w_k) y_k in rank
+            // order, then x += y_shared + acc.
+            const int r = m.rb + tid;
+            float acc = 0.0f;
+            for (int k = 0; k < K; ++k) {
+                if (!a.routed_enabled || !W.down_q || s_topk[k] < 0) continue;
+                acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(s_topw[k], 1.8f), ys[k * kPTile + tid]));
+            }
+            a.x[r] = __fadd_rn(__ldcg(a.x + r), __fadd_rn(ys[K * kPTile + tid], acc));
+        }
+        if (li + 1 < a.n_layers && !grid_sync(a, P, nbar, tid, s_ok)) return;
+    }
+}
+
+// ------------------------------------------------------------- launcher
+
+cudaError_t persistent_check(const MoeDims& d, int num_sms, size_t* smem_out) {
+    if (d.K < 1 || d.K > kMaxTopK || d.K > d.E || d.E > num_sms || d.E % 4 || d.gs != 32 || d.D % 128 ||
+        d.D > 2048 || d.F % 128 || d.F > 128 * kPCons * kPHsh || (d.D + kPTile - 1) / kPTile > num_sms)
+        return cudaErrorInvalidValue;
+    const int slot = p_slot_bytes(d.D, d.F, d.E);
+    const size_t smem = PSmem(d.D, d.F, d.E, d.K, slot).total;
+    if (smem > 227 * 1024 - 1024) return cudaErrorInvalidValue;
+    if (smem_out) *smem_out = smem;
+    return cudaSuccess;
+}
+
+cudaError_t launch_moe_persistent(const MoeLayerDev* layers_dev, int first, int n_layers, const MoeDims& d,
+                                  const MoeScratch& s, float* x, int32_t* topk_out, float* topkw_out,
+                                  int routed_enabled, int num_sms, cudaStream_t stream) {
+    size_t smem = 0;
+    cudaError_t err = persistent_check(d, num_sms, &smem);
+    if (err != cudaSuccess) return err;
+    static size_t cap = 0;
+    if (smem > cap) {
+        if ((err = cudaFuncSetAttribute(moe_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)smem)))
+            return err;
+        cap = smem;
+    }
+    if ((err = cudaMemsetAsync(s.grid_bar, 0, sizeof(unsigned int), stream))) return err;
+    PersistArgs a{layers_dev, first, n_layers, x, s.h, s.center, s.bound, topk_out, topkw_out, s.grid_bar, s.status,
+                  s.stats, d.D, d.F, d.E, d.K, routed_enabled, p_slot_bytes(d.D, d.F, d.E)};
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(num_sms);
+    cfg.blockDim = dim3(kPThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, moe_persistent_kernel, a);
+}
+
+}  // namespace glmq

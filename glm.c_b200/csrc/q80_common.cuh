@@ -152,4 +152,203 @@ __device__ __forceinline__ float quad_sum(float v) {
     return v;
 }
 
+// ------------------------------------------------------------ L2 loads
+
+// Loads of data another CTA wrote (read through L2, never L1) that the
+// compiler must issue exactly where they are written: a batch of these goes
+// out back to back instead of being sunk to its uses one round trip at a time.
+__device__ __forceinline__ float ldcg_f32(const float* p) {
+    float v;
+    asm volatile("ld.global.cg.f32 %0, [%1];\n" : "=f"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ double ldcg_f64(const double* p) {
+    double v;
+    asm volatile("ld.global.cg.f64 %0, [%1];\n" : "=d"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ float4 ldcg_f4(const float* p) {
+    float4 v;
+    asm volatile("ld.global.cg.v4.f32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+
+// ------------------------------------------------ vectorised quantisation
+//
+// The same group quantisation as quantize_to_planes, laid out for
+// throughput: 8 lanes per 32-element group, 4 consecutive elements per lane,
+// so a warp step covers 4 groups with one 16-byte load and three 4-byte digit
+// stores per lane. Step s covers groups 4s .. 4s+3; warp w of nwarps takes
+// steps w, w + nwarps, ... q4_load fetches kB such steps (global memory
+// through L2 when kGlobal), q4_store quantises and stores them. For a group
+// maximum a >= 2^-100 the powers of two 2^e and 2^-e are formed from exponent
+// bits (the scaling products are exact, so the digits equal the ldexpf form);
+// e = ilogb(a) - 22, plus one when a * 2^-e = 2^22 + mant(a)/2 would exceed
+// 127*65793, i.e. when the 23-bit mantissa field of a exceeds 8322814.
+template <bool kGlobal, int kB>
+__device__ __forceinline__ void q4_load(const float* src, int groups, int s0, int nwarps, int lane,
+                                        float4 (&v)[kB]) {
+#pragma unroll
+    for (int u = 0; u < kB; ++u) {
+        const int g = 4 * (s0 + u * nwarps) + (lane >> 3);
+        const float* p = src + g * 32 + (lane & 7) * 4;
+        v[u] = g < groups ? (kGlobal ? ldcg_f4(p) : *reinterpret_cast<const float4*>(p))
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+}
+
+__device__ __forceinline__ unsigned pack_digit_bytes(int a, int b, int c, int d) {
+    return (unsigned)(a & 255) | ((unsigned)(b & 255) << 8) | ((unsigned)(c & 255) << 16) | ((unsigned)d << 24);
+}
+
+template <int kB>
+__device__ __forceinline__ void q4_store(const float4 (&v)[kB], int groups, int s0, int nwarps, int lane,
+                                         int8_t* planes, float* sxg) {
+#pragma unroll
+    for (int u = 0; u < kB; ++u) {
+        const int g = 4 * (s0 + u * nwarps) + (lane >> 3);
+        const float x[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+        unsigned am = 0u;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) am = max(am, __float_as_uint(x[j]) & 0x7fffffffu);
+        am = max(am, __shfl_xor_sync(0xffffffffu, am, 1));
+        am = max(am, __shfl_xor_sync(0xffffffffu, am, 2));
+        am = max(am, __shfl_xor_sync(0xffffffffu, am, 4));
+        int X[4] = {0, 0, 0, 0};
+        float sx = 0.0f;
+        if (am >= 0x7f800000u) {  // inf or NaN in the group
+            sx = __int_as_float(0x7fc00000);
+        } else if (am >= (27u << 23)) {
+            const int e = (int)(am >> 23) - 149 + ((am & 0x7fffffu) > 8322814u ? 1 : 0);
+            sx = __uint_as_float((unsigned)(e + 127) << 23);
+            const float inv = __uint_as_float((unsigned)(127 - e) << 23);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) X[j] = __float2int_rn(__fmul_rn(x[j], inv));
+        } else if (am != 0u) {  // tiny group: library scaling
+            const float a = __uint_as_float(am);
+            int e = ilogbf(a) - 22;
+            if (ldexpf(a, -e) > kDigitMax) e += 1;
+            sx = ldexpf(1.0f, e);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) X[j] = __float2int_rn(ldexpf(x[j], -e));
+        }
+        int hi[4], mid[4], lo[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            lo[j] = ((X[j] + 128) & 255) - 128;
+            const int x1 = (X[j] - lo[j]) >> 8;
+            mid[j] = ((x1 + 128) & 255) - 128;
+            hi[j] = (x1 - mid[j]) >> 8;
+        }
+        if (g < groups) {
+            unsigned* c = reinterpret_cast<unsigned*>(planes + (g >> 1) * kChunkBytes + (g & 1) * 32 + (lane & 7) * 4);
+            c[0] = pack_digit_bytes(hi[0], hi[1], hi[2], hi[3]);
+            c[16] = pack_digit_bytes(mid[0], mid[1], mid[2], mid[3]);
+            c[32] = pack_digit_bytes(lo[0], lo[1], lo[2], lo[3]);
+            if ((lane & 7) == 0) sxg[g] = sx;
+        }
+    }
+}
+
+// Per-chunk epilogue factors from the group scales (threads [0, nthreads)):
+// lane-in-quad t of the MMA output holds B columns 2t and 2t+1, i.e.
+// (g0 hi, g0 mid), (g1 hi, g1 mid), (g0 lo, g1 lo), unused.
+__device__ __forceinline__ void fill_sxtab(const float* sxg, float* sxtab, int chunks, int tid, int nthreads) {
+    for (int i = tid; i < chunks * 4; i += nthreads) {
+        const int c = i >> 2, t = i & 3;
+        const float s0 = sxg[2 * c], s1 = sxg[2 * c + 1];
+        float A, B;
+        if (t == 0) { A = 65536.0f * s0; B = 256.0f * s0; }
+        else if (t == 1) { A = 65536.0f * s1; B = 256.0f * s1; }
+        else if (t == 2) { A = s0; B = s1; }
+        else { A = 0.0f; B = 0.0f; }
+        sxtab[c * kChunkTab + 2 * t] = A;
+        sxtab[c * kChunkTab + 2 * t + 1] = B;
+    }
+}
+
+// Quantise src[0, n) (n % 64 == 0) into planes/sxg/sxtab, run by threads
+// [0, nthreads) of a block that synchronise with `sync()` (e.g. the consumer
+// warps of a warp-specialised kernel). kGlobal: src is global memory written
+// by other CTAs; otherwise shared memory. Ends with sync().
+template <bool kGlobal, typename Sync>
+__device__ __forceinline__ void quantize_planes_part(const float* src, int n, int8_t* planes, float* sxg,
+                                                     float* sxtab, int tid, int nthreads, Sync sync) {
+    constexpr int kB = 4;
+    const int groups = n >> 5, warp = tid >> 5, nwarps = nthreads >> 5, lane = tid & 31;
+    for (int s0 = warp; 4 * s0 < groups; s0 += nwarps * kB) {
+        float4 v[kB];
+        q4_load<kGlobal, kB>(src, groups, s0, nwarps, lane, v);
+        q4_store<kB>(v, groups, s0, nwarps, lane, planes, sxg);
+    }
+    sync();
+    fill_sxtab(sxg, sxtab, n >> 6, tid, nthreads);
+    sync();
+}
+
+// ------------------------------------------------------- TMA and mbarriers
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+// Make mbarrier initialisation visible to the async (TMA) proxy.
+__device__ __forceinline__ void mbar_init_fence() {
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// Arrive and register `bytes` of expected TMA traffic on the same phase.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: every spin gives up after kWaitPolls polls (each poll may
+// itself suspend for a hardware-defined slice), so a copy that never lands
+// becomes an error status instead of a hung GPU.
+constexpr uint32_t kWaitPolls = 1u << 22;
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kWaitPolls; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+
+// One contiguous global->shared bulk copy (TMA engine, no registers used);
+// completion is counted in bytes on `bar`. dst, src and bytes must be
+// multiples of 16. No cluster multicast.
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// 16-byte shared-memory load of an A/B fragment.
+__device__ __forceinline__ int4 lds16(const int8_t* p) { return *reinterpret_cast<const int4*>(p); }
+
 }  // namespace glmq

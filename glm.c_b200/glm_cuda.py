@@ -49,6 +49,9 @@ def _signatures(L: ctypes.CDLL) -> None:
     L.glm_cuda_moe_layer.argtypes = [_I, _P, _I, _P, _P]
     L.glm_cuda_moe_layer_async.argtypes = [_I, _P, _I, _P, _P, _P]
     L.glm_cuda_moe_layer_profile.argtypes = [_I, _P, _P]
+    L.glm_cuda_moe_layers_async.argtypes = [_I, _I, _P, _P, _P, _P]
+    L.glm_cuda_set_decode_path.argtypes = [_I]
+    L.glm_cuda_decode_path.argtypes = []
     L.glm_cuda_moe_layer_noalloc.argtypes = [_P] * 15 + [_I] * 5 + [_P, _I, _P, _P, _P]
     L.glm_cuda_moe_layer_noalloc.restype = _I
     L.glm_cuda_matvec_q80.argtypes = [_P, _P, _P, _P, _I, _I, _I]
@@ -63,6 +66,7 @@ def _signatures(L: ctypes.CDLL) -> None:
     L.glm_cuda_free.restype = None
     for name in ("glm_cuda_init", "glm_cuda_upload_moe_layer", "glm_cuda_bind_moe_layer_device",
                  "glm_cuda_moe_layer", "glm_cuda_moe_layer_async", "glm_cuda_moe_layer_profile",
+                 "glm_cuda_moe_layers_async", "glm_cuda_set_decode_path", "glm_cuda_decode_path",
                  "glm_cuda_matvec_q80",
                  "glm_cuda_matvec_q80_async", "glm_cuda_synchronize", "glm_cuda_route_stats"):
         getattr(L, name).restype = _I
@@ -136,6 +140,23 @@ class GlmCuda:
         self._check("glm_cuda_moe_layer_async",
                     self.L.glm_cuda_moe_layer_async(layer, _ptr(x_dev), n_tokens, _ptr(idx_dev), _ptr(w_dev),
                                                     stream))
+
+    def moe_layers_async(self, first: int, n_layers: int, x_dev, idx_dev=None, w_dev=None, stream=None) -> None:
+        """One token through MoE layers first .. first+n_layers-1 in one launch."""
+        self._check("glm_cuda_moe_layers_async",
+                    self.L.glm_cuda_moe_layers_async(first, n_layers, _ptr(x_dev), _ptr(idx_dev), _ptr(w_dev),
+                                                     stream))
+
+    PATH_AUTO, PATH_PERSISTENT, PATH_CHAIN = 0, 1, 2
+
+    def set_decode_path(self, path: int) -> None:
+        self._check("glm_cuda_set_decode_path", self.L.glm_cuda_set_decode_path(path))
+
+    def decode_path(self) -> int:
+        rc = self.L.glm_cuda_decode_path()
+        if rc < 0:
+            self._check("glm_cuda_decode_path", rc)
+        return rc
 
     def moe_layer_profile(self, layer: int, x_dev) -> tuple[float, float, float]:
         """(route, gate_up, down) kernel milliseconds for one token, x_dev in place."""

@@ -52,7 +52,7 @@ int glm_cuda_upload_moe_layer(int layer, const float *ffn_norm, const float *gat
                               const int8_t *down_q, const float *down_s);
 
 /* As glm_cuda_upload_moe_layer, but the pointers are device memory that the
- * caller owns and keeps alive; nothing is copied. */
+ * caller owns and keeps alive (16-byte aligned); nothing is copied. */
 int glm_cuda_bind_moe_layer_device(int layer, const float *ffn_norm, const float *gate_inp,
                                    const float *exp_probs_b, const int8_t *gate_sh_q, const float *gate_sh_s,
                                    const int8_t *up_sh_q, const float *up_sh_s, const int8_t *down_sh_q,
@@ -76,7 +76,37 @@ int glm_cuda_moe_layer(int layer, float *x, int n_tokens, int32_t *topk_idx, flo
 int glm_cuda_moe_layer_async(int layer, float *x_dev, int n_tokens, int32_t *topk_idx_dev, float *topk_w_dev,
                              void *stream);
 
-/* Instrumented single-token run of glm_cuda_moe_layer_async on device
+/* Decode kernels behind glm_cuda_moe_layer / _async. PERSISTENT: one
+ * cooperative launch per token and layer, one CTA per SM streaming every
+ * weight tile through shared memory with TMA (needs n_routed_experts <= SM
+ * count and a multiple of 4, dim <= 2048, moe_ffn_dim % 128 == 0 and <= 3840).
+ * CHAIN: three dependent kernels per token and layer (router, gate/up, down).
+ * AUTO (the default) picks PERSISTENT when the sizes allow. Both give the
+ * same expert ids and agree on x to fp32 rounding. */
+#define GLM_CUDA_PATH_AUTO 0
+#define GLM_CUDA_PATH_PERSISTENT 1
+#define GLM_CUDA_PATH_CHAIN 2
+
+/* Select the decode kernels (GLM_CUDA_PATH_*). No counterpart in glm.c. */
+int glm_cuda_set_decode_path(int path);
+
+/* The decode kernels the next call will use: GLM_CUDA_PATH_PERSISTENT or
+ * GLM_CUDA_PATH_CHAIN (negative on error). */
+int glm_cuda_decode_path(void);
+
+/* One token through the MoE FFN of layers first_layer .. first_layer +
+ * n_layers - 1 in turn (x_dev[dim] in place), as consecutive calls of
+ * glm_cuda_moe_layer_async with n_tokens = 1 would do, in a single
+ * persistent launch: glm.c's per-layer MoE call (apply_moe_shared_ffn_layer,
+ * infer.c:1087-1216) repeated over a stack of MoE layers with nothing between
+ * them. In the full decoder attention runs between MoE layers and
+ * glm_cuda_moe_layer_async is the call to use. topk_idx_dev / topk_w_dev (may
+ * be NULL) receive [n_layers][n_experts_used]. Fails with GLM_CUDA_ERR_ARG
+ * when the sizes do not fit the persistent kernel. */
+int glm_cuda_moe_layers_async(int first_layer, int n_layers, float *x_dev, int32_t *topk_idx_dev,
+                              float *topk_w_dev, void *stream);
+
+/* Instrumented single-token run of the CHAIN decode kernels on device
  * memory: CUDA events are recorded between the three decode kernels (router,
  * gate/up+SwiGLU, down+combine) and ms_out[0..2] receive their durations.
  * Synchronises the library stream. For profiling; no counterpart in glm.c
@@ -117,7 +147,9 @@ int glm_cuda_matvec_q80(const int8_t *qmat, const float *smat, const float *x, f
 int glm_cuda_matvec_q80_async(const int8_t *q_dev, const float *s_dev, const float *x_dev, float *y_dev, int rows,
                               int dim, int gs, void *stream);
 
-/* Wait for all work the library enqueued on its own stream. */
+/* Wait for all work on the device (the library's stream and the streams
+ * passed to the _async calls); GLM_CUDA_ERR_CUDA if a decode kernel's bounded
+ * wait gave up since the last check. */
 int glm_cuda_synchronize(void);
 
 /* Router statistics since init: out[0] routed tokens, out[1] tokens whose

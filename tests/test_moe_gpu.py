@@ -28,17 +28,23 @@ def lib(pkg):
     L.free()
 
 
-def run_layer(lib, L, x, routed=True):
+PATHS = {"persistent": 1, "chain": 2}
+
+
+def run_layer(lib, L, x, routed=True, path="persistent"):
     lib.init(0, L["dim"], L["ffn"], L["n_experts"], L["k_used"], L["gs"], 1)
     lib.upload_moe_layer(0, L)
+    lib.set_decode_path(PATHS[path])
+    assert lib.decode_path() == PATHS[path]
     with routed_env(routed):
         return lib.moe_layer(0, x, L["k_used"])
 
 
+@pytest.mark.parametrize("path", sorted(PATHS))
 @pytest.mark.parametrize("name", GPU_CASES)
-def test_moe_decode_matches_golden(name, lib, golden):
+def test_moe_decode_matches_golden(name, path, lib, golden):
     L, x, routed, exp = golden.load_case(name)
-    x_out, idx, w = run_layer(lib, L, x, routed)
+    x_out, idx, w = run_layer(lib, L, x, routed, path)
     np.testing.assert_array_equal(idx, exp["topk_idx"])
     valid = exp["topk_idx"] >= 0
     np.testing.assert_allclose(w[valid], exp["topk_w"][valid], rtol=0, atol=TOL_W)
@@ -54,13 +60,20 @@ def test_moe_decode_rejects_gs16(lib, golden):
         lib.init(0, L["dim"], L["ffn"], L["n_experts"], L["k_used"], L["gs"], 1)
 
 
-def test_moe_config0_routing_256_tokens(lib, pkg, oracle_mod):
+def test_auto_path_is_persistent_at_config0(lib, pkg):
+    c = pkg.synth.CONFIG0
+    lib.init(0, c["dim"], c["ffn"], c["n_experts"], c["k_used"], c["gs"], 2)
+    assert lib.decode_path() == lib.PATH_PERSISTENT
+
+
+@pytest.mark.parametrize("path", sorted(PATHS))
+def test_moe_config0_routing_256_tokens(path, lib, pkg, oracle_mod):
     """256 decode tokens through the config-0 layer: every expert id equals the
     oracle's (pinned to the compiled reference), outputs within 1e-3."""
     synth = pkg.synth
     L = synth.moe_layer(seed=42, **synth.CONFIG0)
     x = synth.tokens(4242, 256, 2048)
-    x_out, idx, w = run_layer(lib, L, x)
+    x_out, idx, w = run_layer(lib, L, x, path=path)
     x_ref, idx_ref, w_ref = oracle_mod.moe_layer(L, x, impl="orc")
     np.testing.assert_array_equal(idx, idx_ref)
     np.testing.assert_allclose(w, w_ref, rtol=0, atol=TOL_W)
@@ -112,6 +125,34 @@ def test_moe_two_layers_in_sequence(lib, pkg, oracle_mod):
     np.testing.assert_array_equal(i1, j1)
     np.testing.assert_array_equal(i2, j2)
     check_moe_outputs(x, y, r, TOL)
+
+
+@pytest.mark.parametrize("cfg", [dict(dim=512, ffn=256, n_experts=32, k_used=4, gs=32),
+                                 dict(dim=2048, ffn=1536, n_experts=64, k_used=4, gs=32)])
+def test_moe_layer_stack_one_launch(cfg, lib, pkg, oracle_mod):
+    """glm_cuda_moe_layers_async: one token through a stack of MoE layers in
+    one persistent launch equals the oracle applied layer by layer (expert
+    ids bit-exact per layer, output within 1e-3)."""
+    import torch
+
+    synth = pkg.synth
+    n = 4 if cfg["dim"] < 2048 else 2
+    layers = [synth.moe_layer(seed=31, layer=l, **cfg) for l in range(1, n + 1)]
+    x = synth.tokens(31, 1, cfg["dim"])
+    lib.init(0, cfg["dim"], cfg["ffn"], cfg["n_experts"], cfg["k_used"], cfg["gs"], n + 1)
+    for l, L in enumerate(layers, start=1):
+        lib.upload_moe_layer(l, L)
+    xd = torch.from_numpy(x.copy()).cuda()
+    idx_d = torch.full((n, cfg["k_used"]), -7, dtype=torch.int32, device="cuda")
+    w_d = torch.zeros((n, cfg["k_used"]), dtype=torch.float32, device="cuda")
+    lib.moe_layers_async(1, n, xd, idx_d, w_d)
+    lib.synchronize()
+    r = x
+    for l, L in enumerate(layers):
+        r, j, wr = oracle_mod.moe_layer(L, r, impl="orc")
+        np.testing.assert_array_equal(idx_d[l].cpu().numpy(), j[0])
+        np.testing.assert_allclose(w_d[l].cpu().numpy(), wr[0], rtol=0, atol=TOL_W)
+    check_moe_outputs(x, xd.cpu().numpy(), r, TOL)
 
 
 def test_moe_layer_not_uploaded_is_an_error(lib):
