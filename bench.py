@@ -10,13 +10,18 @@ algorithmic bytes (53,633,280 per token per layer, q80_bytes composition of
 infer.c:1464-1542) over time.
 
   value     device time (CUDA events) of K replays of a CUDA graph that holds
-            the 46 layer calls (138 kernels), inputs already in HBM.
+            the 46 per-layer calls glm.c's layer loop makes
+            (glm_cuda_moe_layer_async, one persistent launch each), inputs
+            already in HBM.
+  stacked   the same 46 layers as ONE launch (glm_cuda_moe_layers_async):
+            the kernel's steady state without per-layer launch gaps.
   e2e       the same work through the host-memory C-ABI entry point
             glm_cuda_moe_layer (what glm.c's layer loop would call): per layer
             an 8 KB H2D of x from pinned memory, the kernels, an 8 KB D2H.
-  roofline  the dominant kernel (gate/up + SwiGLU), its algorithmic bytes per
-            launch over its mean CUDA-event duration, measured right after the
-            timed region over the same 46 layers, against MEASURED_PEAKS.json.
+  roofline  the dominant kernel (moe_persistent_kernel: the whole layer), its
+            algorithmic bytes per launch (one layer) over its mean CUDA-event
+            duration, measured right after the timed region over the same 46
+            layers, against MEASURED_PEAKS.json.
   cpu_baseline  glm.c's own apply_moe_shared_ffn_layer (compiled from its
             sources, OpenMP on all host cores) on a bounded sample.
 
@@ -260,6 +265,9 @@ def run_ours(args) -> None:
     pkg = load_package()
     lib = pkg.glm_cuda.GlmCuda()
     lib.init(local, D, F, E, K, GS, N_MOE_LAYERS)
+    lib.set_decode_path({"auto": 0, "persistent": 1, "chain": 2}[args.path])
+    persistent = lib.decode_path() == lib.PATH_PERSISTENT
+    kernels_per_layer = 1 if persistent else 3
     layers = make_device_layers(torch, N_MOE_LAYERS, args.seed + rank, dev)
     for li, L in enumerate(layers):
         lib.bind_moe_layer_device(li, L)
@@ -317,23 +325,61 @@ def run_ours(args) -> None:
     lb = layer_bytes()
     value = world * args.steps * N_MOE_LAYERS * lb / (ms / 1e3) / 1e9
 
-    # Per-kernel durations (CUDA events between the three kernels) over the
-    # same 46 layers, for the roofline of the dominant kernel.
-    prof = np.zeros(3)
-    n_prof = 0
-    for rep in range(args.profile_tokens):
-        x_work.copy_(tokens[rep % n_tok])
-        torch.cuda.synchronize()
-        for li in range(N_MOE_LAYERS):
-            prof += np.array(lib.moe_layer_profile(li, x_work))
-            n_prof += 1
-    prof /= max(n_prof, 1)
-    kernel_bytes = [route_bytes(), gate_up_bytes(), down_bytes()]
-    names = ["moe_route_kernel", "moe_gate_up_kernel", "moe_down_kernel"]
+    # Per-launch durations over the same 46 layers, for the roofline of the
+    # dominant kernel: CUDA events on the launching stream around each layer's
+    # launch (persistent) or between the three kernels (chain).
+    if persistent:
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(N_MOE_LAYERS + 1)]
+        prof = np.zeros(1)
+        n_prof = 0
+        for rep in range(args.profile_tokens):
+            with torch.cuda.stream(stream):
+                x_work.copy_(tokens[rep % n_tok])
+                evs[0].record(stream)
+                for li in range(N_MOE_LAYERS):
+                    lib.moe_layer_async(li, x_work, 1, stream=stream.cuda_stream)
+                    evs[li + 1].record(stream)
+            torch.cuda.synchronize()
+            prof[0] += sum(evs[i].elapsed_time(evs[i + 1]) for i in range(N_MOE_LAYERS))
+            n_prof += N_MOE_LAYERS
+        prof /= max(n_prof, 1)
+        kernel_bytes = [layer_bytes()]
+        names = ["moe_persistent_kernel"]
+    else:
+        prof = np.zeros(3)
+        n_prof = 0
+        for rep in range(args.profile_tokens):
+            x_work.copy_(tokens[rep % n_tok])
+            torch.cuda.synchronize()
+            for li in range(N_MOE_LAYERS):
+                prof += np.array(lib.moe_layer_profile(li, x_work))
+                n_prof += 1
+        prof /= max(n_prof, 1)
+        kernel_bytes = [route_bytes(), gate_up_bytes(), down_bytes()]
+        names = ["moe_route_kernel", "moe_gate_up_kernel", "moe_down_kernel"]
     dom = int(np.argmax(prof))
     peaks = measured_peaks()
     achieved = kernel_bytes[dom] / (prof[dom] / 1e3) / 1e9
     traffic = ncu_traffic().get(names[dom])
+
+    # The 46 layers as one launch (the persistent kernel's steady state).
+    stacked = None
+    if persistent:
+        s_ms = []
+        for i in range(args.warmup + args.stack_steps):
+            with torch.cuda.stream(stream):
+                x_work.copy_(tokens[i % n_tok])
+                start.record(stream)
+                lib.moe_layers_async(0, N_MOE_LAYERS, x_work, stream=stream.cuda_stream)
+                stop.record(stream)
+            torch.cuda.synchronize()
+            if i >= args.warmup:
+                s_ms.append(start.elapsed_time(stop))
+        s_mean = float(np.mean(s_ms))
+        stacked = {"value": round(N_MOE_LAYERS * layer_bytes() / (s_mean / 1e3) / 1e9, 2), "unit": UNIT,
+                   "layer_us": round(s_mean / N_MOE_LAYERS * 1e3, 3), "launches": len(s_ms),
+                   "api": "glm_cuda_moe_layers_async (46 layers, one launch)"}
+    lib.synchronize()  # raises if a bounded wait in the kernel gave up
 
     # End to end through the host-memory C-ABI (pinned x, sync per layer).
     e2e_steps = max(1, min(args.steps, args.e2e_steps))
@@ -388,10 +434,13 @@ def run_ours(args) -> None:
             "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": N_MOE_LAYERS * D * 4,
                     "d2h_bytes_per_step": N_MOE_LAYERS * D * 4, "steps": e2e_steps,
                     "api": "glm_cuda_moe_layer (host pointers, synchronous per layer)"},
-            "gpu_launches": args.steps * N_MOE_LAYERS * 3,
+            "gpu_launches": args.steps * N_MOE_LAYERS * kernels_per_layer,
+            "decode_path": "persistent" if persistent else "chain",
             "clocks": clocks.report(),
             "route_stats": lib.route_stats(),
         }
+        if stacked is not None:
+            line["stacked"] = stacked
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line))
@@ -412,6 +461,9 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=N_MOE_LAYERS,
                     help="distinct MoE layers per step (46 = GLM-4.7-Flash; fewer only for profiler captures)")
     ap.add_argument("--e2e-steps", type=int, default=50)
+    ap.add_argument("--path", choices=["auto", "persistent", "chain"], default="auto",
+                    help="decode kernels (auto = persistent where the sizes allow)")
+    ap.add_argument("--stack-steps", type=int, default=20)
     ap.add_argument("--profile-tokens", type=int, default=4)
     ap.add_argument("--cpu-budget-s", type=float, default=8.0)
     ap.add_argument("--ref-budget-s", type=float, default=90.0,
