@@ -588,6 +588,7 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
             cons_release(P, it);
             ++it;
         }
+        cons_sync();  // xs complete before any thread quantises it
         quantize_planes_part<false>(xs, D, px, gx, tx, tid, kPConsThreads, sync);
 
         // ---- P1: router logit of expert c; shared-expert gate/up rows
