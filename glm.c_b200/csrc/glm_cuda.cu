@@ -144,6 +144,11 @@ int publish_layer(int layer) {
 
 bool use_persistent() { return g.persistent_ok && g.decode_path != GLM_CUDA_PATH_CHAIN; }
 
+// The layer glm.c's loop calls after `layer` (infer.c:1845), if it has weights.
+int next_moe_layer(int layer) {
+    return layer + 1 < (int)g.layers.size() && g.layers[layer + 1].ready ? layer + 1 : -1;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 bool routed_disabled_by_env() {
@@ -197,7 +202,7 @@ int moe_enqueue(int layer, float* x_dev, int n_tokens, int32_t* idx_dev, float* 
             cudaError_t e = glmq::launch_moe_persistent(g.layers_dev, layer, 1, d, g.scratch, x_dev + (size_t)t * d.D,
                                                         idx_dev ? idx_dev + (size_t)t * d.K : nullptr,
                                                         w_dev ? w_dev + (size_t)t * d.K : nullptr, routed,
-                                                        g.num_sms, st);
+                                                        g.num_sms, st, t + 1 < n_tokens ? layer : next_moe_layer(layer));
             g.launches += 1;
             if (e != cudaSuccess)
                 return fail(GLM_CUDA_ERR_CUDA, "moe persistent launch: %s", cudaGetErrorString(e));
@@ -388,7 +393,8 @@ int glm_cuda_moe_layers_async(int first_layer, int n_layers, float* x_dev, int32
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : g.stream;
     const int routed = routed_disabled_by_env() ? 0 : 1;
     cudaError_t e = glmq::launch_moe_persistent(g.layers_dev, first_layer, n_layers, g.dims, g.scratch, x_dev,
-                                                topk_idx_dev, topk_w_dev, routed, g.num_sms, st);
+                                                topk_idx_dev, topk_w_dev, routed, g.num_sms, st,
+                                                next_moe_layer(first_layer + n_layers - 1));
     g.launches += 1;
     if (e != cudaSuccess) return fail(GLM_CUDA_ERR_CUDA, "moe persistent launch: %s", cudaGetErrorString(e));
     return 0;

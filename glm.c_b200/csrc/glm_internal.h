@@ -61,10 +61,12 @@ cudaError_t persistent_check(const MoeDims& d, int num_sms, size_t* smem_out);
 // One token through the MoE FFN of layers [first, first + n_layers) of the
 // device table `layers_dev`, in one cooperative launch of one CTA per SM:
 // x <- x + FFN_l(x) for each layer in turn. topk_out / topkw_out (optional,
-// [n_layers][K]) receive each layer's expert ids and weights.
+// [n_layers][K]) receive each layer's expert ids and weights. next_layer
+// (table index or -1) names the layer expected after the last one: its
+// routing-independent weights are pulled into L2 while the last layer runs.
 cudaError_t launch_moe_persistent(const MoeLayerDev* layers_dev, int first, int n_layers, const MoeDims& d,
                                   const MoeScratch& s, float* x, int32_t* topk_out, float* topkw_out,
-                                  int routed_enabled, int num_sms, cudaStream_t stream);
+                                  int routed_enabled, int num_sms, cudaStream_t stream, int next_layer);
 
 // y = Q8(q, s) . x for a rows x cols planar Q8 matrix (gs = 32, cols % 64 == 0).
 cudaError_t launch_q80_matvec(const int8_t* q, const float* s, const float* x, float* y, int rows, int cols,

@@ -14,20 +14,26 @@
 //                       ahead across phases and layers and stops only where
 //                       data depends on routing: the routed gate/up and down
 //                       rows of layer l wait for that layer's expert ids.
-//   warps 0-14          consume the tiles phase by phase:
+//   warps 0-14          consume the tiles phase by phase, in 5 groups of 3
+//                       warps; group g owns ring slot g and processes the
+//                       weight items that land there (a gate/up item holds
+//                       8 gate rows and their 8 up rows, so SwiGLU finishes
+//                       in-lane; a down item 16 output rows of one matrix):
 //     P0  rmsnorm of x (every CTA), xn quantised to int8 digit planes
-//     P1  CTA c < E: router logit centre/bound of expert c; all CTAs: their
-//         slice of the shared expert's gate/up rows -> h
+//     P1  CTA c < E: router logit centre/bound of expert c
 //     --  grid barrier A
 //     P2  every CTA ranks the experts itself (identical, certified result)
-//         and hands the ids to its producer; the shared expert's h is
-//         complete, so this CTA's output rows of the shared down matrix are
-//         computed while the routed rows stream in; then its routed gate/up
-//         rows -> h
+//         and hands the ids to its producer, which prefetches all of the
+//         CTA's routed rows into L2; the shared gate/up items (already in
+//         the ring) then the routed ones -> h
 //     --  grid barrier B
-//     P3  routed h quantised; this CTA's output rows of the K routed down
-//         matrices; weighted combine in rank order + residual -> x
+//     P3  h quantised; this CTA's output rows of the shared and the K routed
+//         down matrices; weighted combine in rank order + residual -> x
 //     --  grid barrier C (between layers)
+//
+// While a layer's routing is decided, the producer also pulls the next
+// layer's routing-independent weights (router row, shared expert rows) into
+// L2.
 //
 // Grid barriers are a global arrival counter polled with acquire loads. Every
 // wait in this kernel (barriers, ring slots, routing hand-off) gives up after
@@ -45,6 +51,8 @@
 namespace glmq {
 
 constexpr int kPCons = 15;                     // consumer warps (+1 producer: 512 threads, 128 regs)
+constexpr int kPGroupWarps = 3;                // consumer warps per group; group g owns ring slot g
+constexpr int kPGroups = kPCons / kPGroupWarps;
 constexpr int kPConsThreads = kPCons * 32;
 constexpr int kPThreads = kPConsThreads + 32;
 constexpr int kPSlots = 5;
@@ -55,9 +63,9 @@ constexpr int kPSlots = 5;
 // up to kPSlots landed tiles, but fewer bytes in flight keep the queueing
 // delay of the kernel's small critical-path loads short.
 constexpr int kPInflight = GLM_P_INFLIGHT;
+static_assert(kPGroups == kPSlots, "one consumer group per ring slot");
 constexpr int kPTile = 16;                     // rows per ring item
-constexpr int kPHsh = 2;                       // 4-group steps of the shared h per consumer warp
-constexpr uint32_t kPollLimit = 1u << 22;
+constexpr int kPHRows = 8;                     // h rows per gate/up item (8 gate rows + their 8 up rows)
 constexpr unsigned kStatBarrier = 4u, kStatFull = 8u, kStatEmpty = 16u, kStatRoute = 32u;
 constexpr unsigned kStatAbort = kStatBarrier | kStatFull | kStatEmpty | kStatRoute;
 
@@ -74,6 +82,7 @@ struct PersistArgs {
     unsigned* status;
     unsigned long long* stats;
     int D, F, E, K, routed_enabled, slot_bytes;
+    int next_layer;     // table index whose shared weights to pull into L2 during the last layer, or -1
 };
 
 __host__ __device__ inline size_t p_take(size_t& o, size_t n) {
@@ -100,7 +109,7 @@ struct PSmem {
         gx = p_take(o, (size_t)(D >> 5) * 4);
         th = p_take(o, (size_t)NS * nchF * kChunkTab * 4);
         gh = p_take(o, (size_t)NS * (F >> 5) * 4);
-        part = p_take(o, (size_t)(K > 4 ? 8 : 4) * kPCons * kPTile * 4);
+        part = p_take(o, (size_t)kPGroups * 2 * kPGroupWarps * kPTile * 4);
         ys = p_take(o, (size_t)NS * kPTile * 4);
         bias = p_take(o, (size_t)E * 4);
         cen = p_take(o, (size_t)E * 8);
@@ -152,8 +161,8 @@ struct PRows {
         rb = (int)((long long)c * D / G);
         re = (int)((long long)(c + 1) * D / G);
     }
-    __device__ int n_sh_tiles() const { return (nsh + kPTile - 1) / kPTile; }
-    __device__ int n_rt_tiles() const { return (nrt + kPTile - 1) / kPTile; }
+    __device__ int n_sh_items() const { return (nsh + kPHRows - 1) / kPHRows; }
+    __device__ int n_rt_items() const { return (nrt + kPHRows - 1) / kPHRows; }
 };
 
 struct GRow {
@@ -162,13 +171,15 @@ struct GRow {
     int hidx = -1;              // index into h, -1 past the end of the tile
 };
 
-// Row j of gate/up tile t, matrix mat (0 gate, 1 up): shared rows, or routed
-// rows once `topk` is known.
+// Row j (0-15) of gate/up item t: rows 0-7 are the gate rows of this CTA's
+// h entries 8t .. 8t+7 (shared rows, or routed rows once `topk` is known),
+// rows 8-15 their up rows, so one MMA tile yields gate and up of an h entry
+// in the same lane.
 __device__ __forceinline__ GRow gate_row(const MoeLayerDev& W, const PersistArgs& a, const PRows& m, bool routed,
-                                         int t, int j, int mat, const int* topk) {
+                                         int t, int j, const int* topk) {
     GRow r;
     const size_t D = (size_t)a.D, sgrp = D >> 5;
-    const int i = t * kPTile + j;
+    const int i = t * kPHRows + (j & (kPHRows - 1)), mat = j >= kPHRows;
     if (!routed) {
         if (i >= m.nsh) return r;
         const int rr = m.sh0 + i;
@@ -191,15 +202,15 @@ __device__ __forceinline__ GRow gate_row(const MoeLayerDev& W, const PersistArgs
 
 // ------------------------------------------------------------ producer
 
-// Producer lanes: gate/up tile t (one matrix) into `buf`: each maximal run of
-// rows with contiguous sources is one q copy and one s copy.
-__device__ void produce_gate_tile(const MoeLayerDev& W, const PersistArgs& a, const PRows& m, bool routed, int t,
-                                  int mat, const int* topk, unsigned char* buf, uint64_t* bar) {
+// Producer lanes: gate/up item t into `buf`: each maximal run of rows with
+// contiguous sources is one q copy and one s copy.
+__device__ void produce_gate_item(const MoeLayerDev& W, const PersistArgs& a, const PRows& m, bool routed, int t,
+                                  const int* topk, unsigned char* buf, uint64_t* bar) {
     const unsigned full = 0xffffffffu;
     const int lane = threadIdx.x & 31;
     const size_t D = (size_t)a.D, sgrp = D >> 5;
     GRow r;
-    if (lane < kPTile) r = gate_row(W, a, m, routed, t, lane, mat, topk);
+    if (lane < kPTile) r = gate_row(W, a, m, routed, t, lane, topk);
     const bool take = lane < kPTile && r.q != nullptr;
     const unsigned tmask = __ballot_sync(full, take);
     const auto pq = reinterpret_cast<const int8_t*>(__shfl_up_sync(full, reinterpret_cast<unsigned long long>(r.q), 1));
@@ -252,6 +263,67 @@ __device__ void produce_down(const MoeLayerDev& W, const PersistArgs& a, const P
     __syncwarp();
 }
 
+// L2 prefetch of [p, p + bytes) (16-byte aligned, multiple of 16): the
+// weights then stream from HBM at full rate while the ring, which holds only
+// a few tiles, is refilled from L2.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+    if (p && bytes) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Producer lanes: this CTA's routed gate, up and down rows of layer W
+// (expert ids in topk) into L2, one range per lane.
+__device__ void prefetch_routed(const MoeLayerDev& W, const PersistArgs& a, const PRows& m, const int* topk) {
+    const int lane = threadIdx.x & 31;
+    if (!a.routed_enabled || !W.gate_q || m.nrt <= 0) return;
+    const size_t D = (size_t)a.D, F = (size_t)a.F;
+    // gate/up: routed rows [rt0, rt0 + nrt) span at most a few slots
+    const int s_first = m.rt0 / a.F, s_last = (m.rt0 + m.nrt - 1) / a.F;
+    for (int sl = s_first; sl <= s_last; ++sl) {
+        const int e = topk[sl];
+        if (e < 0) continue;
+        const int r0 = (m.rt0 > sl * a.F ? m.rt0 : sl * a.F) - sl * a.F;
+        const int r1 = (m.rt0 + m.nrt < (sl + 1) * a.F ? m.rt0 + m.nrt : (sl + 1) * a.F) - sl * a.F;
+        const size_t row = (size_t)e * F + r0, n = (size_t)(r1 - r0);
+        const int base = 4 * (sl - s_first);
+        if (lane == base) prefetch_l2(W.gate_q + row * D, (uint32_t)(n * D));
+        if (lane == base + 1) prefetch_l2(W.gate_s + row * (D >> 5), (uint32_t)(n * (D >> 3)));
+        if (lane == base + 2) prefetch_l2(W.up_q + row * D, (uint32_t)(n * D));
+        if (lane == base + 3) prefetch_l2(W.up_s + row * (D >> 5), (uint32_t)(n * (D >> 3)));
+    }
+    const int n = m.re - m.rb;
+    if (n > 0 && lane >= 16 && lane < 16 + 2 * a.K) {
+        const int k = (lane - 16) >> 1, e = topk[k];
+        if (e >= 0) {
+            const size_t row = (size_t)e * D + m.rb;
+            if ((lane & 1) == 0)
+                prefetch_l2(W.down_q + row * F, (uint32_t)(n * F));
+            else
+                prefetch_l2(W.down_s + row * (F >> 5), (uint32_t)(n * (F >> 3)));
+        }
+    }
+}
+
+// Producer lanes: the routing-independent weights this CTA needs of layer W
+// (router row, shared expert rows, norm and bias) into L2.
+__device__ void prefetch_shared(const MoeLayerDev& W, const PersistArgs& a, const PRows& m, int c) {
+    const int lane = threadIdx.x & 31;
+    const size_t D = (size_t)a.D, F = (size_t)a.F;
+    const int n = m.re - m.rb;
+    // (a table entry whose weights are absent has null pointers: skip those)
+    switch (lane) {
+        case 0: if (W.router && c < a.E) prefetch_l2(W.router + (size_t)c * D, (uint32_t)(D * 4)); break;
+        case 1: if (W.gate_sh_q && m.nsh > 0) prefetch_l2(W.gate_sh_q + (size_t)m.sh0 * D, (uint32_t)(m.nsh * D)); break;
+        case 2: if (W.gate_sh_s && m.nsh > 0) prefetch_l2(W.gate_sh_s + (size_t)m.sh0 * (D >> 5), (uint32_t)(m.nsh * (D >> 3))); break;
+        case 3: if (W.up_sh_q && m.nsh > 0) prefetch_l2(W.up_sh_q + (size_t)m.sh0 * D, (uint32_t)(m.nsh * D)); break;
+        case 4: if (W.up_sh_s && m.nsh > 0) prefetch_l2(W.up_sh_s + (size_t)m.sh0 * (D >> 5), (uint32_t)(m.nsh * (D >> 3))); break;
+        case 5: if (W.down_sh_q && n > 0) prefetch_l2(W.down_sh_q + (size_t)m.rb * F, (uint32_t)(n * F)); break;
+        case 6: if (W.down_sh_s && n > 0) prefetch_l2(W.down_sh_s + (size_t)m.rb * (F >> 5), (uint32_t)(n * (F >> 3))); break;
+        case 7: if (c == 0) prefetch_l2(W.ffn_norm, (uint32_t)(D * 4)); break;
+        case 8: if (c == 0) prefetch_l2(W.router_bias, (uint32_t)(a.E * 4)); break;
+        default: break;
+    }
+}
+
 // ------------------------------------------------------------ consumers
 
 struct PCtx {
@@ -278,8 +350,8 @@ __device__ __forceinline__ void cons_wait(const PCtx& P, uint32_t it) {
     }
 }
 
-// A consumer warp is done reading item `it`: one arrival per warp hands the
-// slot back once all kPCons warps are done.
+// A consumer warp of the slot's group is done reading item `it`: one arrival
+// per warp hands the slot back once the group's kPGroupWarps warps are done.
 __device__ __forceinline__ void cons_release(const PCtx& P, uint32_t it) {
     __syncwarp();
     if ((threadIdx.x & 31) == 0) mbar_arrive(&P.empty[it % kPSlots]);
@@ -295,7 +367,8 @@ __device__ bool grid_sync(const PersistArgs& a, const PCtx& P, unsigned& nbar, i
         __threadfence();
         if (!*P.abort_flag) atomicAdd(a.bar, 1u);
         const unsigned target = nbar * gridDim.x;
-        for (uint32_t i = 0; i < kPollLimit && !*P.abort_flag; ++i) {
+        const uint64_t t0 = global_ns();
+        for (uint32_t i = 0; !*P.abort_flag && global_ns() - t0 < kWaitNs; ++i) {
             if (ld_acquire_gpu(a.bar) >= target) {
                 ok = 1;
                 break;
@@ -362,7 +435,7 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
     if (tid == 0) {
         for (int i = 0; i < kPSlots; ++i) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], kPCons);
+            mbar_init(&empty[i], kPGroupWarps);
         }
         mbar_init(route_ready, 1);
         *s_abort = 0;
@@ -373,26 +446,25 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
     // ------------------------------------------------------------- producer
     if (warp == kPCons) {
         uint32_t it = 0;
+        // Lane 0 waits (the hardware suspends it until the phase completes);
+        // gives up after kWaitNs or when the consumers abort.
+        auto wait_phase = [&](uint64_t* bar, uint32_t parity) -> bool {
+            bool ok = false;
+            if (lane == 0) {
+                ok = mbar_try_wait(bar, parity);
+                const uint64_t t0 = global_ns();
+                while (!ok && !*s_abort && global_ns() - t0 < kWaitNs)
+                    ok = mbar_try_wait_sleep(bar, parity, kSuspendNs);
+            }
+            return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        };
         // Ring slot of item i is free (its previous item was released) and
         // at most kPInflight items are in flight.
         auto acquire = [&](uint32_t i) -> bool {
-            if (i >= (uint32_t)kPSlots) {
-                const uint32_t slot = i % kPSlots, par = ((i / kPSlots) - 1) & 1u;
-                bool ok = false;
-                for (uint32_t k = 0; k < kPollLimit && !ok; ++k) {
-                    ok = mbar_try_wait(&empty[slot], par);
-                    if (*s_abort) return false;
-                }
-                if (!ok) return false;
-            }
+            if (i >= (uint32_t)kPSlots && !wait_phase(&empty[i % kPSlots], ((i / kPSlots) - 1) & 1u)) return false;
             if (kPInflight < kPSlots && i >= (uint32_t)kPInflight) {
                 const uint32_t j = i - kPInflight;
-                bool ok = false;
-                for (uint32_t k = 0; k < kPollLimit && !ok; ++k) {
-                    ok = mbar_try_wait(&full[j % kPSlots], (j / kPSlots) & 1u);
-                    if (*s_abort) return false;
-                }
-                if (!ok) return false;
+                if (!wait_phase(&full[j % kPSlots], (j / kPSlots) & 1u)) return false;
             }
             return true;
         };
@@ -400,7 +472,7 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
         for (int li = 0; li < a.n_layers && alive; ++li) {
             const MoeLayerDev W = a.layers[a.first + li];
             // layer constants: ffn_norm and the router bias
-            if (!(alive = __all_sync(0xffffffffu, acquire(it)))) break;
+            if (!(alive = acquire(it))) break;
             if (lane == 0) {
                 uint64_t* bar = &full[it % kPSlots];
                 unsigned char* buf = slot_buf(P, it);
@@ -411,7 +483,7 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
             __syncwarp();
             ++it;
             if (c < E) {  // this CTA's router row
-                if (!(alive = __all_sync(0xffffffffu, acquire(it)))) break;
+                if (!(alive = acquire(it))) break;
                 if (lane == 0) {
                     uint64_t* bar = &full[it % kPSlots];
                     mbar_arrive_expect_tx(bar, (uint32_t)(D * 4));
@@ -420,36 +492,35 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
                 __syncwarp();
                 ++it;
             }
-            for (int t = 0; t < m.n_sh_tiles() && alive; ++t)
-                for (int mat = 0; mat < 2; ++mat) {
-                    if (!(alive = __all_sync(0xffffffffu, acquire(it)))) break;
-                    produce_gate_tile(W, a, m, false, t, mat, nullptr, slot_buf(P, it), &full[it % kPSlots]);
-                    ++it;
-                }
-            if (!alive) break;
-            // the shared down rows do not depend on routing either
-            if (!(alive = __all_sync(0xffffffffu, acquire(it)))) break;
-            produce_down(W, a, m, K, s_topk, slot_buf(P, it), &full[it % kPSlots]);
-            ++it;
-            // routed rows need this layer's expert ids
-            bool got = false;
-            for (uint32_t k = 0; k < kPollLimit && !got; ++k) {
-                got = mbar_try_wait(route_ready, (uint32_t)li & 1u);
-                if (*s_abort) break;
+            for (int t = 0; t < m.n_sh_items() && alive; ++t) {
+                if (!(alive = acquire(it))) break;
+                produce_gate_item(W, a, m, false, t, nullptr, slot_buf(P, it), &full[it % kPSlots]);
+                ++it;
             }
-            if (!(alive = __all_sync(0xffffffffu, got))) {
+            if (!alive) break;
+            // While this layer's routing is decided HBM is nearly idle: pull
+            // the next layer's routing-independent weights into L2.
+            const int nl = li + 1 < a.n_layers ? a.first + li + 1 : a.next_layer;
+            if (nl >= 0) prefetch_shared(a.layers[nl], a, m, c);
+            // routed rows need this layer's expert ids
+            if (!(alive = wait_phase(route_ready, (uint32_t)li & 1u))) {
                 if (lane == 0) atomicOr(a.status, kStatRoute);
                 break;
             }
-            for (int t = 0; t < m.n_rt_tiles() && alive; ++t)
-                for (int mat = 0; mat < 2; ++mat) {
-                    if (!(alive = __all_sync(0xffffffffu, acquire(it)))) break;
-                    produce_gate_tile(W, a, m, true, t, mat, s_topk, slot_buf(P, it), &full[it % kPSlots]);
-                    ++it;
-                }
-            for (int slot = 0; slot < K && alive; ++slot) {
-                if (!(alive = __all_sync(0xffffffffu, acquire(it)))) break;
-                produce_down(W, a, m, slot, s_topk, slot_buf(P, it), &full[it % kPSlots]);
+            // The first routed items go out first; then all routed rows of
+            // this CTA go to L2 at once (HBM at full rate) and the ring
+            // refills from L2.
+            for (int t = 0; t < m.n_rt_items() && alive; ++t) {
+                if (t == kPInflight) prefetch_routed(W, a, m, s_topk);
+                if (!(alive = acquire(it))) break;
+                produce_gate_item(W, a, m, true, t, s_topk, slot_buf(P, it), &full[it % kPSlots]);
+                ++it;
+            }
+            if (m.n_rt_items() <= kPInflight) prefetch_routed(W, a, m, s_topk);
+            // down rows: shared expert first, then the routed slots in rank order
+            for (int q = 0; q <= K && alive; ++q) {
+                if (!(alive = acquire(it))) break;
+                produce_down(W, a, m, q == 0 ? K : q - 1, s_topk, slot_buf(P, it), &full[it % kPSlots]);
                 ++it;
             }
         }
@@ -467,28 +538,35 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
 
     // ------------------------------------------------------------ consumers
     const int gid = lane >> 2, t4 = lane & 3;
+    const int grp = warp / kPGroupWarps, gw = warp % kPGroupWarps;
     const int boff = b_frag_offset(lane);
     const int4 z4 = make_int4(0, 0, 0, 0);
     const float2 z2 = make_float2(0.f, 0.f);
-    constexpr int kPart = kPCons * kPTile;
+    constexpr int kPart = kPGroupWarps * kPTile;
+    float* gpart = part + (size_t)grp * 2 * kPart;  // this group's two partial buffers
     uint32_t it = 0;
     unsigned nbar = 0;
+    int nlocal = 0;  // items this group has processed (parity picks the partial buffer)
     auto sync = []() { cons_sync(); };
+    auto grp_sync = [&]() { asm volatile("bar.sync %0, %1;\n" ::"r"(2 + grp), "n"(kPGroupWarps * 32) : "memory"); };
 
-    // A ring item holds 16 rows (q, then scales). Every consumer warp dots
-    // its share of the 64-column chunks of the rows with the activation
-    // planes, hands the slot back, and leaves its row partials in a `part`
-    // buffer; after one block barrier threads 0-15 add the warps' partials of
-    // their row. Items that belong together (gate and up of a tile, the K
-    // routed down matrices) are waited for and computed in one pass, so a
-    // warp has several independent MMA chains and the group one barrier.
-    auto item_rows = [&](uint32_t item, const int8_t* planes, const float* tab, int cols, bool v0, bool v1,
-                         float* pt) {
+    // Items that every consumer reads (layer constants, router row): after
+    // a block barrier the slot's group hands the slot back.
+    auto release_shared_item = [&](uint32_t item) {
+        if (grp == (int)(item % kPSlots)) cons_release(P, item);
+    };
+
+    // A weight item is processed by the group that owns its ring slot: each
+    // of the group's warps dots its third of the 64-column chunks of the 16
+    // rows with the activation planes and hands the slot back; after the
+    // group barrier one warp adds the three partials of every row.
+    auto group_rows = [&](uint32_t item, const int8_t* planes, const float* tab, int cols, bool v0, bool v1) {
+        cons_wait(P, item);
         const int nch = cols >> 6;
         const int8_t* qb = reinterpret_cast<const int8_t*>(slot_buf(P, item));
         const unsigned char* sb = slot_buf(P, item) + kPTile * cols;
         float acc0 = 0.f, acc1 = 0.f;
-        for (int j = warp * nch / kPCons; j < (warp + 1) * nch / kPCons; ++j) {
+        for (int j = gw * nch / kPGroupWarps; j < (gw + 1) * nch / kPGroupWarps; ++j) {
             const int off = j * kChunkCols + 16 * t4;
             const int4 b4 = boff >= 0 ? lds16(planes + j * kChunkBytes + boff) : z4;
             const float2 tb = *reinterpret_cast<const float2*>(tab + j * kChunkTab + 2 * t4);
@@ -501,55 +579,45 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
         cons_release(P, item);
         acc0 = quad_sum(acc0);
         acc1 = quad_sum(acc1);
+        float* pt = gpart + (nlocal & 1) * kPart;
         if (t4 == 0) {
-            pt[warp * kPTile + gid] = acc0;
-            pt[warp * kPTile + gid + 8] = acc1;
+            pt[gw * kPTile + gid] = acc0;
+            pt[gw * kPTile + gid + 8] = acc1;
         }
+        ++nlocal;
+        grp_sync();
+        return static_cast<const float*>(pt);
     };
-    auto row_total = [&](const float* pt) {
+    auto row_total = [&](const float* pt, int r) {
         float tot = 0.f;
 #pragma unroll
-        for (int w = 0; w < kPCons; ++w) tot += pt[w * kPTile + tid];
+        for (int w = 0; w < kPGroupWarps; ++w) tot += pt[w * kPTile + r];
         return tot;
     };
 
-    // Gate/up tile t (its gate item, then its up item) -> 16 entries of h,
-    // h = silu(gate) * up (infer.c:1184-1188, 1197-1201). part buffers
-    // 2(t&1) and 2(t&1)+1: the next tile writes the other pair.
-    auto gate_tile = [&](const MoeLayerDev& W, bool routed, int t) {
+    // Gate/up item t -> 8 entries of h, h = silu(gate) * up
+    // (infer.c:1184-1188, 1197-1201).
+    auto gate_item = [&](const MoeLayerDev& W, bool routed, int t, uint32_t item) {
         const int* tk = routed ? s_topk : nullptr;
-        float* pg = part + (size_t)(2 * (t & 1)) * kPart;
-        float* pu = pg + kPart;
-        cons_wait(P, it);
-        cons_wait(P, it + 1);
-        item_rows(it, px, tx, D, gate_row(W, a, m, routed, t, gid, 0, tk).q != nullptr,
-                  gate_row(W, a, m, routed, t, gid + 8, 0, tk).q != nullptr, pg);
-        item_rows(it + 1, px, tx, D, gate_row(W, a, m, routed, t, gid, 1, tk).q != nullptr,
-                  gate_row(W, a, m, routed, t, gid + 8, 1, tk).q != nullptr, pu);
-        it += 2;
-        cons_sync();
-        if (tid < kPTile) {
-            const int hidx = gate_row(W, a, m, routed, t, tid, 0, tk).hidx;
-            if (hidx >= 0) a.h[hidx] = silu_p(row_total(pg)) * row_total(pu);
+        const float* pt = group_rows(item, px, tx, D, gate_row(W, a, m, routed, t, gid, tk).q != nullptr,
+                                     gate_row(W, a, m, routed, t, gid + 8, tk).q != nullptr);
+        if (gw == 0 && lane < kPHRows) {
+            const int hidx = gate_row(W, a, m, routed, t, lane, tk).hidx;
+            if (hidx >= 0) a.h[hidx] = silu_p(row_total(pt, lane)) * row_total(pt, lane + kPHRows);
         }
     };
 
-    // This CTA's output rows of the down matrices of slots [s0, s0 + ns)
-    // (slot K = shared) -> ys[slot]; part buffer b0 + i for the i-th.
-    auto down_items = [&](const MoeLayerDev& W, int s0, int ns, int b0) {
+    // This CTA's output rows of down matrix `slot` (K = shared) -> ys[slot].
+    auto down_item = [&](const MoeLayerDev& W, int slot, uint32_t item) {
         const int n = m.re - m.rb;
-        for (int i = 0; i < ns; ++i) cons_wait(P, it + i);
-        for (int i = 0; i < ns; ++i) {
-            const int slot = s0 + i;
-            const bool live = slot == K || (a.routed_enabled && W.down_q && s_topk[slot] >= 0);
-            item_rows(it + i, ph + (size_t)slot * nchF * kChunkBytes, th + (size_t)slot * nchF * kChunkTab, F,
-                      live && gid < n, live && gid + 8 < n, part + (size_t)(b0 + i) * kPart);
-        }
-        it += ns;
-        cons_sync();
-        if (tid < kPTile)
-            for (int i = 0; i < ns; ++i) ys[(s0 + i) * kPTile + tid] = row_total(part + (size_t)(b0 + i) * kPart);
+        const bool live = slot == K || (a.routed_enabled && W.down_q && s_topk[slot] >= 0);
+        const float* pt = group_rows(item, ph + (size_t)slot * nchF * kChunkBytes, th + (size_t)slot * nchF * kChunkTab,
+                                     F, live && gid < n, live && gid + 8 < n);
+        if (gw == 0 && lane < kPTile) ys[slot * kPTile + lane] = row_total(pt, lane);
     };
+
+    // First item index >= from that belongs to this group.
+    auto first_mine = [&](uint32_t from) { return from + (uint32_t)((grp - (int)(from % kPSlots) + kPSlots) % kPSlots); };
 
     for (int li = 0; li < a.n_layers; ++li) {
         const MoeLayerDev W = a.layers[a.first + li];
@@ -585,33 +653,28 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
                 const int i = tid + u * kPConsThreads;
                 if (i < D) xs[i] = __fmul_rn(__fmul_rn(xr[u], inv), norm[i]);
             }
-            cons_release(P, it);
-            ++it;
         }
-        cons_sync();  // xs complete before any thread quantises it
+        cons_sync();  // xs complete before any thread quantises it; the constants are read
+        release_shared_item(it);
+        ++it;
         quantize_planes_part<false>(xs, D, px, gx, tx, tid, kPConsThreads, sync);
 
-        // ---- P1: router logit of expert c; shared-expert gate/up rows
+        // ---- P1: router logit of expert c (CTAs c < E)
         if (c < E) {
             cons_wait(P, it);
             double C = 0.0, B = 0.0;
             block_logit_bound_rows(reinterpret_cast<const float*>(slot_buf(P, it)), xs, D, tid, kPConsThreads, rscr,
                                    sync, C, B);
-            cons_release(P, it);
+            release_shared_item(it);  // the row was read before the function's first barrier
             ++it;
             if (tid == 0) {
                 __stcg(a.center + c, C);
                 __stcg(a.bound + c, B);
             }
         }
-        for (int t = 0; t < m.n_sh_tiles(); ++t) gate_tile(W, false, t);
         if (!grid_sync(a, P, nbar, tid, s_ok)) return;
 
-        // ---- P2: routing (every CTA, identical); shared down; routed gate/up
-        // The shared expert's h is complete: load this warp's groups of it
-        // now, ahead of the routed weight stream the selection releases.
-        float4 hv[kPHsh];
-        q4_load<true, kPHsh>(a.h + (size_t)K * F, F >> 5, warp, kPCons, lane, hv);
+        // ---- P2: routing (every CTA, identical); shared and routed gate/up
         for (int i = tid; i < E; i += kPConsThreads) {
             s_cen[i] = ldcg_f64(a.center + i);
             s_bnd[i] = ldcg_f64(a.bound + i);
@@ -624,20 +687,25 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
             if (a.topk_out) a.topk_out[li * K + tid] = s_topk[tid];
             if (a.topkw_out) a.topkw_out[li * K + tid] = s_topw[tid];
         }
-        // xs is dead from here on; its space holds the h digit planes.
-        q4_store<kPHsh>(hv, F >> 5, warp, kPCons, lane, ph + (size_t)K * nchF * kChunkBytes, gh + (size_t)K * (F >> 5));
-        cons_sync();
-        fill_sxtab(gh + (size_t)K * (F >> 5), th + (size_t)K * nchF * kChunkTab, nchF, tid, kPConsThreads);
-        cons_sync();
-        down_items(W, K, 1, 2);  // part buffer 2: routed tile 0 uses 0 and 1
-        for (int t = 0; t < m.n_rt_tiles(); ++t) gate_tile(W, true, t);
+        // Every group takes the items in its ring slot; the shared items are
+        // already in the ring and fill the wait for the first routed rows.
+        const int nsh = m.n_sh_items(), nitems = nsh + m.n_rt_items();
+        for (uint32_t item = first_mine(it); item < it + (uint32_t)nitems; item += kPSlots) {
+            const int u = (int)(item - it);
+            gate_item(W, u >= nsh, u >= nsh ? u - nsh : u, item);
+        }
+        it += (uint32_t)nitems;
         if (!grid_sync(a, P, nbar, tid, s_ok)) return;
 
-        // ---- P3: routed h -> digit planes; routed down rows; combine
-        quantize_planes_part<true>(a.h, K * F, ph, gh, th, tid, kPConsThreads, sync);
-        // at most 4 items waited for at once (the ring holds kPSlots = 5);
-        // consecutive batches alternate part buffers 0-3 and 4-7
-        for (int s0 = 0, b = 0; s0 < K; s0 += 4, b ^= 4) down_items(W, s0, K - s0 < 4 ? K - s0 : 4, b);
+        // ---- P3: h -> digit planes (xs is dead); down rows; combine
+        quantize_planes_part<true>(a.h, (K + 1) * F, ph, gh, th, tid, kPConsThreads, sync);
+        // down items in the order shared, routed 0 .. K-1; each group takes its own
+        for (uint32_t item = first_mine(it); item < it + (uint32_t)(K + 1); item += kPSlots) {
+            const int q = (int)(item - it);
+            down_item(W, q == 0 ? K : q - 1, item);
+        }
+        it += (uint32_t)(K + 1);
+        cons_sync();  // every group's ys written
         const int n = m.re - m.rb;
         if (tid < n) {
             // infer.c:1175,1192 then 1212-1214: acc += (1.8 w_k) y_k in rank
@@ -658,7 +726,7 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
 
 cudaError_t persistent_check(const MoeDims& d, int num_sms, size_t* smem_out) {
     if (d.K < 1 || d.K > kMaxTopK || d.K > d.E || d.E > num_sms || d.E % 4 || d.gs != 32 || d.D % 128 ||
-        d.D > 2048 || d.F % 128 || d.F > 128 * kPCons * kPHsh || (d.D + kPTile - 1) / kPTile > num_sms)
+        d.D > 2048 || d.F % 128 || (d.D + kPTile - 1) / kPTile > num_sms)
         return cudaErrorInvalidValue;
     const int slot = p_slot_bytes(d.D, d.F, d.E);
     const size_t smem = PSmem(d.D, d.F, d.E, d.K, slot).total;
@@ -669,7 +737,7 @@ cudaError_t persistent_check(const MoeDims& d, int num_sms, size_t* smem_out) {
 
 cudaError_t launch_moe_persistent(const MoeLayerDev* layers_dev, int first, int n_layers, const MoeDims& d,
                                   const MoeScratch& s, float* x, int32_t* topk_out, float* topkw_out,
-                                  int routed_enabled, int num_sms, cudaStream_t stream) {
+                                  int routed_enabled, int num_sms, cudaStream_t stream, int next_layer) {
     size_t smem = 0;
     cudaError_t err = persistent_check(d, num_sms, &smem);
     if (err != cudaSuccess) return err;
@@ -681,8 +749,10 @@ cudaError_t launch_moe_persistent(const MoeLayerDev* layers_dev, int first, int 
         cap = smem;
     }
     if ((err = cudaMemsetAsync(s.grid_bar, 0, sizeof(unsigned int), stream))) return err;
-    PersistArgs a{layers_dev, first, n_layers, x, s.h, s.center, s.bound, topk_out, topkw_out, s.grid_bar, s.status,
-                  s.stats, d.D, d.F, d.E, d.K, routed_enabled, p_slot_bytes(d.D, d.F, d.E)};
+    PersistArgs a{layers_dev, first,    n_layers, x,           s.h,       s.center,
+                  s.bound,    topk_out, topkw_out, s.grid_bar, s.status, s.stats,
+                  d.D,        d.F,      d.E,       d.K,        routed_enabled,
+                  p_slot_bytes(d.D, d.F, d.E), next_layer};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(num_sms);
     cfg.blockDim = dim3(kPThreads);

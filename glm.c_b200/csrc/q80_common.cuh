@@ -326,14 +326,35 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait: every spin gives up after kWaitPolls polls (each poll may
-// itself suspend for a hardware-defined slice), so a copy that never lands
-// becomes an error status instead of a hung GPU.
-constexpr uint32_t kWaitPolls = 1u << 22;
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+    return t;
+}
+
+// try_wait that lets the hardware suspend the thread (up to `hint_ns`) until
+// the phase completes, instead of spinning on the barrier and taking shared
+// memory issue slots from the threads doing the work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: gives up after kWaitNs of wall time (a copy that never lands
+// becomes an error status instead of a hung GPU).
+constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s
+constexpr uint32_t kSuspendNs = 100000;      // 100 us per try
 
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
-    for (uint32_t i = 0; i < kWaitPolls; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    while (global_ns() - t0 < kWaitNs)
+        if (mbar_try_wait_sleep(bar, parity, kSuspendNs)) return true;
     return false;
 }
 
