@@ -57,11 +57,11 @@ constexpr int kPConsThreads = kPCons * 32;
 constexpr int kPThreads = kPConsThreads + 32;
 constexpr int kPSlots = 5;
 #ifndef GLM_P_INFLIGHT
-#define GLM_P_INFLIGHT 3
+#define GLM_P_INFLIGHT 5
 #endif
-// At most this many ring items in flight (issued, not landed): the ring holds
-// up to kPSlots landed tiles, but fewer bytes in flight keep the queueing
-// delay of the kernel's small critical-path loads short.
+// At most this many ring items in flight (issued, not landed); below kPSlots
+// it trades ring throughput for shorter queues behind the kernel's small
+// critical-path loads (measured best: no limit, with the L2 prefetches).
 constexpr int kPInflight = GLM_P_INFLIGHT;
 static_assert(kPGroups == kPSlots, "one consumer group per ring slot");
 constexpr int kPTile = 16;                     // rows per ring item
@@ -270,13 +270,13 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
     if (p && bytes) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p), "r"(bytes) : "memory");
 }
 
-// Producer lanes: this CTA's routed gate, up and down rows of layer W
-// (expert ids in topk) into L2, one range per lane.
-__device__ void prefetch_routed(const MoeLayerDev& W, const PersistArgs& a, const PRows& m, const int* topk) {
+// Producer lanes: this CTA's routed gate and up rows of layer W (expert ids
+// in topk) into L2, one range per lane.
+__device__ void prefetch_routed_gate_up(const MoeLayerDev& W, const PersistArgs& a, const PRows& m, const int* topk) {
     const int lane = threadIdx.x & 31;
     if (!a.routed_enabled || !W.gate_q || m.nrt <= 0) return;
     const size_t D = (size_t)a.D, F = (size_t)a.F;
-    // gate/up: routed rows [rt0, rt0 + nrt) span at most a few slots
+    // routed rows [rt0, rt0 + nrt) span at most a few slots
     const int s_first = m.rt0 / a.F, s_last = (m.rt0 + m.nrt - 1) / a.F;
     for (int sl = s_first; sl <= s_last; ++sl) {
         const int e = topk[sl];
@@ -290,17 +290,21 @@ __device__ void prefetch_routed(const MoeLayerDev& W, const PersistArgs& a, cons
         if (lane == base + 2) prefetch_l2(W.up_q + row * D, (uint32_t)(n * D));
         if (lane == base + 3) prefetch_l2(W.up_s + row * (D >> 5), (uint32_t)(n * (D >> 3)));
     }
+}
+
+// Producer lanes: this CTA's output rows of the K routed down matrices into L2.
+__device__ void prefetch_routed_down(const MoeLayerDev& W, const PersistArgs& a, const PRows& m, const int* topk) {
+    const int lane = threadIdx.x & 31;
     const int n = m.re - m.rb;
-    if (n > 0 && lane >= 16 && lane < 16 + 2 * a.K) {
-        const int k = (lane - 16) >> 1, e = topk[k];
-        if (e >= 0) {
-            const size_t row = (size_t)e * D + m.rb;
-            if ((lane & 1) == 0)
-                prefetch_l2(W.down_q + row * F, (uint32_t)(n * F));
-            else
-                prefetch_l2(W.down_s + row * (F >> 5), (uint32_t)(n * (F >> 3)));
-        }
-    }
+    if (!a.routed_enabled || !W.down_q || n <= 0 || lane >= 2 * a.K) return;
+    const size_t D = (size_t)a.D, F = (size_t)a.F;
+    const int e = topk[lane >> 1];
+    if (e < 0) return;
+    const size_t row = (size_t)e * D + m.rb;
+    if ((lane & 1) == 0)
+        prefetch_l2(W.down_q + row * F, (uint32_t)(n * F));
+    else
+        prefetch_l2(W.down_s + row * (F >> 5), (uint32_t)(n * (F >> 3)));
 }
 
 // Producer lanes: the routing-independent weights this CTA needs of layer W
@@ -507,16 +511,19 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
                 if (lane == 0) atomicOr(a.status, kStatRoute);
                 break;
             }
-            // The first routed items go out first; then all routed rows of
-            // this CTA go to L2 at once (HBM at full rate) and the ring
-            // refills from L2.
-            for (int t = 0; t < m.n_rt_items() && alive; ++t) {
-                if (t == kPInflight) prefetch_routed(W, a, m, s_topk);
+            // The first routed items go out first; then the CTA's remaining
+            // routed gate/up rows go to L2 at once (HBM at full rate) and the
+            // ring refills from L2; the down rows follow once every gate/up
+            // item is issued, so they do not slow the gate/up stream.
+            const int ngate = m.n_rt_items();
+            for (int t = 0; t < ngate && alive; ++t) {
+                if (t == 3) prefetch_routed_gate_up(W, a, m, s_topk);
                 if (!(alive = acquire(it))) break;
                 produce_gate_item(W, a, m, true, t, s_topk, slot_buf(P, it), &full[it % kPSlots]);
                 ++it;
             }
-            if (m.n_rt_items() <= kPInflight) prefetch_routed(W, a, m, s_topk);
+            if (!alive) break;
+            prefetch_routed_down(W, a, m, s_topk);
             // down rows: shared expert first, then the routed slots in rank order
             for (int q = 0; q <= K && alive; ++q) {
                 if (!(alive = acquire(it))) break;
