@@ -30,6 +30,54 @@ struct MatvecEntry {
     int rows = 0, dim = 0, gs = 0;
 };
 
+// Non-MoE weights of one decoder layer (LayerAttnWeights, model.h:46-62).
+struct AttnLayer {
+    const float* attn_norm = nullptr;
+    const float* q_a_norm = nullptr;
+    const float* kv_a_norm = nullptr;
+    const int8_t* q_a_q = nullptr;
+    const float* q_a_s = nullptr;
+    const int8_t* q_b_q = nullptr;
+    const float* q_b_s = nullptr;
+    const int8_t* kv_a_q = nullptr;
+    const float* kv_a_s = nullptr;
+    const int8_t* k_b_q = nullptr;
+    const float* k_b_s = nullptr;
+    const int8_t* v_b_q = nullptr;
+    const float* v_b_s = nullptr;
+    const int8_t* attn_out_q = nullptr;
+    const float* attn_out_s = nullptr;
+    std::vector<void*> owned;
+    bool ready = false;
+};
+
+// The rest of the decoder (Runtime fields, model.h:87-124) and its device
+// buffers (RunState, model.h:126-160).
+struct Model {
+    bool inited = false;
+    GlmCudaModelDims d{};
+    const float* output_norm = nullptr;
+    const int8_t* tok_q = nullptr;
+    const float* tok_s = nullptr;
+    const int8_t* out_q = nullptr;
+    const float* out_s = nullptr;
+    const float* l0_norm = nullptr;
+    const int8_t* l0_gate_q = nullptr;
+    const float* l0_gate_s = nullptr;
+    const int8_t* l0_up_q = nullptr;
+    const float* l0_up_s = nullptr;
+    const int8_t* l0_down_q = nullptr;
+    const float* l0_down_s = nullptr;
+    std::vector<void*> owned_globals;
+    bool globals_ready = false;
+    std::vector<AttnLayer> attn;
+    float *x = nullptr, *xn = nullptr, *q_a = nullptr, *q_full = nullptr, *kv_a = nullptr, *att = nullptr,
+          *ff_gate = nullptr, *ff_up = nullptr, *logits = nullptr, *cache_comp = nullptr, *cache_pe = nullptr;
+    int *pos = nullptr, *token = nullptr, *argmax = nullptr, *prompt = nullptr, *out_ids = nullptr;
+    int prompt_cap = 0, out_cap = 0;
+    int* io_host = nullptr;  // pinned [2]: token, pos
+};
+
 struct State {
     bool inited = false;
     int device = 0;
@@ -52,6 +100,7 @@ struct State {
     glmq::MoeLayerDev* layers_dev = nullptr;  // device copy of every slot's pointers (persistent kernel)
     bool persistent_ok = false;               // sizes fit the persistent kernel on this device
     int decode_path = GLM_CUDA_PATH_AUTO;
+    Model m;
 };
 
 State g;
@@ -92,7 +141,21 @@ void release_layer(LayerSlot& L) {
     L.ready = false;
 }
 
+void release_model() {
+    Model& m = g.m;
+    for (auto& A : m.attn)
+        for (void* p : A.owned) cudaFree(p);
+    for (void* p : m.owned_globals) cudaFree(p);
+    void* bufs[] = {m.x,     m.xn,        m.q_a,      m.q_full, m.kv_a,   m.att,    m.ff_gate, m.ff_up,
+                    m.logits, m.cache_comp, m.cache_pe, m.pos,    m.token,  m.argmax, m.prompt,  m.out_ids};
+    for (void* p : bufs)
+        if (p) cudaFree(p);
+    if (m.io_host) cudaFreeHost(m.io_host);
+    g.m = Model{};
+}
+
 void release_all() {
+    release_model();
     for (auto& L : g.layers) release_layer(L);
     g.layers.clear();
     for (auto& kv : g.mv_cache) {
@@ -228,11 +291,10 @@ int moe_enqueue(int layer, float* x_dev, int n_tokens, int32_t* idx_dev, float* 
 
 void glmq::set_last_error(const char* msg) { g_err = msg ? msg : ""; }
 
-extern "C" {
+namespace {
 
-int glm_cuda_init(int device, int dim, int moe_ffn_dim, int n_routed_experts, int n_experts_used, int group_size,
-                  int n_layers) {
-    std::lock_guard<std::mutex> lk(g_mu);
+int init_locked(int device, int dim, int moe_ffn_dim, int n_routed_experts, int n_experts_used, int group_size,
+                int n_layers) {
     if (g.inited) release_all();
     if (dim <= 0 || dim % 128 || moe_ffn_dim <= 0 || moe_ffn_dim % 64)
         return fail(GLM_CUDA_ERR_ARG, "unsupported dims dim=%d moe_ffn_dim=%d (need dim%%128==0, ffn%%64==0)", dim,
@@ -276,6 +338,16 @@ int glm_cuda_init(int device, int dim, int moe_ffn_dim, int n_routed_experts, in
     g.inited = true;
     g_err.clear();
     return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int glm_cuda_init(int device, int dim, int moe_ffn_dim, int n_routed_experts, int n_experts_used, int group_size,
+                  int n_layers) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    return init_locked(device, dim, moe_ffn_dim, n_routed_experts, n_experts_used, group_size, n_layers);
 }
 
 int glm_cuda_upload_moe_layer(int layer, const float* ffn_norm, const float* gate_inp, const float* exp_probs_b,
@@ -532,6 +604,329 @@ void glm_cuda_free(void) {
         cudaStreamSynchronize(g.stream);
         release_all();
     }
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------ full decoder
+
+namespace {
+
+template <typename T>
+int put(std::vector<void*>& owned, bool copy, const T* src, size_t count, const T** out) {
+    *out = nullptr;
+    if (!src) return 0;
+    if (!copy) {
+        if (reinterpret_cast<uintptr_t>(src) & 15u) return fail(GLM_CUDA_ERR_ARG, "device weights must be 16-byte aligned");
+        *out = src;
+        return 0;
+    }
+    T* d = nullptr;
+    if (int rc = dev_alloc(&d, count)) return rc;
+    owned.push_back(d);
+    CUDA_TRY(cudaMemcpyAsync(d, src, count * sizeof(T), cudaMemcpyHostToDevice, g.stream));
+    *out = d;
+    return 0;
+}
+
+int check_model() {
+    if (!g.inited || !g.m.inited) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_model_init has not been called");
+    if (!g.m.globals_ready) return fail(GLM_CUDA_ERR_STATE, "model globals (embedding, LM head, layer-0 FFN) missing");
+    for (int l = 0; l < g.m.d.n_layers; ++l) {
+        if (!g.m.attn[l].ready) return fail(GLM_CUDA_ERR_STATE, "attention layer %d has no weights", l);
+        if (l > 0 && !g.layers[l].ready) return fail(GLM_CUDA_ERR_STATE, "MoE layer %d has no weights", l);
+    }
+    return 0;
+}
+
+#define LAUNCH_TRY(call)                                                                              \
+    do {                                                                                              \
+        cudaError_t e_ = (call);                                                                      \
+        if (e_ != cudaSuccess) return fail(GLM_CUDA_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+// One decode step at the device-resident (token, pos): glm_cpu_forward_token
+// (infer.c:1767-1901) with every linear layer on the GPU; logits and the
+// argmax land in device memory.
+int enqueue_step(cudaStream_t st) {
+    Model& m = g.m;
+    const GlmCudaModelDims& d = m.d;
+    const int D = d.dim, gs = d.group_size, ns = g.num_sms;
+    const int routed = routed_disabled_by_env() ? 0 : 1;
+    const float kq_scale = 1.0f / sqrtf((float)d.head_k_dim);
+    LAUNCH_TRY(glmq::launch_embed(m.tok_q, m.tok_s, m.token, m.x, D, gs, st));
+    for (int l = 0; l < d.n_layers; ++l) {
+        const AttnLayer& A = m.attn[l];
+        // MLA attention (infer.c:978-1065)
+        LAUNCH_TRY(glmq::launch_rmsnorm(m.x, A.attn_norm, m.xn, D, st));
+        LAUNCH_TRY(glmq::launch_q80_matvec(A.q_a_q, A.q_a_s, m.xn, m.q_a, d.q_lora_rank, D, gs, ns, st));
+        LAUNCH_TRY(glmq::launch_rmsnorm(m.q_a, A.q_a_norm, m.q_a, d.q_lora_rank, st));
+        LAUNCH_TRY(glmq::launch_q80_matvec(A.q_b_q, A.q_b_s, m.q_a, m.q_full, d.n_heads * d.head_k_dim, d.q_lora_rank,
+                                           gs, ns, st));
+        LAUNCH_TRY(glmq::launch_q80_matvec(A.kv_a_q, A.kv_a_s, m.xn, m.kv_a, d.kv_lora_rank + d.rope_dim, D, gs, ns, st));
+        float* comp = m.cache_comp + (size_t)l * d.cache_cap * d.kv_lora_rank;
+        float* pe = m.cache_pe + (size_t)l * d.cache_cap * d.rope_dim;
+        LAUNCH_TRY(glmq::launch_kv_cache_write(m.kv_a, A.kv_a_norm, comp, pe, m.pos, d.kv_lora_rank, d.rope_dim, st));
+        glmq::MlaArgs ma{m.q_full, comp, pe, A.k_b_q, A.k_b_s, A.v_b_q, A.v_b_s, m.att, m.pos,
+                         d.qk_nope_dim, d.rope_dim, d.head_k_dim, d.kv_lora_rank, d.v_head_dim, gs, kq_scale};
+        LAUNCH_TRY(glmq::launch_mla_heads(ma, d.n_heads, d.cache_cap, st));
+        LAUNCH_TRY(glmq::launch_q80_matvec(A.attn_out_q, A.attn_out_s, m.att, m.x, D, d.n_heads * d.v_head_dim, gs,
+                                           ns, st, true));
+        if (l == 0) {
+            // dense SwiGLU FFN (infer.c:1067-1085)
+            LAUNCH_TRY(glmq::launch_rmsnorm(m.x, m.l0_norm, m.xn, D, st));
+            LAUNCH_TRY(glmq::launch_q80_matvec(m.l0_gate_q, m.l0_gate_s, m.xn, m.ff_gate, d.hidden_dim, D, gs, ns, st));
+            LAUNCH_TRY(glmq::launch_q80_matvec(m.l0_up_q, m.l0_up_s, m.xn, m.ff_up, d.hidden_dim, D, gs, ns, st));
+            LAUNCH_TRY(glmq::launch_silu_mul(m.ff_gate, m.ff_up, d.hidden_dim, ns, st));
+            LAUNCH_TRY(glmq::launch_q80_matvec(m.l0_down_q, m.l0_down_s, m.ff_gate, m.x, D, d.hidden_dim, gs, ns, st,
+                                               true));
+            g.launches += 4;
+        } else if (use_persistent()) {
+            LAUNCH_TRY(glmq::launch_moe_persistent(g.layers_dev, l, 1, g.dims, g.scratch, m.x, nullptr, nullptr,
+                                                   routed, ns, st, l + 1 < d.n_layers ? l + 1 : -1));
+        } else {
+            LAUNCH_TRY(glmq::launch_moe_decode(g.layers[l].w, g.dims, g.scratch, m.x, m.x, routed, ns, st));
+            g.launches += 2;
+        }
+        g.launches += 9;
+    }
+    // final norm, LM head, argmax (infer.c:1888-1893, 1218-1228)
+    LAUNCH_TRY(glmq::launch_rmsnorm(m.x, m.output_norm, m.xn, D, st));
+    LAUNCH_TRY(glmq::launch_q80_matvec(m.out_q, m.out_s, m.xn, m.logits, d.vocab_size, D, gs, ns, st));
+    LAUNCH_TRY(glmq::launch_argmax(m.logits, d.vocab_size, m.argmax, st));
+    g.launches += 4;
+    return 0;
+}
+
+int status_check_sync() {
+    CUDA_TRY(cudaMemcpyAsync(g.status_host, g.scratch.status, sizeof(unsigned int), cudaMemcpyDeviceToHost, g.stream));
+    CUDA_TRY(cudaStreamSynchronize(g.stream));
+    return take_device_status();
+}
+
+}  // namespace
+
+extern "C" {
+
+int glm_cuda_model_init(int device, const GlmCudaModelDims* dims) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!dims) return fail(GLM_CUDA_ERR_ARG, "dims must be non-NULL");
+    const GlmCudaModelDims d = *dims;
+    if (d.n_layers < 2 || d.n_heads <= 0 || d.vocab_size <= 0 || d.cache_cap <= 0 || d.hidden_dim <= 0)
+        return fail(GLM_CUDA_ERR_ARG, "bad model dims");
+    if (d.head_k_dim != d.qk_nope_dim + d.rope_dim || d.rope_dim % 2 || d.qk_nope_dim % 32 || d.kv_lora_rank % 64 ||
+        d.q_lora_rank % 64 || (d.n_heads * d.v_head_dim) % 64 || d.hidden_dim % 64 || d.group_size != 32)
+        return fail(GLM_CUDA_ERR_ARG, "unsupported attention/FFN dims");
+    if (int rc = init_locked(device, d.dim, d.moe_ffn_dim, d.n_routed_experts, d.n_experts_used, d.group_size,
+                             d.n_layers))
+        return rc;
+    Model& m = g.m;
+    m.d = d;
+    m.attn.assign(d.n_layers, AttnLayer{});
+    const size_t cache = (size_t)d.n_layers * d.cache_cap;
+    int rc = 0;
+    if ((rc = dev_alloc(&m.x, d.dim)) || (rc = dev_alloc(&m.xn, d.dim)) || (rc = dev_alloc(&m.q_a, d.q_lora_rank)) ||
+        (rc = dev_alloc(&m.q_full, (size_t)d.n_heads * d.head_k_dim)) ||
+        (rc = dev_alloc(&m.kv_a, d.kv_lora_rank + d.rope_dim)) ||
+        (rc = dev_alloc(&m.att, (size_t)d.n_heads * d.v_head_dim)) || (rc = dev_alloc(&m.ff_gate, d.hidden_dim)) ||
+        (rc = dev_alloc(&m.ff_up, d.hidden_dim)) || (rc = dev_alloc(&m.logits, d.vocab_size)) ||
+        (rc = dev_alloc(&m.cache_comp, cache * d.kv_lora_rank)) || (rc = dev_alloc(&m.cache_pe, cache * d.rope_dim)) ||
+        (rc = dev_alloc(&m.pos, 1)) || (rc = dev_alloc(&m.token, 1)) || (rc = dev_alloc(&m.argmax, 1))) {
+        release_all();
+        return rc;
+    }
+    CUDA_TRY(cudaMemset(m.cache_comp, 0, sizeof(float) * cache * d.kv_lora_rank));
+    CUDA_TRY(cudaMemset(m.cache_pe, 0, sizeof(float) * cache * d.rope_dim));
+    CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&m.io_host), 2 * sizeof(int), cudaHostAllocDefault));
+    m.inited = true;
+    return 0;
+}
+
+static int model_globals(bool copy, const float* output_norm, const int8_t* tok_q, const float* tok_s,
+                         const int8_t* out_q, const float* out_s, const float* l0_norm, const int8_t* gq,
+                         const float* gsc, const int8_t* uq, const float* usc, const int8_t* dq, const float* dsc) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited || !g.m.inited) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_model_init has not been called");
+    const void* ptrs[] = {output_norm, tok_q, tok_s, out_q, out_s, l0_norm, gq, gsc, uq, usc, dq, dsc};
+    for (const void* p : ptrs)
+        if (!p) return fail(GLM_CUDA_ERR_ARG, "model globals must be non-NULL");
+    Model& m = g.m;
+    for (void* p : m.owned_globals) cudaFree(p);
+    m.owned_globals.clear();
+    m.globals_ready = false;
+    const GlmCudaModelDims& d = m.d;
+    const size_t D = d.dim, V = d.vocab_size, H = d.hidden_dim, gsz = d.group_size;
+    auto& o = m.owned_globals;
+    int rc = 0;
+    if ((rc = put(o, copy, output_norm, D, &m.output_norm)) || (rc = put(o, copy, tok_q, V * D, &m.tok_q)) ||
+        (rc = put(o, copy, tok_s, V * D / gsz, &m.tok_s)) || (rc = put(o, copy, out_q, V * D, &m.out_q)) ||
+        (rc = put(o, copy, out_s, V * D / gsz, &m.out_s)) || (rc = put(o, copy, l0_norm, D, &m.l0_norm)) ||
+        (rc = put(o, copy, gq, H * D, &m.l0_gate_q)) || (rc = put(o, copy, gsc, H * D / gsz, &m.l0_gate_s)) ||
+        (rc = put(o, copy, uq, H * D, &m.l0_up_q)) || (rc = put(o, copy, usc, H * D / gsz, &m.l0_up_s)) ||
+        (rc = put(o, copy, dq, D * H, &m.l0_down_q)) || (rc = put(o, copy, dsc, D * H / gsz, &m.l0_down_s)))
+        return rc;
+    CUDA_TRY(cudaStreamSynchronize(g.stream));
+    m.globals_ready = true;
+    return 0;
+}
+
+int glm_cuda_upload_model_globals(const float* output_norm, const int8_t* tok_q, const float* tok_s,
+                                  const int8_t* out_q, const float* out_s, const float* l0_ffn_norm,
+                                  const int8_t* l0_gate_q, const float* l0_gate_s, const int8_t* l0_up_q,
+                                  const float* l0_up_s, const int8_t* l0_down_q, const float* l0_down_s) {
+    return model_globals(true, output_norm, tok_q, tok_s, out_q, out_s, l0_ffn_norm, l0_gate_q, l0_gate_s, l0_up_q,
+                         l0_up_s, l0_down_q, l0_down_s);
+}
+
+int glm_cuda_bind_model_globals_device(const float* output_norm, const int8_t* tok_q, const float* tok_s,
+                                       const int8_t* out_q, const float* out_s, const float* l0_ffn_norm,
+                                       const int8_t* l0_gate_q, const float* l0_gate_s, const int8_t* l0_up_q,
+                                       const float* l0_up_s, const int8_t* l0_down_q, const float* l0_down_s) {
+    return model_globals(false, output_norm, tok_q, tok_s, out_q, out_s, l0_ffn_norm, l0_gate_q, l0_gate_s, l0_up_q,
+                         l0_up_s, l0_down_q, l0_down_s);
+}
+
+static int attn_layer(bool copy, int layer, const void* const* p) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited || !g.m.inited) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_model_init has not been called");
+    Model& m = g.m;
+    if (layer < 0 || layer >= m.d.n_layers) return fail(GLM_CUDA_ERR_ARG, "attention layer %d out of range", layer);
+    for (int i = 0; i < 15; ++i)
+        if (!p[i]) return fail(GLM_CUDA_ERR_ARG, "attention layer %d: pointer %d is NULL", layer, i);
+    AttnLayer& A = m.attn[layer];
+    for (void* q : A.owned) cudaFree(q);
+    A = AttnLayer{};
+    const GlmCudaModelDims& d = m.d;
+    const size_t D = d.dim, ql = d.q_lora_rank, kvl = d.kv_lora_rank, H = d.n_heads, gsz = d.group_size;
+    const size_t qb_rows = H * d.head_k_dim, kva_rows = kvl + d.rope_dim, out_cols = H * d.v_head_dim;
+    auto& o = A.owned;
+    int rc = 0;
+    if ((rc = put(o, copy, (const float*)p[0], D, &A.attn_norm)) ||
+        (rc = put(o, copy, (const float*)p[1], ql, &A.q_a_norm)) ||
+        (rc = put(o, copy, (const float*)p[2], kvl, &A.kv_a_norm)) ||
+        (rc = put(o, copy, (const int8_t*)p[3], ql * D, &A.q_a_q)) ||
+        (rc = put(o, copy, (const float*)p[4], ql * D / gsz, &A.q_a_s)) ||
+        (rc = put(o, copy, (const int8_t*)p[5], qb_rows * ql, &A.q_b_q)) ||
+        (rc = put(o, copy, (const float*)p[6], qb_rows * ql / gsz, &A.q_b_s)) ||
+        (rc = put(o, copy, (const int8_t*)p[7], kva_rows * D, &A.kv_a_q)) ||
+        (rc = put(o, copy, (const float*)p[8], kva_rows * D / gsz, &A.kv_a_s)) ||
+        (rc = put(o, copy, (const int8_t*)p[9], H * kvl * d.qk_nope_dim, &A.k_b_q)) ||
+        (rc = put(o, copy, (const float*)p[10], H * kvl * d.qk_nope_dim / gsz, &A.k_b_s)) ||
+        (rc = put(o, copy, (const int8_t*)p[11], H * d.v_head_dim * kvl, &A.v_b_q)) ||
+        (rc = put(o, copy, (const float*)p[12], H * d.v_head_dim * kvl / gsz, &A.v_b_s)) ||
+        (rc = put(o, copy, (const int8_t*)p[13], D * out_cols, &A.attn_out_q)) ||
+        (rc = put(o, copy, (const float*)p[14], D * out_cols / gsz, &A.attn_out_s)))
+        return rc;
+    CUDA_TRY(cudaStreamSynchronize(g.stream));
+    A.ready = true;
+    return 0;
+}
+
+int glm_cuda_upload_attn_layer(int layer, const float* attn_norm, const float* q_a_norm, const float* kv_a_norm,
+                               const int8_t* q_a_q, const float* q_a_s, const int8_t* q_b_q, const float* q_b_s,
+                               const int8_t* kv_a_q, const float* kv_a_s, const int8_t* k_b_q, const float* k_b_s,
+                               const int8_t* v_b_q, const float* v_b_s, const int8_t* attn_out_q,
+                               const float* attn_out_s) {
+    const void* p[15] = {attn_norm, q_a_norm, kv_a_norm, q_a_q, q_a_s, q_b_q, q_b_s, kv_a_q,
+                         kv_a_s,    k_b_q,    k_b_s,     v_b_q, v_b_s, attn_out_q, attn_out_s};
+    return attn_layer(true, layer, p);
+}
+
+int glm_cuda_bind_attn_layer_device(int layer, const float* attn_norm, const float* q_a_norm, const float* kv_a_norm,
+                                    const int8_t* q_a_q, const float* q_a_s, const int8_t* q_b_q, const float* q_b_s,
+                                    const int8_t* kv_a_q, const float* kv_a_s, const int8_t* k_b_q,
+                                    const float* k_b_s, const int8_t* v_b_q, const float* v_b_s,
+                                    const int8_t* attn_out_q, const float* attn_out_s) {
+    const void* p[15] = {attn_norm, q_a_norm, kv_a_norm, q_a_q, q_a_s, q_b_q, q_b_s, kv_a_q,
+                         kv_a_s,    k_b_q,    k_b_s,     v_b_q, v_b_s, attn_out_q, attn_out_s};
+    return attn_layer(false, layer, p);
+}
+
+int glm_cuda_forward_token(int token, int pos, float* logits) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (int rc = check_model()) return rc;
+    Model& m = g.m;
+    if (pos < 0 || pos >= m.d.cache_cap) return fail(GLM_CUDA_ERR_ARG, "position %d outside the cache [0,%d)", pos,
+                                                    m.d.cache_cap);
+    if (token < 0 || token >= m.d.vocab_size) token = 0;  // as infer.c:1781
+    m.io_host[0] = token;
+    m.io_host[1] = pos;
+    CUDA_TRY(cudaMemcpyAsync(m.token, &m.io_host[0], sizeof(int), cudaMemcpyHostToDevice, g.stream));
+    CUDA_TRY(cudaMemcpyAsync(m.pos, &m.io_host[1], sizeof(int), cudaMemcpyHostToDevice, g.stream));
+    if (int rc = enqueue_step(g.stream)) return rc;
+    if (logits)
+        CUDA_TRY(cudaMemcpyAsync(logits, m.logits, sizeof(float) * m.d.vocab_size, cudaMemcpyDeviceToHost, g.stream));
+    return status_check_sync();
+}
+
+int glm_cuda_generate(const int32_t* prompt, int n_prompt, int n_gen, int32_t* out_ids, float* device_ms) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (int rc = check_model()) return rc;
+    Model& m = g.m;
+    if (!prompt || n_prompt <= 0 || n_gen <= 0 || !out_ids) return fail(GLM_CUDA_ERR_ARG, "bad generate arguments");
+    if (n_prompt + n_gen - 1 > m.d.cache_cap)
+        return fail(GLM_CUDA_ERR_ARG, "prompt + generation (%d) exceeds the cache (%d)", n_prompt + n_gen - 1,
+                    m.d.cache_cap);
+    if (n_prompt > m.prompt_cap) {
+        if (m.prompt) cudaFree(m.prompt);
+        m.prompt = nullptr;
+        m.prompt_cap = 0;
+        if (int rc = dev_alloc(&m.prompt, n_prompt)) return rc;
+        m.prompt_cap = n_prompt;
+    }
+    if (n_gen > m.out_cap) {
+        if (m.out_ids) cudaFree(m.out_ids);
+        m.out_ids = nullptr;
+        m.out_cap = 0;
+        if (int rc = dev_alloc(&m.out_ids, n_gen)) return rc;
+        m.out_cap = n_gen;
+    }
+    cudaStream_t st = g.stream;
+    CUDA_TRY(cudaMemcpyAsync(m.prompt, prompt, sizeof(int32_t) * n_prompt, cudaMemcpyHostToDevice, st));
+    int first = prompt[0];
+    if (first < 0 || first >= m.d.vocab_size) first = 0;
+    m.io_host[0] = first;
+    m.io_host[1] = 0;
+    CUDA_TRY(cudaMemcpyAsync(m.token, &m.io_host[0], sizeof(int), cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(m.pos, &m.io_host[1], sizeof(int), cudaMemcpyHostToDevice, st));
+    // One decode step (+ picking the next token) captured once, replayed
+    // for every position: the token and position live in device memory.
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_step(st);
+    if (!rc) {
+        cudaError_t e = glmq::launch_decode_advance(m.pos, m.token, m.argmax, m.prompt, n_prompt, m.out_ids,
+                                                    m.d.vocab_size, st);
+        if (e != cudaSuccess) rc = fail(GLM_CUDA_ERR_CUDA, "decode advance: %s", cudaGetErrorString(e));
+    }
+    cudaError_t ec = cudaStreamEndCapture(st, &graph);
+    if (rc) {
+        if (graph) cudaGraphDestroy(graph);
+        return rc;
+    }
+    if (ec != cudaSuccess) return fail(GLM_CUDA_ERR_CUDA, "graph capture: %s", cudaGetErrorString(ec));
+    ec = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ec != cudaSuccess) return fail(GLM_CUDA_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(ec));
+    cudaEvent_t ev[2] = {nullptr, nullptr};
+    if (device_ms) {
+        cudaEventCreate(&ev[0]);
+        cudaEventCreate(&ev[1]);
+        cudaEventRecord(ev[0], st);
+    }
+    const int steps = n_prompt + n_gen - 1;
+    for (int i = 0; i < steps && ec == cudaSuccess; ++i) ec = cudaGraphLaunch(exec, st);
+    if (device_ms) cudaEventRecord(ev[1], st);
+    g.launches += (unsigned long long)steps;
+    if (ec == cudaSuccess) ec = cudaMemcpyAsync(out_ids, m.out_ids, sizeof(int32_t) * n_gen, cudaMemcpyDeviceToHost, st);
+    if (ec == cudaSuccess) ec = cudaStreamSynchronize(st);
+    if (device_ms && ec == cudaSuccess) cudaEventElapsedTime(device_ms, ev[0], ev[1]);
+    for (auto e : ev)
+        if (e) cudaEventDestroy(e);
+    cudaGraphExecDestroy(exec);
+    if (ec != cudaSuccess) return fail(GLM_CUDA_ERR_CUDA, "generate: %s", cudaGetErrorString(ec));
+    return status_check_sync();
 }
 
 }  // extern "C"

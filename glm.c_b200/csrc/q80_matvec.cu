@@ -24,6 +24,7 @@ struct MatvecArgs {
     const float* x;
     float* y;
     int rows, cols;
+    int accumulate;  // y += result instead of y = result
 };
 
 __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a) {
@@ -88,8 +89,8 @@ __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a)
         if (ks == 1) {
             if (t == 0 && tw < tiles_per_pass && tile < ntiles) {
                 const int r0 = rb + tile * 16 + gid;
-                if (r0 < re) a.y[r0] = acc0;
-                if (r0 + 8 < re) a.y[r0 + 8] = acc1;
+                if (r0 < re) a.y[r0] = a.accumulate ? a.y[r0] + acc0 : acc0;
+                if (r0 + 8 < re) a.y[r0 + 8] = a.accumulate ? a.y[r0 + 8] + acc1 : acc1;
             }
             continue;  // uniform across the CTA: ks is
         }
@@ -104,7 +105,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a)
             if (tile0 + tl < ntiles && r < re) {
                 float sum = 0.f;
                 for (int k = 0; k < ks; ++k) sum += part[(tl * ks + k) * 16 + rr];
-                a.y[r] = sum;
+                a.y[r] = a.accumulate ? a.y[r] + sum : sum;
             }
         }
         __syncthreads();
@@ -117,7 +118,7 @@ size_t q80_matvec_smem_bytes(int cols) {
 }
 
 cudaError_t launch_q80_matvec(const int8_t* q, const float* s, const float* x, float* y, int rows, int cols,
-                              int gs, int num_sms, cudaStream_t stream) {
+                              int gs, int num_sms, cudaStream_t stream, bool accumulate) {
     if (gs != 32 || cols % 64 || rows <= 0) return cudaErrorInvalidValue;
     const size_t smem = q80_matvec_smem_bytes(cols);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
@@ -128,7 +129,7 @@ cudaError_t launch_q80_matvec(const int8_t* q, const float* s, const float* x, f
     }
     int grid = num_sms;
     if (grid > (rows + 15) / 16) grid = (rows + 15) / 16;
-    MatvecArgs a{q, s, x, y, rows, cols};
+    MatvecArgs a{q, s, x, y, rows, cols, accumulate ? 1 : 0};
     q80_matvec_kernel<<<grid, kMvThreads, smem, stream>>>(a);
     return cudaGetLastError();
 }

@@ -50,6 +50,13 @@ def _signatures(L: ctypes.CDLL) -> None:
     L.glm_cuda_moe_layer_async.argtypes = [_I, _P, _I, _P, _P, _P]
     L.glm_cuda_moe_layer_profile.argtypes = [_I, _P, _P]
     L.glm_cuda_moe_layers_async.argtypes = [_I, _I, _P, _P, _P, _P]
+    L.glm_cuda_model_init.argtypes = [_I, _P]
+    L.glm_cuda_upload_model_globals.argtypes = [_P] * 12
+    L.glm_cuda_bind_model_globals_device.argtypes = [_P] * 12
+    L.glm_cuda_upload_attn_layer.argtypes = [_I] + [_P] * 15
+    L.glm_cuda_bind_attn_layer_device.argtypes = [_I] + [_P] * 15
+    L.glm_cuda_forward_token.argtypes = [_I, _I, _P]
+    L.glm_cuda_generate.argtypes = [_P, _I, _I, _P, _P]
     L.glm_cuda_set_decode_path.argtypes = [_I]
     L.glm_cuda_decode_path.argtypes = []
     L.glm_cuda_moe_layer_noalloc.argtypes = [_P] * 15 + [_I] * 5 + [_P, _I, _P, _P, _P]
@@ -67,6 +74,9 @@ def _signatures(L: ctypes.CDLL) -> None:
     for name in ("glm_cuda_init", "glm_cuda_upload_moe_layer", "glm_cuda_bind_moe_layer_device",
                  "glm_cuda_moe_layer", "glm_cuda_moe_layer_async", "glm_cuda_moe_layer_profile",
                  "glm_cuda_moe_layers_async", "glm_cuda_set_decode_path", "glm_cuda_decode_path",
+                 "glm_cuda_model_init", "glm_cuda_upload_model_globals", "glm_cuda_bind_model_globals_device",
+                 "glm_cuda_upload_attn_layer", "glm_cuda_bind_attn_layer_device", "glm_cuda_forward_token",
+                 "glm_cuda_generate",
                  "glm_cuda_matvec_q80",
                  "glm_cuda_matvec_q80_async", "glm_cuda_synchronize", "glm_cuda_route_stats"):
         getattr(L, name).restype = _I
@@ -148,6 +158,41 @@ class GlmCuda:
                                                      stream))
 
     PATH_AUTO, PATH_PERSISTENT, PATH_CHAIN = 0, 1, 2
+
+    # ---- full decoder
+    MODEL_DIMS = ("dim", "hidden_dim", "n_layers", "n_heads", "vocab_size", "rope_dim", "q_lora_rank",
+                  "kv_lora_rank", "qk_nope_dim", "head_k_dim", "v_head_dim", "n_routed_experts", "n_experts_used",
+                  "group_size", "moe_ffn_dim", "cache_cap")
+    GLOBAL_FIELDS = ("output_norm", "tok_q", "tok_s", "out_q", "out_s", "l0_ffn_norm", "l0_gate_q", "l0_gate_s",
+                     "l0_up_q", "l0_up_s", "l0_down_q", "l0_down_s")
+    ATTN_FIELDS = ("attn_norm", "q_a_norm", "kv_a_norm", "q_a_q", "q_a_s", "q_b_q", "q_b_s", "kv_a_q", "kv_a_s",
+                   "k_b_q", "k_b_s", "v_b_q", "v_b_s", "attn_out_q", "attn_out_s")
+
+    def model_init(self, device: int, dims: dict) -> None:
+        arr = (ctypes.c_int32 * len(self.MODEL_DIMS))(*[int(dims[k]) for k in self.MODEL_DIMS])
+        self._check("glm_cuda_model_init", self.L.glm_cuda_model_init(device, ctypes.addressof(arr)))
+
+    def upload_model_globals(self, g: dict, device: bool = False) -> None:
+        fn = "glm_cuda_bind_model_globals_device" if device else "glm_cuda_upload_model_globals"
+        self._check(fn, getattr(self.L, fn)(*[_ptr(g[k]) for k in self.GLOBAL_FIELDS]))
+
+    def upload_attn_layer(self, layer: int, a: dict, device: bool = False) -> None:
+        fn = "glm_cuda_bind_attn_layer_device" if device else "glm_cuda_upload_attn_layer"
+        self._check(fn, getattr(self.L, fn)(layer, *[_ptr(a[k]) for k in self.ATTN_FIELDS]))
+
+    def forward_token(self, token: int, pos: int, vocab: int | None = None):
+        logits = np.zeros(vocab, dtype=np.float32) if vocab else None
+        self._check("glm_cuda_forward_token", self.L.glm_cuda_forward_token(token, pos, _ptr(logits)))
+        return logits
+
+    def generate(self, prompt, n_gen: int):
+        """Greedy ids and the device milliseconds of all steps."""
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(n_gen, dtype=np.int32)
+        ms = ctypes.c_float(0.0)
+        self._check("glm_cuda_generate", self.L.glm_cuda_generate(_ptr(p), len(p), n_gen, _ptr(out),
+                                                                   ctypes.addressof(ms)))
+        return out, float(ms.value)
 
     def set_decode_path(self, path: int) -> None:
         self._check("glm_cuda_set_decode_path", self.L.glm_cuda_set_decode_path(path))

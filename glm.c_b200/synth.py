@@ -39,6 +39,21 @@ _TENSOR_IDS["matvec_x"] = 202
 
 CONFIG0 = dict(dim=2048, ffn=1536, n_experts=64, k_used=4, gs=32)
 
+# Full GLM-4.7-Flash-shaped decoder: field names of
+# GlmCudaModelDims / RuntimeConfig (model.h:7-45).
+CONFIG2 = dict(dim=2048, hidden_dim=10240, n_layers=47, n_heads=20, vocab_size=154880, rope_dim=64,
+               q_lora_rank=768, kv_lora_rank=512, qk_nope_dim=192, head_k_dim=256, v_head_dim=256,
+               n_routed_experts=64, n_experts_used=4, group_size=32, moe_ffn_dim=1536)
+
+# Pointer orders of the decoder tables (C harness and CUDA upload calls):
+# Runtime globals (model.h:87-103) and LayerAttnWeights (model.h:46-62).
+GLOBAL_FIELDS = ("output_norm", "tok_q", "tok_s", "out_q", "out_s", "l0_ffn_norm", "l0_gate_q", "l0_gate_s",
+                 "l0_up_q", "l0_up_s", "l0_down_q", "l0_down_s")
+ATTN_FIELDS = ("attn_norm", "q_a_norm", "kv_a_norm", "q_a_q", "q_a_s", "q_b_q", "q_b_s", "kv_a_q", "kv_a_s",
+               "k_b_q", "k_b_s", "v_b_q", "v_b_s", "attn_out_q", "attn_out_s")
+for _i, _n in enumerate(GLOBAL_FIELDS + ATTN_FIELDS + ("prompt",)):
+    _TENSOR_IDS.setdefault(_n, 300 + _i)
+
 
 def _rng(seed: int, layer: int, name: str) -> np.random.Generator:
     return np.random.default_rng([int(seed), int(layer), _TENSOR_IDS[name]])
@@ -97,6 +112,42 @@ def moe_bytes(dim: int, ffn: int, n_experts: int, k_used: int, gs: int) -> int:
 def q8_matvec_bytes(rows: int, cols: int, gs: int) -> int:
     """R*C*(1+4/gs) weight bytes + fp32 x read + fp32 y written."""
     return rows * cols + rows * (cols // gs) * 4 + 4 * (rows + cols)
+
+
+def decoder_model(seed: int = 42, **dims) -> dict:
+    """Weights of a full decoder with the given GlmCudaModelDims fields:
+    Q8 linear layers as in config 0, all norms 1; layers 1.. are MoE layers
+    of moe_layer(seed, layer). Returns {"dims", "globals", "attn": [..],
+    "moe": [None, ..]}."""
+    d = dict(dims)
+    D, gs, H = d["dim"], d["group_size"], d["n_heads"]
+    g = {"output_norm": np.ones(D, np.float32), "l0_ffn_norm": np.ones(D, np.float32)}
+    g["tok_q"], g["tok_s"] = q8_weights(_rng(seed, 0, "tok_q"), d["vocab_size"], D, gs)
+    g["out_q"], g["out_s"] = q8_weights(_rng(seed, 0, "out_q"), d["vocab_size"], D, gs)
+    for name, (rows, cols) in (("l0_gate", (d["hidden_dim"], D)), ("l0_up", (d["hidden_dim"], D)),
+                               ("l0_down", (D, d["hidden_dim"]))):
+        g[name + "_q"], g[name + "_s"] = q8_weights(_rng(seed, 0, name + "_q"), rows, cols, gs)
+    attn = []
+    for l in range(d["n_layers"]):
+        a = {"attn_norm": np.ones(D, np.float32), "q_a_norm": np.ones(d["q_lora_rank"], np.float32),
+             "kv_a_norm": np.ones(d["kv_lora_rank"], np.float32)}
+        shapes = {"q_a": ((d["q_lora_rank"], D), ()),
+                  "q_b": ((H * d["head_k_dim"], d["q_lora_rank"]), ()),
+                  "kv_a": ((d["kv_lora_rank"] + d["rope_dim"], D), ()),
+                  "k_b": ((d["kv_lora_rank"], d["qk_nope_dim"]), (H,)),
+                  "v_b": ((d["v_head_dim"], d["kv_lora_rank"]), (H,)),
+                  "attn_out": ((D, H * d["v_head_dim"]), ())}
+        for name, ((rows, cols), lead) in shapes.items():
+            a[name + "_q"], a[name + "_s"] = q8_weights(_rng(seed, l, name + "_q"), rows, cols, gs, lead)
+        attn.append(a)
+    moe = [None] + [moe_layer(seed, l, D, d["moe_ffn_dim"], d["n_routed_experts"], d["n_experts_used"], gs)
+                    for l in range(1, d["n_layers"])]
+    return {"dims": d, "globals": g, "attn": attn, "moe": moe}
+
+
+def prompt_ids(seed: int, n: int, vocab: int) -> np.ndarray:
+    """Prompt token ids uniform in [0, vocab)."""
+    return _rng(seed, 0, "prompt").integers(0, vocab, size=n, dtype=np.int32)
 
 
 def digest(arrays) -> str:

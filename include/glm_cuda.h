@@ -164,6 +164,69 @@ uint64_t glm_cuda_launch_count(void);
 /* Message of the most recent failure ("" if none). */
 const char *glm_cuda_last_error(void);
 
+/* ------------------------------------------------------------------------
+ * Full batch-1 decoder (GLM-4.7-Flash: MLA attention in every layer, a dense
+ * SwiGLU FFN in layer 0, MoE FFN in layers 1..n_layers-1), the device side of
+ * glm_backend_forward_token (backend.h:8, backend.c:88-101).
+ * ------------------------------------------------------------------------ */
+
+/* Shapes, named after RuntimeConfig (model.h:7-45). cache_cap = KV-cache
+ * positions (RunState.cache_cap, infer.c:2165-2170). */
+typedef struct GlmCudaModelDims {
+    int32_t dim, hidden_dim, n_layers, n_heads, vocab_size, rope_dim, q_lora_rank, kv_lora_rank;
+    int32_t qk_nope_dim, head_k_dim, v_head_dim, n_routed_experts, n_experts_used, group_size, moe_ffn_dim;
+    int32_t cache_cap;
+} GlmCudaModelDims;
+
+/* Device bring-up for the whole decoder; also does glm_cuda_init for the MoE
+ * layers (then uploaded with glm_cuda_upload_moe_layer, layers 1..). Replaces
+ * glm_backend_init's device part (backend.c:88-101). */
+int glm_cuda_model_init(int device, const GlmCudaModelDims *dims);
+
+/* Runtime's model-wide weights (model.h:87-103): output_norm, token
+ * embedding tok_q/tok_s, LM head out_q/out_s, layer-0 dense FFN norm and
+ * gate/up/down. Host pointers, copied to HBM (planar Q8 kept). */
+int glm_cuda_upload_model_globals(const float *output_norm, const int8_t *tok_q, const float *tok_s,
+                                  const int8_t *out_q, const float *out_s, const float *l0_ffn_norm,
+                                  const int8_t *l0_gate_q, const float *l0_gate_s, const int8_t *l0_up_q,
+                                  const float *l0_up_s, const int8_t *l0_down_q, const float *l0_down_s);
+
+/* As above on caller-owned device memory (16-byte aligned); nothing copied. */
+int glm_cuda_bind_model_globals_device(const float *output_norm, const int8_t *tok_q, const float *tok_s,
+                                       const int8_t *out_q, const float *out_s, const float *l0_ffn_norm,
+                                       const int8_t *l0_gate_q, const float *l0_gate_s, const int8_t *l0_up_q,
+                                       const float *l0_up_s, const int8_t *l0_down_q, const float *l0_down_s);
+
+/* One layer's attention weights in the order of LayerAttnWeights
+ * (model.h:46-62); host pointers, copied to HBM. */
+int glm_cuda_upload_attn_layer(int layer, const float *attn_norm, const float *q_a_norm, const float *kv_a_norm,
+                               const int8_t *q_a_q, const float *q_a_s, const int8_t *q_b_q, const float *q_b_s,
+                               const int8_t *kv_a_q, const float *kv_a_s, const int8_t *k_b_q, const float *k_b_s,
+                               const int8_t *v_b_q, const float *v_b_s, const int8_t *attn_out_q,
+                               const float *attn_out_s);
+
+/* As above on caller-owned device memory (16-byte aligned). */
+int glm_cuda_bind_attn_layer_device(int layer, const float *attn_norm, const float *q_a_norm,
+                                    const float *kv_a_norm, const int8_t *q_a_q, const float *q_a_s,
+                                    const int8_t *q_b_q, const float *q_b_s, const int8_t *kv_a_q,
+                                    const float *kv_a_s, const int8_t *k_b_q, const float *k_b_s,
+                                    const int8_t *v_b_q, const float *v_b_s, const int8_t *attn_out_q,
+                                    const float *attn_out_s);
+
+/* One decode step of token `token` at position `pos` (writing the KV cache
+ * at pos): glm_cpu_forward_token (infer.c:1903) on the GPU. logits (host,
+ * vocab_size floats, may be NULL) receive the LM-head output, as
+ * RunState.logits. Replaces glm_backend_forward_token (backend.c:88-91). */
+int glm_cuda_forward_token(int token, int pos, float *logits);
+
+/* Greedy generation as glm.c's loop runs it at temperature 0
+ * (infer.c:2190-2228; argmax infer.c:1218-1228): the prompt ids are fed one
+ * per position, then n_gen tokens are picked by argmax and fed back; out_ids
+ * receives them. The whole step runs from device memory (one CUDA graph per
+ * call, replayed for every position). device_ms (may be NULL) receives the
+ * device time of the n_prompt + n_gen - 1 steps. */
+int glm_cuda_generate(const int32_t *prompt, int n_prompt, int n_gen, int32_t *out_ids, float *device_ms);
+
 /* Release all device memory and state. Replaces glm_backend_free's device
  * part (backend.c:108-110, glm_metal_free). Safe to call twice. */
 void glm_cuda_free(void);

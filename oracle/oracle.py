@@ -70,6 +70,9 @@ def lib(impl: str = "orc") -> ctypes.CDLL:
         L.ref_time_matvec_q80.restype = I
         L.ref_rmsnorm.argtypes = [P, P, P, I]
         L.ref_omp_max_threads.restype = I
+        if hasattr(L, "ref_decode"):
+            L.ref_decode.argtypes = [P, P, P, P, P, I, I, P, P]
+            L.ref_decode.restype = I
     _libs[impl] = L
     return L
 
@@ -165,3 +168,46 @@ def time_matvec(q, s, x, gs: int, warmup: int, iters: int) -> float:
 
 def omp_threads() -> int:
     return int(lib("ref").ref_omp_max_threads())
+
+
+# Table orders of ref_decode: Runtime globals (model.h:87-103) and
+# LayerAttnWeights (model.h:46-62).
+GLOBAL_FIELDS = ("output_norm", "tok_q", "tok_s", "out_q", "out_s", "l0_ffn_norm", "l0_gate_q", "l0_gate_s",
+                 "l0_up_q", "l0_up_s", "l0_down_q", "l0_down_s")
+ATTN_FIELDS = ("attn_norm", "q_a_norm", "kv_a_norm", "q_a_q", "q_a_s", "q_b_q", "q_b_s", "kv_a_q", "kv_a_s",
+               "k_b_q", "k_b_s", "v_b_q", "v_b_s", "attn_out_q", "attn_out_s")
+DECODER_DIMS = ("dim", "hidden_dim", "n_layers", "n_heads", "vocab_size", "rope_dim", "q_lora_rank",
+                "kv_lora_rank", "qk_nope_dim", "head_k_dim", "v_head_dim", "n_routed_experts", "n_experts_used",
+                "group_size", "moe_ffn_dim", "cache_cap")
+
+
+def ref_decode(model: dict, prompt, n_gen: int, cache_cap: int, with_logits: bool = False):
+    """Greedy ids from glm.c's own forward pass (compiled from its sources):
+    glm_cpu_forward_token per position, argmax at temperature 0, as
+    glm_app_main feeds it (infer.c:2190-2228). model is synth.decoder_model's
+    dict; returns (ids [n_gen], logits [n_gen, vocab] or None)."""
+    d = dict(model["dims"], cache_cap=cache_cap)
+    icfg = np.array([d[k] for k in DECODER_DIMS], dtype=np.int32)
+    keep = []
+
+    def table(ptrs):
+        arr = (ctypes.c_void_p * len(ptrs))(*[None if p is None else p.ctypes.data for p in ptrs])
+        keep.append(arr)
+        return ctypes.cast(arr, ctypes.c_void_p)
+
+    g = model["globals"]
+    glob = table([np.ascontiguousarray(g[k]) for k in GLOBAL_FIELDS])
+    attn = table([np.ascontiguousarray(a[k]) for a in model["attn"] for k in ATTN_FIELDS])
+    moe_ptrs = []
+    for l, m in enumerate(model["moe"]):
+        moe_ptrs += [None] * 15 if m is None else [np.ascontiguousarray(m[k]) for k in MOE_FIELDS]
+    moe = table(moe_ptrs)
+    p = np.ascontiguousarray(prompt, dtype=np.int32)
+    out = np.zeros(n_gen, dtype=np.int32)
+    logits = np.zeros((n_gen, d["vocab_size"]), dtype=np.float32) if with_logits else None
+    rc = lib("ref").ref_decode(icfg.ctypes.data, glob, attn, moe, p.ctypes.data, len(p), n_gen, out.ctypes.data,
+                               None if logits is None else logits.ctypes.data)
+    del keep
+    if rc != 0:
+        raise RuntimeError(f"ref_decode failed ({rc})")
+    return out, logits

@@ -14,6 +14,9 @@
  *   ref_rmsnorm      -> rmsnorm                      (infer.c:746-752)
  *   ref_time_moe_layer: wall-clock timing of the same call with the
  *                      reference's own clock (monotonic_ms, infer.c:1426)
+ *   ref_decode       -> greedy generation with glm_cpu_forward_token
+ *                      (infer.c:1903) and argmax (infer.c:1218), fed as
+ *                      glm_app_main's loop feeds it (infer.c:2190-2228)
  *
  * The Runtime/RunState objects are assembled in memory exactly as
  * runtime_open (infer.c:357-744) would leave them for one MoE layer: the
@@ -141,4 +144,133 @@ int ref_omp_max_threads(void) {
 #else
     return 1;
 #endif
+}
+
+/* Full decoder described by plain tables, assembled in memory as
+ * runtime_open would leave it (infer.c:357-744):
+ *   icfg[16]: dim, hidden_dim, n_layers, n_heads, vocab_size, rope_dim,
+ *             q_lora_rank, kv_lora_rank, qk_nope_dim, head_k_dim, v_head_dim,
+ *             n_routed_experts, n_experts_used, group_size, moe_ffn_dim,
+ *             cache_cap
+ *   glob[12]: output_norm, tok_q, tok_s, out_q, out_s, l0_ffn_norm,
+ *             l0 gate q/s, up q/s, down q/s
+ *   attn[n_layers*15]: LayerAttnWeights fields per layer (model.h:46-62)
+ *   moe[n_layers*15]:  the 15 MoE pointers per layer (layer 0 unused)
+ * The prompt ids are fed one per position; then n_gen tokens are picked
+ * with argmax (temperature 0) and fed back. out_ids receives them; if
+ * logits_out is not NULL it receives the logits of every generating step
+ * ([n_gen][vocab]). Returns 0 or the failing forward's status. */
+int ref_decode(const int32_t *icfg, const void *const *glob, const void *const *attn, const void *const *moe,
+               const int32_t *prompt, int n_prompt, int n_gen, int32_t *out_ids, float *logits_out) {
+    Runtime rt;
+    memset(&rt, 0, sizeof(rt));
+    RuntimeConfig *c = &rt.cfg;
+    c->dim = icfg[0];
+    c->hidden_dim = icfg[1];
+    c->n_layers = icfg[2];
+    c->n_heads = icfg[3];
+    c->n_kv_heads = icfg[3];
+    c->vocab_size = icfg[4];
+    c->rope_dim = icfg[5];
+    c->q_lora_rank = icfg[6];
+    c->kv_lora_rank = icfg[7];
+    c->l0_qk_nope_dim = icfg[8];
+    c->l0_head_k_dim = icfg[9];
+    c->l0_v_head_dim = icfg[10];
+    c->n_routed_experts = icfg[11];
+    c->n_experts_used = icfg[12];
+    c->group_size = (uint64_t)icfg[13];
+    c->moe_ffn_dim = icfg[14];
+    c->seq_len = icfg[15];
+    c->bos_id = -1;
+    c->eos_id = -1;
+    const int L = c->n_layers, gs = icfg[13];
+
+    rt.output_norm = (const float *)glob[0];
+    rt.tok_q = (const int8_t *)glob[1];
+    rt.tok_s = (const float *)glob[2];
+    rt.out_q = (const int8_t *)glob[3];
+    rt.out_s = (const float *)glob[4];
+    rt.has_l0_ffn = 1;
+    rt.l0_ffn_norm = (const float *)glob[5];
+    rt.l0_ffn_gate_q = (const int8_t *)glob[6];
+    rt.l0_ffn_gate_s = (const float *)glob[7];
+    rt.l0_ffn_up_q = (const int8_t *)glob[8];
+    rt.l0_ffn_up_s = (const float *)glob[9];
+    rt.l0_ffn_down_q = (const int8_t *)glob[10];
+    rt.l0_ffn_down_s = (const float *)glob[11];
+
+    LayerAttnWeights *aw = (LayerAttnWeights *)calloc((size_t)L, sizeof(LayerAttnWeights));
+    LayerMoeShared *ms = (LayerMoeShared *)calloc((size_t)L, sizeof(LayerMoeShared));
+    LayerMoeRouted *mr = (LayerMoeRouted *)calloc((size_t)L, sizeof(LayerMoeRouted));
+    if (!aw || !ms || !mr) return -1;
+    for (int l = 0; l < L; l++) {
+        const void *const *a = attn + (size_t)l * 15;
+        aw[l].attn_norm = (const float *)a[0];
+        aw[l].q_a_norm = (const float *)a[1];
+        aw[l].kv_a_norm = (const float *)a[2];
+        aw[l].q_a_q = (const int8_t *)a[3];
+        aw[l].q_a_s = (const float *)a[4];
+        aw[l].q_b_q = (const int8_t *)a[5];
+        aw[l].q_b_s = (const float *)a[6];
+        aw[l].kv_a_q = (const int8_t *)a[7];
+        aw[l].kv_a_s = (const float *)a[8];
+        aw[l].k_b_q = (const int8_t *)a[9];
+        aw[l].k_b_s = (const float *)a[10];
+        aw[l].v_b_q = (const int8_t *)a[11];
+        aw[l].v_b_s = (const float *)a[12];
+        aw[l].attn_out_q = (const int8_t *)a[13];
+        aw[l].attn_out_s = (const float *)a[14];
+        if (l == 0) continue;
+        const void *const *p = moe + (size_t)l * 15;
+        ms[l].ffn_norm = (const float *)p[RP_FFN_NORM];
+        ms[l].gate_inp = (const float *)p[RP_GATE_INP];
+        ms[l].exp_probs_b = (const float *)p[RP_EXP_PROBS_B];
+        ms[l].gate_sh_q = (const int8_t *)p[RP_GATE_SH_Q];
+        ms[l].gate_sh_s = (const float *)p[RP_GATE_SH_S];
+        ms[l].up_sh_q = (const int8_t *)p[RP_UP_SH_Q];
+        ms[l].up_sh_s = (const float *)p[RP_UP_SH_S];
+        ms[l].down_sh_q = (const int8_t *)p[RP_DOWN_SH_Q];
+        ms[l].down_sh_s = (const float *)p[RP_DOWN_SH_S];
+        mr[l].gate_q = (const int8_t *)p[RP_GATE_Q];
+        mr[l].gate_s = (const float *)p[RP_GATE_S];
+        mr[l].up_q = (const int8_t *)p[RP_UP_Q];
+        mr[l].up_s = (const float *)p[RP_UP_S];
+        mr[l].down_q = (const int8_t *)p[RP_DOWN_Q];
+        mr[l].down_s = (const float *)p[RP_DOWN_S];
+    }
+    rt.has_all_attn = 1;
+    rt.attn_layers = aw;
+    rt.has_moe_shared = 1;
+    rt.moe_layers = ms;
+    rt.has_moe_routed = 1;
+    rt.moe_routed_layers = mr;
+
+    RunState st;
+    runstate_build(&st, &rt, icfg[15]);
+    int token = prompt[0];
+    if (token < 0 || token >= c->vocab_size) token = 0;
+    int prompt_index = 1, generated = 0, rc = 0;
+    for (int pos = 0; pos < icfg[15]; pos++) {
+        rc = glm_cpu_forward_token(&rt, &st, token, pos, 0);
+        if (rc != 0) break;
+        int next;
+        if (prompt_index < n_prompt) {
+            next = prompt[prompt_index++];
+            if (next < 0 || next >= c->vocab_size) next = 0;
+        } else {
+            next = argmax(st.logits, c->vocab_size);
+            if (logits_out)
+                memcpy(logits_out + (size_t)generated * c->vocab_size, st.logits, (size_t)c->vocab_size * sizeof(float));
+            out_ids[generated++] = next;
+            if (generated >= n_gen) break;
+        }
+        token = next;
+    }
+    runstate_free(&st);
+    free(aw);
+    free(ms);
+    free(mr);
+    (void)gs;
+    return rc;
 }
