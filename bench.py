@@ -22,6 +22,10 @@ infer.c:1464-1542) over time.
             algorithmic bytes per launch (one layer) over its mean CUDA-event
             duration, measured right after the timed region over the same 46
             layers, against MEASURED_PEAKS.json.
+  decode    BASELINE config 2: the full 47-layer decoder (MLA attention,
+            dense layer 0, these 46 MoE layers, LM head 154880) greedy from a
+            16-token random prompt for 100 tokens through glm_cuda_generate;
+            tok/s = steps / device time, plus the call's wall-clock rate.
   cpu_baseline  glm.c's own apply_moe_shared_ffn_layer (compiled from its
             sources, OpenMP on all host cores) on a bounded sample.
 
@@ -178,6 +182,62 @@ def make_device_layers(torch, n_layers: int, seed: int, device):
         L["down_q"], L["down_s"] = q8((E,), D, F)
         layers.append(L)
     return layers
+
+
+def make_device_decoder(torch, dims: dict, seed: int, device):
+    """Config-2 non-MoE weights generated on the device with the config-0
+    distributions (Q8 int8 uniform, scales |N(0,0.02)|/127, norms 1):
+    embedding, LM head, layer-0 dense FFN and every layer's MLA attention."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed * 7919 + 1)
+    Dm, gs, H = dims["dim"], dims["group_size"], dims["n_heads"]
+
+    def q8(lead, rows, cols):
+        q = torch.randint(-127, 128, lead + (rows, cols), generator=g, device=device, dtype=torch.int8)
+        s = torch.randn(lead + (rows, cols // gs), generator=g, device=device).abs_().mul_(0.02 / 127.0)
+        return q, s
+
+    glob = {"output_norm": torch.ones(Dm, device=device), "l0_ffn_norm": torch.ones(Dm, device=device)}
+    glob["tok_q"], glob["tok_s"] = q8((), dims["vocab_size"], Dm)
+    glob["out_q"], glob["out_s"] = q8((), dims["vocab_size"], Dm)
+    glob["l0_gate_q"], glob["l0_gate_s"] = q8((), dims["hidden_dim"], Dm)
+    glob["l0_up_q"], glob["l0_up_s"] = q8((), dims["hidden_dim"], Dm)
+    glob["l0_down_q"], glob["l0_down_s"] = q8((), Dm, dims["hidden_dim"])
+    attn = []
+    for _ in range(dims["n_layers"]):
+        a = {"attn_norm": torch.ones(Dm, device=device), "q_a_norm": torch.ones(dims["q_lora_rank"], device=device),
+             "kv_a_norm": torch.ones(dims["kv_lora_rank"], device=device)}
+        a["q_a_q"], a["q_a_s"] = q8((), dims["q_lora_rank"], Dm)
+        a["q_b_q"], a["q_b_s"] = q8((), H * dims["head_k_dim"], dims["q_lora_rank"])
+        a["kv_a_q"], a["kv_a_s"] = q8((), dims["kv_lora_rank"] + dims["rope_dim"], Dm)
+        a["k_b_q"], a["k_b_s"] = q8((H,), dims["kv_lora_rank"], dims["qk_nope_dim"])
+        a["v_b_q"], a["v_b_s"] = q8((H,), dims["v_head_dim"], dims["kv_lora_rank"])
+        a["attn_out_q"], a["attn_out_s"] = q8((), Dm, H * dims["v_head_dim"])
+        attn.append(a)
+    return glob, attn
+
+
+def decoder_bytes(dims: dict, pos: int) -> int:
+    """Algorithmic bytes of one decode step (estimate_model_active_bytes,
+    infer.c:1472-1542, plus the KV read at this position): Q8 weights touched
+    once, fp32 cache rows (pos+1) per layer."""
+    q8 = lambda r, c: r * c + r * (c // dims["group_size"]) * 4
+    Dm, H = dims["dim"], dims["n_heads"]
+    attn = (q8(dims["q_lora_rank"], Dm) + q8(H * dims["head_k_dim"], dims["q_lora_rank"])
+            + q8(dims["kv_lora_rank"] + dims["rope_dim"], Dm) + H * q8(dims["kv_lora_rank"], dims["qk_nope_dim"])
+            + H * q8(dims["v_head_dim"], dims["kv_lora_rank"]) + q8(Dm, H * dims["v_head_dim"]))
+    dense = 2 * q8(dims["hidden_dim"], Dm) + q8(Dm, dims["hidden_dim"])
+    moe = (dims["n_layers"] - 1) * moe_layer_bytes_cfg(dims)
+    lm = q8(dims["vocab_size"], Dm) + Dm + (Dm // dims["group_size"]) * 4  # LM head + one embedding row
+    kv = dims["n_layers"] * (pos + 1) * (dims["kv_lora_rank"] + dims["rope_dim"]) * 4
+    return dims["n_layers"] * attn + dense + moe + lm + kv
+
+
+def moe_layer_bytes_cfg(dims: dict) -> int:
+    from __graft_entry__ import load_package
+
+    return load_package().synth.moe_bytes(dims["dim"], dims["moe_ffn_dim"], dims["n_routed_experts"],
+                                           dims["n_experts_used"], dims["group_size"])
 
 
 def cpu_baseline(layer_host: dict, x_host, budget_s: float) -> dict:
@@ -404,6 +464,48 @@ def run_ours(args) -> None:
         e2e_s = float(t.item())
     e2e_value = world * e2e_steps * N_MOE_LAYERS * lb / e2e_s / 1e9
 
+    # Full config-2 decoder (greedy, glm_cuda_generate) on the same 46 MoE
+    # layers plus device-generated attention / embedding / LM head weights.
+    decode = None
+    if N_MOE_LAYERS == 46 and not args.no_decode:
+        synth = pkg.synth
+        dims = dict(synth.CONFIG2, cache_cap=args.decode_prompt + args.decode_gen + 8)
+        glob, attn = make_device_decoder(torch, dims, args.seed + rank, dev)
+        lib.model_init(local, dims)
+        lib.set_decode_path({"auto": 0, "persistent": 1, "chain": 2}[args.path])
+        lib.upload_model_globals(glob, device=True)
+        for l, a in enumerate(attn):
+            lib.upload_attn_layer(l, a, device=True)
+        for l in range(1, dims["n_layers"]):
+            lib.bind_moe_layer_device(l, layers[l - 1])
+        torch.cuda.synchronize()
+        prompt = synth.prompt_ids(args.seed, args.decode_prompt, dims["vocab_size"])
+        lib.generate(prompt, args.decode_gen)  # warm-up
+        runs, walls = [], []
+        for _ in range(args.decode_reps):
+            t0 = time.perf_counter()
+            ids, ms_dec = lib.generate(prompt, args.decode_gen)
+            walls.append(time.perf_counter() - t0)
+            runs.append(ms_dec)
+        steps = args.decode_prompt + args.decode_gen - 1
+        ms_tok = statistics.median(runs) / steps
+        step_bytes = sum(decoder_bytes(dims, p) for p in range(steps)) / steps
+        if world > 1:
+            t = torch.tensor([ms_tok], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms_tok = float(t.item())
+        decode = {"metric": "decode tok/s @bs1 (greedy, GLM-4.7-Flash config 2: 47 layers, vocab 154880)",
+                  "value": round(world * 1000.0 / ms_tok, 2), "unit": "tok/s", "ms_per_token": round(ms_tok, 4),
+                  "prompt": args.decode_prompt, "generated": args.decode_gen, "reps": len(runs),
+                  "bytes_per_token": int(step_bytes),
+                  "achieved_gbs": round(step_bytes / (ms_tok / 1e3) / 1e9, 1),
+                  "frac_of_hbm_peak": round(step_bytes / (ms_tok / 1e3) / 1e9 / measured_peaks()["hbm_gbs"], 4),
+                  "e2e_tok_s": round(world * steps / statistics.median(walls), 2),
+                  "timing": "device time of glm_cuda_generate's step-graph replays (CUDA events); e2e: host "
+                            "wall clock of the call (prompt H2D, graph build, ids D2H)",
+                  "first_ids": ids[:8].tolist(), "api": "glm_cuda_generate"}
+        del glob, attn
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         host_layer = {k: v.cpu().numpy() for k, v in layers[0].items()}
@@ -441,6 +543,8 @@ def run_ours(args) -> None:
         }
         if stacked is not None:
             line["stacked"] = stacked
+        if decode is not None:
+            line["decode"] = decode
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line))
@@ -464,6 +568,10 @@ def main() -> None:
     ap.add_argument("--path", choices=["auto", "persistent", "chain"], default="auto",
                     help="decode kernels (auto = persistent where the sizes allow)")
     ap.add_argument("--stack-steps", type=int, default=20)
+    ap.add_argument("--no-decode", action="store_true", help="skip the full-decoder (config 2) measurement")
+    ap.add_argument("--decode-prompt", type=int, default=16)
+    ap.add_argument("--decode-gen", type=int, default=100)
+    ap.add_argument("--decode-reps", type=int, default=3)
     ap.add_argument("--profile-tokens", type=int, default=4)
     ap.add_argument("--cpu-budget-s", type=float, default=8.0)
     ap.add_argument("--ref-budget-s", type=float, default=90.0,
