@@ -1,7 +1,8 @@
 // Device kernels of the rest of GLM-4.7-Flash's batch-1 decode step around
 // the MoE layers (glm_cpu_forward_token, infer.c:1767-1901): token
 // embedding, rmsnorm, MLA attention with the compressed KV cache, the layer-0
-// dense SwiGLU, and the greedy argmax. The Q8 linear layers run on the
+// dense SwiGLU, and the greedy argmax (the rmsnorms that feed a linear layer
+// run fused into the matvec, q80_matvec.cu). The Q8 linear layers run on the
 // matvec kernel (q80_matvec.cu) and the MoE layers on the persistent kernel.
 //
 // Every kernel reads the token id and the position from device memory, so a
@@ -70,14 +71,6 @@ __global__ void embed_kernel(const int8_t* tok_q, const float* tok_s, const int*
     for (int i = threadIdx.x; i < D; i += blockDim.x) x[i] = (float)q[i] * s[i / gs];
 }
 
-// o = rmsnorm(x) * w; o may alias x.
-__global__ void rmsnorm_kernel(const float* x, const float* w, float* o, int n) {
-    __shared__ double red[32];
-    const float inv = rms_inv(x, n, red);
-    __syncthreads();
-    for (int i = threadIdx.x; i < n; i += blockDim.x) o[i] = x[i] * inv * w[i];
-}
-
 // kv_a[0:kv_lora] <- rmsnorm * kv_a_norm, stored as this position's
 // compressed key; kv_a[kv_lora:] roped, stored as its rope key
 // (infer.c:1003-1016).
@@ -102,46 +95,71 @@ __global__ void kv_cache_write_kernel(float* kv_a, const float* kv_norm, float* 
     }
 }
 
-// One warp: dot of one planar Q8 row with x (shared memory); cols is a
-// multiple of kBytes and of the group size, lane l covers the kBytes-wide
-// pieces l, l + 32, ...
-template <int kBytes>
-__device__ __forceinline__ float q8_row_dot(const int8_t* q, const float* s, const float* x, int cols, int gs) {
+// kR rows of a planar Q8 matrix dotted with x (shared memory) by one warp,
+// all rows' loads issued together: lane l covers the kBytes-wide pieces
+// l, l + 32, ... of every row (cols a multiple of kBytes and of gs).
+template <int kBytes, int kR>
+__device__ __forceinline__ void q8_rows_dot(const int8_t* q, const float* s, const float* x, int cols, int gs,
+                                            int r0, int nrows, float (&out)[kR]) {
     const int lane = threadIdx.x & 31;
-    float acc = 0.f;
+    const int ng = cols / gs;
+#pragma unroll
+    for (int j = 0; j < kR; ++j) out[j] = 0.f;
     for (int c0 = lane * kBytes; c0 < cols; c0 += 32 * kBytes) {
-        const float sc = s[c0 / gs];
-        float d = 0.f;
-        if (kBytes == 16) {
-            const int4 v = *reinterpret_cast<const int4*>(q + c0);
-            const int w[4] = {v.x, v.y, v.z, v.w};
+        int w[kR][kBytes / 4];
+        float sc[kR];
 #pragma unroll
-            for (int k = 0; k < 16; ++k) d += (float)(int8_t)(w[k >> 2] >> (8 * (k & 3))) * x[c0 + k];
-        } else {
-            const int2 v = *reinterpret_cast<const int2*>(q + c0);
-            const int w[2] = {v.x, v.y};
+        for (int j = 0; j < kR; ++j) {
+            const int r = r0 + j;
+            if (r < nrows) {
+                const int8_t* p = q + (size_t)r * cols + c0;
+                if constexpr (kBytes == 16) {
+                    const int4 v = *reinterpret_cast<const int4*>(p);
+                    w[j][0] = v.x;
+                    w[j][1] = v.y;
+                    w[j][2] = v.z;
+                    w[j][3] = v.w;
+                } else {
+                    const int2 v = *reinterpret_cast<const int2*>(p);
+                    w[j][0] = v.x;
+                    w[j][1] = v.y;
+                }
+                sc[j] = s[(size_t)r * ng + c0 / gs];
+            } else {
 #pragma unroll
-            for (int k = 0; k < 8; ++k) d += (float)(int8_t)(w[k >> 2] >> (8 * (k & 3))) * x[c0 + k];
+                for (int k = 0; k < kBytes / 4; ++k) w[j][k] = 0;
+                sc[j] = 0.f;
+            }
         }
-        acc += sc * d;
+#pragma unroll
+        for (int j = 0; j < kR; ++j) {
+            float d = 0.f;
+#pragma unroll
+            for (int k = 0; k < kBytes; ++k) d += (float)(int8_t)(w[j][k >> 2] >> (8 * (k & 3))) * x[c0 + k];
+            out[j] += sc[j] * d;
+        }
     }
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    return acc;
+    for (int j = 0; j < kR; ++j)
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) out[j] += __shfl_xor_sync(0xffffffffu, out[j], off);
 }
 
 // MLA attention of one head per CTA (infer.c:1018-1058): q_pe roped,
 // q_abs = k_b_h . q_nope, scores over the cache, softmax, context, and
-// att_concat[h] = v_b_h . context.
+// att_concat[h] = v_b_h . context. Every stage keeps many independent loads
+// in flight (rows in groups of 8 per warp; cache rows split over the warps).
 __global__ void __launch_bounds__(512) mla_heads_kernel(MlaArgs a) {
     extern __shared__ __align__(16) float smf[];
+    constexpr int kR = 8;
     const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
     const int pos = *a.pos;
     float* q_nope = smf;                   // [qk_nope]
     float* q_pe = q_nope + a.qk_nope;      // [rope]
     float* q_abs = q_pe + a.rope;          // [kv_lora]
     float* ctx = q_abs + a.kv_lora;        // [kv_lora]
-    float* scores = ctx + a.kv_lora;       // [pos + 1]
+    float* scores = ctx + a.kv_lora;       // [cache_cap]
+    float* cpart = scores + a.cache_cap;   // [nw][kv_lora] per-warp context partials
     __shared__ float red[32];
 
     const float* qh = a.q_full + (size_t)h * a.head_k;
@@ -157,25 +175,44 @@ __global__ void __launch_bounds__(512) mla_heads_kernel(MlaArgs a) {
     // q_abs[r] = k_b_h[r] . q_nope  (k_b: [heads][kv_lora][qk_nope])
     const int8_t* kbq = a.k_b_q + (size_t)h * a.kv_lora * a.qk_nope;
     const float* kbs = a.k_b_s + (size_t)h * a.kv_lora * (a.qk_nope / a.gs);
-    for (int r = warp; r < a.kv_lora; r += nw) {
-        const float v = q8_row_dot<8>(kbq + (size_t)r * a.qk_nope, kbs + (size_t)r * (a.qk_nope / a.gs), q_nope,
-                                      a.qk_nope, a.gs);
-        if (lane == 0) q_abs[r] = v;
+    for (int r0 = warp * kR; r0 < a.kv_lora; r0 += nw * kR) {
+        float v[kR];
+        q8_rows_dot<8, kR>(kbq, kbs, q_nope, a.qk_nope, a.gs, r0, a.kv_lora, v);
+        if (lane < kR && r0 + lane < a.kv_lora) {
+            float mine = v[0];
+#pragma unroll
+            for (int j = 1; j < kR; ++j)
+                if (lane == j) mine = v[j];
+            q_abs[r0 + lane] = mine;
+        }
     }
     __syncthreads();
 
-    // scores[t] = (q_abs . kc[t] + q_pe . kp[t]) * kq_scale
+    // scores[t] = (q_abs . kc[t] + q_pe . kp[t]) * kq_scale, two rows per warp step
     const float* cc = a.cache_comp;
     const float* cp = a.cache_pe;
-    for (int t = warp; t <= pos; t += nw) {
+    for (int t = warp; t <= pos; t += 2 * nw) {
+        const int t2 = t + nw;
         const float* kc = cc + (size_t)t * a.kv_lora;
-        const float* kp = cp + (size_t)t * a.rope;
-        float d = 0.f;
-        for (int i = lane; i < a.kv_lora; i += 32) d += q_abs[i] * kc[i];
-        for (int i = lane; i < a.rope; i += 32) d += q_pe[i] * kp[i];
+        const float* kc2 = cc + (size_t)(t2 <= pos ? t2 : t) * a.kv_lora;
+        float d = 0.f, d2 = 0.f;
+        for (int i = lane; i < a.kv_lora; i += 32) {
+            d += q_abs[i] * kc[i];
+            d2 += q_abs[i] * kc2[i];
+        }
+        for (int i = lane; i < a.rope; i += 32) {
+            d += q_pe[i] * cp[(size_t)t * a.rope + i];
+            d2 += q_pe[i] * cp[(size_t)(t2 <= pos ? t2 : t) * a.rope + i];
+        }
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
-        if (lane == 0) scores[t] = d * a.kq_scale;
+        for (int off = 16; off > 0; off >>= 1) {
+            d += __shfl_xor_sync(0xffffffffu, d, off);
+            d2 += __shfl_xor_sync(0xffffffffu, d2, off);
+        }
+        if (lane == 0) {
+            scores[t] = d * a.kq_scale;
+            if (t2 <= pos) scores[t2] = d2 * a.kq_scale;
+        }
     }
     __syncthreads();
 
@@ -199,10 +236,17 @@ __global__ void __launch_bounds__(512) mla_heads_kernel(MlaArgs a) {
     const float inv = sum > 0.f ? 1.0f / sum : 1.0f;
     __syncthreads();
 
-    // ctx = sum_t p[t] kc[t]
+    // ctx = sum_t p[t] kc[t]: warp w takes positions w, w + nw, ... (lanes
+    // over the row), then the warps' partials are added in warp order.
+    for (int i = lane; i < a.kv_lora; i += 32) {
+        float acc = 0.f;
+        for (int t = warp; t <= pos; t += nw) acc += scores[t] * inv * cc[(size_t)t * a.kv_lora + i];
+        cpart[warp * a.kv_lora + i] = acc;
+    }
+    __syncthreads();
     for (int i = tid; i < a.kv_lora; i += blockDim.x) {
         float acc = 0.f;
-        for (int t = 0; t <= pos; ++t) acc += scores[t] * inv * cc[(size_t)t * a.kv_lora + i];
+        for (int w = 0; w < nw; ++w) acc += cpart[w * a.kv_lora + i];
         ctx[i] = acc;
     }
     __syncthreads();
@@ -211,10 +255,16 @@ __global__ void __launch_bounds__(512) mla_heads_kernel(MlaArgs a) {
     const int8_t* vbq = a.v_b_q + (size_t)h * a.v_head * a.kv_lora;
     const float* vbs = a.v_b_s + (size_t)h * a.v_head * (a.kv_lora / a.gs);
     float* out = a.att_concat + (size_t)h * a.v_head;
-    for (int r = warp; r < a.v_head; r += nw) {
-        const float v = q8_row_dot<16>(vbq + (size_t)r * a.kv_lora, vbs + (size_t)r * (a.kv_lora / a.gs), ctx,
-                                       a.kv_lora, a.gs);
-        if (lane == 0) out[r] = v;
+    for (int r0 = warp * kR; r0 < a.v_head; r0 += nw * kR) {
+        float v[kR];
+        q8_rows_dot<16, kR>(vbq, vbs, ctx, a.kv_lora, a.gs, r0, a.v_head, v);
+        if (lane < kR && r0 + lane < a.v_head) {
+            float mine = v[0];
+#pragma unroll
+            for (int j = 1; j < kR; ++j)
+                if (lane == j) mine = v[j];
+            out[r0 + lane] = mine;
+        }
     }
 }
 
@@ -226,15 +276,20 @@ __global__ void silu_mul_kernel(float* g, const float* u, int n) {
     }
 }
 
-// First index of the maximum (argmax, infer.c:1218-1228: strict '>').
-__global__ void argmax_kernel(const float* x, int n, int* out) {
+// First index of the maximum (argmax, infer.c:1218-1228: strict '>'): each
+// CTA reduces a slice to (value, index) in `part`; the last CTA to finish
+// (counter, reset by it) reduces the partials in CTA order.
+__global__ void argmax_kernel(const float* x, int n, float2* part, unsigned* counter, int* out) {
     __shared__ float bv[32];
     __shared__ int bi[32];
+    __shared__ int last;
+    const int per = (n + gridDim.x - 1) / gridDim.x;
+    const int lo = blockIdx.x * per, hi = min(n, lo + per);
     float best = -INFINITY;
     int idx = n;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
         const float v = x[i];
-        if (v > best) {  // i increases per thread: keeps the first maximum
+        if (v > best) {  // i increases per thread: keeps the thread's first maximum
             best = v;
             idx = i;
         }
@@ -260,10 +315,27 @@ __global__ void argmax_kernel(const float* x, int n, int* out) {
                 best = bv[w];
                 idx = bi[w];
             }
-        // glm.c's argmax starts from x[0]: a NaN there (or all-NaN logits)
-        // keeps index 0, since no comparison with NaN succeeds
-        *out = (idx < n && !isnan(x[0])) ? idx : 0;
+        part[blockIdx.x] = make_float2(best, __int_as_float(idx));
+        __threadfence();
+        last = atomicAdd(counter, 1u) == gridDim.x - 1;
     }
+    __syncthreads();
+    if (!last || threadIdx.x != 0) return;
+    __threadfence();
+    float b = -INFINITY;
+    int bix = n;
+    for (int c = 0; c < (int)gridDim.x; ++c) {
+        const float2 p = __ldcg(part + c);
+        const int pi = __float_as_int(p.y);
+        if (p.x > b || (p.x == b && pi < bix)) {
+            b = p.x;
+            bix = pi;
+        }
+    }
+    *counter = 0u;
+    // glm.c's argmax starts from x[0]: a NaN there (or all-NaN logits) keeps
+    // index 0, since no comparison with NaN succeeds
+    *out = (bix < n && !isnan(__ldcg(x))) ? bix : 0;
 }
 
 // End of a decode step at position pos: the next token is the next prompt
@@ -291,11 +363,6 @@ cudaError_t launch_embed(const int8_t* tok_q, const float* tok_s, const int* tok
     return cudaGetLastError();
 }
 
-cudaError_t launch_rmsnorm(const float* x, const float* w, float* o, int n, cudaStream_t st) {
-    rmsnorm_kernel<<<1, 1024, 0, st>>>(x, w, o, n);
-    return cudaGetLastError();
-}
-
 cudaError_t launch_kv_cache_write(float* kv_a, const float* kv_norm, float* cache_comp, float* cache_pe,
                                   const int* pos, int kv_lora, int rope, cudaStream_t st) {
     kv_cache_write_kernel<<<1, 512, 0, st>>>(kv_a, kv_norm, cache_comp, cache_pe, pos, kv_lora, rope);
@@ -303,7 +370,7 @@ cudaError_t launch_kv_cache_write(float* kv_a, const float* kv_norm, float* cach
 }
 
 size_t mla_heads_smem(const MlaArgs& a, int cache_cap) {
-    return sizeof(float) * ((size_t)a.qk_nope + a.rope + 2 * (size_t)a.kv_lora + cache_cap);
+    return sizeof(float) * ((size_t)a.qk_nope + a.rope + 2 * (size_t)a.kv_lora + cache_cap + 16 * (size_t)a.kv_lora);
 }
 
 cudaError_t launch_mla_heads(const MlaArgs& a, int n_heads, int cache_cap, cudaStream_t st) {
@@ -324,8 +391,9 @@ cudaError_t launch_silu_mul(float* g, const float* u, int n, int num_sms, cudaSt
     return cudaGetLastError();
 }
 
-cudaError_t launch_argmax(const float* x, int n, int* out, cudaStream_t st) {
-    argmax_kernel<<<1, 1024, 0, st>>>(x, n, out);
+cudaError_t launch_argmax(const float* x, int n, float2* part, unsigned* counter, int nblocks, int* out,
+                          cudaStream_t st) {
+    argmax_kernel<<<nblocks, 512, 0, st>>>(x, n, part, counter, out);
     return cudaGetLastError();
 }
 

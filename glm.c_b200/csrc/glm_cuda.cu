@@ -74,6 +74,8 @@ struct Model {
     float *x = nullptr, *xn = nullptr, *q_a = nullptr, *q_full = nullptr, *kv_a = nullptr, *att = nullptr,
           *ff_gate = nullptr, *ff_up = nullptr, *logits = nullptr, *cache_comp = nullptr, *cache_pe = nullptr;
     int *pos = nullptr, *token = nullptr, *argmax = nullptr, *prompt = nullptr, *out_ids = nullptr;
+    float2* amax_part = nullptr;      // [num_sms] per-CTA argmax partials
+    unsigned* amax_count = nullptr;   // argmax last-CTA counter
     int prompt_cap = 0, out_cap = 0;
     int* io_host = nullptr;  // pinned [2]: token, pos
 };
@@ -147,7 +149,8 @@ void release_model() {
         for (void* p : A.owned) cudaFree(p);
     for (void* p : m.owned_globals) cudaFree(p);
     void* bufs[] = {m.x,     m.xn,        m.q_a,      m.q_full, m.kv_a,   m.att,    m.ff_gate, m.ff_up,
-                    m.logits, m.cache_comp, m.cache_pe, m.pos,    m.token,  m.argmax, m.prompt,  m.out_ids};
+                    m.logits, m.cache_comp, m.cache_pe, m.pos,    m.token,  m.argmax, m.prompt,  m.out_ids,
+                    m.amax_part, m.amax_count};
     for (void* p : bufs)
         if (p) cudaFree(p);
     if (m.io_host) cudaFreeHost(m.io_host);
@@ -658,25 +661,29 @@ int enqueue_step(cudaStream_t st) {
     for (int l = 0; l < d.n_layers; ++l) {
         const AttnLayer& A = m.attn[l];
         // MLA attention (infer.c:978-1065)
-        LAUNCH_TRY(glmq::launch_rmsnorm(m.x, A.attn_norm, m.xn, D, st));
-        LAUNCH_TRY(glmq::launch_q80_matvec(A.q_a_q, A.q_a_s, m.xn, m.q_a, d.q_lora_rank, D, gs, ns, st));
-        LAUNCH_TRY(glmq::launch_rmsnorm(m.q_a, A.q_a_norm, m.q_a, d.q_lora_rank, st));
+        // (the rmsnorms of x and q_a run fused into the matvecs that read them)
+        LAUNCH_TRY(glmq::launch_q80_matvec(A.q_a_q, A.q_a_s, m.x, m.q_a, d.q_lora_rank, D, gs, ns, st, false,
+                                           A.attn_norm));
         LAUNCH_TRY(glmq::launch_q80_matvec(A.q_b_q, A.q_b_s, m.q_a, m.q_full, d.n_heads * d.head_k_dim, d.q_lora_rank,
-                                           gs, ns, st));
-        LAUNCH_TRY(glmq::launch_q80_matvec(A.kv_a_q, A.kv_a_s, m.xn, m.kv_a, d.kv_lora_rank + d.rope_dim, D, gs, ns, st));
+                                           gs, ns, st, false, A.q_a_norm));
+        LAUNCH_TRY(glmq::launch_q80_matvec(A.kv_a_q, A.kv_a_s, m.x, m.kv_a, d.kv_lora_rank + d.rope_dim, D, gs, ns, st,
+                                           false, A.attn_norm));
         float* comp = m.cache_comp + (size_t)l * d.cache_cap * d.kv_lora_rank;
         float* pe = m.cache_pe + (size_t)l * d.cache_cap * d.rope_dim;
         LAUNCH_TRY(glmq::launch_kv_cache_write(m.kv_a, A.kv_a_norm, comp, pe, m.pos, d.kv_lora_rank, d.rope_dim, st));
-        glmq::MlaArgs ma{m.q_full, comp, pe, A.k_b_q, A.k_b_s, A.v_b_q, A.v_b_s, m.att, m.pos,
-                         d.qk_nope_dim, d.rope_dim, d.head_k_dim, d.kv_lora_rank, d.v_head_dim, gs, kq_scale};
+        glmq::MlaArgs ma{m.q_full,        comp,          pe,           A.k_b_q,         A.k_b_s,
+                         A.v_b_q,         A.v_b_s,       m.att,        m.pos,           d.qk_nope_dim,
+                         d.rope_dim,      d.head_k_dim,  d.kv_lora_rank, d.v_head_dim,  gs,
+                         d.cache_cap,     kq_scale};
         LAUNCH_TRY(glmq::launch_mla_heads(ma, d.n_heads, d.cache_cap, st));
         LAUNCH_TRY(glmq::launch_q80_matvec(A.attn_out_q, A.attn_out_s, m.att, m.x, D, d.n_heads * d.v_head_dim, gs,
                                            ns, st, true));
         if (l == 0) {
             // dense SwiGLU FFN (infer.c:1067-1085)
-            LAUNCH_TRY(glmq::launch_rmsnorm(m.x, m.l0_norm, m.xn, D, st));
-            LAUNCH_TRY(glmq::launch_q80_matvec(m.l0_gate_q, m.l0_gate_s, m.xn, m.ff_gate, d.hidden_dim, D, gs, ns, st));
-            LAUNCH_TRY(glmq::launch_q80_matvec(m.l0_up_q, m.l0_up_s, m.xn, m.ff_up, d.hidden_dim, D, gs, ns, st));
+            LAUNCH_TRY(glmq::launch_q80_matvec(m.l0_gate_q, m.l0_gate_s, m.x, m.ff_gate, d.hidden_dim, D, gs, ns, st,
+                                               false, m.l0_norm));
+            LAUNCH_TRY(glmq::launch_q80_matvec(m.l0_up_q, m.l0_up_s, m.x, m.ff_up, d.hidden_dim, D, gs, ns, st, false,
+                                               m.l0_norm));
             LAUNCH_TRY(glmq::launch_silu_mul(m.ff_gate, m.ff_up, d.hidden_dim, ns, st));
             LAUNCH_TRY(glmq::launch_q80_matvec(m.l0_down_q, m.l0_down_s, m.ff_gate, m.x, D, d.hidden_dim, gs, ns, st,
                                                true));
@@ -684,17 +691,18 @@ int enqueue_step(cudaStream_t st) {
         } else if (use_persistent()) {
             LAUNCH_TRY(glmq::launch_moe_persistent(g.layers_dev, l, 1, g.dims, g.scratch, m.x, nullptr, nullptr,
                                                    routed, ns, st, l + 1 < d.n_layers ? l + 1 : -1));
+            g.launches += 1;
         } else {
             LAUNCH_TRY(glmq::launch_moe_decode(g.layers[l].w, g.dims, g.scratch, m.x, m.x, routed, ns, st));
-            g.launches += 2;
+            g.launches += 3;
         }
-        g.launches += 9;
+        g.launches += 6;
     }
-    // final norm, LM head, argmax (infer.c:1888-1893, 1218-1228)
-    LAUNCH_TRY(glmq::launch_rmsnorm(m.x, m.output_norm, m.xn, D, st));
-    LAUNCH_TRY(glmq::launch_q80_matvec(m.out_q, m.out_s, m.xn, m.logits, d.vocab_size, D, gs, ns, st));
-    LAUNCH_TRY(glmq::launch_argmax(m.logits, d.vocab_size, m.argmax, st));
-    g.launches += 4;
+    // final norm (fused), LM head, argmax (infer.c:1888-1893, 1218-1228)
+    LAUNCH_TRY(glmq::launch_q80_matvec(m.out_q, m.out_s, m.x, m.logits, d.vocab_size, D, gs, ns, st, false,
+                                       m.output_norm));
+    LAUNCH_TRY(glmq::launch_argmax(m.logits, d.vocab_size, m.amax_part, m.amax_count, ns, m.argmax, st));
+    g.launches += 3;  // embedding, LM head, argmax
     return 0;
 }
 
@@ -731,10 +739,12 @@ int glm_cuda_model_init(int device, const GlmCudaModelDims* dims) {
         (rc = dev_alloc(&m.att, (size_t)d.n_heads * d.v_head_dim)) || (rc = dev_alloc(&m.ff_gate, d.hidden_dim)) ||
         (rc = dev_alloc(&m.ff_up, d.hidden_dim)) || (rc = dev_alloc(&m.logits, d.vocab_size)) ||
         (rc = dev_alloc(&m.cache_comp, cache * d.kv_lora_rank)) || (rc = dev_alloc(&m.cache_pe, cache * d.rope_dim)) ||
-        (rc = dev_alloc(&m.pos, 1)) || (rc = dev_alloc(&m.token, 1)) || (rc = dev_alloc(&m.argmax, 1))) {
+        (rc = dev_alloc(&m.pos, 1)) || (rc = dev_alloc(&m.token, 1)) || (rc = dev_alloc(&m.argmax, 1)) ||
+        (rc = dev_alloc(&m.amax_part, g.num_sms)) || (rc = dev_alloc(&m.amax_count, 1))) {
         release_all();
         return rc;
     }
+    CUDA_TRY(cudaMemset(m.amax_count, 0, sizeof(unsigned)));
     CUDA_TRY(cudaMemset(m.cache_comp, 0, sizeof(float) * cache * d.kv_lora_rank));
     CUDA_TRY(cudaMemset(m.cache_pe, 0, sizeof(float) * cache * d.rope_dim));
     CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&m.io_host), 2 * sizeof(int), cudaHostAllocDefault));

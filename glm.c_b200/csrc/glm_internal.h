@@ -69,9 +69,11 @@ cudaError_t launch_moe_persistent(const MoeLayerDev* layers_dev, int first, int 
                                   int routed_enabled, int num_sms, cudaStream_t stream, int next_layer);
 
 // y = Q8(q, s) . x for a rows x cols planar Q8 matrix (gs = 32, cols % 64 == 0);
-// with `accumulate`, y += Q8(q, s) . x.
+// with `accumulate`, y += Q8(q, s) . x; with `norm`, x is first replaced by
+// rmsnorm(x) * norm (glm.c's rmsnorm, infer.c:746-752).
 cudaError_t launch_q80_matvec(const int8_t* q, const float* s, const float* x, float* y, int rows, int cols,
-                              int gs, int num_sms, cudaStream_t stream, bool accumulate = false);
+                              int gs, int num_sms, cudaStream_t stream, bool accumulate = false,
+                              const float* norm = nullptr);
 
 // ---- decoder around the MoE layers (decoder.cu)
 
@@ -85,23 +87,24 @@ struct MlaArgs {
     const float* v_b_s;
     float* att_concat;        // [n_heads][v_head]
     const int* pos;           // device: current position
-    int qk_nope, rope, head_k, kv_lora, v_head, gs;
+    int qk_nope, rope, head_k, kv_lora, v_head, gs, cache_cap;
     float kq_scale;
 };
 
 cudaError_t launch_embed(const int8_t* tok_q, const float* tok_s, const int* token, float* x, int D, int gs,
                          cudaStream_t st);
-cudaError_t launch_rmsnorm(const float* x, const float* w, float* o, int n, cudaStream_t st);
 cudaError_t launch_kv_cache_write(float* kv_a, const float* kv_norm, float* cache_comp, float* cache_pe,
                                   const int* pos, int kv_lora, int rope, cudaStream_t st);
 size_t mla_heads_smem(const MlaArgs& a, int cache_cap);
 cudaError_t launch_mla_heads(const MlaArgs& a, int n_heads, int cache_cap, cudaStream_t st);
 cudaError_t launch_silu_mul(float* g, const float* u, int n, int num_sms, cudaStream_t st);
-cudaError_t launch_argmax(const float* x, int n, int* out, cudaStream_t st);
+// part: nblocks float2 scratch; counter: one word, zero between calls.
+cudaError_t launch_argmax(const float* x, int n, float2* part, unsigned* counter, int nblocks, int* out,
+                          cudaStream_t st);
 cudaError_t launch_decode_advance(int* pos, int* token, const int* argmax, const int* prompt, int n_prompt,
                                   int* out_ids, int vocab, cudaStream_t st);
 
-size_t q80_matvec_smem_bytes(int cols);
+size_t q80_matvec_smem_bytes(int cols, bool norm = false);
 
 // Record the message glm_cuda_last_error() returns for this thread.
 void set_last_error(const char* msg);

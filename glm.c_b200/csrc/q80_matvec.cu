@@ -24,7 +24,8 @@ struct MatvecArgs {
     const float* x;
     float* y;
     int rows, cols;
-    int accumulate;  // y += result instead of y = result
+    int accumulate;      // y += result instead of y = result
+    const float* norm;   // if set: x is first replaced by rmsnorm(x) * norm (infer.c:746-752)
 };
 
 __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a) {
@@ -34,6 +35,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a)
     float* sxg = reinterpret_cast<float*>(sm + (size_t)nch * kChunkBytes);
     float* sxtab = sxg + (a.cols >> 5);
     float* part = sxtab + (size_t)nch * kChunkTab;  // [kMvWarps][16]
+    float* xs = part + kMvWarps * 16;                 // [cols] normalised x (with a.norm)
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, t = lane & 3;
     const int rb = (int)((long long)blockIdx.x * a.rows / gridDim.x);
@@ -43,7 +45,26 @@ __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a)
     ks = ks < 1 ? 1 : (ks > nch ? nch : ks);
     const int tiles_per_pass = kMvWarps / ks;
 
-    quantize_to_planes(a.x, a.cols, planes, sxg, sxtab);
+    if (a.norm) {
+        // rmsnorm fused into the activation load: every CTA forms the same
+        // xn = x * (1/sqrtf(mean(x^2) + 1e-5)) * w (sum of squares in fp64).
+        __shared__ double red[kMvWarps];
+        double ss = 0.0;
+        for (int i = threadIdx.x; i < a.cols; i += kMvThreads) ss += (double)a.x[i] * (double)a.x[i];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        double tot = 0.0;
+        for (int w = 0; w < kMvWarps; ++w) tot += red[w];
+        const float mean = (float)(tot / (double)a.cols);
+        const float inv = 1.0f / sqrtf(mean + 1e-5f);
+        for (int i = threadIdx.x; i < a.cols; i += kMvThreads) xs[i] = a.x[i] * inv * a.norm[i];
+        __syncthreads();
+        quantize_to_planes(xs, a.cols, planes, sxg, sxtab);
+    } else {
+        quantize_to_planes(a.x, a.cols, planes, sxg, sxtab);
+    }
 
     const int boff = b_frag_offset(lane);
     const int kq = warp % ks, tw = warp / ks;
@@ -112,15 +133,16 @@ __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a)
     }
 }
 
-size_t q80_matvec_smem_bytes(int cols) {
+size_t q80_matvec_smem_bytes(int cols, bool norm) {
     const int nch = cols >> 6;
-    return (size_t)nch * kChunkBytes + (size_t)(cols >> 5) * 4 + (size_t)nch * kChunkTab * 4 + kMvWarps * 16 * 4;
+    return (size_t)nch * kChunkBytes + (size_t)(cols >> 5) * 4 + (size_t)nch * kChunkTab * 4 + kMvWarps * 16 * 4 +
+           (norm ? (size_t)cols * 4 : 0);
 }
 
 cudaError_t launch_q80_matvec(const int8_t* q, const float* s, const float* x, float* y, int rows, int cols,
-                              int gs, int num_sms, cudaStream_t stream, bool accumulate) {
+                              int gs, int num_sms, cudaStream_t stream, bool accumulate, const float* norm) {
     if (gs != 32 || cols % 64 || rows <= 0) return cudaErrorInvalidValue;
-    const size_t smem = q80_matvec_smem_bytes(cols);
+    const size_t smem = q80_matvec_smem_bytes(cols, norm != nullptr);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
     static bool attr_set = false;
     if (!attr_set) {
@@ -129,7 +151,7 @@ cudaError_t launch_q80_matvec(const int8_t* q, const float* s, const float* x, f
     }
     int grid = num_sms;
     if (grid > (rows + 15) / 16) grid = (rows + 15) / 16;
-    MatvecArgs a{q, s, x, y, rows, cols, accumulate ? 1 : 0};
+    MatvecArgs a{q, s, x, y, rows, cols, accumulate ? 1 : 0, norm};
     q80_matvec_kernel<<<grid, kMvThreads, smem, stream>>>(a);
     return cudaGetLastError();
 }
