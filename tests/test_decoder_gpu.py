@@ -82,3 +82,25 @@ def test_decoder_config2_shapes_greedy(lib, pkg, oracle_mod):
     ids, ms = lib.generate(prompt, n_gen)
     print(f"config-2 shapes x3 layers: {ids.tolist()} ({ms:.2f} ms)")
     np.testing.assert_array_equal(ids, ids_ref)
+
+
+def test_decoder_config2_full_greedy_100(lib, pkg, oracle_mod):
+    """BASELINE config 2 as stated: 47 layers (dense layer 0, 46 config-0 MoE
+    layers), 16 random prompt ids, 100 greedy tokens -- identical to glm.c's
+    own forward pass. Needs ~70 GB of host memory for the two copies of the
+    31.7 GB model (numpy weights + the reference's view of them) and a few
+    minutes; skipped on hosts without that memory."""
+    psutil = pytest.importorskip("psutil")
+    if psutil.virtual_memory().available < 80e9:
+        pytest.skip("needs ~80 GB of free host memory for the full 47-layer model")
+    synth = pkg.synth
+    dims = dict(synth.CONFIG2)
+    model = synth.decoder_model(2024, **dims)
+    prompt = synth.prompt_ids(2024, 16, dims["vocab_size"])
+    n_gen, cap = 100, 16 + 100 + 8
+    ids_ref, _ = oracle_mod.ref_decode(model, prompt, n_gen, cap)
+    load_model(lib, model, cap)
+    ids, ms = lib.generate(prompt, n_gen)
+    steps = len(prompt) + n_gen - 1
+    print(f"config 2 full: {steps} steps in {ms:.1f} ms ({1000.0 * steps / ms:.1f} tok/s); first ids {ids[:8].tolist()}")
+    np.testing.assert_array_equal(ids, ids_ref)
