@@ -102,6 +102,11 @@ struct State {
     glmq::MoeLayerDev* layers_dev = nullptr;  // device copy of every slot's pointers (persistent kernel)
     bool persistent_ok = false;               // sizes fit the persistent kernel on this device
     int decode_path = GLM_CUDA_PATH_AUTO;
+    // batched prefill (calls with n_tokens >= prefill_min_tokens)
+    bool prefill_ok = false;   // sizes fit the prefill kernels
+    int prefill_min_tokens = 32;
+    unsigned char* pf_ws = nullptr;
+    size_t pf_ws_cap = 0;
     Model m;
 };
 
@@ -169,9 +174,13 @@ void release_all() {
     void* bufs[] = {g.scratch.xn,     g.scratch.h,     g.scratch.center, g.scratch.bound,  g.scratch.topk_idx,
                     g.scratch.topk_w, g.scratch.counter, g.scratch.stats, g.scratch.status, g.scratch.grid_bar,
                     g.x_dev,          g.idx_dev,       g.w_dev,          g.mv_x,           g.mv_y,
-                    g.layers_dev};
+                    g.layers_dev,     g.pf_ws};
     for (void* p : bufs)
         if (p) cudaFree(p);
+    g.pf_ws = nullptr;
+    g.pf_ws_cap = 0;
+    g.prefill_ok = false;
+    g.prefill_min_tokens = 32;
     g.scratch = glmq::MoeScratch{};
     g.x_dev = nullptr;
     g.idx_dev = nullptr;
@@ -190,8 +199,9 @@ void release_all() {
 }
 
 // After a synchronisation that copied scratch.status into status_host: a
-// nonzero word means one of the persistent kernel's bounded waits gave up
-// (bit 2 grid barrier, 3 weight tile, 4 ring slot, 5 routing hand-off).
+// nonzero word means one of the bounded waits gave up (persistent decode
+// kernel: bit 2 grid barrier, 3 weight tile, 4 ring slot, 5 routing hand-off;
+// prefill GEMM: bit 6 tensor-core commit).
 int take_device_status() {
     const unsigned int st = g.status_host ? *g.status_host : 0u;
     if (st == 0) return 0;
@@ -259,10 +269,33 @@ int ensure_stage(int n_tokens) {
     return 0;
 }
 
+int ensure_prefill_ws(int n_tokens) {
+    const size_t need = glmq::prefill_workspace_bytes(g.dims, n_tokens);
+    if (need <= g.pf_ws_cap) return 0;
+    if (g.pf_ws) cudaFree(g.pf_ws);
+    g.pf_ws = nullptr;
+    g.pf_ws_cap = 0;
+    if (int rc = dev_alloc(&g.pf_ws, need)) return rc;
+    g.pf_ws_cap = need;
+    return 0;
+}
+
+bool use_prefill(int n_tokens) {
+    return g.prefill_ok && g.prefill_min_tokens > 0 && n_tokens >= g.prefill_min_tokens;
+}
+
 int moe_enqueue(int layer, float* x_dev, int n_tokens, int32_t* idx_dev, float* w_dev, cudaStream_t st) {
     const LayerSlot& L = g.layers[layer];
     const int routed = routed_disabled_by_env() ? 0 : 1;
     const auto& d = g.dims;
+    if (use_prefill(n_tokens)) {
+        if (int rc = ensure_prefill_ws(n_tokens)) return rc;
+        cudaError_t e = glmq::launch_moe_prefill(L.w, d, g.pf_ws, x_dev, n_tokens, idx_dev, w_dev, routed, g.num_sms,
+                                                 g.scratch.status, g.scratch.stats, st);
+        g.launches += 7;
+        if (e != cudaSuccess) return fail(GLM_CUDA_ERR_CUDA, "moe prefill launch: %s", cudaGetErrorString(e));
+        return 0;
+    }
     if (use_persistent()) {
         for (int t = 0; t < n_tokens; ++t) {
             cudaError_t e = glmq::launch_moe_persistent(g.layers_dev, layer, 1, d, g.scratch, x_dev + (size_t)t * d.D,
@@ -336,6 +369,7 @@ int init_locked(int device, int dim, int moe_ffn_dim, int n_routed_experts, int 
     CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&g.status_host), sizeof(unsigned int), cudaHostAllocDefault));
     *g.status_host = 0;
     g.persistent_ok = glmq::persistent_check(g.dims, g.num_sms, nullptr) == cudaSuccess;
+    g.prefill_ok = glmq::prefill_check(g.dims) == cudaSuccess;
     g.layers.assign(n_layers, LayerSlot{});
     g.launches = 0;
     g.inited = true;
@@ -484,6 +518,17 @@ int glm_cuda_set_decode_path(int path) {
         return fail(GLM_CUDA_ERR_ARG, "these model sizes do not fit the persistent decode kernel on this device");
     g.decode_path = path;
     return 0;
+}
+
+int glm_cuda_set_prefill_tokens(int min_tokens) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_init has not been called");
+    if (min_tokens < 0) return fail(GLM_CUDA_ERR_ARG, "min_tokens must be >= 0");
+    if (min_tokens > 0 && !g.prefill_ok)
+        return fail(GLM_CUDA_ERR_ARG, "these model sizes do not fit the prefill kernels");
+    const int old = g.prefill_ok ? g.prefill_min_tokens : 0;
+    g.prefill_min_tokens = min_tokens;
+    return old;
 }
 
 int glm_cuda_decode_path(void) {

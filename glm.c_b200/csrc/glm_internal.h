@@ -106,6 +106,53 @@ cudaError_t launch_decode_advance(int* pos, int* token, const int* argmax, const
 
 size_t q80_matvec_smem_bytes(int cols, bool norm = false);
 
+// ---- batched prefill (moe_prefill.cu)
+
+struct PrefillRouteArgs {
+    const float* x;        // [T][D]
+    const float* norm;     // [D] ffn_norm
+    const float* router;   // [E][D]
+    const float* bias;     // [E]
+    float* xn;             // [T][D] rmsnorm(x) * norm
+    int32_t* topk_idx;     // [T][K]
+    float* topk_w;         // [T][K]
+    unsigned long long* stats;
+    int T, D, E, K;
+};
+
+struct PrefillDispatchArgs {
+    const int32_t* topk_idx;  // [T][K]
+    int T, K, E, routed;
+    int mt1, mt2;             // weight-row tiles of gate/up (F / 128) and of down (D / 128)
+    int* counts;              // [0] rows, [1] gate/up tiles, [2] down tiles
+    int* row_tok;             // [rows] token of each row
+    int* tok_row;             // [T][K + 1] row of each (token, slot); slot K = shared expert; -1 = none
+    int4* items1;             // gate/up tiles {group, row0, nrows, m-tile | mat << 16}
+    int4* items2;             // down tiles {group, row0, nrows, m-tile}
+};
+
+struct GroupGemmArgs {
+    MoeLayerDev w;
+    const int4* items1;
+    const int4* items2;
+    const int* counts;
+    const void* bhi;   // [rows][K] bf16 activations, high part
+    const void* blo;   // [rows][K] bf16 activations, low part
+    float* out0;       // [rows][Mtot] (gate, or down)
+    float* out1;       // [rows][Mtot] (up)
+    unsigned* status;  // bit 64: a bounded wait gave up
+    int K, Mtot, E, mode;  // mode 0: gate/up (K = D, Mtot = F); 1: down (K = F, Mtot = D)
+};
+
+cudaError_t prefill_check(const MoeDims& d);
+size_t prefill_workspace_bytes(const MoeDims& d, int T);
+// T tokens (x [T][D] on the device, updated in place) through one MoE layer.
+// ws: prefill_workspace_bytes() of device scratch. topk_idx / topk_w
+// (optional, [T][K]) receive the routing.
+cudaError_t launch_moe_prefill(const MoeLayerDev& w, const MoeDims& d, unsigned char* ws, float* x, int T,
+                               int32_t* topk_idx, float* topk_w, int routed, int num_sms, unsigned* status,
+                               unsigned long long* stats, cudaStream_t st);
+
 // Record the message glm_cuda_last_error() returns for this thread.
 void set_last_error(const char* msg);
 

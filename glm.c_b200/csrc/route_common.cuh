@@ -27,6 +27,8 @@ namespace glmq {
 
 constexpr int kMaxTopK = 8;
 
+__host__ __device__ __forceinline__ int pad64(int i) { return i + (i >> 6); }
+
 __device__ __forceinline__ double warp_sum_d(double v) {
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
@@ -192,6 +194,45 @@ __device__ __forceinline__ void block_logit_bound_rows(const float* wr, const fl
             B = 1.01 * u * sum_abs_prefix + 0x1p-38 * (double)ab;
         }
     }
+}
+
+// Centre and bound of one router logit by one warp, lane-contiguous form:
+// lane l takes elements [l*per, (l+1)*per) (per = D/32) of the router row
+// (global memory) and of xn (`xsp`, shared memory in the padded layout
+// pad64, so the lanes' strided reads hit distinct banks). The products are
+// summed in fp64 and the reference's prefixes come from an fp64 warp scan
+// plus a per-lane running sum, so their own error is negligible next to the
+// fp32 rounding of the serial sum: B = 1.01 * 2^-24 * sum_i |P_i| +
+// 2^-40 * sum_i |p_i|. Returned in lane 0.
+__device__ __forceinline__ void warp_logit_bound_contig(const float* __restrict__ wrow, const float* xsp, int D,
+                                                        double& C, double& B) {
+    const int lane = threadIdx.x & 31, per = D >> 5, base = lane * per;
+    const float* wr = wrow + base;
+    double L = 0.0, sum_abs_p = 0.0;
+    for (int j = 0; j < per; j += 4) {
+        const float4 w4 = __ldg(reinterpret_cast<const float4*>(wr + j));
+        const float p0 = __fmul_rn(w4.x, xsp[pad64(base + j)]);
+        const float p1 = __fmul_rn(w4.y, xsp[pad64(base + j + 1)]);
+        const float p2 = __fmul_rn(w4.z, xsp[pad64(base + j + 2)]);
+        const float p3 = __fmul_rn(w4.w, xsp[pad64(base + j + 3)]);
+        L += (double)p0 + (double)p1 + (double)p2 + (double)p3;
+        sum_abs_p += fabs((double)p0) + fabs((double)p1) + fabs((double)p2) + fabs((double)p3);
+    }
+    double inc = L;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const double y = __shfl_up_sync(0xffffffffu, inc, off);
+        if (lane >= off) inc += y;
+    }
+    C = __shfl_sync(0xffffffffu, inc, 31);
+    double run = inc - L, sabs = 0.0;
+    for (int j = 0; j < per; ++j) {
+        run += (double)__fmul_rn(__ldg(wr + j), xsp[pad64(base + j)]);
+        sabs += fabs(run);
+    }
+    sabs = warp_sum_d(sabs);
+    sum_abs_p = warp_sum_d(sum_abs_p);
+    B = 1.01 * 0x1p-24 * sabs + 0x1p-40 * sum_abs_p;
 }
 
 // Rank of expert i by (sel desc, id asc) among the experts with sel > -inf

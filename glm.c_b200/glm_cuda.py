@@ -59,6 +59,7 @@ def _signatures(L: ctypes.CDLL) -> None:
     L.glm_cuda_generate.argtypes = [_P, _I, _I, _P, _P]
     L.glm_cuda_set_decode_path.argtypes = [_I]
     L.glm_cuda_decode_path.argtypes = []
+    L.glm_cuda_set_prefill_tokens.argtypes = [_I]
     L.glm_cuda_moe_layer_noalloc.argtypes = [_P] * 15 + [_I] * 5 + [_P, _I, _P, _P, _P]
     L.glm_cuda_moe_layer_noalloc.restype = _I
     L.glm_cuda_matvec_q80.argtypes = [_P, _P, _P, _P, _I, _I, _I]
@@ -74,6 +75,7 @@ def _signatures(L: ctypes.CDLL) -> None:
     for name in ("glm_cuda_init", "glm_cuda_upload_moe_layer", "glm_cuda_bind_moe_layer_device",
                  "glm_cuda_moe_layer", "glm_cuda_moe_layer_async", "glm_cuda_moe_layer_profile",
                  "glm_cuda_moe_layers_async", "glm_cuda_set_decode_path", "glm_cuda_decode_path",
+                 "glm_cuda_set_prefill_tokens",
                  "glm_cuda_model_init", "glm_cuda_upload_model_globals", "glm_cuda_bind_model_globals_device",
                  "glm_cuda_upload_attn_layer", "glm_cuda_bind_attn_layer_device", "glm_cuda_forward_token",
                  "glm_cuda_generate",
@@ -196,6 +198,14 @@ class GlmCuda:
 
     def set_decode_path(self, path: int) -> None:
         self._check("glm_cuda_set_decode_path", self.L.glm_cuda_set_decode_path(path))
+
+    def set_prefill_tokens(self, min_tokens: int) -> int:
+        """Route calls with n_tokens >= min_tokens to the batched prefill
+        kernels (0 disables); returns the previous threshold."""
+        rc = self.L.glm_cuda_set_prefill_tokens(min_tokens)
+        if rc < 0:
+            self._check("glm_cuda_set_prefill_tokens", rc)
+        return rc
 
     def decode_path(self) -> int:
         rc = self.L.glm_cuda_decode_path()

@@ -68,15 +68,36 @@ def q8_weights(rng: np.random.Generator, rows: int, cols: int, gs: int, lead: tu
     return q, s
 
 
+# Router-bias scale of zipf_bias: with N(0,1) tokens, N(0,0.02) router rows,
+# D = 2048, E = 64 and K = 4, bias_e = -ZIPF_BETA * ln(rank_e) makes the
+# expert pick counts fall off as rank^-1.1 (least-squares log-log slope over
+# 4096 tokens: -1.100).
+ZIPF_BETA = 0.0885
+
+
+def zipf_bias(seed: int, layer: int, n_experts: int, s: float = 1.1) -> np.ndarray:
+    """Router bias giving Zipf(s)-like expert popularity (configs 3 and 4):
+    each expert gets a popularity rank from a seeded permutation and
+    bias = -ZIPF_BETA * (s / 1.1) * ln(rank)."""
+    rank = _rng(seed, layer, "router_bias").permutation(n_experts) + 1
+    return (-(ZIPF_BETA * s / 1.1) * np.log(rank)).astype(np.float32)
+
+
 def moe_layer(seed: int = 42, layer: int = 0, dim: int = 2048, ffn: int = 1536,
-              n_experts: int = 64, k_used: int = 4, gs: int = 32, routed: bool = True) -> dict:
-    """Weights of one MoE FFN layer (shared expert + routed experts + router)."""
+              n_experts: int = 64, k_used: int = 4, gs: int = 32, routed: bool = True,
+              zipf: float | None = None) -> dict:
+    """Weights of one MoE FFN layer (shared expert + routed experts + router).
+    zipf=s draws the router bias with zipf_bias instead of N(0, 0.01)."""
     if dim % gs or ffn % gs:
         raise ValueError("dim and ffn must be multiples of the group size")
     L = dict(dim=dim, ffn=ffn, n_experts=n_experts, k_used=k_used, gs=gs)
     L["ffn_norm"] = np.ones(dim, dtype=np.float32)
     L["router"] = _rng(seed, layer, "router").standard_normal((n_experts, dim), dtype=np.float32) * np.float32(0.02)
-    L["router_bias"] = _rng(seed, layer, "router_bias").standard_normal(n_experts, dtype=np.float32) * np.float32(0.01)
+    if zipf is None:
+        L["router_bias"] = (_rng(seed, layer, "router_bias").standard_normal(n_experts, dtype=np.float32)
+                            * np.float32(0.01))
+    else:
+        L["router_bias"] = zipf_bias(seed, layer, n_experts, zipf)
     for name, (rows, cols) in (("gate_sh", (ffn, dim)), ("up_sh", (ffn, dim)), ("down_sh", (dim, ffn))):
         L[name + "_q"], L[name + "_s"] = q8_weights(_rng(seed, layer, name + "_q"), rows, cols, gs)
     if routed:

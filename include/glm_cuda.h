@@ -90,6 +90,19 @@ int glm_cuda_moe_layer_async(int layer, float *x_dev, int n_tokens, int32_t *top
 /* Select the decode kernels (GLM_CUDA_PATH_*). No counterpart in glm.c. */
 int glm_cuda_set_decode_path(int path);
 
+/* Calls of glm_cuda_moe_layer / _async with n_tokens >= min_tokens run the
+ * batched prefill kernels instead of the per-token decode kernels: exact
+ * routing of all tokens in one launch, then the routed and shared experts
+ * as grouped GEMMs on the tensor cores (Q8 weights dequantised in shared
+ * memory to bf16 pairs), then the weighted combine. Same expert ids; x
+ * agrees with the decode kernels within ~1e-5 relative. 0 disables it.
+ * Default 32 where the sizes fit (dim and moe_ffn_dim multiples of 128,
+ * n_routed_experts <= 256, gs == 32). The first call with a larger n_tokens
+ * than before allocates the kernels' scratch. Returns the previous value,
+ * or a negative error. No counterpart in glm.c, whose prefill runs the
+ * token loop of glm_app_main (infer.c:2190-2228). */
+int glm_cuda_set_prefill_tokens(int min_tokens);
+
 /* The decode kernels the next call will use: GLM_CUDA_PATH_PERSISTENT or
  * GLM_CUDA_PATH_CHAIN (negative on error). */
 int glm_cuda_decode_path(void);

@@ -34,6 +34,7 @@ PATHS = {"persistent": 1, "chain": 2}
 def run_layer(lib, L, x, routed=True, path="persistent"):
     lib.init(0, L["dim"], L["ffn"], L["n_experts"], L["k_used"], L["gs"], 1)
     lib.upload_moe_layer(0, L)
+    lib.set_prefill_tokens(0)  # per-token decode kernels at every n_tokens
     lib.set_decode_path(PATHS[path])
     assert lib.decode_path() == PATHS[path]
     with routed_env(routed):
