@@ -124,22 +124,20 @@ struct PrefillDispatchArgs {
     const int32_t* topk_idx;  // [T][K]
     int T, K, E, routed;
     int mt1, mt2;             // weight-row tiles of gate/up (F / 128) and of down (D / 128)
-    int* counts;              // [0] rows, [1] gate/up tiles, [2] down tiles
+    int* counts;              // [0] rows, [1] gate/up items, [2] down items
     int* row_tok;             // [rows] token of each row
     int* tok_row;             // [T][K + 1] row of each (token, slot); slot K = shared expert; -1 = none
-    int4* items1;             // gate/up tiles {group, row0, nrows, m-tile | mat << 16}
-    int4* items2;             // down tiles {group, row0, nrows, m-tile}
+    int4* items1;             // gate/up items {group, row0, nrows, m-tile}
+    int4* items2;             // down items {group, row0, nrows, m-tile}
 };
 
 struct GroupGemmArgs {
-    MoeLayerDev w;
     const int4* items1;
     const int4* items2;
     const int* counts;
-    const void* bhi;   // [rows][K] bf16 activations, high part
-    const void* blo;   // [rows][K] bf16 activations, low part
-    float* out0;       // [rows][Mtot] (gate, or down)
-    float* out1;       // [rows][Mtot] (up)
+    void* hhi;         // mode 0 output: h = SwiGLU(gate, up) [rows][Mtot] bf16 high part
+    void* hlo;         //                                       low part
+    float* y;          // mode 1 output [rows][Mtot]
     unsigned* status;  // bit 64: a bounded wait gave up
     int K, Mtot, E, mode;  // mode 0: gate/up (K = D, Mtot = F); 1: down (K = F, Mtot = D)
 };

@@ -32,6 +32,8 @@
 // TMEM; four warps read it back with tcgen05.ld (thread = weight row).
 #include <cstdint>
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -45,17 +47,9 @@ namespace {
 
 constexpr int kMaxGroups = 257;  // routed experts + the shared expert
 constexpr int kTM = 128;     // weight rows per tile (MMA M)
-constexpr int kTN = 64;      // token rows per tile (MMA N)
+constexpr int kTN = 128;     // token rows per tile (MMA N <= 128)
 constexpr int kTK = 64;      // K per stage (bf16: 128 bytes per row = one swizzle atom)
-constexpr int kGBufs = 3;    // operand buffers (two stages of loads in flight)
-constexpr int kGThreads = 256;
 constexpr uint64_t kGWaitNs = 2000000000ull;
-
-// Byte offset of element (row, k) in a K-major tile with 64 bf16 per row,
-// 128-byte swizzle (16-byte chunk index XOR row % 8).
-__device__ __forceinline__ uint32_t sw128(int row, int chunk16) {
-    return (uint32_t)row * 128u + ((uint32_t)(chunk16 ^ (row & 7)) << 4);
-}
 
 // tcgen05 shared-memory descriptor: K-major, 128-byte swizzle, 8-row groups
 // 1024 bytes apart (SBO), LBO 16 bytes, descriptor version 1.
@@ -64,33 +58,15 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-// Instruction descriptor: bf16 x bf16 -> f32, both K-major, M = 128, N = 64.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTN >> 3) << 17) |
-                            ((uint32_t)(kTM >> 4) << 24);
-
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
                  : "memory");
 }
 
-__device__ __forceinline__ void cp_async8(uint32_t dst, const void* src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(dst), "l"(src) : "memory");
-}
-
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-
-__device__ __forceinline__ void cp_async_wait2() { asm volatile("cp.async.wait_group 2;\n" ::: "memory"); }
 
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
-
-__device__ __forceinline__ void tc_mma(uint32_t tmem, uint64_t ad, uint64_t bd, uint32_t acc) {
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
-            tmem),
-        "l"(ad), "l"(bd), "r"(kIdesc), "r"(acc)
-        : "memory");
-}
 
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_addr(bar))
@@ -110,15 +86,6 @@ __device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-}
-
-// Bounded wait on an mbarrier phase (2 s of wall time); false if it gave up.
-__device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = global_ns();
-    while (global_ns() - t0 < kGWaitNs)
-        if (mbar_try_wait_sleep(bar, parity, 20000)) return true;
-    return false;
 }
 
 __device__ __forceinline__ void split_bf16(float v, __nv_bfloat16& hi, __nv_bfloat16& lo) {
@@ -189,16 +156,207 @@ __global__ void __launch_bounds__(512) prefill_route_kernel(PrefillRouteArgs a) 
     }
 }
 
+// Batched form: one CTA routes kRT tokens with 2 warps per token (each warp
+// takes every other expert); the router rows stream through shared memory
+// (cp.async, 3 buffers, 4 rows per stage) and are read by every token's
+// warps, so each row leaves L2 once per CTA. Lane l holds its token's xn
+// elements [l*PER, (l+1)*PER) and their products with the row in registers.
+//
+// Bound (lane-contiguous, fp32 inner sums): the reference's prefixes are
+// P_{l,j} = R_l + sum_{k<=j} p_k with R_l the exact sum before lane l (fp64
+// warp scan, error < 2^-46 sum|p|). The lane's fp32 running sum r_j starts at
+// fl32(R_l) and |r_j - P_{l,j}| <= u|R_l| + u sum_{k<=j}|r_k| (+ the scan
+// error), so sum_j |P_{l,j}| <= S_l (1 + PER u) + PER u |R_l| (+ PER * 2^-46
+// sum|p|, negligible after the factor u below), with S_l = sum_j |r_j| <=
+// sabs_l / (1 - PER u) for the fp32 sum sabs_l of those PER terms. The
+// centre C sums the products in fp32 fours ((p0 + p1) + (p2 + p3), within
+// 2u of their exact sum each) and those in fp64. Then
+// B = 1.01 u sum_i |P_i| + (2.0001 u + 2^-40) sum_i |p_i|.
+constexpr int kRT = 2;        // tokens per CTA
+constexpr int kRBufs = 3;     // router-row stages in flight
+constexpr int kRRows = 4;     // router rows per stage
+constexpr int kRThreads = 64 * kRT;
+
+__host__ __device__ __forceinline__ int pad68(int i) { return i + 4 * (i >> 6); }
+
+__device__ __forceinline__ void cp_async_wait2() { asm volatile("cp.async.wait_group 2;\n" ::: "memory"); }
+
+__device__ __forceinline__ void token_bar(int tb) {
+    asm volatile("bar.sync %0, 64;\n" ::"r"(1 + tb) : "memory");
+}
+
+template <int PER>
+__global__ void __launch_bounds__(kRThreads) prefill_route_batched_kernel(PrefillRouteArgs a) {
+    extern __shared__ __align__(16) unsigned char smr[];
+    const int D = PER * 32, E = a.E, K = a.K;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tb = warp >> 1, half = warp & 1, ltid = tid & 63;
+    const int t = blockIdx.x * kRT + tb;
+    const bool live = t < a.T;
+    const int rowf = pad68(D - 1) + 1;                       // padded row length (floats)
+    const int rowf4 = (rowf + 3) & ~3;
+    float* rows = reinterpret_cast<float*>(smr);              // [kRBufs][kRRows][rowf4]
+    double* cen = reinterpret_cast<double*>(rows + kRBufs * kRRows * rowf4);  // [kRT][E]
+    double* bnd = cen + kRT * E;                              // [kRT][E]
+    float* selb = reinterpret_cast<float*>(bnd + kRT * E);    // [kRT][5E]
+    int* miscb = reinterpret_cast<int*>(selb + kRT * 5 * E);  // [kRT][64]
+
+    // rmsnorm of this warp's token: each warp sums its token's squares itself
+    const int base = lane * PER;
+    float xr[PER];
+    double ss = 0.0;
+    if (live) {
+        const float* xt = a.x + (size_t)t * D + base;
+#pragma unroll
+        for (int j = 0; j < PER; j += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(xt + j);
+            xr[j] = v.x;
+            xr[j + 1] = v.y;
+            xr[j + 2] = v.z;
+            xr[j + 3] = v.w;
+        }
+#pragma unroll
+        for (int j = 0; j < PER; ++j) ss += (double)xr[j] * (double)xr[j];
+    }
+    ss = warp_sum_d(ss);
+    float inv = 0.0f;
+    if (live && lane == 0)
+        inv = rms_inv_certified(ss, a.x + (size_t)t * D, D, (a.stats && half == 0) ? &a.stats[3] : nullptr);
+    inv = __shfl_sync(0xffffffffu, inv, 0);
+    if (live) {
+        const float* nrm = a.norm + base;
+#pragma unroll
+        for (int j = 0; j < PER; ++j) xr[j] = __fmul_rn(__fmul_rn(xr[j], inv), __ldg(nrm + j));  // infer.c:751
+        if (half == 0) {
+            float* xo = a.xn + (size_t)t * D + base;
+#pragma unroll
+            for (int j = 0; j < PER; j += 4)
+                *reinterpret_cast<float4*>(xo + j) = make_float4(xr[j], xr[j + 1], xr[j + 2], xr[j + 3]);
+        }
+    }
+
+    // router rows, kRRows per stage, kRBufs stages
+    const int nstage = (E + kRRows - 1) / kRRows;
+    auto issue = [&](int st) {
+        float* dst = rows + (st % kRBufs) * kRRows * rowf4;
+        const int chunks = D / 4;
+        for (int c = tid; c < kRRows * chunks; c += kRThreads) {
+            const int r = c / chunks, q = c - r * chunks;
+            const int e = st * kRRows + r;
+            const bool ok = e < E;
+            cp_async16(smem_addr(dst + r * rowf4 + pad68(4 * q)), a.router + (size_t)(ok ? e : 0) * D + 4 * q, ok);
+        }
+        cp_async_commit();
+    };
+    issue(0);
+    if (nstage > 1) issue(1);
+    else cp_async_commit();
+    for (int st = 0; st < nstage; ++st) {
+        if (st + 2 < nstage) issue(st + 2);
+        else cp_async_commit();
+        cp_async_wait2();
+        __syncthreads();
+        const float* buf = rows + (st % kRBufs) * kRRows * rowf4;
+        for (int rr = half; rr < kRRows; rr += 2) {
+            const int e = st * kRRows + rr;
+            if (!live || e >= E) continue;  // warp-uniform
+            const float* wr = buf + rr * rowf4;
+            float pr[PER];
+            double L = 0.0;
+            float sap = 0.0f;
+#pragma unroll
+            for (int j = 0; j < PER; j += 4) {
+                const float4 w4 = *reinterpret_cast<const float4*>(wr + pad68(base + j));
+                pr[j] = __fmul_rn(w4.x, xr[j]);
+                pr[j + 1] = __fmul_rn(w4.y, xr[j + 1]);
+                pr[j + 2] = __fmul_rn(w4.z, xr[j + 2]);
+                pr[j + 3] = __fmul_rn(w4.w, xr[j + 3]);
+            }
+#pragma unroll
+            for (int j = 0; j < PER; j += 4) {
+                L += (double)__fadd_rn(__fadd_rn(pr[j], pr[j + 1]), __fadd_rn(pr[j + 2], pr[j + 3]));
+                sap = __fadd_rn(__fadd_rn(sap, fabsf(pr[j])), fabsf(pr[j + 1]));
+                sap = __fadd_rn(__fadd_rn(sap, fabsf(pr[j + 2])), fabsf(pr[j + 3]));
+            }
+            double inc = L;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const double y = __shfl_up_sync(0xffffffffu, inc, off);
+                if (lane >= off) inc += y;
+            }
+            const double C = __shfl_sync(0xffffffffu, inc, 31);
+            const double R = inc - L;
+            float run = __double2float_rn(R), sabs = 0.0f;
+#pragma unroll
+            for (int j = 0; j < PER; ++j) {
+                run = __fadd_rn(run, pr[j]);
+                sabs = __fadd_rn(sabs, fabsf(run));
+            }
+            // per-lane bound on sum_j |P_{l,j}|; (1 + PER u) / (1 - PER u) < 1 + 2^-15 for PER <= 64
+            double tl = (double)sabs * (1.0 + 0x1p-15) + (double)PER * 0x1p-24 * fabs(R);
+            double ap = (double)sap * 1.0001;
+            tl = warp_sum_d(tl);
+            ap = warp_sum_d(ap);
+            if (lane == 0) {
+                cen[tb * E + e] = C;
+                bnd[tb * E + e] = 1.01 * 0x1p-24 * tl + (2.0001 * 0x1p-24 + 0x1p-40) * ap;
+            }
+        }
+        __syncthreads();  // buffer st % kRBufs is refilled at st + kRBufs
+    }
+
+    // selection: the token's two warps, synchronised on their own barrier
+    if (!live) return;
+    float* sel = selb + tb * 5 * E;
+    int* misc = miscb + tb * 64;
+    SelectScratch S;
+    S.sel_c = sel;
+    S.sel_lo = sel + E;
+    S.sel_hi = sel + 2 * E;
+    S.p_c = sel + 3 * E;
+    S.taken = reinterpret_cast<int*>(sel + 4 * E);
+    S.rank = misc;
+    S.cert = misc + 16;
+    int* s_idx = misc + 32;
+    float* s_w = reinterpret_cast<float*>(misc + 48);
+    token_bar(tb);
+    block_select(cen + tb * E, bnd + tb * E, a.bias, E, K, a.router, a.xn + (size_t)t * D, D, ltid, 64, S, s_idx,
+                 s_w, half == 0 ? a.stats : nullptr, [tb]() { token_bar(tb); });
+    if (ltid < K) {
+        a.topk_idx[(size_t)t * K + ltid] = s_idx[ltid];
+        a.topk_w[(size_t)t * K + ltid] = s_w[ltid];
+    }
+}
+
+size_t route_batched_smem(int D, int E) {
+    const int rowf4 = ((pad68(D - 1) + 1) + 3) & ~3;
+    return sizeof(float) * kRBufs * kRRows * rowf4 + sizeof(double) * 2 * kRT * E + sizeof(float) * kRT * 5 * E +
+           sizeof(int) * kRT * 64;
+}
+
+template <int PER>
+cudaError_t launch_route_batched(const PrefillRouteArgs& ra, cudaStream_t st) {
+    const size_t smem = route_batched_smem(PER * 32, ra.E);
+    cudaError_t err =
+        cudaFuncSetAttribute(prefill_route_batched_kernel<PER>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (err) return err;
+    prefill_route_batched_kernel<PER><<<(ra.T + kRT - 1) / kRT, kRThreads, smem, st>>>(ra);
+    return cudaGetLastError();
+}
+
 // ----------------------------------------------------------------- dispatch
 
 // One CTA. Groups 0..E-1 are the routed experts, group E the shared expert.
+// Rows of a group are contiguous; a group's rows are cut into tiles of at
+// most kTN rows; work item = (group, first row, rows, weight-row tile).
 __global__ void __launch_bounds__(1024) prefill_dispatch_kernel(PrefillDispatchArgs a) {
     const int T = a.T, K = a.K, E = a.E, G = E + 1;
-    __shared__ int cnt[kMaxGroups], off[kMaxGroups + 1], cur[kMaxGroups], tiles[kMaxGroups], toff[kMaxGroups + 1];
+    __shared__ int cnt[kMaxGroups], off[kMaxGroups + 1], cur[kMaxGroups], toff[kMaxGroups + 1];
     for (int g = threadIdx.x; g < G; g += blockDim.x) {
         cnt[g] = g == E ? T : 0;
         cur[g] = 0;
     }
+    for (int i = threadIdx.x; i < T * (K + 1); i += blockDim.x) a.tok_row[i] = -1;
     __syncthreads();
     if (a.routed)
         for (int i = threadIdx.x; i < T * K; i += blockDim.x) {
@@ -211,21 +369,18 @@ __global__ void __launch_bounds__(1024) prefill_dispatch_kernel(PrefillDispatchA
         for (int g = 0; g < G; ++g) {
             off[g] = o;
             o += cnt[g];
-            tiles[g] = (cnt[g] + kTN - 1) / kTN;
             toff[g] = to;
-            to += tiles[g];
+            to += (cnt[g] + kTN - 1) / kTN;
         }
         off[G] = o;
         toff[G] = to;
-        a.counts[0] = o;                                    // rows
-        a.counts[1] = to * 2 * a.mt1;                       // gate/up tiles
-        a.counts[2] = to * a.mt2;                           // down tiles
+        a.counts[0] = o;           // rows
+        a.counts[1] = to * a.mt1;  // gate/up items
+        a.counts[2] = to * a.mt2;  // down items
     }
     __syncthreads();
-    // rows: (token, slot); routed order inside a group does not matter (rows
-    // are independent), the shared expert's rows follow token order
-    for (int i = threadIdx.x; i < T * (K + 1); i += blockDim.x) a.tok_row[i] = -1;
-    __syncthreads();
+    // rows: (token, slot). Routed rows of a group in any order (rows are
+    // independent); the shared expert's rows in token order.
     if (a.routed)
         for (int i = threadIdx.x; i < T * K; i += blockDim.x) {
             const int e = a.topk_idx[i];
@@ -240,314 +395,598 @@ __global__ void __launch_bounds__(1024) prefill_dispatch_kernel(PrefillDispatchA
         a.row_tok[r] = t;
         a.tok_row[t * (K + 1) + K] = r;
     }
-    // tiles: item = {group, row0, nrows, m-tile | mat << 16}
-    for (int g = threadIdx.x; g < G; g += blockDim.x)
-        for (int j = 0; j < tiles[g]; ++j) {
-            const int row0 = off[g] + j * kTN;
-            const int nrows = min(kTN, off[g] + cnt[g] - row0);
-            const int tile = toff[g] + j;
-            for (int mat = 0; mat < 2; ++mat)
-                for (int mt = 0; mt < a.mt1; ++mt)
-                    a.items1[(tile * 2 + mat) * a.mt1 + mt] = make_int4(g, row0, nrows, mt | (mat << 16));
-            for (int mt = 0; mt < a.mt2; ++mt) a.items2[tile * a.mt2 + mt] = make_int4(g, row0, nrows, mt);
+    // items, weight-row tile fastest: item = tile * mt + m-tile
+    const int ntiles = toff[G];
+    for (int tile = threadIdx.x; tile < ntiles; tile += blockDim.x) {
+        int lo = 0, hi = G - 1;  // group with toff[g] <= tile < toff[g + 1]
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (toff[mid] <= tile) lo = mid;
+            else hi = mid - 1;
         }
-}
-
-// Activation rows (token xn) as bf16 hi + lo.
-__global__ void gather_split_kernel(const float* xn, const int* row_tok, const int* counts, int D,
-                                    __nv_bfloat16* hi, __nv_bfloat16* lo) {
-    const int R = counts[0];
-    for (int r = blockIdx.x; r < R; r += gridDim.x) {
-        const float* src = xn + (size_t)row_tok[r] * D;
-        for (int i = threadIdx.x; i < D; i += blockDim.x) split_bf16(src[i], hi[(size_t)r * D + i], lo[(size_t)r * D + i]);
+        const int g = lo;
+        const int row0 = off[g] + (tile - toff[g]) * kTN;
+        const int nrows = min(kTN, off[g] + cnt[g] - row0);
+        for (int mt = 0; mt < a.mt1; ++mt) a.items1[tile * a.mt1 + mt] = make_int4(g, row0, nrows, mt);
+        for (int mt = 0; mt < a.mt2; ++mt) a.items2[tile * a.mt2 + mt] = make_int4(g, row0, nrows, mt);
     }
 }
 
-// h = silu(G) * U (infer.c:1184-1188, 1197-1201) as bf16 hi + lo.
-__global__ void swiglu_split_kernel(const float* Gm, const float* Um, const int* counts, int F, __nv_bfloat16* hi,
-                                    __nv_bfloat16* lo) {
-    const size_t n = (size_t)counts[0] * F;
+// Activation rows (token xn) as bf16 hi + lo, 8 elements per thread.
+__global__ void gather_split_kernel(const float* __restrict__ xn, const int* __restrict__ row_tok,
+                                    const int* __restrict__ counts, int D, __nv_bfloat16* hi, __nv_bfloat16* lo) {
+    const int per_row = D / 8;
+    const size_t n = (size_t)counts[0] * per_row;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-        const float g = Gm[i];
-        split_bf16(g / (1.0f + expf(-g)) * Um[i], hi[i], lo[i]);
+        const int r = (int)(i / per_row), c = (int)(i - (size_t)r * per_row) * 8;
+        const float* src = xn + (size_t)row_tok[r] * D + c;
+        const float4 v0 = *reinterpret_cast<const float4*>(src), v1 = *reinterpret_cast<const float4*>(src + 4);
+        const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        __align__(16) __nv_bfloat16 h[8], l[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) split_bf16(v[j], h[j], l[j]);
+        *reinterpret_cast<int4*>(hi + (size_t)r * D + c) = *reinterpret_cast<const int4*>(h);
+        *reinterpret_cast<int4*>(lo + (size_t)r * D + c) = *reinterpret_cast<const int4*>(l);
     }
 }
 
 // ------------------------------------------------------------- grouped GEMM
+//
+// Work item = (group, weight tile, up to kTN token rows). The weight tile is
+// the MMA's A operand (M = 128 rows) and lives in TMEM; the token rows are the
+// B operand (shared memory, 128-byte swizzle); the fp32 accumulator is in
+// TMEM.
+//   mode 0 (gate/up): the tile stacks 64 gate rows over the same 64 up rows,
+//           so one accumulator holds both halves of SwiGLU for 64 features.
+//   mode 1 (down): 128 rows of the down matrix.
+// B holds the token rows' high parts followed by their low parts (n = rows
+// rounded up to 32, loaded in 32-row boxes), so per
+// K = 16 two MMAs compute the three products of the split:
+//   D[:, 0:2n]  = A_hi . [B_hi; B_lo]      (first n columns: hi.hi, next n: hi.lo)
+//   D[:, 0:n]  += A_lo . B_hi
+// and the epilogue adds the two column halves.
+//
+// Warp roles (512 threads):
+//   warps 0-3   epilogue: TMEM -> registers (thread = tile row), SwiGLU via a
+//               shared-memory exchange of the gate and up halves (mode 0) or
+//               plain store (mode 1)
+//   warp 4      weight producer: TMA of raw int8 tiles (64-byte swizzle) and
+//               their fp32 scales [rows][4 groups]
+//   warp 5      MMA issuer (one thread) and TMEM owner
+//   warp 6      activation producer: TMA of bf16 hi/lo rows (128-byte swizzle)
+//   warp 7      idle
+//   warps 8-15  dequantisers: raw tile -> A_hi / A_lo in TMEM with
+//               tcgen05.st (thread = tile row r, half h of the 64 columns;
+//               warp w may only reach TMEM lanes 32 (w % 4) .. + 31)
+//
+// TMEM columns: accumulator [0, 2 kTN); A stages [256, 512), kASlots x
+// (A_hi 32 + A_lo 32 columns).
 
-struct GemmSmem {
-    // per buffer: A_hi, A_lo [128][64] bf16, B_hi, B_lo [64][64] bf16 (swizzled),
-    // raw int8 weights [128][64] and their scales [128][2]
-    static constexpr uint32_t kA = kTM * 128, kB = kTN * 128, kRaw = kTM * kTK, kSc = kTM * 8;
-    static constexpr uint32_t kBuf = 2 * kA + 2 * kB + kRaw + kSc;  // multiple of 1024
-    static constexpr uint32_t kBars = kGBufs * kBuf;
-    static constexpr uint32_t kTotal = kBars + 128;
+constexpr int kGemmThreads = 512;
+constexpr int kRawSlots = 8, kASlots = 4, kBSlots = 4;
+constexpr uint32_t kBBytes = 2 * kTN * 128; // bf16 rows [hi: n][lo: n], 128 bytes each
+constexpr uint32_t kRawBytes = kTM * kTK;   // int8 [128][64]
+constexpr uint32_t kScBytes = kTM * 16;     // fp32 scales [128][4]: groups of this k-slice pair
+constexpr uint32_t kRawSlotBytes = kRawBytes + 2048;
+constexpr uint32_t kTmemA = 256;            // first TMEM column of the A stages
+constexpr int kStageLd = 33;                // epilogue exchange row stride (floats)
+
+struct GemmLayout {
+    static constexpr uint32_t b = 0;                                   // kBSlots
+    static constexpr uint32_t raw = b + kBSlots * kBBytes;             // kRawSlots
+    static constexpr uint32_t stage = raw + kRawSlots * kRawSlotBytes; // [2][64][kStageLd] fp32
+    static constexpr uint32_t bars = stage + 2 * 64 * kStageLd * 4;
+    static constexpr uint32_t total = bars + 512;
 };
-static_assert(GemmSmem::kBuf % 1024 == 0, "operand buffers must keep 1024-byte alignment");
+static_assert(GemmLayout::raw % 1024 == 0 && kRawSlotBytes % 1024 == 0, "tiles stay 1024-byte aligned");
+static_assert(GemmLayout::total + 1024 <= 227 * 1024, "shared memory per CTA");
+static_assert(kTmemA + kASlots * 64 <= 512 && 2 * kTN <= (int)kTmemA, "TMEM columns");
 
-__global__ void __launch_bounds__(kGThreads, 1) q8_group_gemm_kernel(GroupGemmArgs a) {
+struct GemmBars {
+    uint64_t raw_full[kRawSlots], raw_empty[kRawSlots];
+    uint64_t a_full[kASlots], a_empty[kASlots];
+    uint64_t b_full[kBSlots], b_empty[kBSlots];
+    uint64_t acc_full, acc_empty;
+    uint32_t tmem;
+    int abort;
+};
+static_assert(sizeof(GemmBars) <= 512, "barrier block");
+
+struct GemmMaps {
+    CUtensorMap w[2];     // routed weights, matrix 0 / 1 ([E * Mtot rows][K] int8)
+    CUtensorMap w_sh[2];  // shared expert weights ([Mtot rows][K] int8)
+    CUtensorMap s[2];     // routed scales ([E * Mtot rows][K / 32] fp32)
+    CUtensorMap s_sh[2];  // shared expert scales
+    CUtensorMap bhi, blo; // activations [rows][K] bf16, 16-row boxes
+};
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
+            dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// D (TMEM) (+)= A (TMEM) . B (shared memory descriptor)
+__device__ __forceinline__ void tc_mma_ts(uint32_t d, uint32_t a, uint64_t bd, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(
+            d),
+        "r"(a), "l"(bd), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(
+            taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;\n" ::: "memory"); }
+
+// Wait for a phase; on a timeout flag the CTA (and the launch status) and
+// return false so that every role leaves its loop.
+__device__ __forceinline__ bool role_wait(GemmBars* B, uint64_t* bar, uint32_t parity, unsigned* status) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    while (global_ns() - t0 < kGWaitNs) {
+        if (mbar_try_wait_sleep(bar, parity, 20000)) return true;
+        if (*reinterpret_cast<volatile int*>(&B->abort)) return false;
+    }
+    *reinterpret_cast<volatile int*>(&B->abort) = 1;
+    atomicOr(status, 64u);
+    return false;
+}
+
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+    return (uint64_t)__float_as_uint(lo) | ((uint64_t)__float_as_uint(hi) << 32);
+}
+
+// Weights q * s of bytes b0, b1 of u (each byte q + 128) as bf16 pairs
+// w_hi + w_lo: q comes out of the byte exactly as (2^23 + byte) - (2^23 + 128),
+// w = q * s rounded once as in fp32, w_hi = w with its low 16 bits cleared,
+// w_lo = bf16(w - w_hi) (the difference is exact in fp32). Packed f32x2
+// arithmetic: two weights per instruction.
+__device__ __forceinline__ void dequant_pair(uint32_t u, int b0, int b1, uint64_t s2, uint32_t& hi2, uint32_t& lo2) {
+    const uint64_t magic = f2_pack(8388736.0f, 8388736.0f);
+    uint64_t q = (uint64_t)__byte_perm(u, 0x4B000000u, 0x7650 | b0) |
+                 ((uint64_t)__byte_perm(u, 0x4B000000u, 0x7650 | b1) << 32);
+    uint64_t w, l;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(q) : "l"(q), "l"(magic));
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(w) : "l"(q), "l"(s2));
+    const uint32_t x0 = (uint32_t)w, x1 = (uint32_t)(w >> 32);
+    hi2 = __byte_perm(x0, x1, 0x7632);
+    const uint64_t h = (uint64_t)(x0 & 0xFFFF0000u) | ((uint64_t)(x1 & 0xFFFF0000u) << 32);
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(l) : "l"(w), "l"(h));
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(lo2) : "f"(__uint_as_float((uint32_t)(l >> 32))),
+        "f"(__uint_as_float((uint32_t)l)));
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    q8_group_gemm_kernel(const __grid_constant__ GemmMaps maps, const GroupGemmArgs a) {
     extern __shared__ __align__(1024) unsigned char gsm_raw[];
     unsigned char* sm = gsm_raw + ((1024u - (smem_addr(gsm_raw) & 1023u)) & 1023u);
-    uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + GemmSmem::kBars);
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + GemmSmem::kBars + 64);
+    GemmBars* B = reinterpret_cast<GemmBars*>(sm + GemmLayout::bars);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n_items = a.counts[a.mode == 0 ? 1 : 2];
-    const int Kd = a.K, nst = Kd / kTK, sgrp = Kd >> 5;
+    const int mode = a.mode;
+    const int n_items = a.counts[mode == 0 ? 1 : 2];
+    const int4* items = mode == 0 ? a.items1 : a.items2;
+    const int Kd = a.K, nk = Kd / kTK, E = a.E, Mtot = a.Mtot;
+    const int tile_rows = mode == 0 ? kTM / 2 : kTM;  // rows of one weight matrix per tile
 
     if (tid == 0) {
-        for (int b = 0; b < kGBufs; ++b) mbar_init(&mbar[b], 1);
+        for (int i = 0; i < kRawSlots; ++i) {
+            mbar_init(&B->raw_full[i], 1);
+            mbar_init(&B->raw_empty[i], 8);  // the 8 dequant warps
+        }
+        for (int i = 0; i < kASlots; ++i) {
+            mbar_init(&B->a_full[i], 8);
+            mbar_init(&B->a_empty[i], 1);    // tcgen05.commit
+        }
+        for (int i = 0; i < kBSlots; ++i) {
+            mbar_init(&B->b_full[i], 1);
+            mbar_init(&B->b_empty[i], 1);
+        }
+        mbar_init(&B->acc_full, 1);
+        mbar_init(&B->acc_empty, 4);  // the 4 epilogue warps
+        B->abort = 0;
         mbar_init_fence();
     }
-    if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_addr(tslot)),
-                     "r"(kTN)
+    if (warp == 5) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;\n" ::"r"(smem_addr(&B->tmem))
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *tslot;
+    const uint32_t tmem = B->tmem;
 
-    uint32_t ncommit[kGBufs] = {0, 0, 0};
-    unsigned gstage = 0;  // running stage count: buffer = gstage % kGBufs
-    bool failed = false;
-
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-        const int4 it = (a.mode == 0 ? a.items1 : a.items2)[item];
-        const int g = it.x, row0 = it.y, nrows = it.z, mt = it.w & 0xffff, mat = it.w >> 16;
-        const int m0 = mt * kTM;
-        const int8_t* wq;
-        const float* ws;
-        size_t moff;  // expert offset in rows of the weight matrix
-        if (a.mode == 0) {
-            const bool sh = g == a.E;
-            wq = mat ? (sh ? a.w.up_sh_q : a.w.up_q) : (sh ? a.w.gate_sh_q : a.w.gate_q);
-            ws = mat ? (sh ? a.w.up_sh_s : a.w.up_s) : (sh ? a.w.gate_sh_s : a.w.gate_s);
-            moff = sh ? 0 : (size_t)g * a.Mtot;
-        } else {
-            const bool sh = g == a.E;
-            wq = sh ? a.w.down_sh_q : a.w.down_q;
-            ws = sh ? a.w.down_sh_s : a.w.down_s;
-            moff = sh ? 0 : (size_t)g * a.Mtot;
+    if (warp == 4) {
+        // ---- weight producer
+        if (lane == 0) {
+            uint32_t rs = 0;
+            for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+                const int4 it = items[item];
+                const bool sh = it.x == E;
+                const int wrow = (sh ? 0 : it.x * Mtot) + it.w * tile_rows;
+                for (int ks = 0; ks < nk; ++ks, ++rs) {
+                    const int slot = rs % kRawSlots;
+                    if (!role_wait(B, &B->raw_empty[slot], ((rs / kRawSlots) & 1) ^ 1, a.status)) goto done;
+                    mbar_arrive_expect_tx(&B->raw_full[slot], kRawBytes + kScBytes);
+                    const uint32_t dst = smem_addr(sm + GemmLayout::raw + slot * kRawSlotBytes);
+                    // scales: groups 4 * (ks / 2) .. + 3, a 16-byte box covering both k-slices of the pair
+                    if (mode == 0) {
+                        tma_load_2d(dst, sh ? &maps.w_sh[0] : &maps.w[0], ks * kTK, wrow, &B->raw_full[slot]);
+                        tma_load_2d(dst + 64 * kTK, sh ? &maps.w_sh[1] : &maps.w[1], ks * kTK, wrow,
+                                    &B->raw_full[slot]);
+                        tma_load_2d(dst + kRawBytes, sh ? &maps.s_sh[0] : &maps.s[0], 4 * (ks >> 1), wrow,
+                                    &B->raw_full[slot]);
+                        tma_load_2d(dst + kRawBytes + 64 * 16, sh ? &maps.s_sh[1] : &maps.s[1], 4 * (ks >> 1), wrow,
+                                    &B->raw_full[slot]);
+                    } else {
+                        tma_load_2d(dst, sh ? &maps.w_sh[0] : &maps.w[0], ks * kTK, wrow, &B->raw_full[slot]);
+                        tma_load_2d(dst + kRawBytes, sh ? &maps.s_sh[0] : &maps.s[0], 4 * (ks >> 1), wrow,
+                                    &B->raw_full[slot]);
+                    }
+                }
+            }
         }
-        const int8_t* wrow0 = wq + (moff + m0) * (size_t)Kd;
-        const float* srow0 = ws + (moff + m0) * (size_t)sgrp;
-        const __nv_bfloat16* bhi = static_cast<const __nv_bfloat16*>(a.bhi) + (size_t)row0 * Kd;
-        const __nv_bfloat16* blo = static_cast<const __nv_bfloat16*>(a.blo) + (size_t)row0 * Kd;
-
-        // stage s of this item -> copies into buffer b (weights raw, scales, token tiles)
-        auto issue = [&](int s, int b) {
-            unsigned char* buf = sm + (size_t)b * GemmSmem::kBuf;
-            const uint32_t sA_raw = smem_addr(buf + 2 * GemmSmem::kA + 2 * GemmSmem::kB);
-            const uint32_t sSc = sA_raw + GemmSmem::kRaw;
-            const uint32_t sBhi = smem_addr(buf + 2 * GemmSmem::kA), sBlo = sBhi + GemmSmem::kB;
-            const int k0 = s * kTK;
-            for (int c = tid; c < kTM * 4; c += kGThreads) {  // 128 rows x 4 x 16 bytes
-                const int r = c >> 2, p = c & 3;
-                cp_async16(sA_raw + r * kTK + p * 16, wrow0 + (size_t)r * Kd + k0 + p * 16, true);
+    } else if (warp == 6) {
+        // ---- activation producer: rows [row0, row0 + n) high parts, then low parts
+        if (lane == 0) {
+            uint32_t bs = 0;
+            for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+                const int4 it = items[item];
+                const int n_eff = (it.z + 31) & ~31, nb = n_eff >> 5;
+                for (int ks = 0; ks < nk; ++ks, ++bs) {
+                    const int slot = bs % kBSlots;
+                    if (!role_wait(B, &B->b_empty[slot], ((bs / kBSlots) & 1) ^ 1, a.status)) goto done;
+                    mbar_arrive_expect_tx(&B->b_full[slot], (uint32_t)n_eff * 128 * 2);
+                    const uint32_t dst = smem_addr(sm + GemmLayout::b + slot * kBBytes);
+                    for (int j = 0; j < nb; ++j) {
+                        tma_load_2d(dst + j * 4096, &maps.bhi, ks * kTK, it.y + 32 * j, &B->b_full[slot]);
+                        tma_load_2d(dst + n_eff * 128 + j * 4096, &maps.blo, ks * kTK, it.y + 32 * j,
+                                    &B->b_full[slot]);
+                    }
+                }
             }
-            for (int r = tid; r < kTM; r += kGThreads) cp_async8(sSc + r * 8, srow0 + (size_t)r * sgrp + (k0 >> 5));
-            for (int c = tid; c < kTN * 8; c += kGThreads) {  // 64 rows x 8 x 16 bytes, hi and lo
-                const int n = c >> 3, p = c & 7;
-                const bool valid = n < nrows;
-                const size_t src = (size_t)(valid ? n : 0) * Kd + k0 + p * 8;
-                cp_async16(sBhi + sw128(n, p), bhi + src, valid);
-                cp_async16(sBlo + sw128(n, p), blo + src, valid);
-            }
-        };
-
-        for (int s = 0; s < 2 && s < nst; ++s) {
-            const unsigned gs = gstage + s;
-            const int b = gs % kGBufs;
-            if (ncommit[b]) failed |= !bar_wait(&mbar[b], (ncommit[b] - 1) & 1u);
-            issue(s, b);
-            cp_async_commit();
         }
-        if (nst < 2) cp_async_commit();
-        for (int s = 0; s < nst; ++s) {
-            const unsigned gs = gstage + s;
-            const int b = gs % kGBufs;
-            if (s + 2 < nst) {
-                const int b2 = (gs + 2) % kGBufs;
-                if (ncommit[b2]) failed |= !bar_wait(&mbar[b2], (ncommit[b2] - 1) & 1u);
-                issue(s + 2, b2);
-            }
-            cp_async_commit();  // (possibly empty) group: keeps "stage s landed" = wait_group 2
-            cp_async_wait2();
-            __syncthreads();
-            // dequantise the weight tile: 128 rows x 64 int8 -> A_hi, A_lo
-            unsigned char* buf = sm + (size_t)b * GemmSmem::kBuf;
-            const int8_t* raw = reinterpret_cast<const int8_t*>(buf + 2 * GemmSmem::kA + 2 * GemmSmem::kB);
-            const float* sc = reinterpret_cast<const float*>(buf + 2 * GemmSmem::kA + 2 * GemmSmem::kB +
-                                                             GemmSmem::kRaw);
-            for (int c = tid; c < kTM * 4; c += kGThreads) {  // 16 int8 per item
-                const int r = c >> 2, p = c & 3;
-                const int4 q = *reinterpret_cast<const int4*>(raw + r * kTK + p * 16);
-                const float scale = sc[r * 2 + (p >> 1)];
-                const int qw[4] = {q.x, q.y, q.z, q.w};
-                __align__(16) __nv_bfloat16 h[16], l[16];
-#pragma unroll
-                for (int j = 0; j < 16; ++j) split_bf16((float)(int8_t)(qw[j >> 2] >> (8 * (j & 3))) * scale, h[j], l[j]);
-                const int ch = p * 2;  // two 16-byte chunks (8 bf16 each)
-                *reinterpret_cast<int4*>(buf + sw128(r, ch)) = *reinterpret_cast<const int4*>(h);
-                *reinterpret_cast<int4*>(buf + sw128(r, ch + 1)) = *reinterpret_cast<const int4*>(h + 8);
-                *reinterpret_cast<int4*>(buf + GemmSmem::kA + sw128(r, ch)) = *reinterpret_cast<const int4*>(l);
-                *reinterpret_cast<int4*>(buf + GemmSmem::kA + sw128(r, ch + 1)) = *reinterpret_cast<const int4*>(l + 8);
-            }
-            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-            __syncthreads();
-            if (tid == 0) {
+    } else if (warp == 5) {
+        // ---- MMA issuer
+        if (lane == 0) {
+            uint32_t as = 0, bs = 0, ac = 0;
+            for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++ac) {
+                const int4 it = items[item];
+                const uint32_t n_eff = (uint32_t)((it.z + 31) & ~31);
+                const uint32_t id_base = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTM >> 4) << 24);
+                const uint32_t id_cat = id_base | ((2 * n_eff >> 3) << 17), id_hi = id_base | ((n_eff >> 3) << 17);
+                if (!role_wait(B, &B->acc_empty, (ac & 1) ^ 1, a.status)) goto done;
                 tc_fence_after();
-                const uint32_t aHi = smem_addr(buf), aLo = aHi + GemmSmem::kA;
-                const uint32_t bHi = aHi + 2 * GemmSmem::kA, bLo = bHi + GemmSmem::kB;
+                for (int ks = 0; ks < nk; ++ks, ++bs, ++as) {
+                    const int bslot = bs % kBSlots, aslot = as % kASlots;
+                    if (!role_wait(B, &B->b_full[bslot], (bs / kBSlots) & 1, a.status)) goto done;
+                    if (!role_wait(B, &B->a_full[aslot], (as / kASlots) & 1, a.status)) goto done;
+                    tc_fence_after();
+                    const uint32_t bAddr = smem_addr(sm + GemmLayout::b + bslot * kBBytes);
+                    const uint32_t aHi = tmem + kTmemA + aslot * 64, aLo = aHi + 32;
 #pragma unroll
-                for (int kk = 0; kk < kTK / 16; ++kk) {
-                    const uint32_t o = kk * 32;
-                    const uint32_t first = (s == 0 && kk == 0) ? 0u : 1u;
-                    tc_mma(tmem, umma_desc(aHi + o), umma_desc(bHi + o), first);
-                    tc_mma(tmem, umma_desc(aHi + o), umma_desc(bLo + o), 1u);
-                    tc_mma(tmem, umma_desc(aLo + o), umma_desc(bHi + o), 1u);
+                    for (int kk = 0; kk < kTK / 16; ++kk) {
+                        const uint64_t bd = umma_desc(bAddr + kk * 32);
+                        tc_mma_ts(tmem, aHi + kk * 8, bd, id_cat, (ks | kk) ? 1u : 0u);
+                        tc_mma_ts(tmem, aLo + kk * 8, bd, id_hi, 1u);
+                    }
+                    tc_commit(&B->a_empty[aslot]);
+                    tc_commit(&B->b_empty[bslot]);
                 }
-                tc_commit(&mbar[b]);
-            }
-            ++ncommit[b];
-        }
-        // the last commit covers every MMA of this tile
-        const int blast = (gstage + nst - 1) % kGBufs;
-        failed |= !bar_wait(&mbar[blast], (ncommit[blast] - 1) & 1u);
-        gstage += nst;
-        tc_fence_after();
-        if (warp < 4) {
-            float* out = a.mode == 0 ? (mat ? a.out1 : a.out0) : a.out0;
-            const int m = warp * 32 + lane;
-            for (int half = 0; half < kTN / 32; ++half) {
-                float v[32];
-                tc_ld32(tmem + ((uint32_t)(warp * 32) << 16) + half * 32, v);
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int n = half * 32 + j;
-                    if (n < nrows) out[(size_t)(row0 + n) * a.Mtot + m0 + m] = v[j];
-                }
+                tc_commit(&B->acc_full);
             }
         }
-        tc_fence_before();
-        // a commit that never arrived stops this CTA (no further MMAs issued)
-        if (__syncthreads_or(failed)) {
-            failed = true;
-            break;
+    } else if (warp >= 8) {
+        // ---- dequantisers
+        const int quarter = warp & 3, h = (warp - 8) >> 2, r = quarter * 32 + lane;
+        const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+        const int swz = (r >> 1) & 3;  // 64-byte swizzle of the raw tile: chunk c of row r at c ^ swz
+        uint32_t rs = 0;
+        for (int item = blockIdx.x; item < n_items; item += gridDim.x)
+            for (int ks = 0; ks < nk; ++ks, ++rs) {
+                const int rslot = rs % kRawSlots, aslot = rs % kASlots;
+                if (!role_wait(B, &B->raw_full[rslot], (rs / kRawSlots) & 1, a.status)) goto done;
+                const unsigned char* slotp = sm + GemmLayout::raw + rslot * kRawSlotBytes;
+                const unsigned char* rowp = slotp + r * kTK;
+                const int4 v0 = *reinterpret_cast<const int4*>(rowp + 16 * ((2 * h) ^ swz));
+                const int4 v1 = *reinterpret_cast<const int4*>(rowp + 16 * ((2 * h + 1) ^ swz));
+                const float s = reinterpret_cast<const float*>(slotp + kRawBytes)[r * 4 + 2 * (ks & 1) + h];
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&B->raw_empty[rslot]);
+                const uint64_t s2 = f2_pack(s, s);
+                uint32_t hv[16], lv[16];
+                const uint32_t qw[8] = {(uint32_t)v0.x, (uint32_t)v0.y, (uint32_t)v0.z, (uint32_t)v0.w,
+                                        (uint32_t)v1.x, (uint32_t)v1.y, (uint32_t)v1.z, (uint32_t)v1.w};
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const uint32_t u = qw[j] ^ 0x80808080u;  // bytes q + 128
+                    dequant_pair(u, 0, 1, s2, hv[2 * j], lv[2 * j]);
+                    dequant_pair(u, 2, 3, s2, hv[2 * j + 1], lv[2 * j + 1]);
+                }
+                if (!role_wait(B, &B->a_empty[aslot], ((rs / kASlots) & 1) ^ 1, a.status)) goto done;
+                const uint32_t ta = tmem + lane_base + kTmemA + aslot * 64 + h * 16;
+                tc_st16(ta, hv);
+                tc_st16(ta + 32, lv);
+                asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&B->a_full[aslot]);
+            }
+    } else if (warp < 4) {
+        // ---- epilogue: thread = tile row (warp * 32 + lane)
+        float* stage = reinterpret_cast<float*>(sm + GemmLayout::stage);  // [2][64][kStageLd]
+        const int row = warp * 32 + lane;
+        uint32_t ac = 0;
+        for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++ac) {
+            const int4 it = items[item];
+            const int row0 = it.y, nrows = it.z, n_eff = (nrows + 31) & ~31;
+            if (!role_wait(B, &B->acc_full, ac & 1, a.status)) goto done;
+            tc_fence_after();
+            const uint32_t tb = tmem + ((uint32_t)(warp * 32) << 16);
+            for (int n0 = 0; n0 < nrows; n0 += 32) {
+                float v[32], w2[32];
+                tc_ld32(tb + n0, v);        // hi.hi + lo.hi
+                tc_ld32(tb + n_eff + n0, w2);  // hi.lo (columns past 2 n_eff are never used)
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] += w2[j];
+                if (n0 + 32 >= nrows) {  // accumulator read out: let the next item's MMAs start
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&B->acc_empty);
+                }
+                if (mode == 0) {
+                    // rows 0-63 gate, 64-127 up (same 64 features): exchange through shared memory
+                    float* st = stage + (row >> 6) * 64 * kStageLd + (row & 63) * kStageLd;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) st[j] = v[j];
+                    epi_bar();
+                    const int f = tid & 63, j0 = (tid >> 6) * 16;
+                    const int col = it.w * 64 + f;
+                    const float* gs = stage + f * kStageLd;
+                    const float* us = stage + 64 * kStageLd + f * kStageLd;
+#pragma unroll
+                    for (int j = j0; j < j0 + 16; ++j) {
+                        if (n0 + j >= nrows) break;
+                        const float g = gs[j];
+                        const float hval = __fdividef(g, 1.0f + __expf(-g)) * us[j];  // infer.c:1184-1188, 1197-1201
+                        __nv_bfloat16 hh, hl;
+                        split_bf16(hval, hh, hl);
+                        const size_t o = (size_t)(row0 + n0 + j) * Mtot + col;
+                        static_cast<__nv_bfloat16*>(a.hhi)[o] = hh;
+                        static_cast<__nv_bfloat16*>(a.hlo)[o] = hl;
+                    }
+                    epi_bar();  // stage is rewritten by the next chunk
+                } else {
+                    const int col = it.w * kTM + row;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        if (n0 + j >= nrows) break;
+                        a.y[(size_t)(row0 + n0 + j) * Mtot + col] = v[j];
+                    }
+                }
+            }
         }
     }
-    if (failed && tid == 0) atomicOr(a.status, 64u);
+done:
     __syncthreads();
-    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTN) : "memory");
+    if (warp == 5) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;\n" ::"r"(tmem) : "memory");
+    }
 }
 
 // ------------------------------------------------------------------ combine
 
 // x[t] += y_shared + sum_k (1.8 w_k) y_k in rank order (infer.c:1175,1192,
-// 1212-1214).
-__global__ void prefill_combine_kernel(float* x, const float* Y, const int* tok_row, const float* topk_w, int D,
-                                       int K, int routed) {
-    const int t = blockIdx.x;
-    const int* tr = tok_row + (size_t)t * (K + 1);
-    for (int i = threadIdx.x; i < D; i += blockDim.x) {
-        float acc = 0.0f;
+// 1212-1214), 4 elements per thread.
+__global__ void prefill_combine_kernel(float* x, const float* __restrict__ Y, const int* __restrict__ tok_row,
+                                       const float* __restrict__ topk_w, int T, int D, int K, int routed) {
+    const int per_tok = D / 4;
+    const size_t n = (size_t)T * per_tok;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i / per_tok), c = (int)(i - (size_t)t * per_tok) * 4;
+        const int* tr = tok_row + (size_t)t * (K + 1);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         if (routed)
             for (int k = 0; k < K; ++k) {
                 const int r = tr[k];
                 if (r < 0) continue;
-                acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(topk_w[(size_t)t * K + k], 1.8f), Y[(size_t)r * D + i]));
+                const float wk = __fmul_rn(topk_w[(size_t)t * K + k], 1.8f);
+                const float4 y = *reinterpret_cast<const float4*>(Y + (size_t)r * D + c);
+                acc.x = __fadd_rn(acc.x, __fmul_rn(wk, y.x));
+                acc.y = __fadd_rn(acc.y, __fmul_rn(wk, y.y));
+                acc.z = __fadd_rn(acc.z, __fmul_rn(wk, y.z));
+                acc.w = __fadd_rn(acc.w, __fmul_rn(wk, y.w));
             }
-        const float ysh = Y[(size_t)tr[K] * D + i];
-        x[(size_t)t * D + i] = __fadd_rn(x[(size_t)t * D + i], __fadd_rn(ysh, acc));
+        const float4 ys = *reinterpret_cast<const float4*>(Y + (size_t)tr[K] * D + c);
+        float4* xp = reinterpret_cast<float4*>(x + (size_t)t * D + c);
+        float4 xv = *xp;
+        xv.x = __fadd_rn(xv.x, __fadd_rn(ys.x, acc.x));
+        xv.y = __fadd_rn(xv.y, __fadd_rn(ys.y, acc.y));
+        xv.z = __fadd_rn(xv.z, __fadd_rn(ys.z, acc.z));
+        xv.w = __fadd_rn(xv.w, __fadd_rn(ys.w, acc.w));
+        *xp = xv;
     }
+}
+
+// ------------------------------------------------------------ tensor maps
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// 2-D map over a row-major [rows][cols] matrix, box [box_rows][box_cols].
+bool make_map(CUtensorMap* m, const void* base, CUtensorMapDataType type, int elem, uint64_t rows, uint64_t cols,
+              uint32_t box_rows, uint32_t box_cols, CUtensorMapSwizzle swz) {
+    auto fn = encode_fn();
+    if (!fn || !base) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * (uint64_t)elem};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, type, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace
 
 cudaError_t prefill_check(const MoeDims& d) {
-    if (d.gs != 32 || d.D % kTM || d.F % kTM || d.D % kTK || d.F % kTK || d.E + 1 > kMaxGroups || d.K < 1 ||
-        d.K > kMaxTopK || d.D > 8192)
+    if (d.gs != 32 || d.D % kTM || d.F % kTM || d.E < 1 || d.E + 1 > kMaxGroups || d.K < 1 || d.K > kMaxTopK ||
+        d.K > d.E || d.D > 8192 || d.F > 16384)
         return cudaErrorInvalidValue;
     return cudaSuccess;
 }
 
-size_t prefill_workspace_bytes(const MoeDims& d, int T) {
+namespace {
+
+struct PrefillWs {
+    float* xn;
+    int32_t* ids;
+    float* wts;
+    int* row_tok;
+    int* tok_row;
+    int* counts;
+    int4* items1;
+    int4* items2;
+    __nv_bfloat16 *xhi, *xlo, *hhi, *hlo;
+    float* y;
+    size_t bytes;
+};
+
+PrefillWs carve(unsigned char* base, const MoeDims& d, int T) {
     const size_t R = (size_t)T * (d.K + 1), tiles = R / kTN + d.E + 1;
+    PrefillWs w{};
     size_t b = 0;
-    auto take = [&](size_t n) { b += (n + 255) & ~(size_t)255; };
-    take((size_t)T * d.D * 4);              // xn
-    take((size_t)T * d.K * 4 * 2);          // ids, weights
-    take(R * 4);                            // row_tok
-    take((size_t)T * (d.K + 1) * 4);        // tok_row
-    take(4 * 4);                            // counts
-    take(tiles * 2 * (d.F / kTM) * 16);     // items1
-    take(tiles * (d.D / kTM) * 16);         // items2
-    take(R * d.D * 2 * 2);                  // x hi/lo
-    take(R * d.F * 4 * 2);                  // G, U
-    take(R * d.F * 2 * 2);                  // h hi/lo
-    take(R * d.D * 4);                      // Y
-    return b;
+    auto take = [&](size_t n) {
+        unsigned char* r = base ? base + b : nullptr;
+        b += (n + 255) & ~(size_t)255;
+        return r;
+    };
+    w.xn = reinterpret_cast<float*>(take((size_t)T * d.D * 4));
+    w.ids = reinterpret_cast<int32_t*>(take((size_t)T * d.K * 4));
+    w.wts = reinterpret_cast<float*>(take((size_t)T * d.K * 4));
+    w.row_tok = reinterpret_cast<int*>(take(R * 4));
+    w.tok_row = reinterpret_cast<int*>(take(R * 4));
+    w.counts = reinterpret_cast<int*>(take(16));
+    w.items1 = reinterpret_cast<int4*>(take(tiles * (d.F / (kTM / 2)) * 16));
+    w.items2 = reinterpret_cast<int4*>(take(tiles * (d.D / kTM) * 16));
+    w.xhi = reinterpret_cast<__nv_bfloat16*>(take(R * d.D * 2));
+    w.xlo = reinterpret_cast<__nv_bfloat16*>(take(R * d.D * 2));
+    w.hhi = reinterpret_cast<__nv_bfloat16*>(take(R * d.F * 2));
+    w.hlo = reinterpret_cast<__nv_bfloat16*>(take(R * d.F * 2));
+    w.y = reinterpret_cast<float*>(take(R * d.D * 4));
+    w.bytes = b;
+    return w;
 }
+
+}  // namespace
+
+size_t prefill_workspace_bytes(const MoeDims& d, int T) { return carve(nullptr, d, T).bytes; }
 
 cudaError_t launch_moe_prefill(const MoeLayerDev& w, const MoeDims& d, unsigned char* ws, float* x, int T,
                                int32_t* topk_idx, float* topk_w, int routed, int num_sms, unsigned* status,
                                unsigned long long* stats, cudaStream_t st) {
     cudaError_t err = prefill_check(d);
-    if (err != cudaSuccess || T <= 0) return err != cudaSuccess ? err : cudaErrorInvalidValue;
-    const size_t R = (size_t)T * (d.K + 1), tiles = R / kTN + d.E + 1;
-    const int mt1 = d.F / kTM, mt2 = d.D / kTM;
-    unsigned char* p = ws;
-    auto take = [&](size_t n) {
-        unsigned char* r = p;
-        p += (n + 255) & ~(size_t)255;
-        return r;
+    if (err != cudaSuccess) return err;
+    if (T <= 0) return cudaErrorInvalidValue;
+    const bool use_routed = routed && w.gate_q && w.up_q && w.down_q;
+    const size_t R = (size_t)T * (d.K + 1);
+    const int mt1 = d.F / (kTM / 2), mt2 = d.D / kTM;  // gate/up tiles: 64 features
+    const PrefillWs p = carve(ws, d, T);
+
+    // tensor maps: weights (box 128 rows x 64 bytes) and activations (box 32 rows x 64 bf16, 128-byte swizzle)
+    GemmMaps m1{}, m2{};
+    const uint64_t er = (uint64_t)d.E;
+    bool ok = true;
+    // weights: box [rows][64 bytes]; gate/up tiles stack 64 + 64 rows, down tiles 128 rows
+    auto wmap = [&](CUtensorMap* mp, const int8_t* q, uint64_t rows, int cols, uint32_t box_rows,
+                    const CUtensorMap* alt) {
+        if (q) ok = ok && make_map(mp, q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rows, cols, box_rows, kTK,
+                                   CU_TENSOR_MAP_SWIZZLE_64B);
+        else if (alt) *mp = *alt;  // never read: no routed items
     };
-    float* xn = reinterpret_cast<float*>(take((size_t)T * d.D * 4));
-    int32_t* ids = reinterpret_cast<int32_t*>(take((size_t)T * d.K * 4 * 2));
-    float* wts = reinterpret_cast<float*>(ids + (size_t)T * d.K);
-    int* row_tok = reinterpret_cast<int*>(take(R * 4));
-    int* tok_row = reinterpret_cast<int*>(take((size_t)T * (d.K + 1) * 4));
-    int* counts = reinterpret_cast<int*>(take(16));
-    int4* items1 = reinterpret_cast<int4*>(take(tiles * 2 * mt1 * 16));
-    int4* items2 = reinterpret_cast<int4*>(take(tiles * mt2 * 16));
-    __nv_bfloat16* xhi = reinterpret_cast<__nv_bfloat16*>(take(R * d.D * 2 * 2));
-    __nv_bfloat16* xlo = xhi + R * d.D;
-    float* Gm = reinterpret_cast<float*>(take(R * d.F * 4 * 2));
-    float* Um = Gm + R * d.F;
-    __nv_bfloat16* hhi = reinterpret_cast<__nv_bfloat16*>(take(R * d.F * 2 * 2));
-    __nv_bfloat16* hlo = hhi + R * d.F;
-    float* Y = reinterpret_cast<float*>(take(R * d.D * 4));
+    auto smap = [&](CUtensorMap* mp, const float* sc, uint64_t rows, int cols, uint32_t box_rows,
+                    const CUtensorMap* alt) {
+        if (sc) ok = ok && make_map(mp, sc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, rows, cols / 32, box_rows, 4,
+                                    CU_TENSOR_MAP_SWIZZLE_NONE);
+        else if (alt) *mp = *alt;
+    };
+    const uint32_t r1 = kTM / 2, r2 = kTM;
+    wmap(&m1.w_sh[0], w.gate_sh_q, d.F, d.D, r1, nullptr);
+    wmap(&m1.w_sh[1], w.up_sh_q, d.F, d.D, r1, nullptr);
+    wmap(&m1.w[0], use_routed ? w.gate_q : nullptr, er * d.F, d.D, r1, &m1.w_sh[0]);
+    wmap(&m1.w[1], use_routed ? w.up_q : nullptr, er * d.F, d.D, r1, &m1.w_sh[1]);
+    smap(&m1.s_sh[0], w.gate_sh_s, d.F, d.D, r1, nullptr);
+    smap(&m1.s_sh[1], w.up_sh_s, d.F, d.D, r1, nullptr);
+    smap(&m1.s[0], use_routed ? w.gate_s : nullptr, er * d.F, d.D, r1, &m1.s_sh[0]);
+    smap(&m1.s[1], use_routed ? w.up_s : nullptr, er * d.F, d.D, r1, &m1.s_sh[1]);
+    wmap(&m2.w_sh[0], w.down_sh_q, d.D, d.F, r2, nullptr);
+    wmap(&m2.w[0], use_routed ? w.down_q : nullptr, er * d.D, d.F, r2, &m2.w_sh[0]);
+    smap(&m2.s_sh[0], w.down_sh_s, d.D, d.F, r2, nullptr);
+    smap(&m2.s[0], use_routed ? w.down_s : nullptr, er * d.D, d.F, r2, &m2.s_sh[0]);
+    m2.w_sh[1] = m2.w_sh[0];
+    m2.w[1] = m2.w[0];
+    m2.s_sh[1] = m2.s_sh[0];
+    m2.s[1] = m2.s[0];
+    ok = ok && make_map(&m1.bhi, p.xhi, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, R, d.D, 32, kTK, CU_TENSOR_MAP_SWIZZLE_128B);
+    ok = ok && make_map(&m1.blo, p.xlo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, R, d.D, 32, kTK, CU_TENSOR_MAP_SWIZZLE_128B);
+    ok = ok && make_map(&m2.bhi, p.hhi, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, R, d.F, 32, kTK, CU_TENSOR_MAP_SWIZZLE_128B);
+    ok = ok && make_map(&m2.blo, p.hlo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, R, d.F, 32, kTK, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!ok) return cudaErrorInvalidValue;
 
     // 1 routing
-    PrefillRouteArgs ra{x, w.ffn_norm, w.router, w.router_bias, xn, ids, wts, stats, T, d.D, d.E, d.K};
-    const size_t rsmem = sizeof(float) * ((pad64(d.D) + 3) & ~3) + sizeof(float) * d.D + 16 * (size_t)d.E +
-                         20 * (size_t)d.E + 256;
-    if ((err = cudaFuncSetAttribute(prefill_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsmem)))
-        return err;
-    prefill_route_kernel<<<T, 512, rsmem, st>>>(ra);
+    PrefillRouteArgs ra{x, w.ffn_norm, w.router, w.router_bias, p.xn, p.ids, p.wts, stats, T, d.D, d.E, d.K};
+    switch (d.D / 32) {
+        case 16: err = launch_route_batched<16>(ra, st); break;
+        case 32: err = launch_route_batched<32>(ra, st); break;
+        case 48: err = launch_route_batched<48>(ra, st); break;
+        case 64: err = launch_route_batched<64>(ra, st); break;
+        default: {
+            const size_t rsmem = sizeof(float) * ((pad64(d.D) + 3) & ~3) + sizeof(float) * d.D +
+                                 16 * (size_t)d.E + 20 * (size_t)d.E + 256;
+            if ((err = cudaFuncSetAttribute(prefill_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)rsmem)))
+                return err;
+            prefill_route_kernel<<<T, 512, rsmem, st>>>(ra);
+        }
+    }
+    if (err) return err;
     // 2 dispatch
-    PrefillDispatchArgs da{ids, T, d.K, d.E, routed && w.gate_q != nullptr, mt1, mt2, counts, row_tok, tok_row,
-                           items1, items2};
+    PrefillDispatchArgs da{p.ids, T, d.K, d.E, use_routed ? 1 : 0, mt1, mt2, p.counts, p.row_tok, p.tok_row,
+                           p.items1, p.items2};
     prefill_dispatch_kernel<<<1, 1024, 0, st>>>(da);
     // 3 activations
-    gather_split_kernel<<<num_sms * 4, 256, 0, st>>>(xn, row_tok, counts, d.D, xhi, xlo);
-    // 4 gate / up
-    if ((err = cudaFuncSetAttribute(q8_group_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)(GemmSmem::kTotal + 1024))))
+    gather_split_kernel<<<num_sms * 4, 256, 0, st>>>(p.xn, p.row_tok, p.counts, d.D, p.xhi, p.xlo);
+    // 4 gate/up + SwiGLU, 5 down
+    const int gsmem = (int)GemmLayout::total + 1024;
+    if ((err = cudaFuncSetAttribute(q8_group_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gsmem)))
         return err;
-    GroupGemmArgs g1{w, items1, items2, counts, xhi, xlo, Gm, Um, status, d.D, d.F, d.E, 0};
-    q8_group_gemm_kernel<<<num_sms, kGThreads, GemmSmem::kTotal + 1024, st>>>(g1);
-    // 5 SwiGLU
-    swiglu_split_kernel<<<num_sms * 4, 256, 0, st>>>(Gm, Um, counts, d.F, hhi, hlo);
-    // 6 down
-    GroupGemmArgs g2{w, items1, items2, counts, hhi, hlo, Y, nullptr, status, d.F, d.D, d.E, 1};
-    q8_group_gemm_kernel<<<num_sms, kGThreads, GemmSmem::kTotal + 1024, st>>>(g2);
-    // 7 combine
-    prefill_combine_kernel<<<T, 256, 0, st>>>(x, Y, tok_row, wts, d.D, d.K, routed && w.gate_q != nullptr);
-    if (topk_idx) cudaMemcpyAsync(topk_idx, ids, sizeof(int32_t) * T * d.K, cudaMemcpyDeviceToDevice, st);
-    if (topk_w) cudaMemcpyAsync(topk_w, wts, sizeof(float) * T * d.K, cudaMemcpyDeviceToDevice, st);
+    GroupGemmArgs g1{p.items1, p.items2, p.counts, p.hhi, p.hlo, nullptr, status, d.D, d.F, d.E, 0};
+    q8_group_gemm_kernel<<<num_sms, kGemmThreads, gsmem, st>>>(m1, g1);
+    GroupGemmArgs g2{p.items1, p.items2, p.counts, nullptr, nullptr, p.y, status, d.F, d.D, d.E, 1};
+    q8_group_gemm_kernel<<<num_sms, kGemmThreads, gsmem, st>>>(m2, g2);
+    // 6 combine
+    prefill_combine_kernel<<<num_sms * 4, 256, 0, st>>>(x, p.y, p.tok_row, p.wts, T, d.D, d.K, use_routed ? 1 : 0);
+    if (topk_idx) cudaMemcpyAsync(topk_idx, p.ids, sizeof(int32_t) * T * d.K, cudaMemcpyDeviceToDevice, st);
+    if (topk_w) cudaMemcpyAsync(topk_w, p.wts, sizeof(float) * T * d.K, cudaMemcpyDeviceToDevice, st);
     return cudaGetLastError();
 }
 

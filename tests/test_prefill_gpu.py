@@ -98,7 +98,9 @@ def test_prefill_routed_off(lib, pkg, oracle_mod):
 
 
 def test_prefill_agrees_with_decode_kernels(lib, pkg):
-    """Same ids as the per-token decode kernels; x within 1e-4 relative."""
+    """Same ids as the per-token decode kernels; routing weights within 1e-4
+    (both take the weight from their own estimate of the router logit, so
+    they may differ in the last bit); x within 1e-4 relative."""
     synth = pkg.synth
     cfg = dict(dim=1024, ffn=512, n_experts=64, k_used=4, gs=32)
     L = synth.moe_layer(seed=14, zipf=1.1, **cfg)
@@ -107,7 +109,7 @@ def test_prefill_agrees_with_decode_kernels(lib, pkg):
     lib.set_prefill_tokens(0)
     xd, idd, wd = lib.moe_layer(0, x, 4)
     np.testing.assert_array_equal(ip, idd)
-    np.testing.assert_array_equal(wp, wd)
+    np.testing.assert_allclose(wp, wd, rtol=0, atol=TOL_W)
     check_moe_outputs(x, xp, xd, 1e-4)
 
 
