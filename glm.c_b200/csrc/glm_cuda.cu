@@ -107,6 +107,11 @@ struct State {
     int prefill_min_tokens = 32;
     unsigned char* pf_ws = nullptr;
     size_t pf_ws_cap = 0;
+    // expert parallelism (glm_cuda_ep_setup): routed weights hold this shard's experts
+    int ep_shards = 1, ep_shard = 0;
+    glmq::EpShape ep{};
+    unsigned char* ep_ws = nullptr;
+    int ep_layer = -1, ep_T = 0, ep_nrecv = -1;  // the layer in flight
     Model m;
 };
 
@@ -174,9 +179,14 @@ void release_all() {
     void* bufs[] = {g.scratch.xn,     g.scratch.h,     g.scratch.center, g.scratch.bound,  g.scratch.topk_idx,
                     g.scratch.topk_w, g.scratch.counter, g.scratch.stats, g.scratch.status, g.scratch.grid_bar,
                     g.x_dev,          g.idx_dev,       g.w_dev,          g.mv_x,           g.mv_y,
-                    g.layers_dev,     g.pf_ws};
+                    g.layers_dev,     g.pf_ws,         g.ep_ws};
     for (void* p : bufs)
         if (p) cudaFree(p);
+    g.ep_ws = nullptr;
+    g.ep_shards = 1;
+    g.ep_shard = 0;
+    g.ep = glmq::EpShape{};
+    g.ep_layer = -1;
     g.pf_ws = nullptr;
     g.pf_ws_cap = 0;
     g.prefill_ok = false;
@@ -233,8 +243,10 @@ bool routed_disabled_by_env() {
     return v && v[0] && v[0] != '0';
 }
 
-int check_layer(int layer) {
+int check_layer(int layer, bool sharded_ok = false) {
     if (!g.inited) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_init has not been called");
+    if (g.ep_shards > 1 && !sharded_ok)
+        return fail(GLM_CUDA_ERR_STATE, "experts are sharded (glm_cuda_ep_setup): use the glm_cuda_ep_* calls");
     if (layer < 0 || layer >= (int)g.layers.size())
         return fail(GLM_CUDA_ERR_ARG, "layer %d out of range [0,%zu)", layer, g.layers.size());
     if (!g.layers[layer].ready) return fail(GLM_CUDA_ERR_STATE, "layer %d has no weights", layer);
@@ -402,7 +414,8 @@ int glm_cuda_upload_moe_layer(int layer, const float* ffn_norm, const float* gat
     if (routed && (!gate_s || !up_q || !up_s || !down_q || !down_s))
         return fail(GLM_CUDA_ERR_ARG, "layer %d: routed block is incomplete", layer);
     const auto& d = g.dims;
-    const size_t D = d.D, F = d.F, E = d.E, gD = D / d.gs, gF = F / d.gs;
+    const size_t D = d.D, F = d.F, gD = D / d.gs, gF = F / d.gs;
+    const size_t E = d.E, Er = d.E / g.ep_shards;  // router: all experts; routed block: this shard's
     LayerSlot& L = g.layers[layer];
     release_layer(L);
     auto& w = L.w;
@@ -416,9 +429,9 @@ int glm_cuda_upload_moe_layer(int layer, const float* ffn_norm, const float* gat
         return rc;
     }
     if (routed) {
-        if ((rc = upload(L, gate_q, E * F * D, &w.gate_q)) || (rc = upload(L, gate_s, E * F * gD, &w.gate_s)) ||
-            (rc = upload(L, up_q, E * F * D, &w.up_q)) || (rc = upload(L, up_s, E * F * gD, &w.up_s)) ||
-            (rc = upload(L, down_q, E * D * F, &w.down_q)) || (rc = upload(L, down_s, E * D * gF, &w.down_s))) {
+        if ((rc = upload(L, gate_q, Er * F * D, &w.gate_q)) || (rc = upload(L, gate_s, Er * F * gD, &w.gate_s)) ||
+            (rc = upload(L, up_q, Er * F * D, &w.up_q)) || (rc = upload(L, up_s, Er * F * gD, &w.up_s)) ||
+            (rc = upload(L, down_q, Er * D * F, &w.down_q)) || (rc = upload(L, down_s, Er * D * gF, &w.down_s))) {
             release_layer(L);
             return rc;
         }
@@ -529,6 +542,98 @@ int glm_cuda_set_prefill_tokens(int min_tokens) {
     const int old = g.prefill_ok ? g.prefill_min_tokens : 0;
     g.prefill_min_tokens = min_tokens;
     return old;
+}
+
+int glm_cuda_ep_setup(int n_shards, int shard, int max_tokens) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_init has not been called");
+    for (const auto& L : g.layers)
+        if (L.ready) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_ep_setup must come before any layer is uploaded");
+    if (glmq::ep_check(g.dims, n_shards) != cudaSuccess)
+        return fail(GLM_CUDA_ERR_ARG, "n_shards %d must divide n_routed_experts %d (at most 8 shards) with the "
+                    "prefill kernels' sizes", n_shards, g.dims.E);
+    if (shard < 0 || shard >= n_shards || max_tokens < 1)
+        return fail(GLM_CUDA_ERR_ARG, "shard %d of %d, max_tokens %d", shard, n_shards, max_tokens);
+    glmq::EpShape e{};
+    e.D = g.dims.D;
+    e.F = g.dims.F;
+    e.K = g.dims.K;
+    e.n_shards = n_shards;
+    e.e_local = g.dims.E / n_shards;
+    e.T_max = max_tokens;
+    e.n_recv_cap = n_shards * max_tokens * (g.dims.K < e.e_local ? g.dims.K : e.e_local);
+    if (g.ep_ws) cudaFree(g.ep_ws);
+    g.ep_ws = nullptr;
+    if (int rc = dev_alloc(&g.ep_ws, glmq::ep_workspace_bytes(e))) return rc;
+    g.ep = e;
+    g.ep_shards = n_shards;
+    g.ep_shard = shard;
+    g.ep_layer = -1;
+    return 0;
+}
+
+int glm_cuda_ep_dispatch(int layer, const float* x_dev, int n_tokens, float* send_rows_dev,
+                         int32_t* send_expert_dev, int32_t* send_counts_dev, void* stream) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (int rc = check_layer(layer, true)) return rc;
+    if (!g.ep_ws) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_ep_setup has not been called");
+    if (!x_dev || !send_rows_dev || !send_expert_dev || !send_counts_dev || n_tokens < 1 || n_tokens > g.ep.T_max)
+        return fail(GLM_CUDA_ERR_ARG, "ep_dispatch: buffers must be non-NULL and 1 <= n_tokens <= %d", g.ep.T_max);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : g.stream;
+    cudaError_t e = glmq::launch_ep_dispatch(g.layers[layer].w, g.dims, g.ep, g.ep_ws, x_dev, n_tokens, send_rows_dev,
+                                             send_expert_dev, send_counts_dev, routed_disabled_by_env() ? 0 : 1,
+                                             g.num_sms, g.scratch.stats, st);
+    g.launches += 3;
+    if (e != cudaSuccess) return fail(GLM_CUDA_ERR_CUDA, "ep dispatch launch: %s", cudaGetErrorString(e));
+    g.ep_layer = layer;
+    g.ep_T = n_tokens;
+    g.ep_nrecv = -1;
+    return 0;
+}
+
+int glm_cuda_ep_experts(int layer, const float* recv_rows_dev, const int32_t* recv_expert_dev, int n_recv,
+                        float* out_rows_dev, void* stream) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (int rc = check_layer(layer, true)) return rc;
+    if (g.ep_layer != layer) return fail(GLM_CUDA_ERR_STATE, "ep_experts: layer %d was not dispatched last", layer);
+    if (n_recv < 0 || n_recv > g.ep.n_recv_cap || (n_recv > 0 && (!recv_rows_dev || !recv_expert_dev || !out_rows_dev)))
+        return fail(GLM_CUDA_ERR_ARG, "ep_experts: n_recv %d (cap %d) or NULL buffers", n_recv, g.ep.n_recv_cap);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : g.stream;
+    glmq::MoeDims dl = g.dims;
+    dl.E = g.ep.e_local;
+    cudaError_t e = glmq::launch_ep_experts(g.layers[layer].w, dl, g.ep, g.ep_ws, g.ep_T, recv_rows_dev,
+                                            recv_expert_dev, n_recv, out_rows_dev,
+                                            routed_disabled_by_env() ? 0 : 1, g.num_sms, g.scratch.status, st);
+    g.launches += n_recv > 0 ? 5 : 4;
+    if (e != cudaSuccess) return fail(GLM_CUDA_ERR_CUDA, "ep experts launch: %s", cudaGetErrorString(e));
+    g.ep_nrecv = n_recv;
+    return 0;
+}
+
+int glm_cuda_ep_combine(int layer, float* x_dev, const float* back_rows_dev, int32_t* topk_idx_dev,
+                        float* topk_w_dev, void* stream) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (int rc = check_layer(layer, true)) return rc;
+    if (g.ep_layer != layer || g.ep_nrecv < 0)
+        return fail(GLM_CUDA_ERR_STATE, "ep_combine: layer %d has not been through ep_dispatch and ep_experts", layer);
+    if (!x_dev) return fail(GLM_CUDA_ERR_ARG, "ep_combine: x_dev must be non-NULL");
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : g.stream;
+    cudaError_t e = glmq::launch_ep_combine(g.dims, g.ep, g.ep_ws, x_dev, g.ep_T, g.ep_nrecv, back_rows_dev,
+                                            g.num_sms, st);
+    if (e == cudaSuccess) e = glmq::ep_copy_routing(g.ep, g.ep_ws, g.ep_T, topk_idx_dev, topk_w_dev, st);
+    g.launches += 1;
+    if (e != cudaSuccess) return fail(GLM_CUDA_ERR_CUDA, "ep combine launch: %s", cudaGetErrorString(e));
+    g.ep_layer = -1;
+    return 0;
+}
+
+int glm_cuda_ep_status(void) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_init has not been called");
+    CUDA_TRY(cudaMemcpyAsync(g.status_host, g.scratch.status, sizeof(unsigned int), cudaMemcpyDeviceToHost,
+                             g.stream));
+    CUDA_TRY(cudaStreamSynchronize(g.stream));
+    return take_device_status();
 }
 
 int glm_cuda_decode_path(void) {

@@ -147,6 +147,37 @@ size_t prefill_workspace_bytes(const MoeDims& d, int T);
 // T tokens (x [T][D] on the device, updated in place) through one MoE layer.
 // ws: prefill_workspace_bytes() of device scratch. topk_idx / topk_w
 // (optional, [T][K]) receive the routing.
+// ---- expert parallelism (moe_prefill.cu): experts sharded over n_shards ranks
+
+struct EpShape {
+    int D, F, K;        // model dims (K = experts per token)
+    int n_shards;       // ranks the routed experts are split over
+    int e_local;        // routed experts held by this rank (E / n_shards)
+    int T_max;          // most tokens this rank routes per call
+    int n_recv_cap;     // most (token, slot) rows this rank can receive per call
+};
+
+cudaError_t ep_check(const MoeDims& d, int n_shards);
+size_t ep_workspace_bytes(const EpShape& s);
+// Route T own tokens (global expert ids) and lay out the send buffer:
+// send_rows [rows][D] (xn of each (token, slot) pair, grouped by destination
+// rank), send_expert [rows] (expert id local to the destination),
+// send_counts [n_shards]. Keeps xn, ids, weights and the send positions in ws.
+cudaError_t launch_ep_dispatch(const MoeLayerDev& w, const MoeDims& d, const EpShape& s, unsigned char* ws,
+                               const float* x, int T, float* send_rows, int32_t* send_expert, int32_t* send_counts,
+                               int routed, int num_sms, unsigned long long* stats, cudaStream_t st);
+// This rank's experts (w: routed arrays hold its e_local experts; dl.E =
+// e_local) on n_recv received rows, plus the shared expert on its own T
+// tokens of the last dispatch. out_rows [n_recv][D] in the received order.
+cudaError_t launch_ep_experts(const MoeLayerDev& w, const MoeDims& dl, const EpShape& s, unsigned char* ws, int T,
+                              const float* recv_rows, const int32_t* recv_expert, int n_recv, float* out_rows,
+                              int routed, int num_sms, unsigned* status, cudaStream_t st);
+// x[t] += shared + sum_k 1.8 w_k y_k with y_k = back_rows[send position].
+cudaError_t launch_ep_combine(const MoeDims& d, const EpShape& s, unsigned char* ws, float* x, int T, int n_recv,
+                              const float* back_rows, int num_sms, cudaStream_t st);
+cudaError_t ep_copy_routing(const EpShape& s, unsigned char* ws, int T, int32_t* topk_idx, float* topk_w,
+                            cudaStream_t st);
+
 cudaError_t launch_moe_prefill(const MoeLayerDev& w, const MoeDims& d, unsigned char* ws, float* x, int T,
                                int32_t* topk_idx, float* topk_w, int routed, int num_sms, unsigned* status,
                                unsigned long long* stats, cudaStream_t st);

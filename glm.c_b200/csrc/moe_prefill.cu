@@ -819,6 +819,226 @@ __global__ void prefill_combine_kernel(float* x, const float* __restrict__ Y, co
     }
 }
 
+// ------------------------------------------------------- expert parallelism
+//
+// Experts are sharded over n_shards ranks, e_local consecutive experts each;
+// every rank routes its own tokens, sends each (token, slot) pair's xn row
+// to the rank that holds its expert, runs its experts on what it received
+// (plus the replicated shared expert on its own tokens), and gets the expert
+// outputs back in the order it sent them.
+
+constexpr int kMaxShards = 8;
+
+// Send layout: pairs (t, k) in (token, slot) order within each destination,
+// destinations in rank order. One CTA; thread i owns a contiguous chunk of
+// the T*K pairs. send_pos[t*K + k] = row in the send buffer (-1: not sent).
+__global__ void __launch_bounds__(1024) ep_pack_kernel(const int32_t* __restrict__ ids, int T, int K, int e_local,
+                                                     int n_shards, int routed, int* send_pos, int* send_counts,
+                                                     int32_t* send_expert) {
+    __shared__ int pre[kMaxShards][1024];
+    __shared__ int base[kMaxShards + 1];
+    const int n = T * K, tid = threadIdx.x, nt = blockDim.x;
+    const int chunk = (n + nt - 1) / nt, lo = min(n, tid * chunk), hi = min(n, lo + chunk);
+    int c[kMaxShards];
+#pragma unroll
+    for (int d = 0; d < kMaxShards; ++d) c[d] = 0;
+    for (int i = lo; i < hi; ++i) {
+        const int e = ids[i];
+        if (!routed || e < 0) continue;
+        const int d = e / e_local;
+#pragma unroll
+        for (int q = 0; q < kMaxShards; ++q) c[q] += q == d;
+    }
+#pragma unroll
+    for (int d = 0; d < kMaxShards; ++d) pre[d][tid] = c[d];
+    __syncthreads();
+    // inclusive scans over threads, one destination per pass (Hillis-Steele)
+    for (int off = 1; off < nt; off <<= 1) {
+        int v[kMaxShards];
+#pragma unroll
+        for (int d = 0; d < kMaxShards; ++d) v[d] = tid >= off ? pre[d][tid - off] : 0;
+        __syncthreads();
+#pragma unroll
+        for (int d = 0; d < kMaxShards; ++d) pre[d][tid] += v[d];
+        __syncthreads();
+    }
+    if (tid == 0) {
+        int o = 0;
+        for (int d = 0; d < n_shards; ++d) {
+            base[d] = o;
+            send_counts[d] = pre[d][nt - 1];
+            o += pre[d][nt - 1];
+        }
+        base[n_shards] = o;
+    }
+    __syncthreads();
+    int run[kMaxShards];
+#pragma unroll
+    for (int d = 0; d < kMaxShards; ++d) run[d] = 0;
+    for (int i = lo; i < hi; ++i) {
+        const int e = ids[i];
+        if (!routed || e < 0) {
+            send_pos[i] = -1;
+            continue;
+        }
+        const int d = e / e_local;
+        int r = 0;
+#pragma unroll
+        for (int q = 0; q < kMaxShards; ++q)
+            if (q == d) r = run[q]++;
+        const int pos = base[d] + pre[d][tid] - c[d] + r;
+        send_pos[i] = pos;
+        send_expert[pos] = e - d * e_local;
+    }
+}
+
+// send_rows[send_pos[t*K + k]] = xn[t] (one warp per pair).
+__global__ void ep_pack_rows_kernel(const float* __restrict__ xn, const int* __restrict__ send_pos, int T, int K, int D,
+                                    float* send_rows) {
+    const int warps = (gridDim.x * blockDim.x) >> 5, lane = threadIdx.x & 31;
+    for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < T * K; i += warps) {
+        const int pos = send_pos[i];
+        if (pos < 0) continue;
+        const float4* src = reinterpret_cast<const float4*>(xn + (size_t)(i / K) * D);
+        float4* dst = reinterpret_cast<float4*>(send_rows + (size_t)pos * D);
+        for (int c = lane; c < D / 4; c += 32) dst[c] = src[c];
+    }
+}
+
+// Rows of the local expert GEMMs: received rows grouped by local expert
+// (groups 0 .. e_local - 1), then this rank's own tokens for the shared
+// expert (group e_local). Sources: s < n_recv -> received row s, else own
+// token s - n_recv. row_src[row] = source; pos_of_src[source] = row.
+__global__ void __launch_bounds__(1024) ep_group_kernel(const int32_t* __restrict__ recv_expert, int n_recv, int T,
+                                                      int e_local, int routed, int mt1, int mt2, int* counts,
+                                                      int* row_src, int* pos_of_src, int4* items1, int4* items2) {
+    const int G = e_local + 1;
+    __shared__ int cnt[kMaxGroups], off[kMaxGroups + 1], cur[kMaxGroups], toff[kMaxGroups + 1];
+    for (int g = threadIdx.x; g < G; g += blockDim.x) {
+        cnt[g] = g == e_local ? T : 0;
+        cur[g] = 0;
+    }
+    __syncthreads();
+    if (routed)
+        for (int i = threadIdx.x; i < n_recv; i += blockDim.x) {
+            const int e = recv_expert[i];
+            if (e >= 0 && e < e_local) atomicAdd(&cnt[e], 1);
+        }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int o = 0, to = 0;
+        for (int g = 0; g < G; ++g) {
+            off[g] = o;
+            o += cnt[g];
+            toff[g] = to;
+            to += (cnt[g] + kTN - 1) / kTN;
+        }
+        off[G] = o;
+        toff[G] = to;
+        counts[0] = o;
+        counts[1] = to * mt1;
+        counts[2] = to * mt2;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < n_recv; i += blockDim.x) {
+        const int e = recv_expert[i];
+        if (!routed || e < 0 || e >= e_local) {
+            pos_of_src[i] = -1;
+            continue;
+        }
+        const int r = off[e] + atomicAdd(&cur[e], 1);
+        row_src[r] = i;
+        pos_of_src[i] = r;
+    }
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
+        const int r = off[e_local] + t;
+        row_src[r] = n_recv + t;
+        pos_of_src[n_recv + t] = r;
+    }
+    const int ntiles = toff[G];
+    for (int tile = threadIdx.x; tile < ntiles; tile += blockDim.x) {
+        int lo = 0, hi = G - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (toff[mid] <= tile) lo = mid;
+            else hi = mid - 1;
+        }
+        const int g = lo;
+        const int row0 = off[g] + (tile - toff[g]) * kTN;
+        const int nrows = min(kTN, off[g] + cnt[g] - row0);
+        for (int mt = 0; mt < mt1; ++mt) items1[tile * mt1 + mt] = make_int4(g, row0, nrows, mt);
+        for (int mt = 0; mt < mt2; ++mt) items2[tile * mt2 + mt] = make_int4(g, row0, nrows, mt);
+    }
+}
+
+// Activation rows of the local GEMMs as bf16 hi + lo, 8 elements per thread.
+__global__ void ep_gather_split_kernel(const float* __restrict__ recv_rows, const float* __restrict__ xn,
+                                       const int* __restrict__ row_src, const int* __restrict__ counts, int n_recv,
+                                       int D, __nv_bfloat16* hi, __nv_bfloat16* lo) {
+    const int per_row = D / 8;
+    const size_t n = (size_t)counts[0] * per_row;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int r = (int)(i / per_row), c = (int)(i - (size_t)r * per_row) * 8;
+        const int sidx = row_src[r];
+        const float* src = (sidx < n_recv ? recv_rows + (size_t)sidx * D : xn + (size_t)(sidx - n_recv) * D) + c;
+        const float4 v0 = *reinterpret_cast<const float4*>(src), v1 = *reinterpret_cast<const float4*>(src + 4);
+        const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        __align__(16) __nv_bfloat16 h[8], l[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) split_bf16(v[j], h[j], l[j]);
+        *reinterpret_cast<int4*>(hi + (size_t)r * D + c) = *reinterpret_cast<const int4*>(h);
+        *reinterpret_cast<int4*>(lo + (size_t)r * D + c) = *reinterpret_cast<const int4*>(l);
+    }
+}
+
+// out_rows[i] = Y[pos_of_src[i]] for the received rows (one warp per row).
+__global__ void ep_scatter_kernel(const float* __restrict__ Y, const int* __restrict__ pos_of_src, int n_recv, int D,
+                                  float* out_rows) {
+    const int warps = (gridDim.x * blockDim.x) >> 5, lane = threadIdx.x & 31;
+    for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < n_recv; i += warps) {
+        const int r = pos_of_src[i];
+        float4* dst = reinterpret_cast<float4*>(out_rows + (size_t)i * D);
+        if (r < 0) {
+            for (int c = lane; c < D / 4; c += 32) dst[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+            continue;
+        }
+        const float4* src = reinterpret_cast<const float4*>(Y + (size_t)r * D);
+        for (int c = lane; c < D / 4; c += 32) dst[c] = src[c];
+    }
+}
+
+// x[t] += y_shared[t] + sum_k (1.8 w_k) y_k in rank order (infer.c:1175,1192,
+// 1212-1214); y_k = back_rows[send_pos[t*K + k]] came back from the expert's
+// rank, y_shared = Y[pos_of_src[n_recv + t]].
+__global__ void ep_combine_kernel(float* x, const float* __restrict__ Y, const int* __restrict__ pos_of_src,
+                                  const float* __restrict__ back_rows, const int* __restrict__ send_pos,
+                                  const float* __restrict__ topk_w, int T, int D, int K, int n_recv) {
+    const int per_tok = D / 4;
+    const size_t n = (size_t)T * per_tok;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i / per_tok), c = (int)(i - (size_t)t * per_tok) * 4;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int k = 0; k < K; ++k) {
+            const int pos = send_pos[t * K + k];
+            if (pos < 0) continue;
+            const float wk = __fmul_rn(topk_w[(size_t)t * K + k], 1.8f);
+            const float4 y = *reinterpret_cast<const float4*>(back_rows + (size_t)pos * D + c);
+            acc.x = __fadd_rn(acc.x, __fmul_rn(wk, y.x));
+            acc.y = __fadd_rn(acc.y, __fmul_rn(wk, y.y));
+            acc.z = __fadd_rn(acc.z, __fmul_rn(wk, y.z));
+            acc.w = __fadd_rn(acc.w, __fmul_rn(wk, y.w));
+        }
+        const float4 ys = *reinterpret_cast<const float4*>(Y + (size_t)pos_of_src[n_recv + t] * D + c);
+        float4* xp = reinterpret_cast<float4*>(x + (size_t)t * D + c);
+        float4 xv = *xp;
+        xv.x = __fadd_rn(xv.x, __fadd_rn(ys.x, acc.x));
+        xv.y = __fadd_rn(xv.y, __fadd_rn(ys.y, acc.y));
+        xv.z = __fadd_rn(xv.z, __fadd_rn(ys.z, acc.z));
+        xv.w = __fadd_rn(xv.w, __fadd_rn(ys.w, acc.w));
+        *xp = xv;
+    }
+}
+
 // ------------------------------------------------------------ tensor maps
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -901,22 +1121,38 @@ PrefillWs carve(unsigned char* base, const MoeDims& d, int T) {
 
 size_t prefill_workspace_bytes(const MoeDims& d, int T) { return carve(nullptr, d, T).bytes; }
 
-cudaError_t launch_moe_prefill(const MoeLayerDev& w, const MoeDims& d, unsigned char* ws, float* x, int T,
-                               int32_t* topk_idx, float* topk_w, int routed, int num_sms, unsigned* status,
-                               unsigned long long* stats, cudaStream_t st) {
-    cudaError_t err = prefill_check(d);
-    if (err != cudaSuccess) return err;
-    if (T <= 0) return cudaErrorInvalidValue;
-    const bool use_routed = routed && w.gate_q && w.up_q && w.down_q;
-    const size_t R = (size_t)T * (d.K + 1);
-    const int mt1 = d.F / (kTM / 2), mt2 = d.D / kTM;  // gate/up tiles: 64 features
-    const PrefillWs p = carve(ws, d, T);
+namespace {
 
-    // tensor maps: weights (box 128 rows x 64 bytes) and activations (box 32 rows x 64 bf16, 128-byte swizzle)
+cudaError_t launch_route(const PrefillRouteArgs& ra, cudaStream_t st) {
+    switch (ra.D / 32) {
+        case 16: return launch_route_batched<16>(ra, st);
+        case 32: return launch_route_batched<32>(ra, st);
+        case 48: return launch_route_batched<48>(ra, st);
+        case 64: return launch_route_batched<64>(ra, st);
+        default: break;
+    }
+    const size_t rsmem = sizeof(float) * ((pad64(ra.D) + 3) & ~3) + sizeof(float) * ra.D + 16 * (size_t)ra.E +
+                         20 * (size_t)ra.E + 256;
+    cudaError_t err =
+        cudaFuncSetAttribute(prefill_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsmem);
+    if (err) return err;
+    prefill_route_kernel<<<ra.T, 512, rsmem, st>>>(ra);
+    return cudaGetLastError();
+}
+
+// Gate/up + SwiGLU and down for grouped rows already split into xhi / xlo
+// ([rows][D], rows <= R_cap): groups 0 .. d.E - 1 use the routed weights of
+// `w` (d.E experts), group d.E the shared expert. Y = [rows][D].
+cudaError_t launch_grouped_ffn(const MoeLayerDev& w, const MoeDims& d, bool use_routed, size_t R_cap,
+                               const __nv_bfloat16* xhi, const __nv_bfloat16* xlo, __nv_bfloat16* hhi,
+                               __nv_bfloat16* hlo, float* y, const int* counts, const int4* items1,
+                               const int4* items2, int num_sms, unsigned* status, cudaStream_t st) {
+    // tensor maps: weights (box rows x 64 bytes, 64-byte swizzle), their scales (box rows x 4 groups) and
+    // activations (box 32 rows x 64 bf16, 128-byte swizzle)
     GemmMaps m1{}, m2{};
     const uint64_t er = (uint64_t)d.E;
     bool ok = true;
-    // weights: box [rows][64 bytes]; gate/up tiles stack 64 + 64 rows, down tiles 128 rows
+    // gate/up tiles stack 64 + 64 rows, down tiles 128 rows
     auto wmap = [&](CUtensorMap* mp, const int8_t* q, uint64_t rows, int cols, uint32_t box_rows,
                     const CUtensorMap* alt) {
         if (q) ok = ok && make_map(mp, q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rows, cols, box_rows, kTK,
@@ -946,29 +1182,36 @@ cudaError_t launch_moe_prefill(const MoeLayerDev& w, const MoeDims& d, unsigned 
     m2.w[1] = m2.w[0];
     m2.s_sh[1] = m2.s_sh[0];
     m2.s[1] = m2.s[0];
-    ok = ok && make_map(&m1.bhi, p.xhi, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, R, d.D, 32, kTK, CU_TENSOR_MAP_SWIZZLE_128B);
-    ok = ok && make_map(&m1.blo, p.xlo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, R, d.D, 32, kTK, CU_TENSOR_MAP_SWIZZLE_128B);
-    ok = ok && make_map(&m2.bhi, p.hhi, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, R, d.F, 32, kTK, CU_TENSOR_MAP_SWIZZLE_128B);
-    ok = ok && make_map(&m2.blo, p.hlo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, R, d.F, 32, kTK, CU_TENSOR_MAP_SWIZZLE_128B);
+    const auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const auto sw = CU_TENSOR_MAP_SWIZZLE_128B;
+    ok = ok && make_map(&m1.bhi, xhi, bf, 2, R_cap, d.D, 32, kTK, sw) && make_map(&m1.blo, xlo, bf, 2, R_cap, d.D, 32, kTK, sw);
+    ok = ok && make_map(&m2.bhi, hhi, bf, 2, R_cap, d.F, 32, kTK, sw) && make_map(&m2.blo, hlo, bf, 2, R_cap, d.F, 32, kTK, sw);
     if (!ok) return cudaErrorInvalidValue;
+    const int gsmem = (int)GemmLayout::total + 1024;
+    cudaError_t err = cudaFuncSetAttribute(q8_group_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gsmem);
+    if (err) return err;
+    GroupGemmArgs g1{items1, items2, counts, hhi, hlo, nullptr, status, d.D, d.F, d.E, 0};
+    q8_group_gemm_kernel<<<num_sms, kGemmThreads, gsmem, st>>>(m1, g1);
+    GroupGemmArgs g2{items1, items2, counts, nullptr, nullptr, y, status, d.F, d.D, d.E, 1};
+    q8_group_gemm_kernel<<<num_sms, kGemmThreads, gsmem, st>>>(m2, g2);
+    return cudaGetLastError();
+}
 
+}  // namespace
+
+cudaError_t launch_moe_prefill(const MoeLayerDev& w, const MoeDims& d, unsigned char* ws, float* x, int T,
+                               int32_t* topk_idx, float* topk_w, int routed, int num_sms, unsigned* status,
+                               unsigned long long* stats, cudaStream_t st) {
+    cudaError_t err = prefill_check(d);
+    if (err != cudaSuccess) return err;
+    if (T <= 0) return cudaErrorInvalidValue;
+    const bool use_routed = routed && w.gate_q && w.up_q && w.down_q;
+    const size_t R = (size_t)T * (d.K + 1);
+    const int mt1 = d.F / (kTM / 2), mt2 = d.D / kTM;  // gate/up tiles: 64 features
+    const PrefillWs p = carve(ws, d, T);
     // 1 routing
     PrefillRouteArgs ra{x, w.ffn_norm, w.router, w.router_bias, p.xn, p.ids, p.wts, stats, T, d.D, d.E, d.K};
-    switch (d.D / 32) {
-        case 16: err = launch_route_batched<16>(ra, st); break;
-        case 32: err = launch_route_batched<32>(ra, st); break;
-        case 48: err = launch_route_batched<48>(ra, st); break;
-        case 64: err = launch_route_batched<64>(ra, st); break;
-        default: {
-            const size_t rsmem = sizeof(float) * ((pad64(d.D) + 3) & ~3) + sizeof(float) * d.D +
-                                 16 * (size_t)d.E + 20 * (size_t)d.E + 256;
-            if ((err = cudaFuncSetAttribute(prefill_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            (int)rsmem)))
-                return err;
-            prefill_route_kernel<<<T, 512, rsmem, st>>>(ra);
-        }
-    }
-    if (err) return err;
+    if ((err = launch_route(ra, st))) return err;
     // 2 dispatch
     PrefillDispatchArgs da{p.ids, T, d.K, d.E, use_routed ? 1 : 0, mt1, mt2, p.counts, p.row_tok, p.tok_row,
                            p.items1, p.items2};
@@ -976,18 +1219,123 @@ cudaError_t launch_moe_prefill(const MoeLayerDev& w, const MoeDims& d, unsigned 
     // 3 activations
     gather_split_kernel<<<num_sms * 4, 256, 0, st>>>(p.xn, p.row_tok, p.counts, d.D, p.xhi, p.xlo);
     // 4 gate/up + SwiGLU, 5 down
-    const int gsmem = (int)GemmLayout::total + 1024;
-    if ((err = cudaFuncSetAttribute(q8_group_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gsmem)))
+    if ((err = launch_grouped_ffn(w, d, use_routed, R, p.xhi, p.xlo, p.hhi, p.hlo, p.y, p.counts, p.items1, p.items2,
+                                  num_sms, status, st)))
         return err;
-    GroupGemmArgs g1{p.items1, p.items2, p.counts, p.hhi, p.hlo, nullptr, status, d.D, d.F, d.E, 0};
-    q8_group_gemm_kernel<<<num_sms, kGemmThreads, gsmem, st>>>(m1, g1);
-    GroupGemmArgs g2{p.items1, p.items2, p.counts, nullptr, nullptr, p.y, status, d.F, d.D, d.E, 1};
-    q8_group_gemm_kernel<<<num_sms, kGemmThreads, gsmem, st>>>(m2, g2);
     // 6 combine
     prefill_combine_kernel<<<num_sms * 4, 256, 0, st>>>(x, p.y, p.tok_row, p.wts, T, d.D, d.K, use_routed ? 1 : 0);
     if (topk_idx) cudaMemcpyAsync(topk_idx, p.ids, sizeof(int32_t) * T * d.K, cudaMemcpyDeviceToDevice, st);
     if (topk_w) cudaMemcpyAsync(topk_w, p.wts, sizeof(float) * T * d.K, cudaMemcpyDeviceToDevice, st);
     return cudaGetLastError();
+}
+
+// ------------------------------------------------------- expert parallelism
+
+namespace {
+
+struct EpWs {
+    float* xn;          // [T_max][D]
+    int32_t* ids;       // [T_max][K]
+    float* wts;         // [T_max][K]
+    int* send_pos;      // [T_max][K]
+    int* row_src;       // [R_cap]
+    int* pos_of_src;    // [R_cap]
+    int* counts;        // [4]
+    int4* items1;
+    int4* items2;
+    __nv_bfloat16 *xhi, *xlo, *hhi, *hlo;
+    float* y;           // [R_cap][D]
+    size_t R_cap, bytes;
+};
+
+EpWs ep_carve(unsigned char* base, const EpShape& s) {
+    const size_t R = (size_t)s.n_recv_cap + s.T_max, tiles = R / kTN + s.e_local + 1;
+    EpWs w{};
+    size_t b = 0;
+    auto take = [&](size_t n) {
+        unsigned char* r = base ? base + b : nullptr;
+        b += (n + 255) & ~(size_t)255;
+        return r;
+    };
+    w.xn = reinterpret_cast<float*>(take((size_t)s.T_max * s.D * 4));
+    w.ids = reinterpret_cast<int32_t*>(take((size_t)s.T_max * s.K * 4));
+    w.wts = reinterpret_cast<float*>(take((size_t)s.T_max * s.K * 4));
+    w.send_pos = reinterpret_cast<int*>(take((size_t)s.T_max * s.K * 4));
+    w.row_src = reinterpret_cast<int*>(take(R * 4));
+    w.pos_of_src = reinterpret_cast<int*>(take(R * 4));
+    w.counts = reinterpret_cast<int*>(take(16));
+    w.items1 = reinterpret_cast<int4*>(take(tiles * (s.F / (kTM / 2)) * 16));
+    w.items2 = reinterpret_cast<int4*>(take(tiles * (s.D / kTM) * 16));
+    w.xhi = reinterpret_cast<__nv_bfloat16*>(take(R * s.D * 2));
+    w.xlo = reinterpret_cast<__nv_bfloat16*>(take(R * s.D * 2));
+    w.hhi = reinterpret_cast<__nv_bfloat16*>(take(R * s.F * 2));
+    w.hlo = reinterpret_cast<__nv_bfloat16*>(take(R * s.F * 2));
+    w.y = reinterpret_cast<float*>(take(R * s.D * 4));
+    w.R_cap = R;
+    w.bytes = b;
+    return w;
+}
+
+}  // namespace
+
+cudaError_t ep_check(const MoeDims& d, int n_shards) {
+    if (n_shards < 1 || n_shards > kMaxShards || d.E % n_shards) return cudaErrorInvalidValue;
+    MoeDims dl = d;
+    dl.E = d.E / n_shards;
+    dl.K = d.K < dl.E ? d.K : dl.E;
+    return prefill_check(dl) == cudaSuccess && prefill_check(d) == cudaSuccess ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+size_t ep_workspace_bytes(const EpShape& s) { return ep_carve(nullptr, s).bytes; }
+
+cudaError_t launch_ep_dispatch(const MoeLayerDev& w, const MoeDims& d, const EpShape& s, unsigned char* ws,
+                               const float* x, int T, float* send_rows, int32_t* send_expert, int32_t* send_counts,
+                               int routed, int num_sms, unsigned long long* stats, cudaStream_t st) {
+    if (T <= 0 || T > s.T_max) return cudaErrorInvalidValue;
+    const EpWs p = ep_carve(ws, s);
+    PrefillRouteArgs ra{x, w.ffn_norm, w.router, w.router_bias, p.xn, p.ids, p.wts, stats, T, d.D, d.E, d.K};
+    cudaError_t err = launch_route(ra, st);
+    if (err) return err;
+    ep_pack_kernel<<<1, 1024, 0, st>>>(p.ids, T, d.K, s.e_local, s.n_shards, routed && w.gate_q ? 1 : 0, p.send_pos,
+                                       send_counts, send_expert);
+    ep_pack_rows_kernel<<<num_sms * 4, 256, 0, st>>>(p.xn, p.send_pos, T, d.K, d.D, send_rows);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_experts(const MoeLayerDev& w, const MoeDims& dl, const EpShape& s, unsigned char* ws, int T,
+                              const float* recv_rows, const int32_t* recv_expert, int n_recv, float* out_rows,
+                              int routed, int num_sms, unsigned* status, cudaStream_t st) {
+    if (n_recv < 0 || n_recv > s.n_recv_cap || T <= 0 || T > s.T_max) return cudaErrorInvalidValue;
+    const EpWs p = ep_carve(ws, s);
+    const bool use_routed = routed && w.gate_q && w.up_q && w.down_q;
+    const int mt1 = dl.F / (kTM / 2), mt2 = dl.D / kTM;
+    ep_group_kernel<<<1, 1024, 0, st>>>(recv_expert, n_recv, T, dl.E, use_routed ? 1 : 0, mt1, mt2, p.counts,
+                                        p.row_src, p.pos_of_src, p.items1, p.items2);
+    ep_gather_split_kernel<<<num_sms * 4, 256, 0, st>>>(recv_rows, p.xn, p.row_src, p.counts, n_recv, dl.D, p.xhi,
+                                                        p.xlo);
+    cudaError_t err = launch_grouped_ffn(w, dl, use_routed, p.R_cap, p.xhi, p.xlo, p.hhi, p.hlo, p.y, p.counts,
+                                         p.items1, p.items2, num_sms, status, st);
+    if (err) return err;
+    if (n_recv > 0) ep_scatter_kernel<<<num_sms * 4, 256, 0, st>>>(p.y, p.pos_of_src, n_recv, dl.D, out_rows);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_combine(const MoeDims& d, const EpShape& s, unsigned char* ws, float* x, int T, int n_recv,
+                              const float* back_rows, int num_sms, cudaStream_t st) {
+    if (T <= 0 || T > s.T_max) return cudaErrorInvalidValue;
+    const EpWs p = ep_carve(ws, s);
+    ep_combine_kernel<<<num_sms * 4, 256, 0, st>>>(x, p.y, p.pos_of_src, back_rows, p.send_pos, p.wts, T, d.D, d.K,
+                                                   n_recv);
+    return cudaGetLastError();
+}
+
+cudaError_t ep_copy_routing(const EpShape& s, unsigned char* ws, int T, int32_t* topk_idx, float* topk_w,
+                            cudaStream_t st) {
+    const EpWs p = ep_carve(ws, s);
+    cudaError_t err = cudaSuccess;
+    if (topk_idx) err = cudaMemcpyAsync(topk_idx, p.ids, sizeof(int32_t) * T * s.K, cudaMemcpyDeviceToDevice, st);
+    if (!err && topk_w) err = cudaMemcpyAsync(topk_w, p.wts, sizeof(float) * T * s.K, cudaMemcpyDeviceToDevice, st);
+    return err;
 }
 
 }  // namespace glmq

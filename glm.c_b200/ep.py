@@ -1,0 +1,125 @@
+"""Expert-parallel MoE prefill over ranks (one process per GPU).
+
+The routed experts of every layer are split over the ranks of a process
+group (n_routed_experts / world consecutive experts per rank); the router and
+the shared expert are replicated. Per layer each rank
+
+  1 routes its own tokens and packs one row per (token, slot) pair, grouped
+    by the rank holding the pair's expert       (glm_cuda_ep_dispatch)
+  2 exchanges the row counts, then the rows and their local expert ids
+    (all-to-all)
+  3 runs its experts on the rows it received, and the shared expert on its
+    own tokens                                  (glm_cuda_ep_experts)
+  4 sends every expert output back to the rank its row came from
+    (all-to-all with the splits reversed)
+  5 adds the shared output and the 1.8 w_k-weighted expert outputs in rank
+    order                                       (glm_cuda_ep_combine)
+
+which is apply_moe_shared_ffn_layer (infer.c:1087-1216) applied to every
+token, with the expert products on the ranks that hold the experts. The
+kernels are the library's (`kernels` is a GlmCuda); the exchange is
+torch.distributed's all_to_all_single on the same stream (NCCL on GPUs).
+"""
+from __future__ import annotations
+
+import time
+
+
+class ExpertParallelMoE:
+    """One rank's side of the expert-parallel MoE layers.
+
+    kernels: a GlmCuda on which ep_setup(world, rank, max_tokens) was called
+    and whose layers hold this rank's experts. dim / k_used: model sizes.
+    """
+
+    def __init__(self, kernels, dim: int, k_used: int, max_tokens: int, group=None, device=None):
+        import torch
+        import torch.distributed as dist
+
+        self.torch = torch
+        self.dist = dist
+        self.k = kernels
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.dim = dim
+        self.k_used = k_used
+        self.device = device if device is not None else torch.device("cpu")
+        rows = max_tokens * k_used
+        f32, i32 = torch.float32, torch.int32
+        self.send_rows = torch.empty(rows, dim, dtype=f32, device=self.device)
+        self.send_expert = torch.empty(rows, dtype=i32, device=self.device)
+        self.send_counts = torch.zeros(self.world, dtype=i32, device=self.device)
+        self.recv_counts = torch.zeros(self.world, dtype=i32, device=self.device)
+        cap = self.world * rows
+        self.recv_rows = torch.empty(cap, dim, dtype=f32, device=self.device)
+        self.recv_expert = torch.empty(cap, dtype=i32, device=self.device)
+        self.out_rows = torch.empty(cap, dim, dtype=f32, device=self.device)
+        self.back_rows = torch.empty(rows, dim, dtype=f32, device=self.device)
+        self.last = {}
+
+    def _stream(self):
+        """The handle of torch's current stream, so that the library's kernels
+        and torch's copies and collectives stay in one stream order. torch's
+        default stream has handle 0, which the library would read as its own
+        stream: pass cudaStreamLegacy (handle 1) for it instead."""
+        if self.device.type != "cuda":
+            return None
+        handle = self.torch.cuda.current_stream(self.device).cuda_stream
+        return handle if handle else 1
+
+    def _a2a(self, out, inp, out_splits, in_splits):
+        if self.world == 1:
+            out[: inp.shape[0]].copy_(inp)
+        else:
+            self.dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+
+    def layer(self, layer: int, x, idx=None, w=None) -> None:
+        """x [T][dim] (this rank's tokens, in place) through MoE layer `layer`."""
+        T = x.shape[0]
+        st = self._stream()
+        self.k.ep_dispatch(layer, x, T, self.send_rows, self.send_expert, self.send_counts, stream=st)
+        self._a2a(self.recv_counts, self.send_counts, None, None)
+        sc = self.send_counts.tolist()   # host copy of the splits (synchronises the stream)
+        rc = self.recv_counts.tolist()
+        n_send, n_recv = sum(sc), sum(rc)
+        self._a2a(self.recv_rows[:n_recv], self.send_rows[:n_send], rc, sc)
+        self._a2a(self.recv_expert[:n_recv], self.send_expert[:n_send], rc, sc)
+        self.k.ep_experts(layer, self.recv_rows, self.recv_expert, n_recv, self.out_rows, stream=st)
+        self._a2a(self.back_rows[:n_send], self.out_rows[:n_recv], sc, rc)
+        self.k.ep_combine(layer, x, self.back_rows, idx, w, stream=st)
+        self.last = {"n_send": n_send, "n_recv": n_recv, "send_counts": sc, "recv_counts": rc}
+
+    def layer_timed(self, layer: int, x, events: list) -> None:
+        """layer() with CUDA events recorded between its phases: events[0..5]
+        = before dispatch, after dispatch, after the row exchange, after the
+        experts, after the exchange back, after combine."""
+        T = x.shape[0]
+        st = self._stream()
+        events[0].record()
+        self.k.ep_dispatch(layer, x, T, self.send_rows, self.send_expert, self.send_counts, stream=st)
+        events[1].record()
+        self._a2a(self.recv_counts, self.send_counts, None, None)
+        sc = self.send_counts.tolist()
+        rc = self.recv_counts.tolist()
+        n_send, n_recv = sum(sc), sum(rc)
+        self._a2a(self.recv_rows[:n_recv], self.send_rows[:n_send], rc, sc)
+        self._a2a(self.recv_expert[:n_recv], self.send_expert[:n_send], rc, sc)
+        events[2].record()
+        self.k.ep_experts(layer, self.recv_rows, self.recv_expert, n_recv, self.out_rows, stream=st)
+        events[3].record()
+        self._a2a(self.back_rows[:n_send], self.out_rows[:n_recv], sc, rc)
+        events[4].record()
+        self.k.ep_combine(layer, x, self.back_rows, None, None, stream=st)
+        events[5].record()
+        self.last = {"n_send": n_send, "n_recv": n_recv, "send_counts": sc, "recv_counts": rc}
+
+
+def shard_layer(layer: dict, n_shards: int, shard: int) -> dict:
+    """The arrays rank `shard` holds: router and shared expert whole, the
+    routed blocks cut to experts [shard * E/n, (shard + 1) * E/n)."""
+    e = layer["n_experts"] // n_shards
+    out = dict(layer)
+    for name in ("gate_q", "gate_s", "up_q", "up_s", "down_q", "down_s"):
+        a = layer.get(name)
+        out[name] = None if a is None else a[shard * e:(shard + 1) * e]
+    return out

@@ -60,6 +60,11 @@ def _signatures(L: ctypes.CDLL) -> None:
     L.glm_cuda_set_decode_path.argtypes = [_I]
     L.glm_cuda_decode_path.argtypes = []
     L.glm_cuda_set_prefill_tokens.argtypes = [_I]
+    L.glm_cuda_ep_setup.argtypes = [_I, _I, _I]
+    L.glm_cuda_ep_dispatch.argtypes = [_I, _P, _I, _P, _P, _P, _P]
+    L.glm_cuda_ep_experts.argtypes = [_I, _P, _P, _I, _P, _P]
+    L.glm_cuda_ep_combine.argtypes = [_I, _P, _P, _P, _P, _P]
+    L.glm_cuda_ep_status.argtypes = []
     L.glm_cuda_moe_layer_noalloc.argtypes = [_P] * 15 + [_I] * 5 + [_P, _I, _P, _P, _P]
     L.glm_cuda_moe_layer_noalloc.restype = _I
     L.glm_cuda_matvec_q80.argtypes = [_P, _P, _P, _P, _I, _I, _I]
@@ -75,7 +80,8 @@ def _signatures(L: ctypes.CDLL) -> None:
     for name in ("glm_cuda_init", "glm_cuda_upload_moe_layer", "glm_cuda_bind_moe_layer_device",
                  "glm_cuda_moe_layer", "glm_cuda_moe_layer_async", "glm_cuda_moe_layer_profile",
                  "glm_cuda_moe_layers_async", "glm_cuda_set_decode_path", "glm_cuda_decode_path",
-                 "glm_cuda_set_prefill_tokens",
+                 "glm_cuda_set_prefill_tokens", "glm_cuda_ep_setup", "glm_cuda_ep_dispatch", "glm_cuda_ep_experts",
+                 "glm_cuda_ep_combine", "glm_cuda_ep_status",
                  "glm_cuda_model_init", "glm_cuda_upload_model_globals", "glm_cuda_bind_model_globals_device",
                  "glm_cuda_upload_attn_layer", "glm_cuda_bind_attn_layer_device", "glm_cuda_forward_token",
                  "glm_cuda_generate",
@@ -206,6 +212,28 @@ class GlmCuda:
         if rc < 0:
             self._check("glm_cuda_set_prefill_tokens", rc)
         return rc
+
+    # ---- expert parallelism (stream: a cudaStream_t handle or None)
+    def ep_setup(self, n_shards: int, shard: int, max_tokens: int) -> None:
+        self._check("glm_cuda_ep_setup", self.L.glm_cuda_ep_setup(n_shards, shard, max_tokens))
+
+    def ep_dispatch(self, layer: int, x_dev, n_tokens: int, send_rows, send_expert, send_counts, stream=None) -> None:
+        self._check("glm_cuda_ep_dispatch",
+                    self.L.glm_cuda_ep_dispatch(layer, _ptr(x_dev), n_tokens, _ptr(send_rows), _ptr(send_expert),
+                                                _ptr(send_counts), stream))
+
+    def ep_experts(self, layer: int, recv_rows, recv_expert, n_recv: int, out_rows, stream=None) -> None:
+        self._check("glm_cuda_ep_experts",
+                    self.L.glm_cuda_ep_experts(layer, _ptr(recv_rows), _ptr(recv_expert), n_recv, _ptr(out_rows),
+                                               stream))
+
+    def ep_combine(self, layer: int, x_dev, back_rows, idx_dev=None, w_dev=None, stream=None) -> None:
+        self._check("glm_cuda_ep_combine",
+                    self.L.glm_cuda_ep_combine(layer, _ptr(x_dev), _ptr(back_rows), _ptr(idx_dev), _ptr(w_dev),
+                                               stream))
+
+    def ep_status(self) -> None:
+        self._check("glm_cuda_ep_status", self.L.glm_cuda_ep_status())
 
     def decode_path(self) -> int:
         rc = self.L.glm_cuda_decode_path()

@@ -90,6 +90,49 @@ int glm_cuda_moe_layer_async(int layer, float *x_dev, int n_tokens, int32_t *top
 /* Select the decode kernels (GLM_CUDA_PATH_*). No counterpart in glm.c. */
 int glm_cuda_set_decode_path(int path);
 
+/* ---- expert parallelism (no counterpart in glm.c, which runs every expert
+ * on one host): the routed experts are split over n_shards ranks (one
+ * process per GPU), n_routed_experts / n_shards consecutive experts each;
+ * every rank routes its own tokens, the (token, slot) rows travel to the
+ * rank holding their expert and the expert outputs travel back (the caller
+ * moves the buffers, e.g. with an NCCL all-to-all), the shared expert runs
+ * where the tokens are. Per layer: ep_dispatch -> exchange -> ep_experts ->
+ * exchange back -> ep_combine; one layer at a time. */
+
+/* Make this rank shard `shard` of n_shards; max_tokens bounds n_tokens of
+ * ep_dispatch. Call after glm_cuda_init and before uploading layers: the
+ * routed arrays of later uploads / binds hold only this shard's experts
+ * (gate/up [n_routed_experts / n_shards][moe_ffn_dim][dim] ...), the router
+ * and the shared expert stay whole. The single-rank MoE entry points then
+ * return GLM_CUDA_ERR_STATE. Allocates the exchange scratch. */
+int glm_cuda_ep_setup(int n_shards, int shard, int max_tokens);
+
+/* Route x_dev[n_tokens][dim] (device) exactly as apply_moe_shared_ffn_layer
+ * (infer.c:1098-1145) and lay out the send buffer: for every (token, slot)
+ * pair with a valid expert, its normalised row (rmsnorm(x) * ffn_norm, fp32
+ * [dim]) in send_rows_dev, grouped by destination shard (shard order; pairs
+ * in (token, slot) order within a shard), the expert id local to that shard
+ * in send_expert_dev, and send_counts_dev[n_shards] rows per shard. Buffers
+ * hold n_tokens * n_experts_used rows. Stream-ordered. */
+int glm_cuda_ep_dispatch(int layer, const float *x_dev, int n_tokens, float *send_rows_dev,
+                         int32_t *send_expert_dev, int32_t *send_counts_dev, void *stream);
+
+/* This shard's experts on n_recv received rows (recv_expert_dev: local
+ * expert ids) plus the shared expert on this rank's tokens of the last
+ * dispatch; out_rows_dev[n_recv][dim] receives each row's expert output
+ * (SwiGLU FFN, not yet weighted) in the received order. */
+int glm_cuda_ep_experts(int layer, const float *recv_rows_dev, const int32_t *recv_expert_dev, int n_recv,
+                        float *out_rows_dev, void *stream);
+
+/* x_dev += shared + sum_k 1.8 w_k y_k in rank order (infer.c:1175-1214), with
+ * y_k read from back_rows_dev laid out as the send buffer of the last
+ * dispatch; topk outputs (may be NULL) as in glm_cuda_moe_layer. */
+int glm_cuda_ep_combine(int layer, float *x_dev, const float *back_rows_dev, int32_t *topk_idx_dev,
+                        float *topk_w_dev, void *stream);
+
+/* Synchronise and report a bounded wait that gave up in the ep kernels. */
+int glm_cuda_ep_status(void);
+
 /* Calls of glm_cuda_moe_layer / _async with n_tokens >= min_tokens run the
  * batched prefill kernels instead of the per-token decode kernels: exact
  * routing of all tokens in one launch, then the routed and shared experts
