@@ -306,6 +306,175 @@ def run_reference(args) -> None:
     print(json.dumps(line))
 
 
+def prefill_ncu() -> dict:
+    """Tensor-pipe and DRAM figures of the prefill GEMMs from the committed ncu
+    capture (profiles/prefill_ncu.json), if present."""
+    path = os.path.join(ROOT, "profiles", "prefill_ncu.json")
+    if not os.path.exists(path):
+        return {}
+    with open(path) as f:
+        return json.load(f)
+
+
+def zipf_layer(torch, layer: dict, pkg, seed: int, li: int, dev) -> dict:
+    """A device layer with the Zipf(1.1) router bias of configs 3 and 4."""
+    out = dict(layer)
+    out["router_bias"] = torch.from_numpy(pkg.synth.zipf_bias(seed, li, E)).to(dev)
+    return out
+
+
+def run_prefill_leg(args, torch, pkg, lib, layers, dev, local, rank, world) -> dict:
+    """512 tokens (Zipf expert popularity) through one
+    config-0 MoE layer with the batched prefill kernels."""
+    import numpy as np
+
+    T = args.prefill_tokens
+    lib.init(local, D, F, E, K, GS, 1)
+    layer = zipf_layer(torch, layers[0], pkg, args.seed, 0, dev)  # kept alive: the library holds its pointers
+    lib.bind_moe_layer_device(0, layer)
+    lib.set_prefill_tokens(1)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(args.seed * 11 + rank)
+    x0 = torch.randn(T, D, generator=gen, device=dev)
+    x = torch.empty_like(x0)
+    stream = torch.cuda.Stream(device=dev)
+    sh = stream.cuda_stream
+    for _ in range(max(3, args.warmup // 4)):
+        with torch.cuda.stream(stream):
+            x.copy_(x0)
+            lib.moe_layer_async(0, x, T, stream=sh)
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.prefill_steps)]
+    for a, b in evs:
+        with torch.cuda.stream(stream):
+            x.copy_(x0)
+            a.record(stream)
+            lib.moe_layer_async(0, x, T, stream=sh)
+            b.record(stream)
+    torch.cuda.synchronize()
+    lib.synchronize()
+    ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    # expert weights streamed: every expert some token picked, plus the shared expert
+    idx = torch.zeros(T, K, dtype=torch.int32, device=dev)
+    with torch.cuda.stream(stream):
+        x.copy_(x0)
+        lib.moe_layer_async(0, x, T, idx, stream=sh)
+    torch.cuda.synchronize()
+    used = int(torch.unique(idx[idx >= 0]).numel()) + 1
+    q8 = lambda r, c: r * c + r * (c // GS) * 4  # noqa: E731
+    wbytes = used * (2 * q8(F, D) + q8(D, F))
+    peaks = measured_peaks()
+    # end to end: host memory in and out (pinned), glm_cuda_moe_layer
+    x_pin = torch.empty(T, D, dtype=torch.float32, pin_memory=True)
+    x_host = x0.cpu().numpy()
+    reps = max(3, args.prefill_steps // 2)
+    walls = []
+    for i in range(reps + 1):
+        x_pin.numpy()[:] = x_host
+        t0 = time.perf_counter()
+        lib.moe_layer_host_inplace(0, x_pin.numpy())
+        if i:
+            walls.append(time.perf_counter() - t0)
+    e2e_ms = statistics.median(walls) * 1e3
+    out = {"metric": "MoE prefill tok/s (config 3: 512 tokens, Zipf(1.1) experts, one config-0 layer)",
+           "value": round(world * T / (ms / 1e3), 1), "unit": "tok/s", "ms_per_layer": round(ms, 4),
+           "tokens": T, "steps": len(evs), "experts_streamed": used,
+           "weight_bytes": wbytes, "achieved_gbs": round(wbytes / (ms / 1e3) / 1e9, 1),
+           "frac_of_hbm_peak": round(wbytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
+           "e2e": {"value": round(world * T / (e2e_ms / 1e3), 1), "unit": "tok/s", "ms": round(e2e_ms, 4),
+                   "h2d_bytes_per_step": T * D * 4, "d2h_bytes_per_step": T * D * 4,
+                   "api": "glm_cuda_moe_layer (host pointers, synchronous)"},
+           "gpu_launches_per_layer": 7,
+           "api": "glm_cuda_moe_layer_async (n_tokens >= glm_cuda_set_prefill_tokens threshold)"}
+    prof = prefill_ncu()
+    if prof:
+        out["ncu"] = prof
+    lib.free()
+    return out
+
+
+def run_ep_leg(args, torch, pkg, lib, layers, dev, local, rank, world) -> dict:
+    """4096 tokens (split evenly over the ranks) through
+    8 stacked config-0 MoE layers, experts sharded over the ranks, dispatch
+    and combine by all-to-all; tokens/s and the exposed exchange time."""
+    import numpy as np
+    import torch.distributed as dist
+
+    n_layers = args.ep_layers
+    T = args.ep_tokens // world
+    lib.init(local, D, F, E, K, GS, n_layers)
+    lib.ep_setup(world, rank, T)
+    e_loc = E // world
+    shards = []  # kept alive: the library holds their pointers
+    for li in range(n_layers):
+        L = zipf_layer(torch, layers[li % len(layers)], pkg, args.seed, li, dev)
+        for name in ("gate_q", "gate_s", "up_q", "up_s", "down_q", "down_s"):
+            L[name] = L[name][rank * e_loc:(rank + 1) * e_loc]
+        lib.bind_moe_layer_device(li, L)
+        shards.append(L)
+    moe = pkg.ep.ExpertParallelMoE(lib, D, K, T, device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(args.seed * 13 + rank)
+    x0 = torch.randn(T, D, generator=gen, device=dev)
+    x = torch.empty_like(x0)
+
+    def step():
+        x.copy_(x0)
+        for li in range(n_layers):
+            moe.layer(li, x)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.ep_steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.ep_steps
+    # phase breakdown of one more step: exchange (counts + rows + back) vs kernels
+    x.copy_(x0)
+    phase = np.zeros(5)
+    for li in range(n_layers):
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+        moe.layer_timed(li, x, evs)
+        torch.cuda.synchronize()
+        phase += [evs[i].elapsed_time(evs[i + 1]) for i in range(5)]
+    lib.ep_status()
+    comm = float(phase[1] + phase[3])
+    if world > 1:
+        t = torch.tensor([ms, comm, float(phase.sum())], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, comm, tot = (float(v) for v in t.tolist())
+    else:
+        tot = float(phase.sum())
+    out = {"metric": "EP prefill tok/s (config 4: 4096 tokens x 8 config-0 MoE layers, experts sharded)",
+           "value": round(args.ep_tokens / (ms / 1e3), 1), "unit": "tok/s", "ms_per_step": round(ms, 3),
+           "n_gpus": world, "tokens_per_rank": T, "layers": n_layers, "experts_per_rank": e_loc,
+           "steps": args.ep_steps, "scaling": "strong (4096 tokens in total)",
+           "exposed_comm_fraction": round(comm / max(tot, 1e-9), 4),
+           "phase_ms_rank0": {"dispatch": round(float(phase[0]), 3), "exchange": round(float(phase[1]), 3),
+                              "experts": round(float(phase[2]), 3), "exchange_back": round(float(phase[3]), 3),
+                              "combine": round(float(phase[4]), 3)},
+           "exchange": "torch.distributed all_to_all_single (NCCL) of per-rank row counts, rows and expert ids; "
+                       "rows back the same way",
+           "last_layer_rows": moe.last}
+    lib.free()
+    return out
+
+
 def run_ours(args) -> None:
     import numpy as np
     import torch
@@ -506,6 +675,14 @@ def run_ours(args) -> None:
                   "first_ids": ids[:8].tolist(), "api": "glm_cuda_generate"}
         del glob, attn
 
+    route_stats = lib.route_stats()
+    prefill = None
+    if not args.no_prefill:
+        prefill = run_prefill_leg(args, torch, pkg, lib, layers, dev, local, rank, world)
+    ep_prefill = None
+    if not args.no_ep and args.ep_tokens % world == 0 and E % world == 0:
+        ep_prefill = run_ep_leg(args, torch, pkg, lib, layers, dev, local, rank, world)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         host_layer = {k: v.cpu().numpy() for k, v in layers[0].items()}
@@ -539,7 +716,7 @@ def run_ours(args) -> None:
             "gpu_launches": args.steps * N_MOE_LAYERS * kernels_per_layer,
             "decode_path": "persistent" if persistent else "chain",
             "clocks": clocks.report(),
-            "route_stats": lib.route_stats(),
+            "route_stats": route_stats,
         }
         if stacked is not None:
             line["stacked"] = stacked
@@ -547,6 +724,10 @@ def run_ours(args) -> None:
             line["decode"] = decode
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if prefill is not None:
+            line["prefill"] = prefill
+        if ep_prefill is not None:
+            line["ep_prefill"] = ep_prefill
         print(json.dumps(line))
     lib.free()
     del graphs
@@ -577,6 +758,13 @@ def main() -> None:
     ap.add_argument("--ref-budget-s", type=float, default=90.0,
                     help="total CPU seconds of the reference arm; each step is an equal bounded sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 batched prefill measurement")
+    ap.add_argument("--prefill-tokens", type=int, default=512)
+    ap.add_argument("--prefill-steps", type=int, default=20)
+    ap.add_argument("--no-ep", action="store_true", help="skip the config-4 expert-parallel measurement")
+    ap.add_argument("--ep-tokens", type=int, default=4096)
+    ap.add_argument("--ep-layers", type=int, default=8)
+    ap.add_argument("--ep-steps", type=int, default=5)
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
