@@ -475,6 +475,37 @@ def run_ep_leg(args, torch, pkg, lib, layers, dev, local, rank, world) -> dict:
     return out
 
 
+def run_only(args) -> None:
+    """One leg alone (--only prefill | ep), e.g. for a profiler capture: the
+    same measurement as in the full run, on freshly generated layers."""
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    from __graft_entry__ import load_package
+
+    pkg = load_package()
+    lib = pkg.glm_cuda.GlmCuda()
+    n = 1 if args.only == "prefill" else args.ep_layers
+    layers = make_device_layers(torch, n, args.seed + rank, dev)
+    torch.cuda.synchronize()
+    if args.only == "prefill":
+        out = run_prefill_leg(args, torch, pkg, lib, layers, dev, local, rank, world)
+    else:
+        out = run_ep_leg(args, torch, pkg, lib, layers, dev, local, rank, world)
+    if rank == 0:
+        print(json.dumps(out))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_ours(args) -> None:
     import numpy as np
     import torch
@@ -758,6 +789,8 @@ def main() -> None:
     ap.add_argument("--ref-budget-s", type=float, default=90.0,
                     help="total CPU seconds of the reference arm; each step is an equal bounded sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", choices=["prefill", "ep"], default=None,
+                    help="run only the config-3 prefill or the config-4 expert-parallel measurement")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 batched prefill measurement")
     ap.add_argument("--prefill-tokens", type=int, default=512)
     ap.add_argument("--prefill-steps", type=int, default=20)
@@ -770,6 +803,8 @@ def main() -> None:
         ap.error("--warmup must be >= 3")
     if args.impl == "reference":
         run_reference(args)
+    elif args.only:
+        run_only(args)
     else:
         run_ours(args)
 
