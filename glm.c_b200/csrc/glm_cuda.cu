@@ -230,6 +230,8 @@ int publish_layer(int layer) {
 
 bool use_persistent() { return g.persistent_ok && g.decode_path != GLM_CUDA_PATH_CHAIN; }
 
+bool decode_kernels_ok();
+
 // The layer glm.c's loop calls after `layer` (infer.c:1845), if it has weights.
 int next_moe_layer(int layer) {
     return layer + 1 < (int)g.layers.size() && g.layers[layer + 1].ready ? layer + 1 : -1;
@@ -292,8 +294,13 @@ int ensure_prefill_ws(int n_tokens) {
     return 0;
 }
 
+// The per-token decode kernels take gs = 32 only; other group sizes run every
+// call on the batched kernels.
+bool decode_kernels_ok() { return g.dims.gs == 32; }
+
 bool use_prefill(int n_tokens) {
-    return g.prefill_ok && g.prefill_min_tokens > 0 && n_tokens >= g.prefill_min_tokens;
+    if (!g.prefill_ok) return false;
+    return !decode_kernels_ok() || (g.prefill_min_tokens > 0 && n_tokens >= g.prefill_min_tokens);
 }
 
 int moe_enqueue(int layer, float* x_dev, int n_tokens, int32_t* idx_dev, float* w_dev, cudaStream_t st) {
@@ -347,7 +354,8 @@ int init_locked(int device, int dim, int moe_ffn_dim, int n_routed_experts, int 
     if (dim <= 0 || dim % 128 || moe_ffn_dim <= 0 || moe_ffn_dim % 64)
         return fail(GLM_CUDA_ERR_ARG, "unsupported dims dim=%d moe_ffn_dim=%d (need dim%%128==0, ffn%%64==0)", dim,
                     moe_ffn_dim);
-    if (group_size != 32) return fail(GLM_CUDA_ERR_ARG, "unsupported group size %d (supported: 32)", group_size);
+    if (group_size != 32 && group_size != 16)
+        return fail(GLM_CUDA_ERR_ARG, "unsupported group size %d (supported: 32, 16)", group_size);
     if (n_experts_used < 1 || n_experts_used > 8 || n_experts_used > n_routed_experts || n_routed_experts > 1024)
         return fail(GLM_CUDA_ERR_ARG, "unsupported expert counts E=%d K=%d", n_routed_experts, n_experts_used);
     if (n_layers <= 0) return fail(GLM_CUDA_ERR_ARG, "n_layers must be positive");
@@ -382,6 +390,11 @@ int init_locked(int device, int dim, int moe_ffn_dim, int n_routed_experts, int 
     *g.status_host = 0;
     g.persistent_ok = glmq::persistent_check(g.dims, g.num_sms, nullptr) == cudaSuccess;
     g.prefill_ok = glmq::prefill_check(g.dims) == cudaSuccess;
+    if (group_size != 32 && !g.prefill_ok) {
+        release_all();
+        return fail(GLM_CUDA_ERR_ARG, "group size %d needs the batched kernels: dim and moe_ffn_dim multiples of 128",
+                    group_size);
+    }
     g.layers.assign(n_layers, LayerSlot{});
     g.launches = 0;
     g.inited = true;
@@ -639,6 +652,7 @@ int glm_cuda_ep_status(void) {
 int glm_cuda_decode_path(void) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (!g.inited) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_init has not been called");
+    if (!decode_kernels_ok()) return GLM_CUDA_PATH_BATCHED;
     return use_persistent() ? GLM_CUDA_PATH_PERSISTENT : GLM_CUDA_PATH_CHAIN;
 }
 
@@ -646,6 +660,7 @@ int glm_cuda_moe_layer_profile(int layer, float* x_dev, float ms_out[3]) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (int rc = check_layer(layer)) return rc;
     if (!x_dev || !ms_out) return fail(GLM_CUDA_ERR_ARG, "x_dev and ms_out must be non-NULL");
+    if (!decode_kernels_ok()) return fail(GLM_CUDA_ERR_ARG, "the per-token decode kernels take gs = 32 only");
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
     for (auto& e : ev) CUDA_TRY(cudaEventCreate(&e));
     const int routed = routed_disabled_by_env() ? 0 : 1;
@@ -663,7 +678,8 @@ int glm_cuda_matvec_q80(const int8_t* qmat, const float* smat, const float* x, f
     std::lock_guard<std::mutex> lk(g_mu);
     if (!g.inited) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_init has not been called");
     if (!qmat || !smat || !x || !y || rows <= 0 || dim <= 0) return fail(GLM_CUDA_ERR_ARG, "bad matvec arguments");
-    if (gs != 32 || dim % 64) return fail(GLM_CUDA_ERR_ARG, "matvec: unsupported gs=%d dim=%d", gs, dim);
+    if ((gs != 32 && gs != 16) || dim % 64)
+        return fail(GLM_CUDA_ERR_ARG, "matvec: unsupported gs=%d dim=%d", gs, dim);
     auto it = g.mv_cache.find(qmat);
     if (it != g.mv_cache.end() && (it->second.rows != rows || it->second.dim != dim || it->second.gs != gs)) {
         cudaFree(it->second.q);
@@ -716,7 +732,8 @@ int glm_cuda_matvec_q80_async(const int8_t* q_dev, const float* s_dev, const flo
     if (!g.inited) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_init has not been called");
     if (!q_dev || !s_dev || !x_dev || !y_dev || rows <= 0 || dim <= 0)
         return fail(GLM_CUDA_ERR_ARG, "bad matvec arguments");
-    if (gs != 32 || dim % 64) return fail(GLM_CUDA_ERR_ARG, "matvec: unsupported gs=%d dim=%d", gs, dim);
+    if ((gs != 32 && gs != 16) || dim % 64)
+        return fail(GLM_CUDA_ERR_ARG, "matvec: unsupported gs=%d dim=%d", gs, dim);
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : g.stream;
     cudaError_t e = glmq::launch_q80_matvec(q_dev, s_dev, x_dev, y_dev, rows, dim, gs, g.num_sms, st);
     g.launches += 1;
@@ -838,6 +855,11 @@ int enqueue_step(cudaStream_t st) {
             LAUNCH_TRY(glmq::launch_q80_matvec(m.l0_down_q, m.l0_down_s, m.ff_gate, m.x, D, d.hidden_dim, gs, ns, st,
                                                true));
             g.launches += 4;
+        } else if (!decode_kernels_ok()) {
+            // gs = 16: the batched kernels with one token (workspace sized at model init)
+            LAUNCH_TRY(glmq::launch_moe_prefill(g.layers[l].w, g.dims, g.pf_ws, m.x, 1, nullptr, nullptr, routed, ns,
+                                                g.scratch.status, g.scratch.stats, st));
+            g.launches += 7;
         } else if (use_persistent()) {
             LAUNCH_TRY(glmq::launch_moe_persistent(g.layers_dev, l, 1, g.dims, g.scratch, m.x, nullptr, nullptr,
                                                    routed, ns, st, l + 1 < d.n_layers ? l + 1 : -1));
@@ -873,7 +895,8 @@ int glm_cuda_model_init(int device, const GlmCudaModelDims* dims) {
     if (d.n_layers < 2 || d.n_heads <= 0 || d.vocab_size <= 0 || d.cache_cap <= 0 || d.hidden_dim <= 0)
         return fail(GLM_CUDA_ERR_ARG, "bad model dims");
     if (d.head_k_dim != d.qk_nope_dim + d.rope_dim || d.rope_dim % 2 || d.qk_nope_dim % 32 || d.kv_lora_rank % 64 ||
-        d.q_lora_rank % 64 || (d.n_heads * d.v_head_dim) % 64 || d.hidden_dim % 64 || d.group_size != 32)
+        d.q_lora_rank % 64 || (d.n_heads * d.v_head_dim) % 64 || d.hidden_dim % 64 ||
+        (d.group_size != 32 && d.group_size != 16))
         return fail(GLM_CUDA_ERR_ARG, "unsupported attention/FFN dims");
     if (int rc = init_locked(device, d.dim, d.moe_ffn_dim, d.n_routed_experts, d.n_experts_used, d.group_size,
                              d.n_layers))
@@ -898,6 +921,8 @@ int glm_cuda_model_init(int device, const GlmCudaModelDims* dims) {
     CUDA_TRY(cudaMemset(m.cache_comp, 0, sizeof(float) * cache * d.kv_lora_rank));
     CUDA_TRY(cudaMemset(m.cache_pe, 0, sizeof(float) * cache * d.rope_dim));
     CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&m.io_host), 2 * sizeof(int), cudaHostAllocDefault));
+    if (!decode_kernels_ok())
+        if (int rc2 = ensure_prefill_ws(1)) return rc2;  // the MoE layers of a captured step run batched
     m.inited = true;
     return 0;
 }

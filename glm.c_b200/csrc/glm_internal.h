@@ -140,6 +140,7 @@ struct GroupGemmArgs {
     float* y;          // mode 1 output [rows][Mtot]
     unsigned* status;  // bit 64: a bounded wait gave up
     int K, Mtot, E, mode;  // mode 0: gate/up (K = D, Mtot = F); 1: down (K = F, Mtot = D)
+    int gs;                // weight scale group: 32 or 16
 };
 
 cudaError_t prefill_check(const MoeDims& d);

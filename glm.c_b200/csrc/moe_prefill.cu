@@ -31,6 +31,9 @@
 // to the stage buffer's mbarrier. The accumulator (128 x 64 fp32) lives in
 // TMEM; four warps read it back with tcgen05.ld (thread = weight row).
 #include <cstdint>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -44,6 +47,8 @@
 namespace glmq {
 
 namespace {
+
+cudaError_t ensure_smem_attr(const void* fn, int bytes);
 
 constexpr int kMaxGroups = 257;  // routed experts + the shared expert
 constexpr int kTM = 128;     // weight rows per tile (MMA M)
@@ -337,8 +342,7 @@ size_t route_batched_smem(int D, int E) {
 template <int PER>
 cudaError_t launch_route_batched(const PrefillRouteArgs& ra, cudaStream_t st) {
     const size_t smem = route_batched_smem(PER * 32, ra.E);
-    cudaError_t err =
-        cudaFuncSetAttribute(prefill_route_batched_kernel<PER>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t err = ensure_smem_attr(reinterpret_cast<const void*>(prefill_route_batched_kernel<PER>), (int)smem);
     if (err) return err;
     prefill_route_batched_kernel<PER><<<(ra.T + kRT - 1) / kRT, kRThreads, smem, st>>>(ra);
     return cudaGetLastError();
@@ -466,7 +470,7 @@ constexpr int kGemmThreads = 512;
 constexpr int kRawSlots = 8, kASlots = 4, kBSlots = 4;
 constexpr uint32_t kBBytes = 2 * kTN * 128; // bf16 rows [hi: n][lo: n], 128 bytes each
 constexpr uint32_t kRawBytes = kTM * kTK;   // int8 [128][64]
-constexpr uint32_t kScBytes = kTM * 16;     // fp32 scales [128][4]: groups of this k-slice pair
+constexpr uint32_t kScBytes = kTM * 16;     // fp32 scales [128][4]: 4 groups (gs 32: a k-slice pair; gs 16: one)
 constexpr uint32_t kRawSlotBytes = kRawBytes + 2048;
 constexpr uint32_t kTmemA = 256;            // first TMEM column of the A stages
 constexpr int kStageLd = 33;                // epilogue exchange row stride (floats)
@@ -619,19 +623,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     if (!role_wait(B, &B->raw_empty[slot], ((rs / kRawSlots) & 1) ^ 1, a.status)) goto done;
                     mbar_arrive_expect_tx(&B->raw_full[slot], kRawBytes + kScBytes);
                     const uint32_t dst = smem_addr(sm + GemmLayout::raw + slot * kRawSlotBytes);
-                    // scales: groups 4 * (ks / 2) .. + 3, a 16-byte box covering both k-slices of the pair
+                    // scales: a 16-byte box of 4 groups: gs = 32 -> groups 4 * (ks / 2) .. + 3 (both k-slices
+                    // of the pair); gs = 16 -> groups 4 * ks .. + 3 (this k-slice)
+                    const int sx = a.gs == 16 ? 4 * ks : 4 * (ks >> 1);
                     if (mode == 0) {
                         tma_load_2d(dst, sh ? &maps.w_sh[0] : &maps.w[0], ks * kTK, wrow, &B->raw_full[slot]);
                         tma_load_2d(dst + 64 * kTK, sh ? &maps.w_sh[1] : &maps.w[1], ks * kTK, wrow,
                                     &B->raw_full[slot]);
-                        tma_load_2d(dst + kRawBytes, sh ? &maps.s_sh[0] : &maps.s[0], 4 * (ks >> 1), wrow,
-                                    &B->raw_full[slot]);
-                        tma_load_2d(dst + kRawBytes + 64 * 16, sh ? &maps.s_sh[1] : &maps.s[1], 4 * (ks >> 1), wrow,
+                        tma_load_2d(dst + kRawBytes, sh ? &maps.s_sh[0] : &maps.s[0], sx, wrow, &B->raw_full[slot]);
+                        tma_load_2d(dst + kRawBytes + 64 * 16, sh ? &maps.s_sh[1] : &maps.s[1], sx, wrow,
                                     &B->raw_full[slot]);
                     } else {
                         tma_load_2d(dst, sh ? &maps.w_sh[0] : &maps.w[0], ks * kTK, wrow, &B->raw_full[slot]);
-                        tma_load_2d(dst + kRawBytes, sh ? &maps.s_sh[0] : &maps.s[0], 4 * (ks >> 1), wrow,
-                                    &B->raw_full[slot]);
+                        tma_load_2d(dst + kRawBytes, sh ? &maps.s_sh[0] : &maps.s[0], sx, wrow, &B->raw_full[slot]);
                     }
                 }
             }
@@ -700,16 +704,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 const unsigned char* rowp = slotp + r * kTK;
                 const int4 v0 = *reinterpret_cast<const int4*>(rowp + 16 * ((2 * h) ^ swz));
                 const int4 v1 = *reinterpret_cast<const int4*>(rowp + 16 * ((2 * h + 1) ^ swz));
-                const float s = reinterpret_cast<const float*>(slotp + kRawBytes)[r * 4 + 2 * (ks & 1) + h];
+                // columns 32h .. 32h + 31 of the k-slice: one group (gs = 32) or two (gs = 16)
+                const float* sct = reinterpret_cast<const float*>(slotp + kRawBytes) + r * 4;
+                const float sa = a.gs == 16 ? sct[2 * h] : sct[2 * (ks & 1) + h];
+                const float sb = a.gs == 16 ? sct[2 * h + 1] : sa;
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&B->raw_empty[rslot]);
-                const uint64_t s2 = f2_pack(s, s);
+                const uint64_t s2a = f2_pack(sa, sa), s2b = f2_pack(sb, sb);
                 uint32_t hv[16], lv[16];
                 const uint32_t qw[8] = {(uint32_t)v0.x, (uint32_t)v0.y, (uint32_t)v0.z, (uint32_t)v0.w,
                                         (uint32_t)v1.x, (uint32_t)v1.y, (uint32_t)v1.z, (uint32_t)v1.w};
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                     const uint32_t u = qw[j] ^ 0x80808080u;  // bytes q + 128
+                    const uint64_t s2 = j < 4 ? s2a : s2b;   // words 0-3: columns 0-15, 4-7: 16-31
                     dequant_pair(u, 0, 1, s2, hv[2 * j], lv[2 * j]);
                     dequant_pair(u, 2, 3, s2, hv[2 * j + 1], lv[2 * j + 1]);
                 }
@@ -1039,6 +1047,22 @@ __global__ void ep_combine_kernel(float* x, const float* __restrict__ Y, const i
     }
 }
 
+// Raise a kernel's dynamic shared-memory limit once per device (so that
+// launches captured into a CUDA graph make no attribute calls).
+cudaError_t ensure_smem_attr(const void* fn, int bytes) {
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, int> set;
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err) return err;
+    std::lock_guard<std::mutex> lk(mu);
+    int& have = set[{fn, dev}];
+    if (have >= bytes) return cudaSuccess;
+    err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (!err) have = bytes;
+    return err;
+}
+
 // ------------------------------------------------------------ tensor maps
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -1069,7 +1093,7 @@ bool make_map(CUtensorMap* m, const void* base, CUtensorMapDataType type, int el
 }  // namespace
 
 cudaError_t prefill_check(const MoeDims& d) {
-    if (d.gs != 32 || d.D % kTM || d.F % kTM || d.E < 1 || d.E + 1 > kMaxGroups || d.K < 1 || d.K > kMaxTopK ||
+    if ((d.gs != 32 && d.gs != 16) || d.D % kTM || d.F % kTM || d.E < 1 || d.E + 1 > kMaxGroups || d.K < 1 || d.K > kMaxTopK ||
         d.K > d.E || d.D > 8192 || d.F > 16384)
         return cudaErrorInvalidValue;
     return cudaSuccess;
@@ -1133,8 +1157,7 @@ cudaError_t launch_route(const PrefillRouteArgs& ra, cudaStream_t st) {
     }
     const size_t rsmem = sizeof(float) * ((pad64(ra.D) + 3) & ~3) + sizeof(float) * ra.D + 16 * (size_t)ra.E +
                          20 * (size_t)ra.E + 256;
-    cudaError_t err =
-        cudaFuncSetAttribute(prefill_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsmem);
+    cudaError_t err = ensure_smem_attr(reinterpret_cast<const void*>(prefill_route_kernel), (int)rsmem);
     if (err) return err;
     prefill_route_kernel<<<ra.T, 512, rsmem, st>>>(ra);
     return cudaGetLastError();
@@ -1161,7 +1184,7 @@ cudaError_t launch_grouped_ffn(const MoeLayerDev& w, const MoeDims& d, bool use_
     };
     auto smap = [&](CUtensorMap* mp, const float* sc, uint64_t rows, int cols, uint32_t box_rows,
                     const CUtensorMap* alt) {
-        if (sc) ok = ok && make_map(mp, sc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, rows, cols / 32, box_rows, 4,
+        if (sc) ok = ok && make_map(mp, sc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, rows, cols / d.gs, box_rows, 4,
                                     CU_TENSOR_MAP_SWIZZLE_NONE);
         else if (alt) *mp = *alt;
     };
@@ -1188,11 +1211,11 @@ cudaError_t launch_grouped_ffn(const MoeLayerDev& w, const MoeDims& d, bool use_
     ok = ok && make_map(&m2.bhi, hhi, bf, 2, R_cap, d.F, 32, kTK, sw) && make_map(&m2.blo, hlo, bf, 2, R_cap, d.F, 32, kTK, sw);
     if (!ok) return cudaErrorInvalidValue;
     const int gsmem = (int)GemmLayout::total + 1024;
-    cudaError_t err = cudaFuncSetAttribute(q8_group_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gsmem);
+    cudaError_t err = ensure_smem_attr(reinterpret_cast<const void*>(q8_group_gemm_kernel), gsmem);
     if (err) return err;
-    GroupGemmArgs g1{items1, items2, counts, hhi, hlo, nullptr, status, d.D, d.F, d.E, 0};
+    GroupGemmArgs g1{items1, items2, counts, hhi, hlo, nullptr, status, d.D, d.F, d.E, 0, d.gs};
     q8_group_gemm_kernel<<<num_sms, kGemmThreads, gsmem, st>>>(m1, g1);
-    GroupGemmArgs g2{items1, items2, counts, nullptr, nullptr, y, status, d.F, d.D, d.E, 1};
+    GroupGemmArgs g2{items1, items2, counts, nullptr, nullptr, y, status, d.F, d.D, d.E, 1, d.gs};
     q8_group_gemm_kernel<<<num_sms, kGemmThreads, gsmem, st>>>(m2, g2);
     return cudaGetLastError();
 }

@@ -1,4 +1,5 @@
 // Batch-1 planar Q8 matvec on sm_100a: y[r] = sum_g s[r,g] * sum_k q[r,gs*g+k] x[gs*g+k]
+// (gs = 32: integer tensor-core kernel; gs = 16: CUDA-core kernel below)
 // Replaces matvec_q80_rows (infer.c:765-786) behind matvec_rows (infer.c:792-797).
 //
 // One persistent CTA per SM owns an equal contiguous slice of the rows; its
@@ -133,6 +134,68 @@ __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a)
     }
 }
 
+// gs = 16 (glm.c's own export, glm47_flash_export.py:36): the int8 MMA of
+// the kernel above sums 32 columns under one weight scale, so 16-column
+// groups take this CUDA-core kernel instead. Lane = one 16-byte group per
+// step (coalesced 512-byte warp loads), int8 -> fp32 by the exponent trick,
+// per-group dot, then s[row][group] * dot accumulated as in glm.c's
+// matvec_q80_rows (infer.c:765-786); one warp per row, rows strided over
+// the persistent CTAs.
+constexpr int kG16Warps = 16;
+
+__global__ void __launch_bounds__(kG16Warps * 32) q80_matvec_g16_kernel(MatvecArgs a) {
+    extern __shared__ __align__(16) unsigned char sm16[];
+    float* xs = reinterpret_cast<float*>(sm16);  // [cols]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (a.norm) {
+        __shared__ double red[kG16Warps];
+        double ss = 0.0;
+        for (int i = threadIdx.x; i < a.cols; i += blockDim.x) ss += (double)a.x[i] * (double)a.x[i];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        double tot = 0.0;
+        for (int w = 0; w < kG16Warps; ++w) tot += red[w];
+        const float mean = (float)(tot / (double)a.cols);
+        const float inv = 1.0f / sqrtf(mean + 1e-5f);
+        for (int i = threadIdx.x; i < a.cols; i += blockDim.x) xs[i] = a.x[i] * inv * a.norm[i];
+    } else {
+        for (int i = threadIdx.x; i < a.cols; i += blockDim.x) xs[i] = a.x[i];
+    }
+    __syncthreads();
+    const int ng = a.cols >> 4;
+    for (int r = blockIdx.x * kG16Warps + warp; r < a.rows; r += gridDim.x * kG16Warps) {
+        const int8_t* qr = a.q + (size_t)r * a.cols;
+        const float* sr = a.s + (size_t)r * ng;
+        float acc = 0.0f;
+        for (int g = lane; g < ng; g += 32) {
+            const int4 q = ld_weights16(qr + 16 * g);
+            const float sc = __ldg(sr + g);
+            const float4* xv = reinterpret_cast<const float4*>(xs + 16 * g);
+            const uint32_t w4[4] = {(uint32_t)q.x, (uint32_t)q.y, (uint32_t)q.z, (uint32_t)q.w};
+            float dot = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float4 x4 = xv[j];
+                const uint32_t u = w4[j] ^ 0x80808080u;  // bytes q + 128
+                const float q0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650)) - 8388736.0f;
+                const float q1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7651)) - 8388736.0f;
+                const float q2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7652)) - 8388736.0f;
+                const float q3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7653)) - 8388736.0f;
+                dot = fmaf(q0, x4.x, dot);
+                dot = fmaf(q1, x4.y, dot);
+                dot = fmaf(q2, x4.z, dot);
+                dot = fmaf(q3, x4.w, dot);
+            }
+            acc = fmaf(sc, dot, acc);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+        if (lane == 0) a.y[r] = a.accumulate ? a.y[r] + acc : acc;
+    }
+}
+
 size_t q80_matvec_smem_bytes(int cols, bool norm) {
     const int nch = cols >> 6;
     return (size_t)nch * kChunkBytes + (size_t)(cols >> 5) * 4 + (size_t)nch * kChunkTab * 4 + kMvWarps * 16 * 4 +
@@ -141,7 +204,19 @@ size_t q80_matvec_smem_bytes(int cols, bool norm) {
 
 cudaError_t launch_q80_matvec(const int8_t* q, const float* s, const float* x, float* y, int rows, int cols,
                               int gs, int num_sms, cudaStream_t stream, bool accumulate, const float* norm) {
-    if (gs != 32 || cols % 64 || rows <= 0) return cudaErrorInvalidValue;
+    if ((gs != 32 && gs != 16) || cols % 64 || rows <= 0) return cudaErrorInvalidValue;
+    if (gs == 16) {
+        const size_t smem16 = (size_t)cols * 4;
+        if (smem16 > 200 * 1024) return cudaErrorInvalidValue;
+        cudaError_t e = cudaFuncSetAttribute(q80_matvec_g16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem16);
+        if (e) return e;
+        int grid = num_sms * 2;
+        if (grid > (rows + kG16Warps - 1) / kG16Warps) grid = (rows + kG16Warps - 1) / kG16Warps;
+        MatvecArgs a{q, s, x, y, rows, cols, accumulate ? 1 : 0, norm};
+        q80_matvec_g16_kernel<<<grid, kG16Warps * 32, smem16, stream>>>(a);
+        return cudaGetLastError();
+    }
     const size_t smem = q80_matvec_smem_bytes(cols, norm != nullptr);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
     static bool attr_set = false;

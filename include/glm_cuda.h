@@ -10,8 +10,11 @@
  *
  * Weight layout is glm.c's planar Q8 format, unchanged: int8 q[rows][cols]
  * row-major plus fp32 s[rows][cols/gs] row-major (infer.c:765-786), routed
- * experts stored expert-major (infer.c:697-742). Supported now: gs == 32,
- * dim % 128 == 0, moe_ffn_dim % 64 == 0, 1 <= n_experts_used <= 8.
+ * experts stored expert-major (infer.c:697-742). Supported: gs == 32 or 16
+ * (glm.c's own export uses 16, glm47_flash_export.py:36), dim % 128 == 0,
+ * moe_ffn_dim % 64 == 0 (% 128 for gs == 16), 1 <= n_experts_used <= 8.
+ * With gs == 16 every MoE call runs the batched kernels (the per-token
+ * decode kernels take gs == 32 only) and the Q8 matvec a CUDA-core kernel.
  *
  * Threading: like glm.c's backends (one instance per process, infer.m:18-37)
  * the library keeps one global device context; calls are serialised by an
@@ -86,6 +89,7 @@ int glm_cuda_moe_layer_async(int layer, float *x_dev, int n_tokens, int32_t *top
 #define GLM_CUDA_PATH_AUTO 0
 #define GLM_CUDA_PATH_PERSISTENT 1
 #define GLM_CUDA_PATH_CHAIN 2
+#define GLM_CUDA_PATH_BATCHED 3  /* group_size 16: every call runs the batched kernels */
 
 /* Select the decode kernels (GLM_CUDA_PATH_*). No counterpart in glm.c. */
 int glm_cuda_set_decode_path(int path);
@@ -136,11 +140,11 @@ int glm_cuda_ep_status(void);
 /* Calls of glm_cuda_moe_layer / _async with n_tokens >= min_tokens run the
  * batched prefill kernels instead of the per-token decode kernels: exact
  * routing of all tokens in one launch, then the routed and shared experts
- * as grouped GEMMs on the tensor cores (Q8 weights dequantised in shared
- * memory to bf16 pairs), then the weighted combine. Same expert ids; x
- * agrees with the decode kernels within ~1e-5 relative. 0 disables it.
- * Default 32 where the sizes fit (dim and moe_ffn_dim multiples of 128,
- * n_routed_experts <= 256, gs == 32). The first call with a larger n_tokens
+ * as grouped GEMMs on the tensor cores (Q8 weights dequantised on chip to
+ * bf16 pairs), then the weighted combine. Same expert ids; x agrees with
+ * the decode kernels within ~1e-5 relative. 0 disables it (except with
+ * gs == 16, where every call is batched). Default 32 where the sizes fit
+ * (dim and moe_ffn_dim multiples of 128, n_routed_experts <= 256). The first call with a larger n_tokens
  * than before allocates the kernels' scratch. Returns the previous value,
  * or a negative error. No counterpart in glm.c, whose prefill runs the
  * token loop of glm_app_main (infer.c:2190-2228). */

@@ -42,7 +42,7 @@ def test_calls_before_init_fail_cleanly(pkg):
 
 def test_init_rejects_unsupported_shapes(pkg):
     lib = pkg.glm_cuda.GlmCuda()
-    for args in ((0, 2048, 1536, 64, 4, 16, 1),   # gs=16 not built yet
+    for args in ((0, 2048, 1536, 64, 4, 8, 1),    # gs=8 (supported: 32, 16)
                  (0, 2000, 1536, 64, 4, 32, 1),   # dim % 128
                  (0, 2048, 1536, 64, 9, 32, 1),   # K > 8
                  (0, 2048, 1536, 64, 4, 32, 0)):  # no layers

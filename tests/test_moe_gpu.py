@@ -53,12 +53,17 @@ def test_moe_decode_matches_golden(name, path, lib, golden):
     print(f"{name}: worst FFN-delta rel L2 {worst:.2e}")
 
 
-def test_moe_decode_rejects_gs16(lib, golden):
-    import glm_c_b200.glm_cuda as gc
-
+def test_moe_gs16_runs_batched(lib, golden):
+    """gs = 16 (glm.c's own export): the per-token decode kernels take gs = 32
+    only, so every call runs the batched kernels; results as the reference's."""
     L, x, routed, exp = golden.load_case("moe_tiny_gs16")
-    with pytest.raises(gc.GlmCudaError):
-        lib.init(0, L["dim"], L["ffn"], L["n_experts"], L["k_used"], L["gs"], 1)
+    lib.init(0, L["dim"], L["ffn"], L["n_experts"], L["k_used"], L["gs"], 1)
+    lib.upload_moe_layer(0, L)
+    assert lib.decode_path() == 3  # GLM_CUDA_PATH_BATCHED
+    with routed_env(routed):
+        x_out, idx, w = lib.moe_layer(0, x, L["k_used"])
+    np.testing.assert_array_equal(idx, exp["topk_idx"])
+    check_moe_outputs(x, x_out, exp["x_out"], TOL)
 
 
 def test_auto_path_is_persistent_at_config0(lib, pkg):
