@@ -393,6 +393,7 @@ def run_prefill_leg(args, torch, pkg, lib, layers, dev, local, rank, world) -> d
                    "api": "glm_cuda_moe_layer (host pointers, synchronous)"},
            "gpu_launches_per_layer": 7,
            "api": "glm_cuda_moe_layer_async (n_tokens >= glm_cuda_set_prefill_tokens threshold)"}
+    out["route_stats"] = lib.route_stats()  # calls, interval fallbacks, unresolved ties, mean fallbacks
     prof = prefill_ncu()
     if prof:
         out["ncu"] = prof

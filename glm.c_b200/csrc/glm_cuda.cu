@@ -571,6 +571,7 @@ int glm_cuda_ep_setup(int n_shards, int shard, int max_tokens) {
     e.D = g.dims.D;
     e.F = g.dims.F;
     e.K = g.dims.K;
+    e.E = g.dims.E;
     e.n_shards = n_shards;
     e.e_local = g.dims.E / n_shards;
     e.T_max = max_tokens;

@@ -118,6 +118,8 @@ struct PrefillRouteArgs {
     float* topk_w;         // [T][K]
     unsigned long long* stats;
     int T, D, E, K;
+    double* cen;           // [T][E] router logit centres (scratch)
+    double* bnd;           // [T][E] their error bounds (scratch)
 };
 
 struct PrefillDispatchArgs {
@@ -152,6 +154,7 @@ size_t prefill_workspace_bytes(const MoeDims& d, int T);
 
 struct EpShape {
     int D, F, K;        // model dims (K = experts per token)
+    int E;              // routed experts in total
     int n_shards;       // ranks the routed experts are split over
     int e_local;        // routed experts held by this rank (E / n_shards)
     int T_max;          // most tokens this rank routes per call

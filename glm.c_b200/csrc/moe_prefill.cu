@@ -63,13 +63,6 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
-                 : "memory");
-}
-
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
 
@@ -161,159 +154,188 @@ __global__ void __launch_bounds__(512) prefill_route_kernel(PrefillRouteArgs a) 
     }
 }
 
-// Batched form: one CTA routes kRT tokens with 2 warps per token (each warp
-// takes every other expert); the router rows stream through shared memory
-// (cp.async, 3 buffers, 4 rows per stage) and are read by every token's
-// warps, so each row leaves L2 once per CTA. Lane l holds its token's xn
-// elements [l*PER, (l+1)*PER) and their products with the row in registers.
+// Batched form, two kernels.
 //
-// Bound (lane-contiguous, fp32 inner sums): the reference's prefixes are
-// P_{l,j} = R_l + sum_{k<=j} p_k with R_l the exact sum before lane l (fp64
-// warp scan, error < 2^-46 sum|p|). The lane's fp32 running sum r_j starts at
-// fl32(R_l) and |r_j - P_{l,j}| <= u|R_l| + u sum_{k<=j}|r_k| (+ the scan
-// error), so sum_j |P_{l,j}| <= S_l (1 + PER u) + PER u |R_l| (+ PER * 2^-46
-// sum|p|, negligible after the factor u below), with S_l = sum_j |r_j| <=
-// sabs_l / (1 - PER u) for the fp32 sum sabs_l of those PER terms. The
-// centre C sums the products in fp32 fours ((p0 + p1) + (p2 + p3), within
-// 2u of their exact sum each) and those in fp64. Then
-// B = 1.01 u sum_i |P_i| + (2.0001 u + 2^-40) sum_i |p_i|.
-constexpr int kRT = 2;        // tokens per CTA
-constexpr int kRBufs = 3;     // router-row stages in flight
-constexpr int kRRows = 4;     // router rows per stage
+// route_logits_kernel<PER>: CTA (token block, expert block) = kLT tokens (one
+// warp each) x kLE experts whose router rows sit in shared memory (padded
+// layout pad68, so the lanes' float4 reads are conflict-free). Lane l of a
+// warp holds its token's xn elements [l*PER, (l+1)*PER) in registers (rmsnorm
+// recomputed per expert block: certified mean as everywhere else). Per
+// expert, in one pass over the lane's elements taken as sub-chunks of 16:
+// the fp32 products p (as glm.c forms them), each sub-chunk's running sum q
+// and sum |q|, sum |p|, and the products summed as fp32 fours whose totals go
+// into fp64 sub-chunk totals. Bound: glm.c's serial sum is within
+// u * sum_i |P_i| of the exact sum, P_i its prefixes. With R_c the exact sum
+// before sub-chunk c (fp64 warp scan of the lane totals plus the lane's
+// earlier sub-chunks) and Q_{c,j} the exact in-chunk prefix,
+// |P_i| <= |R_c| + |Q_{c,j}|, so sum_i |P_i| <= sum_c (16 |R_c| + sum_j |Q_{c,j}|);
+// the fp32 q_j are within 16 u A_c (A_c = the sub-chunk's sum |p|) of Q_{c,j},
+// and the fp32 sum of |q_j| within (1 - 16 u)^-1. Hence
+//   B = 1.01 u sum_c [16 |R_c| + (1 + 2^-15) sabs_c + 256 u A_c]
+//       + (2.0001 u + 2^-40) sum |p|,
+// the second term covering the centre's own error (fours: 2u of their
+// magnitude each; fp64 sums: < 2^-40). C and B go to global memory.
+//
+// route_select_kernel: kRT tokens per CTA, 64 threads each on a named
+// barrier: the same certified top-k / exact fallback as the decode path
+// (route_common.cuh).
+constexpr int kLE = 8;                 // experts (router rows) per CTA
+constexpr int kLT = 8;                 // tokens (warps) per CTA
+constexpr int kRT = 1;                 // tokens per select CTA
+constexpr int kSelRows = 8;            // router rows staged at a time for the exact fallback
 constexpr int kRThreads = 64 * kRT;
 
 __host__ __device__ __forceinline__ int pad68(int i) { return i + 4 * (i >> 6); }
-
-__device__ __forceinline__ void cp_async_wait2() { asm volatile("cp.async.wait_group 2;\n" ::: "memory"); }
 
 __device__ __forceinline__ void token_bar(int tb) {
     asm volatile("bar.sync %0, 64;\n" ::"r"(1 + tb) : "memory");
 }
 
 template <int PER>
-__global__ void __launch_bounds__(kRThreads) prefill_route_batched_kernel(PrefillRouteArgs a) {
+__global__ void __launch_bounds__(kLT * 32) route_logits_kernel(PrefillRouteArgs a) {
     extern __shared__ __align__(16) unsigned char smr[];
-    const int D = PER * 32, E = a.E, K = a.K;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int tb = warp >> 1, half = warp & 1, ltid = tid & 63;
-    const int t = blockIdx.x * kRT + tb;
+    const int D = PER * 32, E = a.E;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int e0 = blockIdx.y * kLE, ne = min(kLE, E - e0);
+    const int rowf4 = ((pad68(D - 1) + 1) + 3) & ~3;
+    float* rows = reinterpret_cast<float*>(smr);  // phase 1: x of each warp's token; phase 2: kLE router rows
+    float* nrm = rows + kLE * rowf4;              // ffn_norm, padded layout
+    const int t = blockIdx.x * kLT + warp;
     const bool live = t < a.T;
-    const int rowf = pad68(D - 1) + 1;                       // padded row length (floats)
-    const int rowf4 = (rowf + 3) & ~3;
-    float* rows = reinterpret_cast<float*>(smr);              // [kRBufs][kRRows][rowf4]
-    double* cen = reinterpret_cast<double*>(rows + kRBufs * kRRows * rowf4);  // [kRT][E]
-    double* bnd = cen + kRT * E;                              // [kRT][E]
-    float* selb = reinterpret_cast<float*>(bnd + kRT * E);    // [kRT][5E]
-    int* miscb = reinterpret_cast<int*>(selb + kRT * 5 * E);  // [kRT][64]
-
-    // rmsnorm of this warp's token: each warp sums its token's squares itself
     const int base = lane * PER;
+    // phase 1: coalesced loads into the padded layout, lane-contiguous reads back
+    for (int c = threadIdx.x; c < D / 4; c += blockDim.x)
+        *reinterpret_cast<float4*>(nrm + pad68(4 * c)) = __ldg(reinterpret_cast<const float4*>(a.norm) + c);
+    float* xw = rows + warp * rowf4;
+    if (live)
+        for (int c = lane; c < D / 4; c += 32)
+            *reinterpret_cast<float4*>(xw + pad68(4 * c)) = *(reinterpret_cast<const float4*>(a.x + (size_t)t * D) + c);
+    __syncthreads();
     float xr[PER];
-    double ss = 0.0;
     if (live) {
-        const float* xt = a.x + (size_t)t * D + base;
 #pragma unroll
         for (int j = 0; j < PER; j += 4) {
-            const float4 v = *reinterpret_cast<const float4*>(xt + j);
+            const float4 v = *reinterpret_cast<const float4*>(xw + pad68(base + j));
             xr[j] = v.x;
             xr[j + 1] = v.y;
             xr[j + 2] = v.z;
             xr[j + 3] = v.w;
         }
+        double ss = 0.0;
 #pragma unroll
         for (int j = 0; j < PER; ++j) ss += (double)xr[j] * (double)xr[j];
-    }
-    ss = warp_sum_d(ss);
-    float inv = 0.0f;
-    if (live && lane == 0)
-        inv = rms_inv_certified(ss, a.x + (size_t)t * D, D, (a.stats && half == 0) ? &a.stats[3] : nullptr);
-    inv = __shfl_sync(0xffffffffu, inv, 0);
-    if (live) {
-        const float* nrm = a.norm + base;
+        ss = warp_sum_d(ss);
+        float inv = 0.0f;
+        if (lane == 0) inv = rms_inv_certified_padded(ss, xw, D, (a.stats && blockIdx.y == 0) ? &a.stats[3] : nullptr);
+        inv = __shfl_sync(0xffffffffu, inv, 0);
 #pragma unroll
-        for (int j = 0; j < PER; ++j) xr[j] = __fmul_rn(__fmul_rn(xr[j], inv), __ldg(nrm + j));  // infer.c:751
-        if (half == 0) {
-            float* xo = a.xn + (size_t)t * D + base;
-#pragma unroll
-            for (int j = 0; j < PER; j += 4)
-                *reinterpret_cast<float4*>(xo + j) = make_float4(xr[j], xr[j + 1], xr[j + 2], xr[j + 3]);
+        for (int j = 0; j < PER; j += 4) {
+            const float4 w4 = *reinterpret_cast<const float4*>(nrm + pad68(base + j));
+            xr[j] = __fmul_rn(__fmul_rn(xr[j], inv), w4.x);  // infer.c:751
+            xr[j + 1] = __fmul_rn(__fmul_rn(xr[j + 1], inv), w4.y);
+            xr[j + 2] = __fmul_rn(__fmul_rn(xr[j + 2], inv), w4.z);
+            xr[j + 3] = __fmul_rn(__fmul_rn(xr[j + 3], inv), w4.w);
         }
     }
-
-    // router rows, kRRows per stage, kRBufs stages
-    const int nstage = (E + kRRows - 1) / kRRows;
-    auto issue = [&](int st) {
-        float* dst = rows + (st % kRBufs) * kRRows * rowf4;
+    __syncthreads();  // x staging is dead: the same space takes the router rows
+    {
         const int chunks = D / 4;
-        for (int c = tid; c < kRRows * chunks; c += kRThreads) {
+        for (int c = threadIdx.x; c < kLE * chunks; c += blockDim.x) {
             const int r = c / chunks, q = c - r * chunks;
-            const int e = st * kRRows + r;
-            const bool ok = e < E;
-            cp_async16(smem_addr(dst + r * rowf4 + pad68(4 * q)), a.router + (size_t)(ok ? e : 0) * D + 4 * q, ok);
+            const float4 v = r < ne ? __ldg(reinterpret_cast<const float4*>(a.router + (size_t)(e0 + r) * D) + q)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4*>(rows + r * rowf4 + pad68(4 * q)) = v;
         }
-        cp_async_commit();
-    };
-    issue(0);
-    if (nstage > 1) issue(1);
-    else cp_async_commit();
-    for (int st = 0; st < nstage; ++st) {
-        if (st + 2 < nstage) issue(st + 2);
-        else cp_async_commit();
-        cp_async_wait2();
-        __syncthreads();
-        const float* buf = rows + (st % kRBufs) * kRRows * rowf4;
-        for (int rr = half; rr < kRRows; rr += 2) {
-            const int e = st * kRRows + rr;
-            if (!live || e >= E) continue;  // warp-uniform
-            const float* wr = buf + rr * rowf4;
-            float pr[PER];
-            double L = 0.0;
-            float sap = 0.0f;
-#pragma unroll
-            for (int j = 0; j < PER; j += 4) {
-                const float4 w4 = *reinterpret_cast<const float4*>(wr + pad68(base + j));
-                pr[j] = __fmul_rn(w4.x, xr[j]);
-                pr[j + 1] = __fmul_rn(w4.y, xr[j + 1]);
-                pr[j + 2] = __fmul_rn(w4.z, xr[j + 2]);
-                pr[j + 3] = __fmul_rn(w4.w, xr[j + 3]);
-            }
-#pragma unroll
-            for (int j = 0; j < PER; j += 4) {
-                L += (double)__fadd_rn(__fadd_rn(pr[j], pr[j + 1]), __fadd_rn(pr[j + 2], pr[j + 3]));
-                sap = __fadd_rn(__fadd_rn(sap, fabsf(pr[j])), fabsf(pr[j + 1]));
-                sap = __fadd_rn(__fadd_rn(sap, fabsf(pr[j + 2])), fabsf(pr[j + 3]));
-            }
-            double inc = L;
-#pragma unroll
-            for (int off = 1; off < 32; off <<= 1) {
-                const double y = __shfl_up_sync(0xffffffffu, inc, off);
-                if (lane >= off) inc += y;
-            }
-            const double C = __shfl_sync(0xffffffffu, inc, 31);
-            const double R = inc - L;
-            float run = __double2float_rn(R), sabs = 0.0f;
-#pragma unroll
-            for (int j = 0; j < PER; ++j) {
-                run = __fadd_rn(run, pr[j]);
-                sabs = __fadd_rn(sabs, fabsf(run));
-            }
-            // per-lane bound on sum_j |P_{l,j}|; (1 + PER u) / (1 - PER u) < 1 + 2^-15 for PER <= 64
-            double tl = (double)sabs * (1.0 + 0x1p-15) + (double)PER * 0x1p-24 * fabs(R);
-            double ap = (double)sap * 1.0001;
-            tl = warp_sum_d(tl);
-            ap = warp_sum_d(ap);
-            if (lane == 0) {
-                cen[tb * E + e] = C;
-                bnd[tb * E + e] = 1.01 * 0x1p-24 * tl + (2.0001 * 0x1p-24 + 0x1p-40) * ap;
-            }
-        }
-        __syncthreads();  // buffer st % kRBufs is refilled at st + kRBufs
     }
+    if (live && blockIdx.y == 0) {  // xn rows for the GEMM gather and the exact fallback
+        float* xo = a.xn + (size_t)t * D + base;
+#pragma unroll
+        for (int j = 0; j < PER; j += 4)
+            *reinterpret_cast<float4*>(xo + j) = make_float4(xr[j], xr[j + 1], xr[j + 2], xr[j + 3]);
+    }
+    __syncthreads();
+    if (!live) return;  // no block barrier follows
+    // Per expert, the lane's PER elements as NSUB sub-chunks of 16 with
+    // their own running sums (independent chains in flight); the bound uses
+    // |P_i| <= |prefix before the sub-chunk| + |in-chunk prefix|.
+    constexpr int NSUB = PER / 16;
+    for (int r = 0; r < ne; ++r) {
+        const float* wr = rows + r * rowf4;
+        double Ls[NSUB];
+        float qs[NSUB], sa[NSUB], sap = 0.0f;
+#pragma unroll
+        for (int k = 0; k < NSUB; ++k) {
+            Ls[k] = 0.0;
+            qs[k] = sa[k] = 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) {
+#pragma unroll
+            for (int k = 0; k < NSUB; ++k) {
+                const int jj = 16 * k + j;
+                const float4 w4 = *reinterpret_cast<const float4*>(wr + pad68(base + jj));
+                const float p0 = __fmul_rn(w4.x, xr[jj]), p1 = __fmul_rn(w4.y, xr[jj + 1]);
+                const float p2 = __fmul_rn(w4.z, xr[jj + 2]), p3 = __fmul_rn(w4.w, xr[jj + 3]);
+                Ls[k] += (double)__fadd_rn(__fadd_rn(p0, p1), __fadd_rn(p2, p3));
+                qs[k] = __fadd_rn(qs[k], p0);
+                sa[k] = __fadd_rn(sa[k], fabsf(qs[k]));
+                qs[k] = __fadd_rn(qs[k], p1);
+                sa[k] = __fadd_rn(sa[k], fabsf(qs[k]));
+                qs[k] = __fadd_rn(qs[k], p2);
+                sa[k] = __fadd_rn(sa[k], fabsf(qs[k]));
+                qs[k] = __fadd_rn(qs[k], p3);
+                sa[k] = __fadd_rn(sa[k], fabsf(qs[k]));
+                sap = __fadd_rn(__fadd_rn(sap, fabsf(p0)), __fadd_rn(fabsf(p1), __fadd_rn(fabsf(p2), fabsf(p3))));
+            }
+        }
+        double L = 0.0;
+#pragma unroll
+        for (int k = 0; k < NSUB; ++k) L += Ls[k];
+        double inc = L;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const double y = __shfl_up_sync(0xffffffffu, inc, off);
+            if (lane >= off) inc += y;
+        }
+        const double C = __shfl_sync(0xffffffffu, inc, 31);
+        double pre = inc - L, tl = 0.0;
+#pragma unroll
+        for (int k = 0; k < NSUB; ++k) {
+            tl += 16.0 * fabs(pre) + (double)sa[k] * (1.0 + 0x1p-15);
+            pre += Ls[k];
+        }
+        const double A = (double)sap * 1.0001;
+        tl += 256.0 * 0x1p-24 * A;
+        double ap = A;
+        tl = warp_sum_d(tl);
+        ap = warp_sum_d(ap);
+        if (lane == 0) {
+            a.cen[(size_t)t * E + e0 + r] = C;
+            a.bnd[(size_t)t * E + e0 + r] = 1.01 * 0x1p-24 * tl + (2.0001 * 0x1p-24 + 0x1p-40) * ap;
+        }
+    }
+}
 
-    // selection: the token's two warps, synchronised on their own barrier
-    if (!live) return;
-    float* sel = selb + tb * 5 * E;
-    int* misc = miscb + tb * 64;
+__global__ void __launch_bounds__(kRThreads) route_select_kernel(PrefillRouteArgs a) {
+    extern __shared__ __align__(16) unsigned char smr[];
+    const int E = a.E, K = a.K, D = a.D;
+    const int tid = threadIdx.x, warp = tid >> 5, tb = warp >> 1, ltid = tid & 63;
+    const int t = blockIdx.x * kRT + tb;
+    if (t >= a.T) return;  // both warps of the token leave together; barriers are per token
+    double* cen = reinterpret_cast<double*>(smr) + (size_t)tb * 2 * E;
+    double* bnd = cen + E;
+    float* sel = reinterpret_cast<float*>(reinterpret_cast<double*>(smr) + (size_t)kRT * 2 * E) + (size_t)tb * 5 * E;
+    int* misc = reinterpret_cast<int*>(reinterpret_cast<float*>(reinterpret_cast<double*>(smr) + (size_t)kRT * 2 * E) +
+                                       (size_t)kRT * 5 * E) + tb * 64;
+    float* xs = reinterpret_cast<float*>(reinterpret_cast<int*>(reinterpret_cast<float*>(reinterpret_cast<double*>(smr) +
+                                                                                         (size_t)kRT * 2 * E) +
+                                                                (size_t)kRT * 5 * E) + kRT * 64) + (size_t)tb * D;
+    for (int i = ltid; i < E; i += 64) {
+        cen[i] = a.cen[(size_t)t * E + i];
+        bnd[i] = a.bnd[(size_t)t * E + i];
+    }
+    for (int i = ltid * 4; i < D; i += 256)  // xn for the exact fallback (serial_logit reads it D times)
+        *reinterpret_cast<float4*>(xs + i) = *reinterpret_cast<const float4*>(a.xn + (size_t)t * D + i);
     SelectScratch S;
     S.sel_c = sel;
     S.sel_lo = sel + E;
@@ -325,26 +347,30 @@ __global__ void __launch_bounds__(kRThreads) prefill_route_batched_kernel(Prefil
     int* s_idx = misc + 32;
     float* s_w = reinterpret_cast<float*>(misc + 48);
     token_bar(tb);
-    block_select(cen + tb * E, bnd + tb * E, a.bias, E, K, a.router, a.xn + (size_t)t * D, D, ltid, 64, S, s_idx,
-                 s_w, half == 0 ? a.stats : nullptr, [tb]() { token_bar(tb); });
+    float* rowbuf = reinterpret_cast<float*>(reinterpret_cast<int*>(reinterpret_cast<float*>(
+                        reinterpret_cast<double*>(smr) + (size_t)kRT * 2 * E) + (size_t)kRT * 5 * E) + kRT * 64) +
+                    (size_t)kRT * D + (size_t)tb * kSelRows * D;
+    block_select(cen, bnd, a.bias, E, K, a.router, xs, D, ltid, 64, S, s_idx, s_w,
+                 (warp & 1) == 0 ? a.stats : nullptr, [tb]() { token_bar(tb); }, rowbuf, kSelRows);
     if (ltid < K) {
         a.topk_idx[(size_t)t * K + ltid] = s_idx[ltid];
         a.topk_w[(size_t)t * K + ltid] = s_w[ltid];
     }
 }
 
-size_t route_batched_smem(int D, int E) {
-    const int rowf4 = ((pad68(D - 1) + 1) + 3) & ~3;
-    return sizeof(float) * kRBufs * kRRows * rowf4 + sizeof(double) * 2 * kRT * E + sizeof(float) * kRT * 5 * E +
-           sizeof(int) * kRT * 64;
-}
-
 template <int PER>
 cudaError_t launch_route_batched(const PrefillRouteArgs& ra, cudaStream_t st) {
-    const size_t smem = route_batched_smem(PER * 32, ra.E);
-    cudaError_t err = ensure_smem_attr(reinterpret_cast<const void*>(prefill_route_batched_kernel<PER>), (int)smem);
+    const int D = PER * 32;
+    const size_t rowf4 = (size_t)((((D - 1) + 4 * ((D - 1) >> 6) + 1) + 3) & ~3);
+    static_assert(kLT <= kLE, "the x staging of phase 1 reuses the router-row space");
+    const size_t smem1 = sizeof(float) * (kLE + 1) * rowf4;
+    cudaError_t err = ensure_smem_attr(reinterpret_cast<const void*>(route_logits_kernel<PER>), (int)smem1);
     if (err) return err;
-    prefill_route_batched_kernel<PER><<<(ra.T + kRT - 1) / kRT, kRThreads, smem, st>>>(ra);
+    route_logits_kernel<PER><<<dim3((ra.T + kLT - 1) / kLT, (ra.E + kLE - 1) / kLE), kLT * 32, smem1, st>>>(ra);
+    const size_t smem2 = (size_t)kRT * (2 * ra.E * sizeof(double) + 5 * ra.E * sizeof(float) + 64 * sizeof(int) +
+                                        (1 + kSelRows) * D * sizeof(float));
+    if ((err = ensure_smem_attr(reinterpret_cast<const void*>(route_select_kernel), (int)smem2))) return err;
+    route_select_kernel<<<(ra.T + kRT - 1) / kRT, kRThreads, smem2, st>>>(ra);
     return cudaGetLastError();
 }
 
@@ -1103,6 +1129,7 @@ namespace {
 
 struct PrefillWs {
     float* xn;
+    double *cen, *bnd;  // router logit centre / bound [T][E]
     int32_t* ids;
     float* wts;
     int* row_tok;
@@ -1125,6 +1152,8 @@ PrefillWs carve(unsigned char* base, const MoeDims& d, int T) {
         return r;
     };
     w.xn = reinterpret_cast<float*>(take((size_t)T * d.D * 4));
+    w.cen = reinterpret_cast<double*>(take((size_t)T * d.E * 8));
+    w.bnd = reinterpret_cast<double*>(take((size_t)T * d.E * 8));
     w.ids = reinterpret_cast<int32_t*>(take((size_t)T * d.K * 4));
     w.wts = reinterpret_cast<float*>(take((size_t)T * d.K * 4));
     w.row_tok = reinterpret_cast<int*>(take(R * 4));
@@ -1233,7 +1262,8 @@ cudaError_t launch_moe_prefill(const MoeLayerDev& w, const MoeDims& d, unsigned 
     const int mt1 = d.F / (kTM / 2), mt2 = d.D / kTM;  // gate/up tiles: 64 features
     const PrefillWs p = carve(ws, d, T);
     // 1 routing
-    PrefillRouteArgs ra{x, w.ffn_norm, w.router, w.router_bias, p.xn, p.ids, p.wts, stats, T, d.D, d.E, d.K};
+    PrefillRouteArgs ra{x, w.ffn_norm, w.router, w.router_bias, p.xn, p.ids, p.wts, stats, T, d.D, d.E, d.K,
+                        p.cen, p.bnd};
     if ((err = launch_route(ra, st))) return err;
     // 2 dispatch
     PrefillDispatchArgs da{p.ids, T, d.K, d.E, use_routed ? 1 : 0, mt1, mt2, p.counts, p.row_tok, p.tok_row,
@@ -1258,6 +1288,7 @@ namespace {
 
 struct EpWs {
     float* xn;          // [T_max][D]
+    double *cen, *bnd;  // [T_max][E] router logit centre / bound
     int32_t* ids;       // [T_max][K]
     float* wts;         // [T_max][K]
     int* send_pos;      // [T_max][K]
@@ -1281,6 +1312,8 @@ EpWs ep_carve(unsigned char* base, const EpShape& s) {
         return r;
     };
     w.xn = reinterpret_cast<float*>(take((size_t)s.T_max * s.D * 4));
+    w.cen = reinterpret_cast<double*>(take((size_t)s.T_max * s.E * 8));
+    w.bnd = reinterpret_cast<double*>(take((size_t)s.T_max * s.E * 8));
     w.ids = reinterpret_cast<int32_t*>(take((size_t)s.T_max * s.K * 4));
     w.wts = reinterpret_cast<float*>(take((size_t)s.T_max * s.K * 4));
     w.send_pos = reinterpret_cast<int*>(take((size_t)s.T_max * s.K * 4));
@@ -1316,7 +1349,8 @@ cudaError_t launch_ep_dispatch(const MoeLayerDev& w, const MoeDims& d, const EpS
                                int routed, int num_sms, unsigned long long* stats, cudaStream_t st) {
     if (T <= 0 || T > s.T_max) return cudaErrorInvalidValue;
     const EpWs p = ep_carve(ws, s);
-    PrefillRouteArgs ra{x, w.ffn_norm, w.router, w.router_bias, p.xn, p.ids, p.wts, stats, T, d.D, d.E, d.K};
+    PrefillRouteArgs ra{x, w.ffn_norm, w.router, w.router_bias, p.xn, p.ids, p.wts, stats, T, d.D, d.E, d.K,
+                        p.cen, p.bnd};
     cudaError_t err = launch_route(ra, st);
     if (err) return err;
     ep_pack_kernel<<<1, 1024, 0, st>>>(p.ids, T, d.K, s.e_local, s.n_shards, routed && w.gate_q ? 1 : 0, p.send_pos,

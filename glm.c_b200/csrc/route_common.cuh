@@ -76,11 +76,13 @@ __device__ __forceinline__ void two_sum_merge(float& hi, float& lo, float ohi, f
 __device__ __forceinline__ float sigmoid_of_exp(float e) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, e)); }
 
 // The reference's exact router logit: s = 0; s = s + w[i]*x[i], left to right
-// (infer.c:916-938), with xn in plain shared-memory layout.
-__device__ __forceinline__ float serial_logit(const float* __restrict__ wrow, const float* xs, int D) {
+// (infer.c:916-938), with xn in plain shared-memory layout. wrow may be in
+// global or shared memory (generic loads).
+__device__ __forceinline__ float serial_logit(const float* wrow, const float* xs, int D) {
     float s = 0.0f;
+#pragma unroll 8
     for (int i = 0; i < D; i += 4) {
-        const float4 w4 = __ldg(reinterpret_cast<const float4*>(wrow + i));
+        const float4 w4 = *reinterpret_cast<const float4*>(wrow + i);
         s = __fadd_rn(s, __fmul_rn(w4.x, xs[i]));
         s = __fadd_rn(s, __fmul_rn(w4.y, xs[i + 1]));
         s = __fadd_rn(s, __fmul_rn(w4.z, xs[i + 2]));
@@ -299,7 +301,8 @@ __device__ __forceinline__ void rank_and_certify(const SelectScratch& S, int E, 
 template <typename Sync>
 __device__ void block_select(const double* center, const double* bound, const float* bias, int E, int K,
                              const float* router, const float* xs, int D, int tid, int nthreads,
-                             const SelectScratch& S, int* idx, float* w, unsigned long long* stats, Sync sync) {
+                             const SelectScratch& S, int* idx, float* w, unsigned long long* stats, Sync sync,
+                             float* rowbuf = nullptr, int nbuf = 0) {
     for (int i = tid; i < E; i += nthreads) {
         const double C = center[i], B = bound[i];
         const float b = bias[i];
@@ -329,20 +332,50 @@ __device__ void block_select(const double* center, const double* bound, const fl
             }
         if (nvalid < K) tau = -INFINITY;
         sync();
-        for (int i = tid; i < E; i += nthreads) {
-            if (S.sel_hi[i] >= tau) {
-                const float b = bias[i];
-                const float l = serial_logit(router + (size_t)i * D, xs, D);
-                const float ec = exp_cr(-l);
-                const float p = sigmoid_of_exp(ec);
-                S.p_c[i] = p;
-                S.sel_c[i] = __fadd_rn(p, b);
-                S.sel_lo[i] = __fadd_rn(sigmoid_of_exp(nextafterf(ec, INFINITY)), b);
-                S.sel_hi[i] = __fadd_rn(sigmoid_of_exp(nextafterf(ec, 0.0f)), b);
-            } else {
-                S.sel_c[i] = __int_as_float(0x7fc00000);  // provably out of the top K
-                S.sel_lo[i] = S.sel_c[i];
-                S.sel_hi[i] = S.sel_c[i];
+        auto exact = [&](int i, const float* wrow) {
+            const float b = bias[i];
+            const float l = serial_logit(wrow, xs, D);
+            const float ec = exp_cr(-l);
+            const float p = sigmoid_of_exp(ec);
+            S.p_c[i] = p;
+            S.sel_c[i] = __fadd_rn(p, b);
+            S.sel_lo[i] = __fadd_rn(sigmoid_of_exp(nextafterf(ec, INFINITY)), b);
+            S.sel_hi[i] = __fadd_rn(sigmoid_of_exp(nextafterf(ec, 0.0f)), b);
+        };
+        auto drop = [&](int i) {
+            S.sel_c[i] = __int_as_float(0x7fc00000);  // provably out of the top K
+            S.sel_lo[i] = S.sel_c[i];
+            S.sel_hi[i] = S.sel_c[i];
+        };
+        if (rowbuf && nbuf > 0) {
+            // Candidates in batches of nbuf: their router rows are copied to
+            // shared memory first, so each serial chain reads on-chip data
+            // instead of waiting on L2 for every element.
+            if (tid == 0) {
+                int n = 0;
+                for (int i = 0; i < E; ++i)
+                    if (S.sel_hi[i] >= tau) S.taken[n++] = i;
+                *S.cert = n;
+            }
+            sync();
+            const int ncand = *S.cert;
+            for (int i = tid; i < E; i += nthreads)
+                if (!(S.sel_hi[i] >= tau)) drop(i);
+            for (int b0 = 0; b0 < ncand; b0 += nbuf) {
+                const int nb = ncand - b0 < nbuf ? ncand - b0 : nbuf;
+                for (int v = tid * 4; v < nb * D; v += nthreads * 4) {
+                    const int r = v / D, c = v - r * D;
+                    *reinterpret_cast<float4*>(rowbuf + (size_t)r * D + c) =
+                        __ldg(reinterpret_cast<const float4*>(router + (size_t)S.taken[b0 + r] * D + c));
+                }
+                sync();
+                if (tid < nb) exact(S.taken[b0 + tid], rowbuf + (size_t)tid * D);
+                sync();
+            }
+        } else {
+            for (int i = tid; i < E; i += nthreads) {
+                if (S.sel_hi[i] >= tau) exact(i, router + (size_t)i * D);
+                else drop(i);
             }
         }
         if (tid < R) S.rank[tid] = -1;
@@ -391,6 +424,27 @@ __device__ __forceinline__ float rms_inv_certified(double S, const float* x, int
         double seq = 0.0;
         for (int i = 0; i < D; ++i) {
             const double v = (double)__ldcg(x + i);
+            seq = __dadd_rn(seq, __dmul_rn(v, v));
+        }
+        mean = (float)(seq / (double)D);
+        if (fallbacks) atomicAdd(fallbacks, 1ull);
+    }
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-5f)));
+}
+
+// rms_inv_certified for x held in shared memory in the padded layout
+// (element i at xsp[i + 4 * (i / 64)]): the serial fallback reads on-chip.
+__device__ __forceinline__ float rms_inv_certified_padded(double S, const float* xsp, int D,
+                                                          unsigned long long* fallbacks) {
+    const double b = S * 0x1p-40;
+    const float lo = (float)((S - b) / (double)D), hi = (float)((S + b) / (double)D);
+    float mean;
+    if (lo == hi) {
+        mean = lo;
+    } else {
+        double seq = 0.0;
+        for (int i = 0; i < D; ++i) {
+            const double v = (double)xsp[i + 4 * (i >> 6)];
             seq = __dadd_rn(seq, __dmul_rn(v, v));
         }
         mean = (float)(seq / (double)D);
