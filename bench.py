@@ -461,7 +461,8 @@ def run_ep_leg(args, torch, pkg, lib, layers, dev, local, rank, world) -> dict:
         ms, comm, tot = (float(v) for v in t.tolist())
     else:
         tot = float(phase.sum())
-    out = {"metric": "EP prefill tok/s (config 4: 4096 tokens x 8 config-0 MoE layers, experts sharded)",
+    out = {"metric": f"EP prefill tok/s (config 4: {args.ep_tokens} tokens x {n_layers} config-0 MoE layers, "
+                     "experts sharded)",
            "value": round(args.ep_tokens / (ms / 1e3), 1), "unit": "tok/s", "ms_per_step": round(ms, 3),
            "n_gpus": world, "tokens_per_rank": T, "layers": n_layers, "experts_per_rank": e_loc,
            "steps": args.ep_steps, "scaling": "strong (4096 tokens in total)",
