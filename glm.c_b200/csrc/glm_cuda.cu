@@ -217,6 +217,8 @@ int take_device_status() {
     if (st == 0) return 0;
     *g.status_host = 0;
     cudaMemsetAsync(g.scratch.status, 0, sizeof(unsigned int), g.stream);
+    // a launch that gave up may have left its barrier words set: clear them
+    cudaMemsetAsync(g.scratch.grid_bar, 0, 2 * sizeof(unsigned int), g.stream);
     return fail(GLM_CUDA_ERR_CUDA, "the decode kernel gave up waiting (status 0x%x)", st);
 }
 
@@ -378,13 +380,14 @@ int init_locked(int device, int dim, int moe_ffn_dim, int n_routed_experts, int 
         (rc = dev_alloc(&s.center, n_routed_experts)) || (rc = dev_alloc(&s.bound, n_routed_experts)) ||
         (rc = dev_alloc(&s.topk_idx, n_experts_used)) || (rc = dev_alloc(&s.topk_w, n_experts_used)) ||
         (rc = dev_alloc(&s.counter, 1)) || (rc = dev_alloc(&s.stats, 4)) || (rc = dev_alloc(&s.status, 1)) ||
-        (rc = dev_alloc(&s.grid_bar, 1)) || (rc = dev_alloc(&g.layers_dev, n_layers))) {
+        (rc = dev_alloc(&s.grid_bar, 2)) || (rc = dev_alloc(&g.layers_dev, n_layers))) {
         release_all();
         return rc;
     }
     CUDA_TRY(cudaMemset(s.counter, 0, sizeof(unsigned int)));
     CUDA_TRY(cudaMemset(s.stats, 0, 4 * sizeof(unsigned long long)));
     CUDA_TRY(cudaMemset(s.status, 0, sizeof(unsigned int)));
+    CUDA_TRY(cudaMemset(s.grid_bar, 0, 2 * sizeof(unsigned int)));  // barrier arrivals, exited CTAs
     CUDA_TRY(cudaMemset(g.layers_dev, 0, sizeof(glmq::MoeLayerDev) * n_layers));
     CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&g.status_host), sizeof(unsigned int), cudaHostAllocDefault));
     *g.status_host = 0;

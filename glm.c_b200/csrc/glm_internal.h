@@ -43,7 +43,7 @@ struct MoeScratch {
     unsigned long long* stats;  // [4] calls, interval fallbacks, unresolved near-ties, mean fallbacks
     // Persistent kernel only:
     unsigned int* status = nullptr;    // [1] nonzero after one of its bounded waits gave up
-    unsigned int* grid_bar = nullptr;  // [1] grid-barrier arrivals (zeroed at each launch)
+    unsigned int* grid_bar = nullptr;  // [2] grid-barrier arrivals, exited CTAs (reset by the last CTA out)
 };
 
 // One decode token through one MoE layer: x_out = x_in + FFN(x_in).

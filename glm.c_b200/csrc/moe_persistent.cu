@@ -78,7 +78,8 @@ struct PersistArgs {
     double* bound;
     int32_t* topk_out;  // [n_layers][K] or null
     float* topkw_out;
-    unsigned* bar;      // zero at launch
+    unsigned* bar;      // grid-barrier arrivals; zero at launch (the last CTA to exit resets it)
+    unsigned* done;     // CTAs that have exited; zero at launch
     unsigned* status;
     unsigned long long* stats;
     int D, F, E, K, routed_enabled, slot_bytes;
@@ -444,6 +445,9 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
         mbar_init(route_ready, 1);
         *s_abort = 0;
         mbar_init_fence();
+        // the next launch on this stream may start as SMs free up; it waits
+        // (griddepcontrol.wait) for this grid's completion before it reads x
+        asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     }
     __syncthreads();
 
@@ -626,6 +630,22 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
     // First item index >= from that belongs to this group.
     auto first_mine = [&](uint32_t from) { return from + (uint32_t)((grp - (int)(from % kPSlots) + kPSlots) % kPSlots); };
 
+    // x, the barrier words and the scratch may still be in use by the previous
+    // launch on this stream (programmatic dependent launch): wait for it.
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+    // Every consumer exit goes through here: the last CTA to leave resets the
+    // barrier words for the next launch (no memset between launches).
+    auto leave = [&]() {
+        if (tid == 0) {
+            __threadfence();
+            if (atomicAdd(a.done, 1u) == (unsigned)G - 1u) {
+                *reinterpret_cast<volatile unsigned*>(a.bar) = 0u;
+                *reinterpret_cast<volatile unsigned*>(a.done) = 0u;
+                __threadfence();
+            }
+        }
+    };
+
     for (int li = 0; li < a.n_layers; ++li) {
         const MoeLayerDev W = a.layers[a.first + li];
 
@@ -651,9 +671,28 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
             if (tid == 0) {
                 double tot = 0.0;
                 for (int w = 0; w < kPCons; ++w) tot += red[w];
-                *s_inv = rms_inv_certified(tot, a.x, D, c == 0 ? &a.stats[3] : nullptr);
+                float mean;
+                *s_inv = rms_mean_certify(tot, D, mean) ? rms_inv_of_mean(mean) : __int_as_float(0x7fc00000);
             }
             cons_sync();
+            if (isnan(*s_inv)) {
+                // not certified (or non-finite x): glm.c's serial fp64 sum, over x
+                // staged in shared memory instead of one L2 round trip per element
+#pragma unroll
+                for (int u = 0; u < kXPer; ++u)
+                    if (tid + u * kPConsThreads < D) xs[tid + u * kPConsThreads] = xr[u];
+                cons_sync();
+                if (tid == 0) {
+                    double seq = 0.0;
+                    for (int i = 0; i < D; ++i) {
+                        const double v = (double)xs[i];
+                        seq = __dadd_rn(seq, __dmul_rn(v, v));
+                    }
+                    *s_inv = rms_inv_of_mean((float)(seq / (double)D));
+                    if (c == 0) atomicAdd(&a.stats[3], 1ull);
+                }
+                cons_sync();
+            }
             const float inv = *s_inv;
 #pragma unroll
             for (int u = 0; u < kXPer; ++u) {
@@ -679,7 +718,7 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
                 __stcg(a.bound + c, B);
             }
         }
-        if (!grid_sync(a, P, nbar, tid, s_ok)) return;
+        if (!grid_sync(a, P, nbar, tid, s_ok)) return leave();
 
         // ---- P2: routing (every CTA, identical); shared and routed gate/up
         for (int i = tid; i < E; i += kPConsThreads) {
@@ -702,7 +741,7 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
             gate_item(W, u >= nsh, u >= nsh ? u - nsh : u, item);
         }
         it += (uint32_t)nitems;
-        if (!grid_sync(a, P, nbar, tid, s_ok)) return;
+        if (!grid_sync(a, P, nbar, tid, s_ok)) return leave();
 
         // ---- P3: h -> digit planes (xs is dead); down rows; combine
         quantize_planes_part<true>(a.h, (K + 1) * F, ph, gh, th, tid, kPConsThreads, sync);
@@ -725,8 +764,9 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
             }
             a.x[r] = __fadd_rn(__ldcg(a.x + r), __fadd_rn(ys[K * kPTile + tid], acc));
         }
-        if (li + 1 < a.n_layers && !grid_sync(a, P, nbar, tid, s_ok)) return;
+        if (li + 1 < a.n_layers && !grid_sync(a, P, nbar, tid, s_ok)) return leave();
     }
+    leave();
 }
 
 // ------------------------------------------------------------- launcher
@@ -755,9 +795,8 @@ cudaError_t launch_moe_persistent(const MoeLayerDev* layers_dev, int first, int 
             return err;
         cap = smem;
     }
-    if ((err = cudaMemsetAsync(s.grid_bar, 0, sizeof(unsigned int), stream))) return err;
     PersistArgs a{layers_dev, first,    n_layers, x,           s.h,       s.center,
-                  s.bound,    topk_out, topkw_out, s.grid_bar, s.status, s.stats,
+                  s.bound,    topk_out, topkw_out, s.grid_bar, s.grid_bar + 1, s.status, s.stats,
                   d.D,        d.F,      d.E,       d.K,        routed_enabled,
                   p_slot_bytes(d.D, d.F, d.E), next_layer};
     cudaLaunchConfig_t cfg = {};
@@ -765,11 +804,13 @@ cudaError_t launch_moe_persistent(const MoeLayerDev* layers_dev, int first, int 
     cfg.blockDim = dim3(kPThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, moe_persistent_kernel, a);
 }
 

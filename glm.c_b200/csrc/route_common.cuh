@@ -432,6 +432,19 @@ __device__ __forceinline__ float rms_inv_certified(double S, const float* x, int
     return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-5f)));
 }
 
+// The certification of rms_inv_certified alone: true and the mean glm.c
+// computes if every value in S +- 2^-40 S rounds to the same float mean.
+__device__ __forceinline__ bool rms_mean_certify(double S, int D, float& mean) {
+    const double b = S * 0x1p-40;
+    const float lo = (float)((S - b) / (double)D), hi = (float)((S + b) / (double)D);
+    mean = lo;
+    return lo == hi;
+}
+
+__device__ __forceinline__ float rms_inv_of_mean(float mean) {
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, 1e-5f)));
+}
+
 // rms_inv_certified for x held in shared memory in the padded layout
 // (element i at xsp[i + 4 * (i / 64)]): the serial fallback reads on-chip.
 __device__ __forceinline__ float rms_inv_certified_padded(double S, const float* xsp, int D,
