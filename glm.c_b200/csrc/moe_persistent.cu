@@ -391,6 +391,41 @@ __device__ bool grid_sync(const PersistArgs& a, const PCtx& P, unsigned& nbar, i
     return *s_ok != 0;
 }
 
+// grid_sync in two halves: grid_arrive (after this CTA's writes) and
+// grid_wait (before reading the other CTAs'), with work in between.
+__device__ void grid_arrive(const PersistArgs& a, const PCtx& P, unsigned& nbar, int tid) {
+    cons_sync();
+    ++nbar;
+    if (tid == 0) {
+        __threadfence();
+        if (!*P.abort_flag) atomicAdd(a.bar, 1u);
+    }
+}
+
+__device__ bool grid_wait(const PersistArgs& a, const PCtx& P, unsigned nbar, int tid, volatile int* s_ok) {
+    cons_sync();
+    if (tid == 0) {
+        int ok = 0;
+        const unsigned target = nbar * gridDim.x;
+        const uint64_t t0 = global_ns();
+        for (uint32_t i = 0; !*P.abort_flag && global_ns() - t0 < kWaitNs; ++i) {
+            if (ld_acquire_gpu(a.bar) >= target) {
+                ok = 1;
+                break;
+            }
+            if ((i & 255u) == 255u && (ld_relaxed_gpu(a.status) & kStatAbort)) break;
+        }
+        if (!ok) {
+            atomicOr(a.status, kStatBarrier);
+            *P.abort_flag = 1;
+        }
+        __threadfence();
+        *s_ok = ok;
+    }
+    cons_sync();
+    return *s_ok != 0;
+}
+
 __device__ __forceinline__ float silu_p(float v) { return v / (1.0f + expf(-v)); }
 
 __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArgs a) {
@@ -703,7 +738,6 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
         cons_sync();  // xs complete before any thread quantises it; the constants are read
         release_shared_item(it);
         ++it;
-        quantize_planes_part<false>(xs, D, px, gx, tx, tid, kPConsThreads, sync);
 
         // ---- P1: router logit of expert c (CTAs c < E)
         if (c < E) {
@@ -718,7 +752,12 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
                 __stcg(a.bound + c, B);
             }
         }
-        if (!grid_sync(a, P, nbar, tid, s_ok)) return leave();
+        // arrive as soon as this CTA's router results are out, then turn xn
+        // into digit planes for the gate/up products while the other CTAs'
+        // results come in, then wait
+        grid_arrive(a, P, nbar, tid);
+        quantize_planes_part<false>(xs, D, px, gx, tx, tid, kPConsThreads, sync);
+        if (!grid_wait(a, P, nbar, tid, s_ok)) return leave();
 
         // ---- P2: routing (every CTA, identical); shared and routed gate/up
         for (int i = tid; i < E; i += kPConsThreads) {
