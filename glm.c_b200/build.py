@@ -17,7 +17,7 @@ CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libglm_cuda.so")
 
-SOURCES = ["glm_cuda.cu", "moe_decode.cu", "moe_persistent.cu", "q80_matvec.cu", "moe_noalloc.cu", "decoder.cu", "moe_prefill.cu"]
+SOURCES = ["glm_cuda.cu", "moe_decode.cu", "moe_persistent.cu", "q80_matvec.cu", "moe_noalloc.cu", "decoder.cu", "moe_prefill.cu", "checkpoint.cu"]
 HEADERS = ["glm_internal.h", "q80_common.cuh", "route_common.cuh"]
 
 NVCC_FLAGS = [

@@ -65,6 +65,7 @@ def _signatures(L: ctypes.CDLL) -> None:
     L.glm_cuda_ep_experts.argtypes = [_I, _P, _P, _I, _P, _P]
     L.glm_cuda_ep_combine.argtypes = [_I, _P, _P, _P, _P, _P]
     L.glm_cuda_ep_status.argtypes = []
+    L.glm_cuda_load_checkpoint.argtypes = [ctypes.c_char_p, _I, _I]
     L.glm_cuda_moe_layer_noalloc.argtypes = [_P] * 15 + [_I] * 5 + [_P, _I, _P, _P, _P]
     L.glm_cuda_moe_layer_noalloc.restype = _I
     L.glm_cuda_matvec_q80.argtypes = [_P, _P, _P, _P, _I, _I, _I]
@@ -81,7 +82,7 @@ def _signatures(L: ctypes.CDLL) -> None:
                  "glm_cuda_moe_layer", "glm_cuda_moe_layer_async", "glm_cuda_moe_layer_profile",
                  "glm_cuda_moe_layers_async", "glm_cuda_set_decode_path", "glm_cuda_decode_path",
                  "glm_cuda_set_prefill_tokens", "glm_cuda_ep_setup", "glm_cuda_ep_dispatch", "glm_cuda_ep_experts",
-                 "glm_cuda_ep_combine", "glm_cuda_ep_status",
+                 "glm_cuda_ep_combine", "glm_cuda_ep_status", "glm_cuda_load_checkpoint",
                  "glm_cuda_model_init", "glm_cuda_upload_model_globals", "glm_cuda_bind_model_globals_device",
                  "glm_cuda_upload_attn_layer", "glm_cuda_bind_attn_layer_device", "glm_cuda_forward_token",
                  "glm_cuda_generate",
@@ -204,6 +205,10 @@ class GlmCuda:
 
     def set_decode_path(self, path: int) -> None:
         self._check("glm_cuda_set_decode_path", self.L.glm_cuda_set_decode_path(path))
+
+    def load_checkpoint(self, path: str, device: int, cache_cap: int) -> None:
+        """glm_cuda_load_checkpoint: a glm.c .bin file to the device (model init included)."""
+        self._check("glm_cuda_load_checkpoint", self.L.glm_cuda_load_checkpoint(os.fsencode(path), device, cache_cap))
 
     def set_prefill_tokens(self, min_tokens: int) -> int:
         """Route calls with n_tokens >= min_tokens to the batched prefill

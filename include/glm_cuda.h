@@ -289,6 +289,16 @@ int glm_cuda_generate(const int32_t *prompt, int n_prompt, int n_gen, int32_t *o
 
 /* Release all device memory and state. Replaces glm_backend_free's device
  * part (backend.c:108-110, glm_metal_free). Safe to call twice. */
+/* glm.c's runtime checkpoint (.bin, format version 4 with every layer's
+ * attention, as glm47_flash_export.py writes it) to the device: maps the
+ * file, checks the header and offsets as runtime_open does (infer.c:357-744),
+ * then glm_cuda_model_init(device, dims from the header, cache_cap) and the
+ * upload calls for the globals, every attention layer and every MoE layer.
+ * Replaces runtime_open + glm_backend_init (backend.c:88-101) for the cuda
+ * backend; glm_cuda_forward_token / glm_cuda_generate follow. A malformed
+ * file is GLM_CUDA_ERR_ARG (glm.c exits instead). */
+int glm_cuda_load_checkpoint(const char *path, int device, int cache_cap);
+
 void glm_cuda_free(void);
 
 #ifdef __cplusplus

@@ -73,6 +73,9 @@ def lib(impl: str = "orc") -> ctypes.CDLL:
         if hasattr(L, "ref_decode"):
             L.ref_decode.argtypes = [P, P, P, P, P, I, I, P, P]
             L.ref_decode.restype = I
+        if hasattr(L, "ref_decode_bin"):
+            L.ref_decode_bin.argtypes = [ctypes.c_char_p, P, I, I, I, P]
+            L.ref_decode_bin.restype = I
     _libs[impl] = L
     return L
 
@@ -211,3 +214,14 @@ def ref_decode(model: dict, prompt, n_gen: int, cache_cap: int, with_logits: boo
     if rc != 0:
         raise RuntimeError(f"ref_decode failed ({rc})")
     return out, logits
+
+
+def ref_decode_bin(path: str, prompt, n_gen: int, cache_cap: int):
+    """Greedy ids from glm.c's own loader (runtime_open) and forward pass on a
+    .bin checkpoint file."""
+    p = np.ascontiguousarray(prompt, dtype=np.int32)
+    out = np.zeros(n_gen, dtype=np.int32)
+    rc = lib("ref").ref_decode_bin(os.fsencode(path), p.ctypes.data, len(p), n_gen, cache_cap, out.ctypes.data)
+    if rc != 0:
+        raise RuntimeError(f"ref_decode_bin failed ({rc})")
+    return out

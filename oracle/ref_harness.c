@@ -274,3 +274,39 @@ int ref_decode(const int32_t *icfg, const void *const *glob, const void *const *
     (void)gs;
     return rc;
 }
+
+/* glm.c's own loader on a .bin checkpoint (runtime_open, infer.c:357-744),
+ * then the same greedy loop as ref_decode (glm_cpu_forward_token per
+ * position, argmax at temperature 0, infer.c:2190-2228). runtime_open exits
+ * the process on a malformed file, as glm.c does. */
+int ref_decode_bin(const char *path, const int32_t *prompt, int n_prompt, int n_gen, int cache_cap,
+                   int32_t *out_ids) {
+    Runtime rt;
+    memset(&rt, 0, sizeof(rt));
+    runtime_open(&rt, path);
+    RuntimeConfig *c = &rt.cfg;
+    c->bos_id = -1;
+    c->eos_id = -1;
+    RunState st;
+    runstate_build(&st, &rt, cache_cap);
+    int token = prompt[0];
+    if (token < 0 || token >= c->vocab_size) token = 0;
+    int prompt_index = 1, generated = 0, rc = 0;
+    for (int pos = 0; pos < cache_cap; pos++) {
+        rc = glm_cpu_forward_token(&rt, &st, token, pos, 0);
+        if (rc != 0) break;
+        int next;
+        if (prompt_index < n_prompt) {
+            next = prompt[prompt_index++];
+            if (next < 0 || next >= c->vocab_size) next = 0;
+        } else {
+            next = argmax(st.logits, c->vocab_size);
+            out_ids[generated++] = next;
+            if (generated >= n_gen) break;
+        }
+        token = next;
+    }
+    runstate_free(&st);
+    runtime_close(&rt);
+    return rc;
+}

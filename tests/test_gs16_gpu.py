@@ -69,3 +69,38 @@ def test_gs16_decoder_small(lib, pkg, oracle_mod):
         tok = int(feed[pos])
     print(f"gs16 decoder: worst logits rel L2 {worst:.2e}")
     assert worst <= 1e-3
+
+
+@pytest.mark.parametrize("gs", [32, 16])
+def test_checkpoint_file_decodes_like_glm(gs, lib, pkg, oracle_mod, tmp_path):
+    """A .bin written in glm.c's format: glm_cuda_load_checkpoint + generate
+    gives the greedy ids of glm.c's own loader and forward pass on the file."""
+    from bin_writer import write_runtime_bin
+    from test_decoder_gpu import SMALL
+
+    synth = pkg.synth
+    dims = dict(SMALL, group_size=gs)
+    model = synth.decoder_model(23, **dims)
+    prompt = synth.prompt_ids(23, 8, dims["vocab_size"])
+    path = str(tmp_path / "model.bin")
+    write_runtime_bin(model, path)
+    ids_ref = oracle_mod.ref_decode_bin(path, prompt, 12, 32)
+    lib.load_checkpoint(path, 0, 32)
+    ids, _ = lib.generate(prompt, 12)
+    np.testing.assert_array_equal(ids, ids_ref)
+
+
+def test_checkpoint_config2_shapes(lib, pkg, oracle_mod, tmp_path):
+    """GLM-4.7-Flash shapes (3 layers, vocab 154880) through the .bin path."""
+    from bin_writer import write_runtime_bin
+
+    synth = pkg.synth
+    dims = dict(synth.CONFIG2, n_layers=3)
+    model = synth.decoder_model(24, **dims)
+    prompt = synth.prompt_ids(24, 8, dims["vocab_size"])
+    path = str(tmp_path / "model.bin")
+    write_runtime_bin(model, path)
+    ids_ref = oracle_mod.ref_decode_bin(path, prompt, 6, 24)
+    lib.load_checkpoint(path, 0, 24)
+    ids, _ = lib.generate(prompt, 6)
+    np.testing.assert_array_equal(ids, ids_ref)
