@@ -126,13 +126,14 @@ def _rank(rank, world, port, result_q):
         dist.destroy_process_group()
 
 
-def test_ep_exchange_two_ranks_matches_oracle():
+@pytest.mark.parametrize("world", [2, 4])
+def test_ep_exchange_ranks_match_oracle(world):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -141,13 +142,17 @@ def test_ep_exchange_two_ranks_matches_oracle():
         if p.is_alive():
             p.kill()
         assert p.exitcode == 0, f"rank exited with {p.exitcode}"
-    res = sorted(q.get(timeout=5) for _ in range(2))
+    res = sorted(q.get(timeout=5) for _ in range(world))
     for rank, err, last in res:
-        assert err < 1e-5, f"rank {rank}: relative max error {err}"
+        # the stand-in's SiLU runs in float64: last-bit differences from
+        # glm.c's expf, magnified where the FFN output nearly cancels; a
+        # misrouted row or a wrong split gives errors of order 1
+        assert err < 1e-4, f"rank {rank}: relative max error {err}"
         assert sum(last["send_counts"]) == (5 + 3 * rank) * CFG["k_used"]
-    # what rank 0 sent to rank 1 is what rank 1 received from rank 0
-    assert res[0][2]["send_counts"][1] == res[1][2]["recv_counts"][0]
-    assert res[1][2]["send_counts"][0] == res[0][2]["recv_counts"][1]
+    # what rank a sent to rank b is what rank b received from rank a
+    for a in range(world):
+        for b in range(world):
+            assert res[a][2]["send_counts"][b] == res[b][2]["recv_counts"][a]
 
 
 def test_shard_layer_cuts_routed_blocks(pkg):
