@@ -403,8 +403,11 @@ def run_prefill_leg(args, torch, pkg, lib, layers, dev, local, rank, world) -> d
 
 def run_ep_leg(args, torch, pkg, lib, layers, dev, local, rank, world) -> dict:
     """4096 tokens (split evenly over the ranks) through
-    8 stacked config-0 MoE layers, experts sharded over the ranks, dispatch
-    and combine by all-to-all; tokens/s and the exposed exchange time."""
+    8 stacked config-0 MoE layers, experts sharded over the ranks. Both
+    exchanges are timed on the same inputs: the kernels' own stores into the
+    other ranks' peer regions (PeerExpertParallelMoE, the headline value with
+    --ep-exchange p2p) and NCCL all-to-all with a host copy of the splits
+    (ExpertParallelMoE); their outputs must agree bit for bit."""
     import numpy as np
     import torch.distributed as dist
 
@@ -420,59 +423,89 @@ def run_ep_leg(args, torch, pkg, lib, layers, dev, local, rank, world) -> dict:
             L[name] = L[name][rank * e_loc:(rank + 1) * e_loc]
         lib.bind_moe_layer_device(li, L)
         shards.append(L)
-    moe = pkg.ep.ExpertParallelMoE(lib, D, K, T, device=dev)
+    a2a = pkg.ep.ExpertParallelMoE(lib, D, K, T, device=dev)
+    p2p = pkg.ep.PeerExpertParallelMoE(lib, world, rank)
     gen = torch.Generator(device=dev)
     gen.manual_seed(args.seed * 13 + rank)
     x0 = torch.randn(T, D, generator=gen, device=dev)
     x = torch.empty_like(x0)
 
-    def step():
-        x.copy_(x0)
-        for li in range(n_layers):
-            moe.layer(li, x)
+    def time_steps(layer_fn) -> float:
+        def step():
+            x.copy_(x0)
+            for li in range(n_layers):
+                layer_fn(li, x)
 
-    for _ in range(2):
-        step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    a = torch.cuda.Event(enable_timing=True)
-    b = torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(args.ep_steps):
-        step()
-    b.record()
-    torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / args.ep_steps
-    # phase breakdown of one more step: exchange (counts + rows + back) vs kernels
+        for _ in range(2):
+            step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.ep_steps):
+            step()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / args.ep_steps
+
+    ms_a2a = time_steps(a2a.layer)
+    out_a2a = x.clone()
+    ms_p2p = time_steps(p2p.layer)
+    lib.ep_status()
+    same = bool(torch.equal(x, out_a2a))
+    # phase breakdowns of one more step each
     x.copy_(x0)
-    phase = np.zeros(5)
+    ph_a = np.zeros(5)
     for li in range(n_layers):
         evs = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
-        moe.layer_timed(li, x, evs)
+        a2a.layer_timed(li, x, evs)
         torch.cuda.synchronize()
-        phase += [evs[i].elapsed_time(evs[i + 1]) for i in range(5)]
+        ph_a += [evs[i].elapsed_time(evs[i + 1]) for i in range(5)]
+    x.copy_(x0)
+    ph_p = np.zeros(3)
+    for li in range(n_layers):
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        p2p.layer_timed(li, x, evs)
+        torch.cuda.synchronize()
+        ph_p += [evs[i].elapsed_time(evs[i + 1]) for i in range(3)]
     lib.ep_status()
-    comm = float(phase[1] + phase[3])
+    counts = p2p.counts()
+    comm_a = float(ph_a[1] + ph_a[3])
+    tot_a = float(ph_a.sum())
     if world > 1:
-        t = torch.tensor([ms, comm, float(phase.sum())], device=dev)
+        t = torch.tensor([ms_a2a, ms_p2p, comm_a, tot_a, 0.0 if same else 1.0], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, comm, tot = (float(v) for v in t.tolist())
-    else:
-        tot = float(phase.sum())
+        ms_a2a, ms_p2p, comm_a, tot_a = (float(v) for v in t.tolist()[:4])
+        same = t.tolist()[4] == 0.0
+    ms = ms_p2p if args.ep_exchange == "p2p" else ms_a2a
     out = {"metric": f"EP prefill tok/s (config 4: {args.ep_tokens} tokens x {n_layers} config-0 MoE layers, "
                      "experts sharded)",
            "value": round(args.ep_tokens / (ms / 1e3), 1), "unit": "tok/s", "ms_per_step": round(ms, 3),
            "n_gpus": world, "tokens_per_rank": T, "layers": n_layers, "experts_per_rank": e_loc,
            "steps": args.ep_steps, "scaling": "strong (4096 tokens in total)",
-           "exposed_comm_fraction": round(comm / max(tot, 1e-9), 4),
-           "phase_ms_rank0": {"dispatch": round(float(phase[0]), 3), "exchange": round(float(phase[1]), 3),
-                              "experts": round(float(phase[2]), 3), "exchange_back": round(float(phase[3]), 3),
-                              "combine": round(float(phase[4]), 3)},
-           "exchange": "torch.distributed all_to_all_single (NCCL) of per-rank row counts, rows and expert ids; "
-                       "rows back the same way",
-           "last_layer_rows": moe.last}
+           "exchange": args.ep_exchange,
+           "p2p": {"value": round(args.ep_tokens / (ms_p2p / 1e3), 1), "ms_per_step": round(ms_p2p, 3),
+                   "how": "the kernels store rows, expert ids and counts into the expert owner's peer region "
+                          "(IPC-mapped, NVLink) and the outputs back into the sender's; a flag per rank pair, "
+                          "no collective, no host round trip",
+                   "phase_ms_rank0": {"route_pack_push": round(float(ph_p[0]), 3),
+                                      "wait_rows_experts_push_back": round(float(ph_p[1]), 3),
+                                      "wait_outputs_combine": round(float(ph_p[2]), 3)}},
+           "nccl": {"value": round(args.ep_tokens / (ms_a2a / 1e3), 1), "ms_per_step": round(ms_a2a, 3),
+                    "how": "torch.distributed all_to_all_single (NCCL) of per-rank row counts (host copy of the "
+                           "splits), rows and expert ids; rows back the same way",
+                    "exposed_comm_fraction": round(comm_a / max(tot_a, 1e-9), 4),
+                    "phase_ms_rank0": {"dispatch": round(float(ph_a[0]), 3), "exchange": round(float(ph_a[1]), 3),
+                                       "experts": round(float(ph_a[2]), 3),
+                                       "exchange_back": round(float(ph_a[3]), 3),
+                                       "combine": round(float(ph_a[4]), 3)}},
+           "p2p_equals_nccl_bitwise": same,
+           "last_layer_rows": counts}
+    if world > 1:
+        dist.barrier()  # no rank frees its peer region while another may still store into it
     lib.free()
     return out
 
@@ -800,6 +833,8 @@ def main() -> None:
     ap.add_argument("--ep-tokens", type=int, default=4096)
     ap.add_argument("--ep-layers", type=int, default=8)
     ap.add_argument("--ep-steps", type=int, default=5)
+    ap.add_argument("--ep-exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="which EP exchange the headline EP value uses (both are timed)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -18,7 +18,7 @@ INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libglm_cuda.so")
 
 SOURCES = ["glm_cuda.cu", "moe_decode.cu", "moe_persistent.cu", "q80_matvec.cu", "moe_noalloc.cu", "decoder.cu", "moe_prefill.cu", "checkpoint.cu"]
-HEADERS = ["glm_internal.h", "q80_common.cuh", "route_common.cuh"]
+HEADERS = ["glm_internal.h", "q80_common.cuh", "route_common.cuh", "glm_cuda.map"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -50,7 +50,8 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
     if not force and not ptxas_info and up_to_date():
         return LIB
     host_cc = "/usr/bin/g++" if os.path.exists("/usr/bin/g++") else None
-    cmd = [nvcc(), *NVCC_FLAGS, "-I", INCLUDE, "-I", CSRC, "-shared", "-o", LIB + ".tmp"]
+    cmd = [nvcc(), *NVCC_FLAGS, "-I", INCLUDE, "-I", CSRC, "-shared", "-o", LIB + ".tmp",
+           "-Xlinker", "--version-script=" + os.path.join(CSRC, "glm_cuda.map")]
     if host_cc:
         cmd += ["-ccbin", host_cc]
     if ptxas_info:

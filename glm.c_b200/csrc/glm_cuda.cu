@@ -112,6 +112,13 @@ struct State {
     glmq::EpShape ep{};
     unsigned char* ep_ws = nullptr;
     int ep_layer = -1, ep_T = 0, ep_nrecv = -1;  // the layer in flight
+    // expert parallelism over peer memory (glm_cuda_ep_peer_*, glm_cuda_ep_p2p_*)
+    unsigned char* ep_region = nullptr;  // this rank's peer region (cudaMalloc, IPC-exportable)
+    std::vector<void*> ep_opened;        // peers' regions opened with cudaIpcOpenMemHandle
+    glmq::EpPeers ep_peers{};
+    bool ep_connected = false;
+    unsigned ep_epoch = 0;               // layer calls so far; flags carry it
+    int ep_p2p_stage = 0;                // 0 idle, 1 dispatched, 2 experts done
     Model m;
 };
 
@@ -167,6 +174,19 @@ void release_model() {
     g.m = Model{};
 }
 
+// Close the peers' regions and free this rank's (the peers must have
+// stopped using it: the caller's process group agrees on that).
+void release_ep_peers() {
+    for (void* p : g.ep_opened) cudaIpcCloseMemHandle(p);
+    g.ep_opened.clear();
+    if (g.ep_region) cudaFree(g.ep_region);
+    g.ep_region = nullptr;
+    g.ep_peers = glmq::EpPeers{};
+    g.ep_connected = false;
+    g.ep_epoch = 0;
+    g.ep_p2p_stage = 0;
+}
+
 void release_all() {
     release_model();
     for (auto& L : g.layers) release_layer(L);
@@ -182,6 +202,7 @@ void release_all() {
                     g.layers_dev,     g.pf_ws,         g.ep_ws};
     for (void* p : bufs)
         if (p) cudaFree(p);
+    release_ep_peers();
     g.ep_ws = nullptr;
     g.ep_shards = 1;
     g.ep_shard = 0;
@@ -219,6 +240,9 @@ int take_device_status() {
     cudaMemsetAsync(g.scratch.status, 0, sizeof(unsigned int), g.stream);
     // a launch that gave up may have left its barrier words set: clear them
     cudaMemsetAsync(g.scratch.grid_bar, 0, 2 * sizeof(unsigned int), g.stream);
+    if (st & 128u)
+        return fail(GLM_CUDA_ERR_CUDA, "a peer rank did not answer within 4 s (expert-parallel exchange, status 0x%x)",
+                    st);
     return fail(GLM_CUDA_ERR_CUDA, "the decode kernel gave up waiting (status 0x%x)", st);
 }
 
@@ -581,7 +605,10 @@ int glm_cuda_ep_setup(int n_shards, int shard, int max_tokens) {
     e.n_recv_cap = n_shards * max_tokens * (g.dims.K < e.e_local ? g.dims.K : e.e_local);
     if (g.ep_ws) cudaFree(g.ep_ws);
     g.ep_ws = nullptr;
-    if (int rc = dev_alloc(&g.ep_ws, glmq::ep_workspace_bytes(e))) return rc;
+    release_ep_peers();
+    const size_t ws_bytes = glmq::ep_workspace_bytes(e);
+    if (int rc = dev_alloc(&g.ep_ws, ws_bytes)) return rc;
+    CUDA_TRY(cudaMemset(g.ep_ws, 0, ws_bytes));  // the push / scatter-back kernels' last-CTA counters start at 0
     g.ep = e;
     g.ep_shards = n_shards;
     g.ep_shard = shard;
@@ -641,6 +668,151 @@ int glm_cuda_ep_combine(int layer, float* x_dev, const float* back_rows_dev, int
     g.launches += 1;
     if (e != cudaSuccess) return fail(GLM_CUDA_ERR_CUDA, "ep combine launch: %s", cudaGetErrorString(e));
     g.ep_layer = -1;
+    return 0;
+}
+
+// The shape this rank's peer region is laid out for; every rank's must match.
+// (static: a second copy of this library loaded in the same process must
+// not bind to the first copy's function, which reads the first copy's state)
+static glmq::EpRegionHeader own_region_header() {
+    const glmq::EpRegion R = glmq::ep_region_layout(g.ep);
+    glmq::EpRegionHeader h{};
+    h.magic = glmq::kEpRegionMagic;
+    h.n_shards = g.ep.n_shards;
+    h.cap = R.cap;
+    h.D = g.ep.D;
+    h.K = g.ep.K;
+    h.e_local = g.ep.e_local;
+    h.T_max = g.ep.T_max;
+    h.bytes = R.bytes;
+    return h;
+}
+
+int glm_cuda_ep_peer_region(void** region_dev_out, void* ipc_handle_out) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.ep_ws) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_ep_setup has not been called");
+    if (!g.ep_region) {
+        const glmq::EpRegion R = glmq::ep_region_layout(g.ep);
+        if (int rc = dev_alloc(&g.ep_region, R.bytes)) return rc;
+        CUDA_TRY(cudaMemset(g.ep_region, 0, R.bytes));  // counts 0, flags at epoch 0
+        const glmq::EpRegionHeader h = own_region_header();
+        CUDA_TRY(cudaMemcpy(g.ep_region + R.header, &h, sizeof h, cudaMemcpyHostToDevice));
+    }
+    if (region_dev_out) *region_dev_out = g.ep_region;
+    if (ipc_handle_out) {
+        cudaIpcMemHandle_t h;
+        CUDA_TRY(cudaIpcGetMemHandle(&h, g.ep_region));
+        static_assert(sizeof(h) == GLM_CUDA_IPC_HANDLE_BYTES, "IPC handle size");
+        memcpy(ipc_handle_out, &h, sizeof h);
+    }
+    return 0;
+}
+
+int glm_cuda_ep_peer_open(const void* ipc_handle, void** region_dev_out) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_init has not been called");
+    if (!ipc_handle || !region_dev_out) return fail(GLM_CUDA_ERR_ARG, "ep_peer_open: NULL argument");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, ipc_handle, sizeof h);
+    void* p = nullptr;
+    CUDA_TRY(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+    g.ep_opened.push_back(p);
+    *region_dev_out = p;
+    return 0;
+}
+
+int glm_cuda_ep_peer_connect(void* const* regions) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.ep_ws || !g.ep_region)
+        return fail(GLM_CUDA_ERR_STATE, "glm_cuda_ep_setup and glm_cuda_ep_peer_region come first");
+    if (!regions) return fail(GLM_CUDA_ERR_ARG, "ep_peer_connect: regions must be non-NULL");
+    if (regions[g.ep_shard] != g.ep_region)
+        return fail(GLM_CUDA_ERR_ARG, "ep_peer_connect: entry %d must be this rank's own region", g.ep_shard);
+    glmq::EpPeers p{};
+    const glmq::EpRegionHeader mine = own_region_header();
+    const size_t hdr_off = glmq::ep_region_layout(g.ep).header;
+    for (int d = 0; d < g.ep_shards; ++d) {
+        if (!regions[d] || (reinterpret_cast<uintptr_t>(regions[d]) & 255u))
+            return fail(GLM_CUDA_ERR_ARG, "ep_peer_connect: region %d is NULL or not 256-byte aligned", d);
+        // every rank's region must have this rank's layout, or the kernels'
+        // stores into it would land outside it
+        glmq::EpRegionHeader h{};
+        CUDA_TRY(cudaMemcpy(&h, static_cast<unsigned char*>(regions[d]) + hdr_off, sizeof h, cudaMemcpyDefault));
+        if (memcmp(&h, &mine, sizeof h) != 0)
+            return fail(GLM_CUDA_ERR_ARG,
+                        "ep_peer_connect: region %d was laid out for another shape (n_shards %d, max_tokens %d, "
+                        "dim %d; this rank: %d, %d, %d)", d, h.n_shards, h.T_max, h.D, mine.n_shards, mine.T_max,
+                        mine.D);
+        p.base[d] = static_cast<unsigned char*>(regions[d]);
+    }
+    g.ep_peers = p;
+    g.ep_connected = true;
+    g.ep_p2p_stage = 0;
+    return 0;
+}
+
+int glm_cuda_ep_p2p_dispatch(int layer, const float* x_dev, int n_tokens, void* stream) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (int rc = check_layer(layer, true)) return rc;
+    if (!g.ep_connected) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_ep_peer_connect has not been called");
+    if (g.ep_p2p_stage != 0) return fail(GLM_CUDA_ERR_STATE, "ep_p2p_dispatch: the previous layer was not combined");
+    if (!x_dev || n_tokens < 1 || n_tokens > g.ep.T_max)
+        return fail(GLM_CUDA_ERR_ARG, "ep_p2p_dispatch: x_dev must be non-NULL and 1 <= n_tokens <= %d", g.ep.T_max);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : g.stream;
+    const unsigned epoch = g.ep_epoch + 1;
+    cudaError_t e = glmq::launch_ep_p2p_dispatch(g.layers[layer].w, g.dims, g.ep, g.ep_ws, x_dev, n_tokens,
+                                                 routed_disabled_by_env() ? 0 : 1, g.num_sms, g.scratch.stats,
+                                                 g.ep_peers, g.ep_shard, epoch, st);
+    g.launches += 4;
+    if (e != cudaSuccess) return fail(GLM_CUDA_ERR_CUDA, "ep p2p dispatch launch: %s", cudaGetErrorString(e));
+    g.ep_epoch = epoch;
+    g.ep_layer = layer;
+    g.ep_T = n_tokens;
+    g.ep_p2p_stage = 1;
+    return 0;
+}
+
+int glm_cuda_ep_p2p_experts(int layer, void* stream) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (int rc = check_layer(layer, true)) return rc;
+    if (g.ep_p2p_stage != 1 || g.ep_layer != layer)
+        return fail(GLM_CUDA_ERR_STATE, "ep_p2p_experts: layer %d was not dispatched last", layer);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : g.stream;
+    glmq::MoeDims dl = g.dims;
+    dl.E = g.ep.e_local;
+    cudaError_t e = glmq::launch_ep_p2p_experts(g.layers[layer].w, dl, g.ep, g.ep_ws, g.ep_T,
+                                                routed_disabled_by_env() ? 0 : 1, g.num_sms, g.scratch.status,
+                                                g.ep_peers, g.ep_shard, g.ep_epoch, st);
+    g.launches += 6;
+    if (e != cudaSuccess) return fail(GLM_CUDA_ERR_CUDA, "ep p2p experts launch: %s", cudaGetErrorString(e));
+    g.ep_p2p_stage = 2;
+    return 0;
+}
+
+int glm_cuda_ep_p2p_combine(int layer, float* x_dev, int32_t* topk_idx_dev, float* topk_w_dev, void* stream) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (int rc = check_layer(layer, true)) return rc;
+    if (g.ep_p2p_stage != 2 || g.ep_layer != layer)
+        return fail(GLM_CUDA_ERR_STATE, "ep_p2p_combine: layer %d has not been through ep_p2p_experts", layer);
+    if (!x_dev) return fail(GLM_CUDA_ERR_ARG, "ep_p2p_combine: x_dev must be non-NULL");
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : g.stream;
+    cudaError_t e = glmq::launch_ep_p2p_combine(g.dims, g.ep, g.ep_ws, x_dev, g.ep_T, g.num_sms, g.scratch.status,
+                                                g.ep_peers, g.ep_shard, g.ep_epoch, st);
+    if (e == cudaSuccess) e = glmq::ep_copy_routing(g.ep, g.ep_ws, g.ep_T, topk_idx_dev, topk_w_dev, st);
+    g.launches += 2;
+    if (e != cudaSuccess) return fail(GLM_CUDA_ERR_CUDA, "ep p2p combine launch: %s", cudaGetErrorString(e));
+    g.ep_layer = -1;
+    g.ep_p2p_stage = 0;
+    return 0;
+}
+
+int glm_cuda_ep_p2p_counts(int32_t* send_counts, int32_t* recv_counts) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.ep_connected) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_ep_peer_connect has not been called");
+    if (!send_counts || !recv_counts) return fail(GLM_CUDA_ERR_ARG, "ep_p2p_counts: NULL argument");
+    CUDA_TRY(cudaDeviceSynchronize());  // the layer may have run on the caller's stream
+    cudaError_t e = glmq::ep_p2p_counts(g.ep, g.ep_ws, g.ep_region, send_counts, recv_counts, g.stream);
+    if (e != cudaSuccess) return fail(GLM_CUDA_ERR_CUDA, "ep p2p counts: %s", cudaGetErrorString(e));
     return 0;
 }
 

@@ -182,6 +182,56 @@ cudaError_t launch_ep_combine(const MoeDims& d, const EpShape& s, unsigned char*
 cudaError_t ep_copy_routing(const EpShape& s, unsigned char* ws, int T, int32_t* topk_idx, float* topk_w,
                             cudaStream_t st);
 
+// ---- expert parallelism over peer memory: every rank holds one "peer
+// region" of the same layout; senders write rows, ids and counts straight
+// into the receiver's region and raise a flag per (sender, receiver) pair;
+// the expert outputs go back the same way. Flags carry an epoch that grows
+// by one per layer call, so they never need resetting.
+constexpr int kEpMaxShards = 8;
+
+struct EpRegion {
+    int cap;                 // rows one sender may put in one receiver's region (T_max * min(K, e_local))
+    size_t header;           // EpRegionHeader: the shape the region was laid out for (checked on connect)
+    size_t recv_rows;        // [n_shards][cap][D] fp32: rows from sender s at [s][0 .. count)
+    size_t recv_expert;      // [n_shards][cap] int32 local expert id of each received row
+    size_t back_rows;        // [n_shards][cap][D] fp32: outputs of the rows this rank sent to d, at [d][j]
+    size_t recv_cnt;         // [n_shards] int32 rows from each sender
+    size_t flag_rows;        // [n_shards] u32: epoch of sender s's last completed row push
+    size_t flag_back;        // [n_shards] u32: epoch of receiver d's last completed output push
+    size_t bytes;
+};
+
+struct EpRegionHeader {
+    uint32_t magic;          // kEpRegionMagic
+    int32_t n_shards, cap, D, K, e_local, T_max;
+    uint32_t pad;
+    uint64_t bytes;
+};
+constexpr uint32_t kEpRegionMagic = 0x31525045u;  // "EPR1"
+
+struct EpPeers {
+    unsigned char* base[kEpMaxShards];  // every rank's region as this process addresses it
+};
+
+EpRegion ep_region_layout(const EpShape& s);
+// Route, pack and push this rank's rows into the receivers' regions.
+cudaError_t launch_ep_p2p_dispatch(const MoeLayerDev& w, const MoeDims& d, const EpShape& s, unsigned char* ws,
+                                   const float* x, int T, int routed, int num_sms, unsigned long long* stats,
+                                   const EpPeers& peers, int me, unsigned epoch, cudaStream_t st);
+// Wait for every sender's rows, run this rank's experts (and the shared
+// expert on its own tokens) and push the outputs back to their senders.
+cudaError_t launch_ep_p2p_experts(const MoeLayerDev& w, const MoeDims& dl, const EpShape& s, unsigned char* ws,
+                                  int T, int routed, int num_sms, unsigned* status, const EpPeers& peers, int me,
+                                  unsigned epoch, cudaStream_t st);
+// Wait for every receiver's outputs and combine them in rank order.
+cudaError_t launch_ep_p2p_combine(const MoeDims& d, const EpShape& s, unsigned char* ws, float* x, int T,
+                                  int num_sms, unsigned* status, const EpPeers& peers, int me, unsigned epoch,
+                                  cudaStream_t st);
+// Host copies of the last dispatch's per-destination send counts (ws) and
+// of the per-sender receive counts (this rank's region).
+cudaError_t ep_p2p_counts(const EpShape& s, unsigned char* ws, const unsigned char* region, int32_t* send_counts,
+                          int32_t* recv_counts, cudaStream_t st);
+
 cudaError_t launch_moe_prefill(const MoeLayerDev& w, const MoeDims& d, unsigned char* ws, float* x, int T,
                                int32_t* topk_idx, float* topk_w, int routed, int num_sms, unsigned* status,
                                unsigned long long* stats, cudaStream_t st);

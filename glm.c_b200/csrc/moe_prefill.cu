@@ -861,7 +861,7 @@ __global__ void prefill_combine_kernel(float* x, const float* __restrict__ Y, co
 // (plus the replicated shared expert on its own tokens), and gets the expert
 // outputs back in the order it sent them.
 
-constexpr int kMaxShards = 8;
+constexpr int kMaxShards = kEpMaxShards;
 
 // Send layout: pairs (t, k) in (token, slot) order within each destination,
 // destinations in rank order. One CTA; thread i owns a contiguous chunk of
@@ -941,21 +941,42 @@ __global__ void ep_pack_rows_kernel(const float* __restrict__ xn, const int* __r
 
 // Rows of the local expert GEMMs: received rows grouped by local expert
 // (groups 0 .. e_local - 1), then this rank's own tokens for the shared
-// expert (group e_local). Sources: s < n_recv -> received row s, else own
+// expert (group e_local). Sources: s < n_recv -> received slot s, else own
 // token s - n_recv. row_src[row] = source; pos_of_src[source] = row.
+// Received slots are [0, n_recv) when recv_cnt is null (the all-to-all
+// layout), else the first recv_cnt[q] of each sender q's cap slots
+// [q * cap, q * cap + cap) (the peer-region layout; n_recv = n_src * cap).
 __global__ void __launch_bounds__(1024) ep_group_kernel(const int32_t* __restrict__ recv_expert, int n_recv, int T,
                                                       int e_local, int routed, int mt1, int mt2, int* counts,
-                                                      int* row_src, int* pos_of_src, int4* items1, int4* items2) {
+                                                      int* row_src, int* pos_of_src, int4* items1, int4* items2,
+                                                      const int* recv_cnt, int n_src, int cap) {
     const int G = e_local + 1;
     __shared__ int cnt[kMaxGroups], off[kMaxGroups + 1], cur[kMaxGroups], toff[kMaxGroups + 1];
+    __shared__ int soff[kMaxShards + 1];
+    const int nseg = recv_cnt ? n_src : 1;
+    if (threadIdx.x == 0) {
+        int o = 0;
+        for (int q = 0; q < nseg; ++q) {
+            soff[q] = o;
+            o += recv_cnt ? min(max(__ldcg(recv_cnt + q), 0), cap) : n_recv;
+        }
+        soff[nseg] = o;
+    }
     for (int g = threadIdx.x; g < G; g += blockDim.x) {
         cnt[g] = g == e_local ? T : 0;
         cur[g] = 0;
     }
     __syncthreads();
+    const int n_rows = soff[nseg];
+    auto slot_of = [&](int m) {
+        if (!recv_cnt) return m;
+        int q = 0;
+        while (m >= soff[q + 1]) ++q;
+        return q * cap + (m - soff[q]);
+    };
     if (routed)
-        for (int i = threadIdx.x; i < n_recv; i += blockDim.x) {
-            const int e = recv_expert[i];
+        for (int m = threadIdx.x; m < n_rows; m += blockDim.x) {
+            const int e = recv_expert[slot_of(m)];
             if (e >= 0 && e < e_local) atomicAdd(&cnt[e], 1);
         }
     __syncthreads();
@@ -974,7 +995,8 @@ __global__ void __launch_bounds__(1024) ep_group_kernel(const int32_t* __restric
         counts[2] = to * mt2;
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < n_recv; i += blockDim.x) {
+    for (int m = threadIdx.x; m < n_rows; m += blockDim.x) {
+        const int i = slot_of(m);
         const int e = recv_expert[i];
         if (!routed || e < 0 || e >= e_local) {
             pos_of_src[i] = -1;
@@ -1282,6 +1304,126 @@ cudaError_t launch_moe_prefill(const MoeLayerDev& w, const MoeDims& d, unsigned 
     return cudaGetLastError();
 }
 
+// ---------------------------------------- expert parallelism, peer memory
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+constexpr uint64_t kEpWaitNs = 4000000000ull;  // a peer that has not answered in 4 s is taken as gone
+constexpr unsigned kStatEpPeer = 128u;
+
+// After every CTA's peer stores: the last CTA to finish raises flag `me` of
+// every rank's region (flag_off) to `epoch`, after storing `cnt[d]` into
+// slot `me` of the region's counts (cnt_off) when cnt is given. Every thread
+// of the CTA calls it once, after its own stores.
+__device__ void ep_signal_last(const EpPeers& peers, int n_shards, int me, size_t flag_off, size_t cnt_off,
+                               const int* cnt, unsigned* done, unsigned epoch) {
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    if (atomicAdd(done, 1u) != gridDim.x - 1) return;
+    __threadfence_system();
+    if (cnt)
+        for (int d = 0; d < n_shards; ++d)
+            reinterpret_cast<volatile int*>(peers.base[d] + cnt_off)[me] = cnt[d];
+    __threadfence_system();
+    for (int d = 0; d < n_shards; ++d) st_release_sys(reinterpret_cast<unsigned*>(peers.base[d] + flag_off) + me, epoch);
+    *reinterpret_cast<volatile unsigned*>(done) = 0u;  // for the next launch (stream order)
+}
+
+// Rows of the last pack into the receivers' regions: pair i = (t, k) sent
+// to rank d at position j of d's list lands in slot [me][j] of d's
+// recv_rows / recv_expert; send_pos[i] becomes d * cap + j, where d will put
+// the expert output in this rank's back_rows. One warp per pair.
+__global__ void ep_push_kernel(const float* __restrict__ xn, int* send_pos, const int32_t* __restrict__ ids,
+                               const int32_t* __restrict__ send_counts, int T, int K, int D, int e_local,
+                               int n_shards, int me, const __grid_constant__ EpPeers peers, EpRegion R, unsigned* done,
+                               unsigned epoch) {
+    __shared__ int base[kMaxShards];
+    __shared__ int cnt[kMaxShards];
+    if (threadIdx.x == 0) {
+        int o = 0;
+        for (int d = 0; d < n_shards; ++d) {
+            base[d] = o;
+            cnt[d] = send_counts[d];
+            o += cnt[d];
+        }
+    }
+    __syncthreads();
+    const int warps = (gridDim.x * blockDim.x) >> 5, lane = threadIdx.x & 31;
+    for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < T * K; i += warps) {
+        const int pos = send_pos[i];
+        if (pos < 0) continue;
+        const int e = ids[i], d = e / e_local, j = pos - base[d];
+        const size_t slot = (size_t)me * R.cap + j;
+        const float4* src = reinterpret_cast<const float4*>(xn + (size_t)(i / K) * D);
+        float4* dst = reinterpret_cast<float4*>(peers.base[d] + R.recv_rows) + slot * (size_t)(D / 4);
+        for (int c = lane; c < D / 4; c += 32) dst[c] = src[c];
+        if (lane == 0) {
+            reinterpret_cast<int32_t*>(peers.base[d] + R.recv_expert)[slot] = e - d * e_local;
+            send_pos[i] = d * R.cap + j;
+        }
+    }
+    ep_signal_last(peers, n_shards, me, R.flag_rows, R.recv_cnt, cnt, done, epoch);
+}
+
+// Lane q waits until flags[q] has reached `epoch` (bounded: kEpWaitNs, then
+// status bit kStatEpPeer and the kernel returns).
+__global__ void ep_wait_kernel(const unsigned* flags, int n, unsigned epoch, unsigned* status) {
+    const int q = threadIdx.x;
+    if (q >= n) return;
+    if ((int)(ld_acquire_sys(flags + q) - epoch) >= 0) return;
+    const uint64_t t0 = global_ns();
+    while ((int)(ld_acquire_sys(flags + q) - epoch) < 0) {
+        if (global_ns() - t0 > kEpWaitNs) {
+            atomicOr(status, kStatEpPeer);
+            return;
+        }
+        __nanosleep(256);
+    }
+}
+
+// Expert outputs back to their senders: received slot (q, j) -> row j of
+// back_rows[me] in q's region (zeros for a row no local expert took). One
+// warp per row; then flag_back[me] of every rank's region.
+__global__ void ep_scatter_back_kernel(const float* __restrict__ Y, const int* __restrict__ pos_of_src,
+                                       const int* recv_cnt, int n_shards, int D, int me,
+                                       const __grid_constant__ EpPeers peers, EpRegion R, unsigned* done,
+                                       unsigned epoch) {
+    __shared__ int soff[kMaxShards + 1];
+    if (threadIdx.x == 0) {
+        int o = 0;
+        for (int q = 0; q < n_shards; ++q) {
+            soff[q] = o;
+            o += min(max(__ldcg(recv_cnt + q), 0), R.cap);
+        }
+        soff[n_shards] = o;
+    }
+    __syncthreads();
+    const int warps = (gridDim.x * blockDim.x) >> 5, lane = threadIdx.x & 31;
+    for (int m = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; m < soff[n_shards]; m += warps) {
+        int q = 0;
+        while (m >= soff[q + 1]) ++q;
+        const int j = m - soff[q];
+        const int r = pos_of_src[q * R.cap + j];
+        float4* dst = reinterpret_cast<float4*>(peers.base[q] + R.back_rows) + ((size_t)me * R.cap + j) * (size_t)(D / 4);
+        if (r < 0) {
+            for (int c = lane; c < D / 4; c += 32) dst[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+            continue;
+        }
+        const float4* src = reinterpret_cast<const float4*>(Y + (size_t)r * D);
+        for (int c = lane; c < D / 4; c += 32) dst[c] = src[c];
+    }
+    ep_signal_last(peers, n_shards, me, R.flag_back, 0, nullptr, done, epoch);
+}
+
 // ------------------------------------------------------- expert parallelism
 
 namespace {
@@ -1299,6 +1441,9 @@ struct EpWs {
     int4* items2;
     __nv_bfloat16 *xhi, *xlo, *hhi, *hlo;
     float* y;           // [R_cap][D]
+    int32_t* send_counts;  // [kMaxShards] peer-memory path: rows for each receiver
+    int32_t* send_expert;  // [T_max][K]   peer-memory path: pack's scratch
+    unsigned* done;        // [2] last-CTA counters of the push and scatter-back kernels (zero between launches)
     size_t R_cap, bytes;
 };
 
@@ -1327,6 +1472,9 @@ EpWs ep_carve(unsigned char* base, const EpShape& s) {
     w.hhi = reinterpret_cast<__nv_bfloat16*>(take(R * s.F * 2));
     w.hlo = reinterpret_cast<__nv_bfloat16*>(take(R * s.F * 2));
     w.y = reinterpret_cast<float*>(take(R * s.D * 4));
+    w.send_counts = reinterpret_cast<int32_t*>(take(kMaxShards * 4));
+    w.send_expert = reinterpret_cast<int32_t*>(take((size_t)s.T_max * s.K * 4));
+    w.done = reinterpret_cast<unsigned*>(take(16));
     w.R_cap = R;
     w.bytes = b;
     return w;
@@ -1367,7 +1515,7 @@ cudaError_t launch_ep_experts(const MoeLayerDev& w, const MoeDims& dl, const EpS
     const bool use_routed = routed && w.gate_q && w.up_q && w.down_q;
     const int mt1 = dl.F / (kTM / 2), mt2 = dl.D / kTM;
     ep_group_kernel<<<1, 1024, 0, st>>>(recv_expert, n_recv, T, dl.E, use_routed ? 1 : 0, mt1, mt2, p.counts,
-                                        p.row_src, p.pos_of_src, p.items1, p.items2);
+                                        p.row_src, p.pos_of_src, p.items1, p.items2, nullptr, 0, 0);
     ep_gather_split_kernel<<<num_sms * 4, 256, 0, st>>>(recv_rows, p.xn, p.row_src, p.counts, n_recv, dl.D, p.xhi,
                                                         p.xlo);
     cudaError_t err = launch_grouped_ffn(w, dl, use_routed, p.R_cap, p.xhi, p.xlo, p.hhi, p.hlo, p.y, p.counts,
@@ -1384,6 +1532,94 @@ cudaError_t launch_ep_combine(const MoeDims& d, const EpShape& s, unsigned char*
     ep_combine_kernel<<<num_sms * 4, 256, 0, st>>>(x, p.y, p.pos_of_src, back_rows, p.send_pos, p.wts, T, d.D, d.K,
                                                    n_recv);
     return cudaGetLastError();
+}
+
+EpRegion ep_region_layout(const EpShape& s) {
+    EpRegion r{};
+    r.cap = s.n_recv_cap / s.n_shards;
+    size_t b = 0;
+    auto take = [&](size_t n) {
+        const size_t o = b;
+        b += (n + 255) & ~(size_t)255;
+        return o;
+    };
+    const size_t slots = (size_t)s.n_shards * r.cap;
+    r.header = take(sizeof(EpRegionHeader));
+    r.recv_rows = take(slots * s.D * 4);
+    r.recv_expert = take(slots * 4);
+    r.back_rows = take(slots * s.D * 4);
+    r.recv_cnt = take((size_t)s.n_shards * 4);
+    r.flag_rows = take((size_t)s.n_shards * 4);
+    r.flag_back = take((size_t)s.n_shards * 4);
+    r.bytes = b;
+    return r;
+}
+
+cudaError_t launch_ep_p2p_dispatch(const MoeLayerDev& w, const MoeDims& d, const EpShape& s, unsigned char* ws,
+                                   const float* x, int T, int routed, int num_sms, unsigned long long* stats,
+                                   const EpPeers& peers, int me, unsigned epoch, cudaStream_t st) {
+    if (T <= 0 || T > s.T_max || me < 0 || me >= s.n_shards) return cudaErrorInvalidValue;
+    const EpWs p = ep_carve(ws, s);
+    const EpRegion R = ep_region_layout(s);
+    PrefillRouteArgs ra{x, w.ffn_norm, w.router, w.router_bias, p.xn, p.ids, p.wts, stats, T, d.D, d.E, d.K,
+                        p.cen, p.bnd};
+    cudaError_t err = launch_route(ra, st);
+    if (err) return err;
+    ep_pack_kernel<<<1, 1024, 0, st>>>(p.ids, T, d.K, s.e_local, s.n_shards, routed && w.gate_q ? 1 : 0, p.send_pos,
+                                       p.send_counts, p.send_expert);
+    ep_push_kernel<<<num_sms * 2, 256, 0, st>>>(p.xn, p.send_pos, p.ids, p.send_counts, T, d.K, d.D, s.e_local,
+                                                s.n_shards, me, peers, R, p.done, epoch);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_p2p_experts(const MoeLayerDev& w, const MoeDims& dl, const EpShape& s, unsigned char* ws,
+                                  int T, int routed, int num_sms, unsigned* status, const EpPeers& peers, int me,
+                                  unsigned epoch, cudaStream_t st) {
+    if (T <= 0 || T > s.T_max || me < 0 || me >= s.n_shards) return cudaErrorInvalidValue;
+    const EpWs p = ep_carve(ws, s);
+    const EpRegion R = ep_region_layout(s);
+    unsigned char* own = peers.base[me];
+    const int n_slots = s.n_shards * R.cap;
+    const bool use_routed = routed && w.gate_q && w.up_q && w.down_q;
+    const int mt1 = dl.F / (kTM / 2), mt2 = dl.D / kTM;
+    ep_wait_kernel<<<1, 32, 0, st>>>(reinterpret_cast<const unsigned*>(own + R.flag_rows), s.n_shards, epoch, status);
+    const int* recv_cnt = reinterpret_cast<const int*>(own + R.recv_cnt);
+    ep_group_kernel<<<1, 1024, 0, st>>>(reinterpret_cast<const int32_t*>(own + R.recv_expert), n_slots, T, dl.E,
+                                        use_routed ? 1 : 0, mt1, mt2, p.counts, p.row_src, p.pos_of_src, p.items1,
+                                        p.items2, recv_cnt, s.n_shards, R.cap);
+    ep_gather_split_kernel<<<num_sms * 4, 256, 0, st>>>(reinterpret_cast<const float*>(own + R.recv_rows), p.xn,
+                                                        p.row_src, p.counts, n_slots, dl.D, p.xhi, p.xlo);
+    cudaError_t err = launch_grouped_ffn(w, dl, use_routed, p.R_cap, p.xhi, p.xlo, p.hhi, p.hlo, p.y, p.counts,
+                                         p.items1, p.items2, num_sms, status, st);
+    if (err) return err;
+    ep_scatter_back_kernel<<<num_sms * 2, 256, 0, st>>>(p.y, p.pos_of_src, recv_cnt, s.n_shards, dl.D, me, peers, R,
+                                                        p.done + 1, epoch);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_p2p_combine(const MoeDims& d, const EpShape& s, unsigned char* ws, float* x, int T,
+                                  int num_sms, unsigned* status, const EpPeers& peers, int me, unsigned epoch,
+                                  cudaStream_t st) {
+    if (T <= 0 || T > s.T_max || me < 0 || me >= s.n_shards) return cudaErrorInvalidValue;
+    const EpWs p = ep_carve(ws, s);
+    const EpRegion R = ep_region_layout(s);
+    unsigned char* own = peers.base[me];
+    ep_wait_kernel<<<1, 32, 0, st>>>(reinterpret_cast<const unsigned*>(own + R.flag_back), s.n_shards, epoch, status);
+    ep_combine_kernel<<<num_sms * 4, 256, 0, st>>>(x, p.y, p.pos_of_src, reinterpret_cast<const float*>(own + R.back_rows),
+                                                   p.send_pos, p.wts, T, d.D, d.K, s.n_shards * R.cap);
+    return cudaGetLastError();
+}
+
+cudaError_t ep_p2p_counts(const EpShape& s, unsigned char* ws, const unsigned char* region, int32_t* send_counts,
+                          int32_t* recv_counts, cudaStream_t st) {
+    const EpWs p = ep_carve(ws, s);
+    const EpRegion R = ep_region_layout(s);
+    cudaError_t err = cudaMemcpyAsync(send_counts, p.send_counts, sizeof(int32_t) * s.n_shards,
+                                      cudaMemcpyDeviceToHost, st);
+    if (!err) err = cudaMemcpyAsync(recv_counts, region + R.recv_cnt, sizeof(int32_t) * s.n_shards,
+                                    cudaMemcpyDeviceToHost, st);
+    if (!err) err = cudaStreamSynchronize(st);
+    return err;
 }
 
 cudaError_t ep_copy_routing(const EpShape& s, unsigned char* ws, int T, int32_t* topk_idx, float* topk_w,

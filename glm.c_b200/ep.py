@@ -17,8 +17,10 @@ the shared expert are replicated. Per layer each rank
 
 which is apply_moe_shared_ffn_layer (infer.c:1087-1216) applied to every
 token, with the expert products on the ranks that hold the experts. The
-kernels are the library's (`kernels` is a GlmCuda); the exchange is
-torch.distributed's all_to_all_single on the same stream (NCCL on GPUs).
+kernels are the library's (`kernels` is a GlmCuda). ExpertParallelMoE
+exchanges with torch.distributed's all_to_all_single on the same stream
+(NCCL on GPUs; any backend on CPU); PeerExpertParallelMoE lets the kernels
+store into the other ranks' memory instead (GPUs with peer access).
 """
 from __future__ import annotations
 
@@ -112,6 +114,78 @@ class ExpertParallelMoE:
         self.k.ep_combine(layer, x, self.back_rows, None, None, stream=st)
         events[5].record()
         self.last = {"n_send": n_send, "n_recv": n_recv, "send_counts": sc, "recv_counts": rc}
+
+
+class PeerExpertParallelMoE:
+    """The same layer with the exchange done by the library's kernels over
+    peer memory (glm_cuda_ep_peer_* / glm_cuda_ep_p2p_*): the rows, the
+    expert ids, the counts and the outputs travel by stores into the other
+    ranks' peer regions (NVLink), with a flag per pair of ranks; no
+    collective and no host round trip per layer. The process group is used
+    once, to swap the regions' IPC handles.
+
+    kernels: a GlmCuda on which ep_setup(world, rank, max_tokens) was called
+    (max_tokens equal on every rank). regions: every rank's region address
+    as this process sees it, to connect two library instances of one
+    process directly; None swaps IPC handles over the process group.
+    connect=False leaves the connection to a later connect(regions).
+    """
+
+    def __init__(self, kernels, world: int, rank: int, group=None, regions=None, connect: bool = True):
+        self.k = kernels
+        self.world = world
+        self.rank = rank
+        self.group = group
+        self.region, self.handle = kernels.ep_peer_region()
+        self.last = {}
+        if connect:
+            self.connect(regions if regions is not None else self._swap_handles())
+
+    def _swap_handles(self) -> list[int]:
+        if self.world == 1:
+            return [self.region]
+        import torch.distributed as dist
+
+        handles = [None] * self.world
+        dist.all_gather_object(handles, self.handle, group=self.group)
+        return [self.region if r == self.rank else self.k.ep_peer_open(handles[r]) for r in range(self.world)]
+
+    def connect(self, regions: list[int]) -> None:
+        self.k.ep_peer_connect(list(regions))
+
+    @staticmethod
+    def _stream():
+        import torch
+
+        handle = torch.cuda.current_stream().cuda_stream
+        return handle if handle else 1  # cudaStreamLegacy for torch's default stream
+
+    def layer(self, layer: int, x, idx=None, w=None) -> None:
+        """x [T][dim] (this rank's tokens, device, in place) through MoE layer `layer`."""
+        st = self._stream()
+        self.k.ep_p2p_dispatch(layer, x, x.shape[0], stream=st)
+        self.k.ep_p2p_experts(layer, stream=st)
+        self.k.ep_p2p_combine(layer, x, idx, w, stream=st)
+
+    def layer_timed(self, layer: int, x, events: list) -> None:
+        """layer() with CUDA events between its phases: events[0..3] = before
+        dispatch, after dispatch (rows pushed), after the experts (outputs
+        pushed; includes waiting for the other ranks' rows), after combine
+        (includes waiting for the outputs)."""
+        st = self._stream()
+        events[0].record()
+        self.k.ep_p2p_dispatch(layer, x, x.shape[0], stream=st)
+        events[1].record()
+        self.k.ep_p2p_experts(layer, stream=st)
+        events[2].record()
+        self.k.ep_p2p_combine(layer, x, None, None, stream=st)
+        events[3].record()
+
+    def counts(self) -> dict:
+        """Rows sent to / received from every rank in the last layer (synchronises)."""
+        sc, rc = self.k.ep_p2p_counts(self.world)
+        self.last = {"n_send": sum(sc), "n_recv": sum(rc), "send_counts": sc, "recv_counts": rc}
+        return self.last
 
 
 def shard_layer(layer: dict, n_shards: int, shard: int) -> dict:

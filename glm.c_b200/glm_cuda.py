@@ -65,6 +65,13 @@ def _signatures(L: ctypes.CDLL) -> None:
     L.glm_cuda_ep_experts.argtypes = [_I, _P, _P, _I, _P, _P]
     L.glm_cuda_ep_combine.argtypes = [_I, _P, _P, _P, _P, _P]
     L.glm_cuda_ep_status.argtypes = []
+    L.glm_cuda_ep_peer_region.argtypes = [_P, _P]
+    L.glm_cuda_ep_peer_open.argtypes = [_P, _P]
+    L.glm_cuda_ep_peer_connect.argtypes = [_P]
+    L.glm_cuda_ep_p2p_dispatch.argtypes = [_I, _P, _I, _P]
+    L.glm_cuda_ep_p2p_experts.argtypes = [_I, _P]
+    L.glm_cuda_ep_p2p_combine.argtypes = [_I, _P, _P, _P, _P]
+    L.glm_cuda_ep_p2p_counts.argtypes = [_P, _P]
     L.glm_cuda_load_checkpoint.argtypes = [ctypes.c_char_p, _I, _I]
     L.glm_cuda_moe_layer_noalloc.argtypes = [_P] * 15 + [_I] * 5 + [_P, _I, _P, _P, _P]
     L.glm_cuda_moe_layer_noalloc.restype = _I
@@ -83,6 +90,9 @@ def _signatures(L: ctypes.CDLL) -> None:
                  "glm_cuda_moe_layers_async", "glm_cuda_set_decode_path", "glm_cuda_decode_path",
                  "glm_cuda_set_prefill_tokens", "glm_cuda_ep_setup", "glm_cuda_ep_dispatch", "glm_cuda_ep_experts",
                  "glm_cuda_ep_combine", "glm_cuda_ep_status", "glm_cuda_load_checkpoint",
+                 "glm_cuda_ep_peer_region", "glm_cuda_ep_peer_open", "glm_cuda_ep_peer_connect",
+                 "glm_cuda_ep_p2p_dispatch", "glm_cuda_ep_p2p_experts", "glm_cuda_ep_p2p_combine",
+                 "glm_cuda_ep_p2p_counts",
                  "glm_cuda_model_init", "glm_cuda_upload_model_globals", "glm_cuda_bind_model_globals_device",
                  "glm_cuda_upload_attn_layer", "glm_cuda_bind_attn_layer_device", "glm_cuda_forward_token",
                  "glm_cuda_generate",
@@ -239,6 +249,46 @@ class GlmCuda:
 
     def ep_status(self) -> None:
         self._check("glm_cuda_ep_status", self.L.glm_cuda_ep_status())
+
+    # ---- expert parallelism over peer memory
+    IPC_HANDLE_BYTES = 64
+
+    def ep_peer_region(self) -> tuple[int, bytes]:
+        """(device address, IPC handle bytes) of this rank's peer region."""
+        ptr = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(self.IPC_HANDLE_BYTES)
+        self._check("glm_cuda_ep_peer_region",
+                    self.L.glm_cuda_ep_peer_region(ctypes.byref(ptr), ctypes.cast(handle, ctypes.c_void_p)))
+        return int(ptr.value), handle.raw
+
+    def ep_peer_open(self, handle: bytes) -> int:
+        """Map another rank's region (its IPC handle) into this process."""
+        buf = ctypes.create_string_buffer(bytes(handle), self.IPC_HANDLE_BYTES)
+        ptr = ctypes.c_void_p()
+        self._check("glm_cuda_ep_peer_open",
+                    self.L.glm_cuda_ep_peer_open(ctypes.cast(buf, ctypes.c_void_p), ctypes.byref(ptr)))
+        return int(ptr.value)
+
+    def ep_peer_connect(self, regions: list[int]) -> None:
+        arr = (ctypes.c_void_p * len(regions))(*regions)
+        self._check("glm_cuda_ep_peer_connect", self.L.glm_cuda_ep_peer_connect(ctypes.cast(arr, ctypes.c_void_p)))
+
+    def ep_p2p_dispatch(self, layer: int, x_dev, n_tokens: int, stream=None) -> None:
+        self._check("glm_cuda_ep_p2p_dispatch", self.L.glm_cuda_ep_p2p_dispatch(layer, _ptr(x_dev), n_tokens, stream))
+
+    def ep_p2p_experts(self, layer: int, stream=None) -> None:
+        self._check("glm_cuda_ep_p2p_experts", self.L.glm_cuda_ep_p2p_experts(layer, stream))
+
+    def ep_p2p_combine(self, layer: int, x_dev, idx_dev=None, w_dev=None, stream=None) -> None:
+        self._check("glm_cuda_ep_p2p_combine",
+                    self.L.glm_cuda_ep_p2p_combine(layer, _ptr(x_dev), _ptr(idx_dev), _ptr(w_dev), stream))
+
+    def ep_p2p_counts(self, n_shards: int) -> tuple[list[int], list[int]]:
+        """(rows sent to each rank, rows received from each rank) of the last layer."""
+        send = (ctypes.c_int32 * n_shards)()
+        recv = (ctypes.c_int32 * n_shards)()
+        self._check("glm_cuda_ep_p2p_counts", self.L.glm_cuda_ep_p2p_counts(send, recv))
+        return list(send), list(recv)
 
     def decode_path(self) -> int:
         rc = self.L.glm_cuda_decode_path()

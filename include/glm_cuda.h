@@ -137,6 +137,52 @@ int glm_cuda_ep_combine(int layer, float *x_dev, const float *back_rows_dev, int
 /* Synchronise and report a bounded wait that gave up in the ep kernels. */
 int glm_cuda_ep_status(void);
 
+/* ---- Expert parallelism over peer memory (NVLink), no host round trip.
+ * Same layer as glm_cuda_ep_dispatch / _experts / _combine with the exchange
+ * done by the kernels: every rank holds one "peer region" of the same layout
+ * (sized by glm_cuda_ep_setup's arguments, which must agree on every rank);
+ * the sender writes each (token, slot) row, its local expert id and the row
+ * counts straight into the receiver's region and raises a per-pair flag; the
+ * receiver's expert kernels wait for every sender's flag, and send the
+ * outputs back the same way. Flags carry the layer-call count, so the three
+ * calls below must be made in the same order on every rank, and no call is
+ * ever skipped on one rank. A peer that does not answer within 4 s makes the
+ * waiting kernel give up (glm_cuda_ep_status then returns GLM_CUDA_ERR_CUDA).
+ * The reference has no multi-GPU path; this replaces the all-to-all of the
+ * calls above (infer.c:1166-1195 per token, with the expert products on the
+ * rank that holds the expert). */
+
+#define GLM_CUDA_IPC_HANDLE_BYTES 64
+
+/* Allocate (once) this rank's peer region; *region_dev_out receives its
+ * device address, ipc_handle_out (may be NULL) GLM_CUDA_IPC_HANDLE_BYTES of
+ * cudaIpcMemHandle_t for the other ranks' glm_cuda_ep_peer_open. */
+int glm_cuda_ep_peer_region(void **region_dev_out, void *ipc_handle_out);
+
+/* Map another rank's region (its IPC handle) into this process. */
+int glm_cuda_ep_peer_open(const void *ipc_handle, void **region_dev_out);
+
+/* regions[n_shards]: every rank's region as this process addresses it
+ * (regions[shard] = this rank's own). Two library instances in one process
+ * may pass each other's region addresses directly. */
+int glm_cuda_ep_peer_connect(void *const *regions);
+
+/* Route x_dev[n_tokens][dim], pack, push the rows to their experts' ranks. */
+int glm_cuda_ep_p2p_dispatch(int layer, const float *x_dev, int n_tokens, void *stream);
+
+/* Wait for every rank's rows, run this rank's experts (and the shared
+ * expert on its own tokens), push the outputs back to their senders. */
+int glm_cuda_ep_p2p_experts(int layer, void *stream);
+
+/* Wait for every rank's outputs; x_dev += shared + sum_k 1.8 w_k y_k in rank
+ * order (infer.c:1175-1214); topk outputs (may be NULL) as in
+ * glm_cuda_moe_layer. */
+int glm_cuda_ep_p2p_combine(int layer, float *x_dev, int32_t *topk_idx_dev, float *topk_w_dev, void *stream);
+
+/* Host copies (synchronising the device) of the last dispatch's rows per
+ * receiver and of the rows received from each sender, [n_shards] each. */
+int glm_cuda_ep_p2p_counts(int32_t *send_counts, int32_t *recv_counts);
+
 /* Calls of glm_cuda_moe_layer / _async with n_tokens >= min_tokens run the
  * batched prefill kernels instead of the per-token decode kernels: exact
  * routing of all tokens in one launch, then the routed and shared experts

@@ -45,6 +45,17 @@ def main():
     worst = check_moe_outputs(x, xd.cpu().numpy(), ref, 1e-3)
     print(f"EP-OK rank {rank} worst {worst:.2e} sent {moe.last['send_counts']} recv {moe.last['recv_counts']}",
           flush=True)
+    # the same layer over peer memory (IPC-mapped regions): bit-identical
+    pm = pkg.ep.PeerExpertParallelMoE(lib, world, rank)
+    for _ in range(2):
+        xp = torch.from_numpy(x.copy()).to(dev)
+        ip = torch.zeros((T, 4), dtype=torch.int32, device=dev)
+        pm.layer(0, xp, ip)
+        lib.ep_status()
+        assert torch.equal(xp, xd) and torch.equal(ip, idx)
+    last = pm.counts()
+    assert last["send_counts"] == moe.last["send_counts"] and last["recv_counts"] == moe.last["recv_counts"]
+    print(f"EP-P2P-OK rank {rank}", flush=True)
     dist.barrier()
     lib.free()
     dist.destroy_process_group()

@@ -119,6 +119,88 @@ def test_ep_two_shards_one_gpu(cfg, T, torch_cuda, pkg, oracle_mod, tmp_path):
         lib.free()
 
 
+def test_ep_p2p_one_shard_matches_alltoall_path(torch_cuda, pkg, oracle_mod):
+    """The peer-memory exchange (one shard: the rank pushes into its own
+    region) gives bit-identical outputs, ids and weights to the all-to-all
+    path, over several layer calls (the flags' epochs advance)."""
+    torch = torch_cuda
+    synth = pkg.synth
+    L = synth.moe_layer(seed=5, zipf=1.1, **synth.CONFIG0)
+    T = 256
+    x = synth.tokens(505, T, 2048)
+    lib = pkg.glm_cuda.GlmCuda()
+    lib.init(0, 2048, 1536, 64, 4, 32, 1)
+    lib.ep_setup(1, 0, T)
+    lib.upload_moe_layer(0, L)
+    dev = torch.device("cuda", 0)
+    a2a = pkg.ep.ExpertParallelMoE(lib, 2048, 4, T, device=dev)
+    xa = torch.from_numpy(x.copy()).cuda()
+    ia = torch.zeros((T, 4), dtype=torch.int32, device=dev)
+    wa = torch.zeros((T, 4), dtype=torch.float32, device=dev)
+    a2a.layer(0, xa, ia, wa)
+    p2p = pkg.ep.PeerExpertParallelMoE(lib, 1, 0)
+    for _ in range(3):
+        xp = torch.from_numpy(x.copy()).cuda()
+        ip = torch.zeros((T, 4), dtype=torch.int32, device=dev)
+        wp = torch.zeros((T, 4), dtype=torch.float32, device=dev)
+        p2p.layer(0, xp, ip, wp)
+        lib.ep_status()
+        assert torch.equal(xp, xa) and torch.equal(ip, ia) and torch.equal(wp, wa)
+    last = p2p.counts()
+    assert last["send_counts"] == [T * 4] and last["recv_counts"] == [T * 4]
+    ref, ref_idx, _ = oracle_mod.moe_layer(L, x, impl="orc")
+    np.testing.assert_array_equal(ip.cpu().numpy(), ref_idx)
+    worst = check_moe_outputs(x, xp.cpu().numpy(), ref, TOL)
+    print(f"ep p2p 1 shard: worst rel L2 {worst:.2e}")
+    lib.free()
+
+
+@pytest.mark.parametrize("cfg,T", [(dict(dim=512, ffn=256, n_experts=16, k_used=4, gs=32), (40, 23)),
+                                   (dict(dim=2048, ffn=1536, n_experts=64, k_used=4, gs=32), (200, 131))])
+def test_ep_p2p_two_shards_one_gpu(cfg, T, torch_cuda, pkg, oracle_mod, tmp_path):
+    """Shards 0 and 1 as two library instances on one GPU, connected through
+    each other's peer regions: each phase is issued for both shards before
+    the next phase, in one stream, so every wait is already satisfied when
+    it runs. Two layer calls (epochs 1 and 2)."""
+    torch = torch_cuda
+    synth, ep = pkg.synth, pkg.ep
+    L = synth.moe_layer(seed=6, zipf=1.1, **cfg)
+    D, K = cfg["dim"], cfg["k_used"]
+    xs = [synth.tokens(600 + r, T[r], D) for r in range(2)]
+    libs = [_lib_copy(pkg, tmp_path, f"libglm_p2p{r}.so") for r in range(2)]
+    for r, lib in enumerate(libs):
+        lib.init(0, D, cfg["ffn"], cfg["n_experts"], K, 32, 1)
+        lib.ep_setup(2, r, max(T))
+        lib.upload_moe_layer(0, ep.shard_layer(L, 2, r))
+    pms = [ep.PeerExpertParallelMoE(lib, 2, r, connect=False) for r, lib in enumerate(libs)]
+    regions = [pm.region for pm in pms]
+    for pm in pms:
+        pm.connect(regions)
+    for rep in range(2):
+        xd = [torch.from_numpy(xs[r].copy()).cuda() for r in range(2)]
+        idx = [torch.zeros(T[r], K, dtype=torch.int32, device="cuda") for r in range(2)]
+        for r, lib in enumerate(libs):
+            lib.ep_p2p_dispatch(0, xd[r], T[r], stream=LEGACY)
+        for r, lib in enumerate(libs):
+            lib.ep_p2p_experts(0, stream=LEGACY)
+        for r, lib in enumerate(libs):
+            lib.ep_p2p_combine(0, xd[r], idx[r], None, stream=LEGACY)
+        for lib in libs:
+            lib.ep_status()
+        for r in range(2):
+            ref, ref_idx, _ = oracle_mod.moe_layer(L, xs[r], impl="orc")
+            np.testing.assert_array_equal(idx[r].cpu().numpy(), ref_idx)
+            worst = check_moe_outputs(xs[r], xd[r].cpu().numpy(), ref, TOL)
+            print(f"ep p2p 2 shards call {rep} rank {r}: worst rel L2 {worst:.2e}")
+    c = [pm.counts() for pm in pms]
+    for a in range(2):
+        assert sum(c[a]["send_counts"]) == T[a] * K
+        for b in range(2):
+            assert c[a]["send_counts"][b] == c[b]["recv_counts"][a]
+    for lib in libs:
+        lib.free()
+
+
 def test_ep_single_rank_calls_refuse_sharded_layers(torch_cuda, pkg):
     import glm_c_b200.glm_cuda as gc
 
@@ -133,7 +215,9 @@ def test_ep_single_rank_calls_refuse_sharded_layers(torch_cuda, pkg):
 
 
 def test_ep_two_ranks_nccl(torch_cuda):
-    """Two ranks, one GPU each, NCCL all-to-all (skipped with fewer GPUs)."""
+    """Two ranks, one GPU each: the NCCL all-to-all exchange, then the
+    peer-memory exchange through IPC-mapped regions, bit-identical to it
+    (skipped with fewer GPUs)."""
     torch = torch_cuda
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
@@ -142,3 +226,4 @@ def test_ep_two_ranks_nccl(torch_cuda):
     r = subprocess.run(["timeout", "-k", "30", "600"] + cmd, capture_output=True, text=True, cwd=ROOT)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert r.stdout.count("EP-OK") == 2, r.stdout[-3000:]
+    assert r.stdout.count("EP-P2P-OK") == 2, r.stdout[-3000:]
