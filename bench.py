@@ -424,7 +424,6 @@ def run_ep_leg(args, torch, pkg, lib, layers, dev, local, rank, world) -> dict:
         lib.bind_moe_layer_device(li, L)
         shards.append(L)
     a2a = pkg.ep.ExpertParallelMoE(lib, D, K, T, device=dev)
-    p2p = pkg.ep.PeerExpertParallelMoE(lib, world, rank)
     gen = torch.Generator(device=dev)
     gen.manual_seed(args.seed * 13 + rank)
     x0 = torch.randn(T, D, generator=gen, device=dev)
@@ -453,10 +452,6 @@ def run_ep_leg(args, torch, pkg, lib, layers, dev, local, rank, world) -> dict:
 
     ms_a2a = time_steps(a2a.layer)
     out_a2a = x.clone()
-    ms_p2p = time_steps(p2p.layer)
-    lib.ep_status()
-    same = bool(torch.equal(x, out_a2a))
-    # phase breakdowns of one more step each
     x.copy_(x0)
     ph_a = np.zeros(5)
     for li in range(n_layers):
@@ -464,30 +459,60 @@ def run_ep_leg(args, torch, pkg, lib, layers, dev, local, rank, world) -> dict:
         a2a.layer_timed(li, x, evs)
         torch.cuda.synchronize()
         ph_a += [evs[i].elapsed_time(evs[i + 1]) for i in range(5)]
-    x.copy_(x0)
-    ph_p = np.zeros(3)
-    for li in range(n_layers):
-        evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-        p2p.layer_timed(li, x, evs)
-        torch.cuda.synchronize()
-        ph_p += [evs[i].elapsed_time(evs[i + 1]) for i in range(3)]
-    lib.ep_status()
-    counts = p2p.counts()
     comm_a = float(ph_a[1] + ph_a[3])
     tot_a = float(ph_a.sum())
+
+    # the peer-memory exchange; every rank agrees whether it worked before
+    # any rank relies on it (a rank that failed alone would leave the others
+    # waiting in the next collective)
+    def agree(ok: bool) -> bool:
+        if world == 1:
+            return ok
+        f = torch.tensor([0.0 if ok else 1.0], device=dev)
+        dist.all_reduce(f, op=dist.ReduceOp.MAX)
+        return f.item() == 0.0
+
+    p2p_err = None
+    ms_p2p, same, ph_p, counts = float("nan"), False, np.zeros(3), {}
+    try:
+        p2p = pkg.ep.PeerExpertParallelMoE(lib, world, rank)
+        ok = True
+    except Exception as e:  # noqa: BLE001 - reported in the JSON line
+        ok, p2p_err = False, f"setup: {e}"
+    if agree(ok):
+        try:
+            ms_p2p = time_steps(p2p.layer)
+            lib.ep_status()
+            same = bool(torch.equal(x, out_a2a))
+            x.copy_(x0)
+            for li in range(n_layers):
+                evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+                p2p.layer_timed(li, x, evs)
+                torch.cuda.synchronize()
+                ph_p += [evs[i].elapsed_time(evs[i + 1]) for i in range(3)]
+            lib.ep_status()
+            counts = p2p.counts()
+            ok = True
+        except Exception as e:  # noqa: BLE001
+            ok, p2p_err = False, f"run: {e}"
+        ok = agree(ok)
+    elif p2p_err is None:
+        p2p_err = "setup failed on another rank"
     if world > 1:
-        t = torch.tensor([ms_a2a, ms_p2p, comm_a, tot_a, 0.0 if same else 1.0], device=dev)
+        t = torch.tensor([ms_a2a, ms_p2p if ok else 0.0, comm_a, tot_a, 0.0 if same else 1.0], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_a2a, ms_p2p, comm_a, tot_a = (float(v) for v in t.tolist()[:4])
         same = t.tolist()[4] == 0.0
-    ms = ms_p2p if args.ep_exchange == "p2p" else ms_a2a
+    use_p2p = ok and args.ep_exchange == "p2p"
+    ms = ms_p2p if use_p2p else ms_a2a
     out = {"metric": f"EP prefill tok/s (config 4: {args.ep_tokens} tokens x {n_layers} config-0 MoE layers, "
                      "experts sharded)",
            "value": round(args.ep_tokens / (ms / 1e3), 1), "unit": "tok/s", "ms_per_step": round(ms, 3),
            "n_gpus": world, "tokens_per_rank": T, "layers": n_layers, "experts_per_rank": e_loc,
            "steps": args.ep_steps, "scaling": "strong (4096 tokens in total)",
-           "exchange": args.ep_exchange,
-           "p2p": {"value": round(args.ep_tokens / (ms_p2p / 1e3), 1), "ms_per_step": round(ms_p2p, 3),
+           "exchange": "p2p" if use_p2p else "nccl",
+           "p2p": {"error": p2p_err} if not ok else {
+                   "value": round(args.ep_tokens / (ms_p2p / 1e3), 1), "ms_per_step": round(ms_p2p, 3),
                    "how": "the kernels store rows, expert ids and counts into the expert owner's peer region "
                           "(IPC-mapped, NVLink) and the outputs back into the sender's; a flag per rank pair, "
                           "no collective, no host round trip",
@@ -502,8 +527,8 @@ def run_ep_leg(args, torch, pkg, lib, layers, dev, local, rank, world) -> dict:
                                        "experts": round(float(ph_a[2]), 3),
                                        "exchange_back": round(float(ph_a[3]), 3),
                                        "combine": round(float(ph_a[4]), 3)}},
-           "p2p_equals_nccl_bitwise": same,
-           "last_layer_rows": counts}
+           "p2p_equals_nccl_bitwise": same if ok else None,
+           "last_layer_rows": counts or a2a.last}
     if world > 1:
         dist.barrier()  # no rank frees its peer region while another may still store into it
     lib.free()
