@@ -155,30 +155,37 @@ def test_ep_p2p_one_shard_matches_alltoall_path(torch_cuda, pkg, oracle_mod):
     lib.free()
 
 
-@pytest.mark.parametrize("cfg,T", [(dict(dim=512, ffn=256, n_experts=16, k_used=4, gs=32), (40, 23)),
+SMALL = dict(dim=512, ffn=256, n_experts=16, k_used=4, gs=32)
+
+
+@pytest.mark.parametrize("cfg,T", [(SMALL, (40, 23)), (SMALL, (17, 40, 1, 33)),
+                                   (SMALL, (9, 30, 2, 41, 16, 5, 28, 12)),
                                    (dict(dim=2048, ffn=1536, n_experts=64, k_used=4, gs=32), (200, 131))])
-def test_ep_p2p_two_shards_one_gpu(cfg, T, torch_cuda, pkg, oracle_mod, tmp_path):
-    """Shards 0 and 1 as two library instances on one GPU, connected through
-    each other's peer regions: each phase is issued for both shards before
+def test_ep_p2p_shards_one_gpu(cfg, T, torch_cuda, pkg, oracle_mod, tmp_path):
+    """n = len(T) shards as n library instances on one GPU, connected through
+    each other's peer regions: each phase is issued for every shard before
     the next phase, in one stream, so every wait is already satisfied when
-    it runs. Two layer calls (epochs 1 and 2)."""
+    it runs. Two layer calls (epochs 1 and 2). With 8 shards of 16 experts a
+    rank holds 2 experts, fewer than the 4 a token picks (a token sends at
+    most 2 rows to one rank); one rank routes a single token."""
     torch = torch_cuda
     synth, ep = pkg.synth, pkg.ep
+    n = len(T)
     L = synth.moe_layer(seed=6, zipf=1.1, **cfg)
     D, K = cfg["dim"], cfg["k_used"]
-    xs = [synth.tokens(600 + r, T[r], D) for r in range(2)]
-    libs = [_lib_copy(pkg, tmp_path, f"libglm_p2p{r}.so") for r in range(2)]
+    xs = [synth.tokens(600 + r, T[r], D) for r in range(n)]
+    libs = [_lib_copy(pkg, tmp_path, f"libglm_p2p{r}.so") for r in range(n)]
     for r, lib in enumerate(libs):
         lib.init(0, D, cfg["ffn"], cfg["n_experts"], K, 32, 1)
-        lib.ep_setup(2, r, max(T))
-        lib.upload_moe_layer(0, ep.shard_layer(L, 2, r))
-    pms = [ep.PeerExpertParallelMoE(lib, 2, r, connect=False) for r, lib in enumerate(libs)]
+        lib.ep_setup(n, r, max(T))
+        lib.upload_moe_layer(0, ep.shard_layer(L, n, r))
+    pms = [ep.PeerExpertParallelMoE(lib, n, r, connect=False) for r, lib in enumerate(libs)]
     regions = [pm.region for pm in pms]
     for pm in pms:
         pm.connect(regions)
     for rep in range(2):
-        xd = [torch.from_numpy(xs[r].copy()).cuda() for r in range(2)]
-        idx = [torch.zeros(T[r], K, dtype=torch.int32, device="cuda") for r in range(2)]
+        xd = [torch.from_numpy(xs[r].copy()).cuda() for r in range(n)]
+        idx = [torch.zeros(T[r], K, dtype=torch.int32, device="cuda") for r in range(n)]
         for r, lib in enumerate(libs):
             lib.ep_p2p_dispatch(0, xd[r], T[r], stream=LEGACY)
         for r, lib in enumerate(libs):
@@ -187,16 +194,36 @@ def test_ep_p2p_two_shards_one_gpu(cfg, T, torch_cuda, pkg, oracle_mod, tmp_path
             lib.ep_p2p_combine(0, xd[r], idx[r], None, stream=LEGACY)
         for lib in libs:
             lib.ep_status()
-        for r in range(2):
+        for r in range(n):
             ref, ref_idx, _ = oracle_mod.moe_layer(L, xs[r], impl="orc")
             np.testing.assert_array_equal(idx[r].cpu().numpy(), ref_idx)
             worst = check_moe_outputs(xs[r], xd[r].cpu().numpy(), ref, TOL)
-            print(f"ep p2p 2 shards call {rep} rank {r}: worst rel L2 {worst:.2e}")
+            print(f"ep p2p {n} shards call {rep} rank {r}: worst rel L2 {worst:.2e}")
     c = [pm.counts() for pm in pms]
-    for a in range(2):
+    for a in range(n):
         assert sum(c[a]["send_counts"]) == T[a] * K
-        for b in range(2):
+        for b in range(n):
             assert c[a]["send_counts"][b] == c[b]["recv_counts"][a]
+    for lib in libs:
+        lib.free()
+
+
+def test_ep_p2p_connect_refuses_mismatched_regions(torch_cuda, pkg, tmp_path):
+    """A region laid out for another max_tokens is refused at connect (the
+    kernels' stores into it would otherwise land outside it)."""
+    import glm_c_b200.glm_cuda as gc
+
+    libs = [_lib_copy(pkg, tmp_path, f"libglm_mis{r}.so") for r in range(2)]
+    for r, lib in enumerate(libs):
+        lib.init(0, 512, 256, 16, 4, 32, 1)
+        lib.ep_setup(2, r, 32 if r == 0 else 48)
+    pms = [pkg.ep.PeerExpertParallelMoE(lib, 2, r, connect=False) for r, lib in enumerate(libs)]
+    regions = [pm.region for pm in pms]
+    for pm in pms:
+        with pytest.raises(gc.GlmCudaError):
+            pm.connect(regions)
+    with pytest.raises(gc.GlmCudaError):  # not connected: the layer calls refuse too
+        libs[0].ep_p2p_experts(0, stream=LEGACY)
     for lib in libs:
         lib.free()
 
