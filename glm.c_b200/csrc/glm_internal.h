@@ -133,6 +133,8 @@ struct PrefillDispatchArgs {
     int4* items2;             // down items {group, row0, nrows, m-tile}
 };
 
+constexpr int kEpMaxShards = 8;  // most ranks the routed experts are split over
+
 struct GroupGemmArgs {
     const int4* items1;
     const int4* items2;
@@ -143,6 +145,17 @@ struct GroupGemmArgs {
     unsigned* status;  // bit 64: a bounded wait gave up
     int K, Mtot, E, mode;  // mode 0: gate/up (K = D, Mtot = F); 1: down (K = F, Mtot = D)
     int gs;                // weight scale group: 32 or 16
+    // Mode 1 of expert parallelism over peer memory (row_src non-null): the
+    // output row of a received slot q * cap + j goes straight into row
+    // me * cap + j of back_rows in rank q's region; rows of this rank's own
+    // tokens (sources n_slots + t) go to y. After the last CTA's stores,
+    // flag_back[me] of every region is raised to `epoch`.
+    const int* row_src = nullptr;  // grouped row -> source
+    unsigned char* peer[kEpMaxShards] = {};
+    size_t back_off = 0, flag_off = 0;
+    int n_slots = 0, cap = 0, me = 0, n_shards = 0;
+    unsigned* done = nullptr;      // last-CTA counter, zero between launches
+    unsigned epoch = 0;
 };
 
 cudaError_t prefill_check(const MoeDims& d);
@@ -187,7 +200,6 @@ cudaError_t ep_copy_routing(const EpShape& s, unsigned char* ws, int T, int32_t*
 // into the receiver's region and raise a flag per (sender, receiver) pair;
 // the expert outputs go back the same way. Flags carry an epoch that grows
 // by one per layer call, so they never need resetting.
-constexpr int kEpMaxShards = 8;
 
 struct EpRegion {
     int cap;                 // rows one sender may put in one receiver's region (T_max * min(K, e_local))

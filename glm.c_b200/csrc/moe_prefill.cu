@@ -556,6 +556,16 @@ __device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t (&v)[16])
         : "memory");
 }
 
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;\n" ::: "memory"); }
 
 // Wait for a phase; on a timeout flag the CTA (and the launch status) and
@@ -597,7 +607,7 @@ __device__ __forceinline__ void dequant_pair(uint32_t u, int b0, int b1, uint64_
 }
 
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    q8_group_gemm_kernel(const __grid_constant__ GemmMaps maps, const GroupGemmArgs a) {
+    q8_group_gemm_kernel(const __grid_constant__ GemmMaps maps, const __grid_constant__ GroupGemmArgs a) {
     extern __shared__ __align__(1024) unsigned char gsm_raw[];
     unsigned char* sm = gsm_raw + ((1024u - (smem_addr(gsm_raw) & 1023u)) & 1023u);
     GemmBars* B = reinterpret_cast<GemmBars*>(sm + GemmLayout::bars);
@@ -800,6 +810,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         static_cast<__nv_bfloat16*>(a.hlo)[o] = hl;
                     }
                     epi_bar();  // stage is rewritten by the next chunk
+                } else if (a.row_src) {
+                    // expert parallelism: lane l finds where token row n0 + l goes (the
+                    // sender's back_rows over NVLink, or y for this rank's own tokens)
+                    const int col = it.w * kTM + row;
+                    float* dst_l = nullptr;
+                    if (n0 + lane < nrows) {
+                        const int r = row0 + n0 + lane, src = a.row_src[r];
+                        if (src < a.n_slots) {
+                            const int q = src / a.cap, jj = src - q * a.cap;
+                            dst_l = reinterpret_cast<float*>(a.peer[q] + a.back_off) +
+                                    ((size_t)a.me * a.cap + jj) * Mtot;
+                        } else {
+                            dst_l = a.y + (size_t)r * Mtot;
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        if (n0 + j >= nrows) break;
+                        float* d = reinterpret_cast<float*>(
+                            __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(dst_l), j));
+                        d[col] = v[j];
+                    }
                 } else {
                     const int col = it.w * kTM + row;
 #pragma unroll
@@ -812,10 +844,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
     }
 done:
+    if (a.row_src) __threadfence_system();  // this thread's stores into the other ranks' regions
     __syncthreads();
     if (warp == 5) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;\n" ::"r"(tmem) : "memory");
+    }
+    if (a.row_src && tid == 0 && atomicAdd(a.done, 1u) == gridDim.x - 1) {
+        // every CTA's outputs are out: raise flag_back[me] in every region, unless
+        // a CTA gave up (its rows would be missing; the senders then time out)
+        __threadfence_system();
+        if (!(*reinterpret_cast<volatile unsigned*>(a.status) & 64u))
+            for (int q = 0; q < a.n_shards; ++q)
+                st_release_sys(reinterpret_cast<unsigned*>(a.peer[q] + a.flag_off) + a.me, a.epoch);
+        *reinterpret_cast<volatile unsigned*>(a.done) = 0u;
     }
 }
 
@@ -1220,7 +1262,8 @@ cudaError_t launch_route(const PrefillRouteArgs& ra, cudaStream_t st) {
 cudaError_t launch_grouped_ffn(const MoeLayerDev& w, const MoeDims& d, bool use_routed, size_t R_cap,
                                const __nv_bfloat16* xhi, const __nv_bfloat16* xlo, __nv_bfloat16* hhi,
                                __nv_bfloat16* hlo, float* y, const int* counts, const int4* items1,
-                               const int4* items2, int num_sms, unsigned* status, cudaStream_t st) {
+                               const int4* items2, int num_sms, unsigned* status, cudaStream_t st,
+                               const GroupGemmArgs* peer_out = nullptr) {
     // tensor maps: weights (box rows x 64 bytes, 64-byte swizzle), their scales (box rows x 4 groups) and
     // activations (box 32 rows x 64 bf16, 128-byte swizzle)
     GemmMaps m1{}, m2{};
@@ -1267,6 +1310,18 @@ cudaError_t launch_grouped_ffn(const MoeLayerDev& w, const MoeDims& d, bool use_
     GroupGemmArgs g1{items1, items2, counts, hhi, hlo, nullptr, status, d.D, d.F, d.E, 0, d.gs};
     q8_group_gemm_kernel<<<num_sms, kGemmThreads, gsmem, st>>>(m1, g1);
     GroupGemmArgs g2{items1, items2, counts, nullptr, nullptr, y, status, d.F, d.D, d.E, 1, d.gs};
+    if (peer_out) {
+        g2.row_src = peer_out->row_src;
+        for (int q = 0; q < kEpMaxShards; ++q) g2.peer[q] = peer_out->peer[q];
+        g2.back_off = peer_out->back_off;
+        g2.flag_off = peer_out->flag_off;
+        g2.n_slots = peer_out->n_slots;
+        g2.cap = peer_out->cap;
+        g2.me = peer_out->me;
+        g2.n_shards = peer_out->n_shards;
+        g2.done = peer_out->done;
+        g2.epoch = peer_out->epoch;
+    }
     q8_group_gemm_kernel<<<num_sms, kGemmThreads, gsmem, st>>>(m2, g2);
     return cudaGetLastError();
 }
@@ -1305,16 +1360,6 @@ cudaError_t launch_moe_prefill(const MoeLayerDev& w, const MoeDims& d, unsigned 
 }
 
 // ---------------------------------------- expert parallelism, peer memory
-
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
 
 constexpr uint64_t kEpWaitNs = 4000000000ull;  // a peer that has not answered in 4 s is taken as gone
 constexpr unsigned kStatEpPeer = 128u;
@@ -1589,6 +1634,24 @@ cudaError_t launch_ep_p2p_experts(const MoeLayerDev& w, const MoeDims& dl, const
                                         p.items2, recv_cnt, s.n_shards, R.cap);
     ep_gather_split_kernel<<<num_sms * 4, 256, 0, st>>>(reinterpret_cast<const float*>(own + R.recv_rows), p.xn,
                                                         p.row_src, p.counts, n_slots, dl.D, p.xhi, p.xlo);
+    if (use_routed) {
+        // the down GEMM's epilogue stores each received row's output straight
+        // into its sender's region and raises the flags itself
+        GroupGemmArgs pe{};
+        pe.row_src = p.row_src;
+        for (int q = 0; q < s.n_shards; ++q) pe.peer[q] = peers.base[q];
+        pe.back_off = R.back_rows;
+        pe.flag_off = R.flag_back;
+        pe.n_slots = n_slots;
+        pe.cap = R.cap;
+        pe.me = me;
+        pe.n_shards = s.n_shards;
+        pe.done = p.done + 1;
+        pe.epoch = epoch;
+        return launch_grouped_ffn(w, dl, use_routed, p.R_cap, p.xhi, p.xlo, p.hhi, p.hlo, p.y, p.counts, p.items1,
+                                  p.items2, num_sms, status, st, &pe);
+    }
+    // routed experts off on this rank: zero rows back for whatever was sent
     cudaError_t err = launch_grouped_ffn(w, dl, use_routed, p.R_cap, p.xhi, p.xlo, p.hhi, p.hlo, p.y, p.counts,
                                          p.items1, p.items2, num_sms, status, st);
     if (err) return err;
