@@ -15,6 +15,7 @@
 #include <cstdint>
 
 #include "glm_internal.h"
+#include "q80_common.cuh"
 
 namespace glmq {
 
@@ -65,6 +66,7 @@ __device__ __forceinline__ void rope_pair(float& x0, float& x1, int i, int dim, 
 
 // x = dequant(tok_q[token]) (infer.c:1810-1812).
 __global__ void embed_kernel(const int8_t* tok_q, const float* tok_s, const int* token, float* x, int D, int gs) {
+    pdl_enter();
     const int t = *token;
     const int8_t* q = tok_q + (size_t)t * D;
     const float* s = tok_s + (size_t)t * (D / gs);
@@ -76,6 +78,7 @@ __global__ void embed_kernel(const int8_t* tok_q, const float* tok_s, const int*
 // (infer.c:1003-1016).
 __global__ void kv_cache_write_kernel(float* kv_a, const float* kv_norm, float* cache_comp, float* cache_pe,
                                       const int* pos_dev, int kv_lora, int rope) {
+    pdl_enter();
     __shared__ double red[32];
     const int pos = *pos_dev;
     const float inv = rms_inv(kv_a, kv_lora, red);
@@ -150,6 +153,7 @@ __device__ __forceinline__ void q8_rows_dot(const int8_t* q, const float* s, con
 // att_concat[h] = v_b_h . context. Every stage keeps many independent loads
 // in flight (rows in groups of 8 per warp; cache rows split over the warps).
 __global__ void __launch_bounds__(512) mla_heads_kernel(MlaArgs a) {
+    pdl_enter();
     extern __shared__ __align__(16) float smf[];
     constexpr int kR = 8;
     const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
@@ -270,6 +274,7 @@ __global__ void __launch_bounds__(512) mla_heads_kernel(MlaArgs a) {
 
 // g = silu(g) * u (infer.c:1076-1078).
 __global__ void silu_mul_kernel(float* g, const float* u, int n) {
+    pdl_enter();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const float v = g[i];
         g[i] = v / (1.0f + expf(-v)) * u[i];
@@ -280,6 +285,7 @@ __global__ void silu_mul_kernel(float* g, const float* u, int n) {
 // CTA reduces a slice to (value, index) in `part`; the last CTA to finish
 // (counter, reset by it) reduces the partials in CTA order.
 __global__ void argmax_kernel(const float* x, int n, float2* part, unsigned* counter, int* out) {
+    pdl_enter();
     __shared__ float bv[32];
     __shared__ int bi[32];
     __shared__ int last;
@@ -342,6 +348,7 @@ __global__ void argmax_kernel(const float* x, int n, float2* part, unsigned* cou
 // id while the prompt lasts, else the argmax (recorded as generated).
 __global__ void decode_advance_kernel(int* pos, int* token, const int* argmax, const int* prompt, int n_prompt,
                                       int* out_ids, int vocab) {
+    pdl_enter();
     const int p = *pos;
     int next;
     if (p + 1 < n_prompt) {
@@ -359,14 +366,12 @@ __global__ void decode_advance_kernel(int* pos, int* token, const int* argmax, c
 
 cudaError_t launch_embed(const int8_t* tok_q, const float* tok_s, const int* token, float* x, int D, int gs,
                          cudaStream_t st) {
-    embed_kernel<<<1, 512, 0, st>>>(tok_q, tok_s, token, x, D, gs);
-    return cudaGetLastError();
+    return launch_pdl(embed_kernel, 1, 512, 0, st, tok_q, tok_s, token, x, D, gs);
 }
 
 cudaError_t launch_kv_cache_write(float* kv_a, const float* kv_norm, float* cache_comp, float* cache_pe,
                                   const int* pos, int kv_lora, int rope, cudaStream_t st) {
-    kv_cache_write_kernel<<<1, 512, 0, st>>>(kv_a, kv_norm, cache_comp, cache_pe, pos, kv_lora, rope);
-    return cudaGetLastError();
+    return launch_pdl(kv_cache_write_kernel, 1, 512, 0, st, kv_a, kv_norm, cache_comp, cache_pe, pos, kv_lora, rope);
 }
 
 size_t mla_heads_smem(const MlaArgs& a, int cache_cap) {
@@ -382,25 +387,21 @@ cudaError_t launch_mla_heads(const MlaArgs& a, int n_heads, int cache_cap, cudaS
         if (e != cudaSuccess) return e;
         cap = smem;
     }
-    mla_heads_kernel<<<n_heads, 512, smem, st>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(mla_heads_kernel, n_heads, 512, smem, st, a);
 }
 
 cudaError_t launch_silu_mul(float* g, const float* u, int n, int num_sms, cudaStream_t st) {
-    silu_mul_kernel<<<num_sms, 256, 0, st>>>(g, u, n);
-    return cudaGetLastError();
+    return launch_pdl(silu_mul_kernel, num_sms, 256, 0, st, g, u, n);
 }
 
 cudaError_t launch_argmax(const float* x, int n, float2* part, unsigned* counter, int nblocks, int* out,
                           cudaStream_t st) {
-    argmax_kernel<<<nblocks, 512, 0, st>>>(x, n, part, counter, out);
-    return cudaGetLastError();
+    return launch_pdl(argmax_kernel, nblocks, 512, 0, st, x, n, part, counter, out);
 }
 
 cudaError_t launch_decode_advance(int* pos, int* token, const int* argmax, const int* prompt, int n_prompt,
                                   int* out_ids, int vocab, cudaStream_t st) {
-    decode_advance_kernel<<<1, 1, 0, st>>>(pos, token, argmax, prompt, n_prompt, out_ids, vocab);
-    return cudaGetLastError();
+    return launch_pdl(decode_advance_kernel, 1, 1, 0, st, pos, token, argmax, prompt, n_prompt, out_ids, vocab);
 }
 
 }  // namespace glmq

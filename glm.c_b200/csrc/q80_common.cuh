@@ -26,6 +26,8 @@
 #pragma once
 
 #include <cstdint>
+#include <utility>
+
 #include <cuda_runtime.h>
 
 namespace glmq {
@@ -324,6 +326,33 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "r"(smem_addr(bar)), "r"(parity)
         : "memory");
     return ok != 0;
+}
+
+// Programmatic dependent launch. A kernel started with launch_pdl may be
+// scheduled while the previous kernel of its stream is still draining;
+// pdl_enter(), its first statement, waits until that kernel has completed
+// and its writes are visible, then lets the next kernel of the stream be
+// scheduled early in turn. Every kernel launched with launch_pdl calls it
+// before touching memory another kernel wrote.
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 __device__ __forceinline__ uint64_t global_ns() {

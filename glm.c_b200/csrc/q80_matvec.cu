@@ -30,6 +30,7 @@ struct MatvecArgs {
 };
 
 __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a) {
+    pdl_enter();
     extern __shared__ __align__(16) unsigned char sm[];
     const int nch = a.cols >> 6;
     int8_t* planes = reinterpret_cast<int8_t*>(sm);
@@ -144,6 +145,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a)
 constexpr int kG16Warps = 16;
 
 __global__ void __launch_bounds__(kG16Warps * 32) q80_matvec_g16_kernel(MatvecArgs a) {
+    pdl_enter();
     extern __shared__ __align__(16) unsigned char sm16[];
     float* xs = reinterpret_cast<float*>(sm16);  // [cols]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -214,8 +216,7 @@ cudaError_t launch_q80_matvec(const int8_t* q, const float* s, const float* x, f
         int grid = num_sms * 2;
         if (grid > (rows + kG16Warps - 1) / kG16Warps) grid = (rows + kG16Warps - 1) / kG16Warps;
         MatvecArgs a{q, s, x, y, rows, cols, accumulate ? 1 : 0, norm};
-        q80_matvec_g16_kernel<<<grid, kG16Warps * 32, smem16, stream>>>(a);
-        return cudaGetLastError();
+        return launch_pdl(q80_matvec_g16_kernel, grid, kG16Warps * 32, smem16, stream, a);
     }
     const size_t smem = q80_matvec_smem_bytes(cols, norm != nullptr);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
@@ -227,8 +228,7 @@ cudaError_t launch_q80_matvec(const int8_t* q, const float* s, const float* x, f
     int grid = num_sms;
     if (grid > (rows + 15) / 16) grid = (rows + 15) / 16;
     MatvecArgs a{q, s, x, y, rows, cols, accumulate ? 1 : 0, norm};
-    q80_matvec_kernel<<<grid, kMvThreads, smem, stream>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(q80_matvec_kernel, grid, kMvThreads, smem, stream, a);
 }
 
 }  // namespace glmq
