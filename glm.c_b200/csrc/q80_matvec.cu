@@ -18,6 +18,7 @@ namespace glmq {
 constexpr int kMvWarps = 16;
 constexpr int kMvThreads = kMvWarps * 32;
 constexpr int kMvUnroll = 4;
+constexpr size_t kMvPrefetch = 32768;  // weight bytes per CTA pulled into L2 before the launch wait
 
 struct MatvecArgs {
     const int8_t* q;
@@ -30,6 +31,22 @@ struct MatvecArgs {
 };
 
 __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a) {
+    {
+        // Before waiting for the previous kernel (which writes x, never the
+        // weights' values this kernel reads afterwards): pull the first
+        // kMvPrefetch bytes of this CTA's weight rows and their scales into
+        // L2, so the stream starts while the previous kernel drains. A hint
+        // only: the loads below come after the wait.
+        const long long r0 = (long long)blockIdx.x * a.rows / gridDim.x;
+        const long long r1 = (long long)(blockIdx.x + 1) * a.rows / gridDim.x;
+        const size_t qb = (size_t)(r1 - r0) * a.cols, sb = qb / 8;  // gs = 32: 4 bytes of scale per 32 weights
+        const char* qp = reinterpret_cast<const char*>(a.q) + (size_t)r0 * a.cols;
+        const char* sp = reinterpret_cast<const char*>(a.s) + (size_t)r0 * (a.cols / 8);
+        for (size_t o = (size_t)threadIdx.x * 128; o < qb && o < kMvPrefetch; o += (size_t)kMvThreads * 128)
+            asm volatile("prefetch.global.L2 [%0];\n" ::"l"(qp + o));
+        for (size_t o = (size_t)threadIdx.x * 128; o < sb && o < kMvPrefetch / 8; o += (size_t)kMvThreads * 128)
+            asm volatile("prefetch.global.L2 [%0];\n" ::"l"(sp + o));
+    }
     pdl_enter();
     extern __shared__ __align__(16) unsigned char sm[];
     const int nch = a.cols >> 6;
