@@ -40,6 +40,34 @@ def test_calls_before_init_fail_cleanly(pkg):
     lib.free()  # idempotent
 
 
+def test_expert_parallel_calls_before_setup_fail_cleanly(pkg):
+    """Every expert-parallel entry point, called before glm_cuda_init (or
+    before glm_cuda_ep_setup / _peer_connect), returns the state error and
+    touches no device."""
+    import numpy as np
+
+    gc = pkg.glm_cuda
+    lib = gc.GlmCuda()
+    lib.free()
+    x = np.zeros((4, 256), np.float32)
+    calls = [
+        lambda: lib.ep_setup(2, 0, 4),
+        lambda: lib.ep_peer_region(),
+        lambda: lib.ep_peer_open(bytes(64)),
+        lambda: lib.ep_peer_connect([16 << 20, 32 << 20]),
+        lambda: lib.ep_p2p_dispatch(0, x, 4),
+        lambda: lib.ep_p2p_experts(0),
+        lambda: lib.ep_p2p_combine(0, x),
+        lambda: lib.ep_p2p_counts(2),
+        lambda: lib.ep_status(),
+    ]
+    for call in calls:
+        with pytest.raises(gc.GlmCudaError) as e:
+            call()
+        assert e.value.rc == -2, str(e.value)
+    lib.free()
+
+
 def test_init_rejects_unsupported_shapes(pkg):
     lib = pkg.glm_cuda.GlmCuda()
     for args in ((0, 2048, 1536, 64, 4, 8, 1),    # gs=8 (supported: 32, 16)

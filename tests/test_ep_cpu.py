@@ -160,3 +160,68 @@ def test_shard_layer_cuts_routed_blocks(pkg):
     s = pkg.ep.shard_layer(L, 4, 2)
     assert s["gate_q"].shape[0] == 2 and np.array_equal(s["gate_q"], L["gate_q"][4:6])
     assert s["router"] is L["router"] and s["down_sh_q"] is L["down_sh_q"]
+
+
+class _FakePeerKernels:
+    """Records what PeerExpertParallelMoE asks of the library's peer calls
+    (test infrastructure only): region addresses and IPC handles are made up
+    from the rank, opening a handle maps it to a distinct made-up address."""
+
+    def __init__(self, rank):
+        self.rank = rank
+        self.opened = []
+        self.connected = None
+
+    def ep_peer_region(self):
+        return 0x10000000 * (self.rank + 1), bytes([self.rank + 1]) * 64
+
+    def ep_peer_open(self, handle):
+        self.opened.append(handle)
+        return 0x70000000 + 0x100000 * handle[0]
+
+    def ep_peer_connect(self, regions):
+        self.connected = list(regions)
+
+
+def _peer_rank(rank, world, port, result_q):
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from __graft_entry__ import load_package
+
+        pkg = load_package()
+        k = _FakePeerKernels(rank)
+        pkg.ep.PeerExpertParallelMoE(k, world, rank)
+        result_q.put((rank, k.connected, [h[0] for h in k.opened]))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_peer_regions_swap_handles_over_the_group(world):
+    """Every rank connects to `world` regions in rank order: its own region
+    at its own index, every other rank's opened from that rank's handle."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_rank, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+        assert p.exitcode == 0, f"rank exited with {p.exitcode}"
+    res = sorted(q.get(timeout=5) for _ in range(world))
+    for rank, connected, opened in res:
+        assert len(connected) == world
+        for r in range(world):
+            want = 0x10000000 * (rank + 1) if r == rank else 0x70000000 + 0x100000 * (r + 1)
+            assert connected[r] == want
+        assert sorted(opened) == [r + 1 for r in range(world) if r != rank]
