@@ -1,6 +1,7 @@
 """Host-side checks that need no GPU: the C-ABI library loads, exports every
 entry point include/glm_cuda.h declares, and rejects calls cleanly before
 initialisation; the algorithmic-byte formulas match glm.c's q80_bytes."""
+import os
 import subprocess
 
 import pytest
@@ -98,3 +99,41 @@ def test_algorithmic_bytes_match_reference_formula(pkg):
     assert s.q8_matvec_bytes(2048, 1536, 32) == 3_553_280
     assert s.q8_matvec_bytes(4608, 2048, 32) == 10_643_456
     assert s.q8_matvec_bytes(154880, 2048, 32) == 357_471_232
+
+
+def test_header_is_plain_c_and_links(pkg, tmp_path):
+    """A C99 translation unit that includes include/glm_cuda.h and takes the
+    address of every declared entry point compiles with -Wall -Werror, links
+    against the built library and runs (calls only glm_cuda_free and
+    glm_cuda_last_error): the boundary needs no C++, CUDA or torch types."""
+    import shutil
+
+    gcc = shutil.which("gcc")
+    if not gcc:
+        pytest.skip("no C compiler")
+    pkg.build.build()
+    names = pkg.glm_cuda.declared_functions()
+    src = tmp_path / "abi_check.c"
+    body = "\n".join(f"    table[n++] = (void (*)(void))&{fn};" for fn in names)
+    src.write_text(f'''#include <stdio.h>
+#include "glm_cuda.h"
+int main(void) {{
+    void (*table[{len(names) + 1}])(void);
+    int n = 0;
+{body}
+    int linked = 0;
+    for (int i = 0; i < n; ++i) linked += table[i] != NULL;
+    glm_cuda_free();
+    printf("%d entry points\\n", linked);
+    return linked == {len(names)} ? 0 : 1;
+}}
+''')
+    exe = tmp_path / "abi_check"
+    lib_dir = os.path.dirname(pkg.build.LIB)
+    r = subprocess.run([gcc, "-std=c99", "-Wall", "-Werror", "-Wno-pedantic", "-I", pkg.build.INCLUDE, str(src),
+                        "-o", str(exe), "-L", lib_dir, "-lglm_cuda", f"-Wl,-rpath,{lib_dir}"],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert f"{len(names)} entry points" in r.stdout
