@@ -240,6 +240,29 @@ def moe_layer_bytes_cfg(dims: dict) -> int:
                                            dims["n_experts_used"], dims["group_size"])
 
 
+def time_cpu_calls(oracle, layer: dict, x, warmup: int, calls: int) -> float:
+    """Milliseconds for `calls` one-token MoE-layer calls on the host, tokens
+    of x in rotation: glm.c's own apply_moe_shared_ffn_layer (oracle/_ref,
+    OpenMP) when it was built, else the oracle's single-threaded C
+    restatement of it."""
+    if oracle.ref_available():
+        return oracle.time_moe_layer(layer, x, warmup, calls)
+    n = x.shape[0]
+    for i in range(warmup):
+        oracle.moe_layer(layer, x[i % n:i % n + 1], impl="orc")
+    t0 = time.perf_counter()
+    for i in range(calls):
+        oracle.moe_layer(layer, x[i % n:i % n + 1], impl="orc")
+    return (time.perf_counter() - t0) * 1e3
+
+
+def cpu_kind(oracle) -> tuple[str, int, str]:
+    """(kind, threads, what) of the host code time_cpu_calls runs."""
+    if oracle.ref_available():
+        return "reference", oracle.omp_threads(), "glm.c apply_moe_shared_ffn_layer"
+    return "port", 1, "the oracle's C restatement of apply_moe_shared_ffn_layer (oracle/_ref not built)"
+
+
 def cpu_baseline(layer_host: dict, x_host, budget_s: float) -> dict:
     """glm.c's own apply_moe_shared_ffn_layer on the host cores, bounded sample."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -249,17 +272,14 @@ def cpu_baseline(layer_host: dict, x_host, budget_s: float) -> dict:
     os.environ.setdefault("OMP_PLACES", "cores")
     import oracle
 
-    kind = "reference" if oracle.ref_available() else "port"
-    if kind == "port":
-        return {"value": None, "unit": UNIT, "cores": 1, "kind": "port",
-                "sample": "oracle/_ref missing; no CPU baseline measured"}
-    probe = oracle.time_moe_layer(layer_host, x_host, 2, 5) / 5.0
+    kind, threads, what = cpu_kind(oracle)
+    probe = time_cpu_calls(oracle, layer_host, x_host, 2, 5) / 5.0
     iters = max(5, int(budget_s * 1000.0 / max(probe, 1e-3)))
-    ms = oracle.time_moe_layer(layer_host, x_host, 2, iters)
+    ms = time_cpu_calls(oracle, layer_host, x_host, 2, iters)
     gbps = iters * layer_bytes() / (ms / 1e3) / 1e9
-    return {"value": round(gbps, 3), "unit": UNIT, "cores": oracle.omp_threads(), "kind": kind,
-            "sample": f"{iters} calls of apply_moe_shared_ffn_layer (one config-0 layer, {x_host.shape[0]} "
-                      f"rotating tokens), {ms / iters:.3f} ms/call, OMP_NUM_THREADS={os.environ['OMP_NUM_THREADS']}"}
+    return {"value": round(gbps, 3), "unit": UNIT, "cores": threads, "kind": kind,
+            "sample": f"{iters} calls of {what} (one config-0 layer, {x_host.shape[0]} "
+                      f"rotating tokens), {ms / iters:.3f} ms/call, threads={threads}"}
 
 
 def run_reference(args) -> None:
@@ -276,22 +296,19 @@ def run_reference(args) -> None:
     os.environ.setdefault("OMP_PLACES", "cores")
     import oracle
 
-    if not oracle.ref_available():
-        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libglmref.so was not built "
-                          "(reference sources absent where build() ran)"}))
-        return
+    kind, threads, what = cpu_kind(oracle)
     L = synth.moe_layer(seed=42, **synth.CONFIG0)
     x = synth.tokens(42, 64, D)
-    probe = oracle.time_moe_layer(L, x, 1, 3) / 3.0
+    probe = time_cpu_calls(oracle, L, x, 1, 3) / 3.0
     step_s = args.ref_budget_s / max(1, args.steps + args.warmup)
     calls = max(2, int(step_s * 1000.0 / max(probe, 1e-3)))
     for _ in range(args.warmup):
-        oracle.time_moe_layer(L, x, 0, calls)
+        time_cpu_calls(oracle, L, x, 0, calls)
     total_ms = 0.0
     for _ in range(args.steps):
-        total_ms += oracle.time_moe_layer(L, x, 0, calls)
+        total_ms += time_cpu_calls(oracle, L, x, 0, calls)
     gbps = args.steps * calls * layer_bytes() / (total_ms / 1e3) / 1e9
-    sample = (f"each step = {calls} calls of glm.c apply_moe_shared_ffn_layer on one config-0 layer with 64 "
+    sample = (f"each step = {calls} calls of {what} on one config-0 layer with 64 "
               f"rotating tokens ({total_ms / (args.steps * calls):.3f} ms/call)")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbps, 3), "unit": UNIT, "n_gpus": world,
@@ -299,8 +316,8 @@ def run_reference(args) -> None:
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32/int8",
         "data": "synthetic (seeded; BASELINE config-0 distributions)",
         "config": {"workload": "moe_decode", "layer": "config-0 MoE FFN", "batch": 1, "group_size": GS},
-        "cpu_baseline": {"value": round(gbps, 3), "unit": UNIT, "cores": oracle.omp_threads(),
-                         "kind": "reference", "sample": sample},
+        "cpu_baseline": {"value": round(gbps, 3), "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": sample},
         "e2e": {"value": round(gbps, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
