@@ -51,6 +51,8 @@ sys.path.insert(0, ROOT)
 D, F, E, K, GS = 2048, 1536, 64, 4, 32
 N_MOE_LAYERS = 46
 METRIC = "MoE-layer HBM GB/s (bs1 decode, 46 config-0 MoE layers per token)"
+# the Q8 matvec shapes (rows x cols)
+MATVEC_SHAPES = ((1536, 2048), (2048, 1536), (4608, 2048), (154880, 2048))
 UNIT = "GB/s"
 
 
@@ -240,49 +242,152 @@ def moe_layer_bytes_cfg(dims: dict) -> int:
                                            dims["n_experts_used"], dims["group_size"])
 
 
-def time_cpu_calls(oracle, layer: dict, x, warmup: int, calls: int) -> float:
-    """Milliseconds for `calls` one-token MoE-layer calls on the host, tokens
-    of x in rotation: glm.c's own apply_moe_shared_ffn_layer (oracle/_ref,
-    OpenMP) when it was built, else the oracle's single-threaded C
-    restatement of it."""
-    if oracle.ref_available():
-        return oracle.time_moe_layer(layer, x, warmup, calls)
-    n = x.shape[0]
-    for i in range(warmup):
-        oracle.moe_layer(layer, x[i % n:i % n + 1], impl="orc")
-    t0 = time.perf_counter()
-    for i in range(calls):
-        oracle.moe_layer(layer, x[i % n:i % n + 1], impl="orc")
-    return (time.perf_counter() - t0) * 1e3
+def workload_config(world: int, n_layers: int = N_MOE_LAYERS) -> dict:
+    """The workload both arms run (identical dicts, so the two lines compare):
+    one batch-1 decode token through n_layers distinct config-0 MoE layers per
+    step (46, GLM-4.7-Flash's layers 1..46, unless --layers says otherwise)."""
+    return {"workload": f"moe_decode: 1 token x {n_layers} distinct GLM-4.7-Flash MoE FFN layers per step",
+            "dim": D, "moe_ffn_dim": F, "experts": E, "top_k": K, "group_size": GS,
+            "layers_per_step": n_layers, "global_batch": world, "parallelism": f"replicas x{world}"}
 
 
-def cpu_kind(oracle) -> tuple[str, int, str]:
-    """(kind, threads, what) of the host code time_cpu_calls runs."""
-    if oracle.ref_available():
-        return "reference", oracle.omp_threads(), "glm.c apply_moe_shared_ffn_layer"
-    return "port", 1, "the oracle's C restatement of apply_moe_shared_ffn_layer (oracle/_ref not built)"
+def host_moe_stack(synth, n_layers: int, seed: int) -> tuple[list, int]:
+    """`n_layers` config-0 layers for the CPU legs, as many of them distinct
+    (own memory, different weights) as half of the available host memory
+    holds: one seeded layer and rotated copies of it (synth.rolled_moe_layer),
+    which takes seconds where generating every layer afresh takes minutes.
+    Returns (layers, number of distinct ones); layer l is distinct layer
+    l % distinct."""
+    base = synth.moe_layer(seed=seed, **synth.CONFIG0)
+    per = sum(v.nbytes for v in base.values() if hasattr(v, "nbytes"))
+    try:
+        import psutil
+
+        avail = psutil.virtual_memory().available
+    except Exception:  # noqa: BLE001 - no psutil: assume a modest host
+        avail = 16 << 30
+    distinct = max(1, min(n_layers, int(0.5 * avail // per)))
+    uniq = [base] + [synth.rolled_moe_layer(base, l) for l in range(1, distinct)]
+    return [uniq[l % distinct] for l in range(n_layers)], distinct
 
 
-def cpu_baseline(layer_host: dict, x_host, budget_s: float) -> dict:
-    """glm.c's own apply_moe_shared_ffn_layer on the host cores, bounded sample."""
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+def cpu_model_name() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_threads_env(oracle) -> int:
     ncores = os.cpu_count() or 1
     os.environ.setdefault("OMP_NUM_THREADS", str(ncores))
     os.environ.setdefault("OMP_PROC_BIND", "true")
     os.environ.setdefault("OMP_PLACES", "cores")
+    return ncores
+
+
+def cpu_stack_gbps(oracle, stack: list, x, warmup: int, budget_s: float) -> tuple[float, int, float]:
+    """glm.c's apply_moe_shared_ffn_layer on one token per step through the
+    whole stack (oracle/_ref), steps sized to ~budget_s: (GB/s, steps, ms per
+    step)."""
+    probe = oracle.time_moe_stack(stack, x, warmup, 1)
+    steps = max(2, int(budget_s * 1000.0 / max(probe, 1e-3)))
+    ms = oracle.time_moe_stack(stack, x, 0, steps)
+    return len(stack) * steps * layer_bytes() / (ms / 1e3) / 1e9, steps, ms / steps
+
+
+def cpu_port_gbps(oracle, stack: list, x, steps: int) -> tuple[float, float]:
+    """The oracle's single-threaded C restatement (where glm.c was not
+    compiled): (GB/s, ms per step)."""
+    t0 = time.perf_counter()
+    for i in range(steps):
+        xt = x[i % x.shape[0]:i % x.shape[0] + 1]
+        for L in stack:
+            xt, _, _ = oracle.moe_layer(L, xt, impl="orc")
+    ms = (time.perf_counter() - t0) * 1e3
+    return len(stack) * steps * layer_bytes() / (ms / 1e3) / 1e9, ms / steps
+
+
+def cpu_baseline(args, synth) -> dict:
+    """glm.c's own CPU path (compiled from its sources, OpenMP on all host
+    cores) on bounded samples of every benchmark configuration, in this
+    process on the GPU box's host: config 0 on the headline workload (the
+    line's value), a 1-thread line, config-1 matvec shapes, config-2 decode
+    forwards, config-3 and config-4 token loops."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
 
-    kind, threads, what = cpu_kind(oracle)
-    probe = time_cpu_calls(oracle, layer_host, x_host, 2, 5) / 5.0
-    iters = max(5, int(budget_s * 1000.0 / max(probe, 1e-3)))
-    ms = time_cpu_calls(oracle, layer_host, x_host, 2, iters)
-    gbps = iters * layer_bytes() / (ms / 1e3) / 1e9
-    return {"value": round(gbps, 3), "unit": UNIT, "cores": threads, "kind": kind,
-            "sample": f"{iters} calls of {what} (one config-0 layer, {x_host.shape[0]} "
-                      f"rotating tokens), {ms / iters:.3f} ms/call, threads={threads}"}
+    cpu_threads_env(oracle)
+    stack, distinct = host_moe_stack(synth, args.layers, args.seed)
+    x = synth.tokens(args.seed, 64, D)
+    out = {"unit": UNIT, "cpu_model": cpu_model_name()}
+    if not oracle.ref_available():
+        gbps, ms = cpu_port_gbps(oracle, stack, x, 1)
+        out.update(value=round(gbps, 3), cores=1, kind="port",
+                   sample=f"1 token x {len(stack)} layers ({distinct} distinct) through the oracle's C "
+                          f"restatement of apply_moe_shared_ffn_layer (oracle/_ref not built), {ms:.1f} ms/token")
+        return out
+    threads = oracle.omp_threads()
+    gbps, steps, ms = cpu_stack_gbps(oracle, stack, x, 1, args.cpu_budget_s)
+    out.update(value=round(gbps, 3), cores=threads, kind="reference",
+               sample=f"{steps} tokens x {len(stack)} layers ({distinct} distinct in host memory) through glm.c "
+                      f"apply_moe_shared_ffn_layer, {ms:.2f} ms/token ({ms / len(stack):.3f} ms/layer), "
+                      f"threads={threads}")
+    # one thread, the same workload
+    oracle.set_omp_threads(1)
+    g1, s1, m1 = cpu_stack_gbps(oracle, stack, x, 0, max(1.0, args.cpu_budget_s / 4))
+    oracle.set_omp_threads(threads)
+    out["one_thread"] = {"value": round(g1, 3), "unit": UNIT, "ms_per_layer": round(m1 / len(stack), 3),
+                         "sample": f"{s1} tokens x {len(stack)} layers, threads=1"}
+    # config 1: matvec shapes (glm.c's matvec_q80_rows)
+    mv = {}
+    for rows, cols in MATVEC_SHAPES:
+        q, sc, xv = synth.matvec_case(args.seed, rows, cols, GS)
+        probe = oracle.time_matvec(q, sc, xv, GS, 1, 2) / 2
+        iters = max(3, int(0.5 * 1000.0 / max(probe, 1e-3)))
+        ms_mv = oracle.time_matvec(q, sc, xv, GS, 1, iters) / iters
+        mv[f"{rows}x{cols}"] = {"ms": round(ms_mv, 4),
+                                "gbps": round(synth.q8_matvec_bytes(rows, cols, GS) / (ms_mv / 1e3) / 1e9, 2)}
+    out["matvec"] = mv
+    # configs 3 and 4: token loops through Zipf-routed layers
+    zl = dict(stack[0], router_bias=synth.zipf_bias(args.seed, 0, E))
+    xt = synth.tokens(args.seed, args.prefill_tokens, D)
+    ms3 = oracle.time_moe_layer(zl, xt, 1, args.prefill_tokens)
+    out["prefill"] = {"tokens": args.prefill_tokens, "ms": round(ms3, 2),
+                      "tok_s": round(args.prefill_tokens / (ms3 / 1e3), 1),
+                      "sample": f"{args.prefill_tokens} tokens one by one through one config-0 layer, Zipf(1.1) bias"}
+    n4 = 128
+    zstack = [dict(stack[l], router_bias=synth.zipf_bias(args.seed, l, E)) for l in range(args.ep_layers)]
+    ms4 = oracle.time_moe_stack(zstack, synth.tokens(args.seed + 1, n4, D), 1, n4)
+    out["ep_prefill"] = {"tokens": n4, "layers": args.ep_layers, "ms": round(ms4, 2),
+                         "tok_s": round(n4 / (ms4 / 1e3), 1),
+                         "sample": f"{n4} of config 4's 4096 tokens one by one through {args.ep_layers} layers "
+                                   "(per-token cost is constant on the CPU)"}
+    # config 2: glm_cpu_forward_token on the full decoder, a short greedy run
+    if not args.no_decode:
+        dims = dict(synth.CONFIG2)
+        moe = [stack[l % len(stack)] for l in range(dims["n_layers"] - 1)]
+        model = synth.decoder_model(args.seed, moe_layers=moe, **dims)
+        n_p, n_g = 4, 4
+        prompt = synth.prompt_ids(args.seed, n_p, dims["vocab_size"])
+        t0 = time.perf_counter()
+        oracle.ref_decode(model, prompt, n_g, n_p + n_g + 8)
+        sec = time.perf_counter() - t0
+        out["decode"] = {"tok_s": round((n_p + n_g) / sec, 3), "forwards": n_p + n_g,
+                         "sample": f"glm_cpu_forward_token for {n_p} prompt + {n_g} greedy tokens (wall clock of "
+                                   "the loop, one forward per token), 47 layers, vocab 154880"}
+        del model
+    return out
 
 
 def run_reference(args) -> None:
+    """BASELINE's reference arm: glm.c's own CPU implementation of the path on
+    this box's host cores (rank 0 only), on the repo arm's workload: one token
+    per step through 46 distinct config-0 MoE layers."""
     world, rank, _ = dist_setup()
     if rank != 0:
         return
@@ -290,36 +395,38 @@ def run_reference(args) -> None:
 
     synth = load_package().synth
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    ncores = os.cpu_count() or 1
-    os.environ.setdefault("OMP_NUM_THREADS", str(ncores))
-    os.environ.setdefault("OMP_PROC_BIND", "true")
-    os.environ.setdefault("OMP_PLACES", "cores")
     import oracle
 
-    kind, threads, what = cpu_kind(oracle)
-    L = synth.moe_layer(seed=42, **synth.CONFIG0)
-    x = synth.tokens(42, 64, D)
-    probe = time_cpu_calls(oracle, L, x, 1, 3) / 3.0
-    step_s = args.ref_budget_s / max(1, args.steps + args.warmup)
-    calls = max(2, int(step_s * 1000.0 / max(probe, 1e-3)))
-    for _ in range(args.warmup):
-        time_cpu_calls(oracle, L, x, 0, calls)
-    total_ms = 0.0
-    for _ in range(args.steps):
-        total_ms += time_cpu_calls(oracle, L, x, 0, calls)
-    gbps = args.steps * calls * layer_bytes() / (total_ms / 1e3) / 1e9
-    sample = (f"each step = {calls} calls of {what} on one config-0 layer with 64 "
-              f"rotating tokens ({total_ms / (args.steps * calls):.3f} ms/call)")
+    cpu_threads_env(oracle)
+    stack, distinct = host_moe_stack(synth, args.layers, args.seed)
+    x = synth.tokens(args.seed, 64, D)
+    if oracle.ref_available():
+        kind, threads = "reference", oracle.omp_threads()
+        oracle.time_moe_stack(stack, x, 0, args.warmup)
+        total_ms = oracle.time_moe_stack(stack, x, 0, args.steps)
+        what = "glm.c apply_moe_shared_ffn_layer (compiled from its sources, OpenMP)"
+    else:
+        kind, threads = "port", 1
+        steps = max(1, min(args.steps, 3))
+        _, ms = cpu_port_gbps(oracle, stack, x, steps)
+        total_ms = ms * args.steps
+        what = "the oracle's single-threaded C restatement (glm.c was not compiled on this box)"
+    gbps = args.steps * len(stack) * layer_bytes() / (total_ms / 1e3) / 1e9
+    sample = (f"each step = 1 token through {len(stack)} layers ({distinct} distinct in host memory) of {what}, "
+              f"{total_ms / args.steps:.2f} ms/step")
     line = {
-        "impl": "reference", "metric": METRIC, "value": round(gbps, 3), "unit": UNIT, "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 3),
+        "impl": "reference", "kind": kind, "metric": METRIC, "value": round(gbps, 3), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32/int8",
         "data": "synthetic (seeded; BASELINE config-0 distributions)",
-        "config": {"workload": "moe_decode", "layer": "config-0 MoE FFN", "batch": 1, "group_size": GS},
-        "cpu_baseline": {"value": round(gbps, 3), "unit": UNIT, "cores": threads, "kind": kind,
-                         "sample": sample},
+        "config": workload_config(world, len(stack)),
+        "cpu_baseline": {"value": round(gbps, 3), "unit": UNIT, "cores": threads, "kind": kind, "sample": sample,
+                         "cpu_model": cpu_model_name()},
         "e2e": {"value": round(gbps, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if kind == "port":
+        line["note"] = ("kind port: a 1-thread restatement, not glm.c's OpenMP build; a ratio against it "
+                        "overstates the speed-up")
     print(json.dumps(line))
 
 
@@ -338,6 +445,54 @@ def zipf_layer(torch, layer: dict, pkg, seed: int, li: int, dev) -> dict:
     out = dict(layer)
     out["router_bias"] = torch.from_numpy(pkg.synth.zipf_bias(seed, li, E)).to(dev)
     return out
+
+
+def run_matvec_leg(torch, lib, dev, world: int) -> dict:
+    """glm_cuda_matvec_q80_async on each shape, L2-cold:
+    the launches rotate over enough distinct weight copies (>= 3x L2 in
+    total) that every launch streams its matrix from HBM. GB/s = the shape's
+    q80 bytes (infer.c:1464-1470) + x and y, over the mean launch time
+    (CUDA events around a run of back-to-back launches)."""
+    from __graft_entry__ import load_package
+
+    synth = load_package().synth
+    peaks = measured_peaks()
+    out = {}
+    g = torch.Generator(device=dev)
+    g.manual_seed(4242)
+    st = torch.cuda.Stream(device=dev)
+    for rows, cols in MATVEC_SHAPES:
+        nb = synth.q8_matvec_bytes(rows, cols, GS)
+        copies = max(2, -(-384 * 2**20 // nb))
+        qs = [torch.randint(-127, 128, (rows, cols), generator=g, device=dev, dtype=torch.int8) for _ in range(copies)]
+        ss = [torch.randn(rows, cols // GS, generator=g, device=dev).abs_().mul_(0.02 / 127.0) for _ in range(copies)]
+        x = torch.randn(cols, generator=g, device=dev)
+        y = torch.empty(rows, device=dev)
+        reps = max(copies, 64)
+        for i in range(copies):  # warm-up: attributes, code
+            lib.matvec_async(qs[i], ss[i], x, y, rows, cols, GS, stream=st.cuda_stream)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record(st)
+        for i in range(reps):
+            lib.matvec_async(qs[i % copies], ss[i % copies], x, y, rows, cols, GS, stream=st.cuda_stream)
+        b.record(st)
+        torch.cuda.synchronize()
+        us = a.elapsed_time(b) * 1e3 / reps
+        if world > 1:
+            import torch.distributed as dist
+
+            t = torch.tensor([us], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            us = float(t.item())
+        gbps = nb / (us / 1e6) / 1e9
+        out[f"{rows}x{cols}"] = {"us": round(us, 3), "gbps": round(gbps, 1),
+                                 "frac_of_hbm_peak": round(gbps / peaks["hbm_gbs"], 4), "bytes": nb,
+                                 "copies_rotated": copies}
+        del qs, ss
+    torch.cuda.empty_cache()
+    return {"metric": "Q8 matvec GB/s per shape (config 1, batch 1, L2-cold)", "shapes": out,
+            "api": "glm_cuda_matvec_q80_async (back-to-back launches over rotating weight copies)"}
 
 
 def run_prefill_leg(args, torch, pkg, lib, layers, dev, local, rank, world) -> dict:
@@ -784,6 +939,7 @@ def run_ours(args) -> None:
         del glob, attn
 
     route_stats = lib.route_stats()
+    matvec = None if args.no_matvec else run_matvec_leg(torch, lib, dev, world)
     prefill = None
     if not args.no_prefill:
         prefill = run_prefill_leg(args, torch, pkg, lib, layers, dev, local, rank, world)
@@ -793,9 +949,7 @@ def run_ours(args) -> None:
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        host_layer = {k: v.cpu().numpy() for k, v in layers[0].items()}
-        host_layer.update(dim=D, ffn=F, n_experts=E, k_used=K, gs=GS)
-        cpu = cpu_baseline(host_layer, tok_host, args.cpu_budget_s)
+        cpu = cpu_baseline(args, pkg.synth)
 
     if rank == 0:
         line = {
@@ -803,13 +957,9 @@ def run_ours(args) -> None:
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8 weights x int8-digit activations -> int32; fp32 scales/accum",
             "data": "synthetic (seeded, BASELINE config-0 distributions, generated on device)",
-            "config": {"workload": "moe_decode: 1 token x 46 distinct GLM-4.7-Flash MoE FFN layers per step",
-                       "dim": D, "moe_ffn_dim": F, "experts": E, "top_k": K, "group_size": GS,
-                       "layers_per_step": N_MOE_LAYERS, "global_batch": world,
-                       "parallelism": f"replicas x{world}",
-                       "l2": "inputs larger than L2: 46 distinct layers = %.1f GB per GPU" %
-                             (N_MOE_LAYERS * 690.1e6 / 1e9),
-                       "timing": "CUDA-graph replays, CUDA events, max over ranks"},
+            "config": workload_config(world, N_MOE_LAYERS),
+            "l2": "inputs larger than L2: 46 distinct layers = %.1f GB per GPU" % (N_MOE_LAYERS * 690.1e6 / 1e9),
+            "timing": "CUDA-graph replays, CUDA events, max over ranks",
             "layer_us": round(ms / args.steps / N_MOE_LAYERS * 1e3, 3),
             "roofline": {"bound": "hbm", "kernel": names[dom], "achieved": round(achieved, 1),
                          "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
@@ -828,6 +978,8 @@ def run_ours(args) -> None:
         }
         if stacked is not None:
             line["stacked"] = stacked
+        if matvec is not None:
+            line["matvec"] = matvec
         if decode is not None:
             line["decode"] = decode
         if cpu is not None:
@@ -869,6 +1021,7 @@ def main() -> None:
     ap.add_argument("--only", choices=["prefill", "ep"], default=None,
                     help="run only the config-3 prefill or the config-4 expert-parallel measurement")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 batched prefill measurement")
+    ap.add_argument("--no-matvec", action="store_true", help="skip the config-1 matvec measurement")
     ap.add_argument("--prefill-tokens", type=int, default=512)
     ap.add_argument("--prefill-steps", type=int, default=20)
     ap.add_argument("--no-ep", action="store_true", help="skip the config-4 expert-parallel measurement")

@@ -2,7 +2,7 @@
 // mapped read-only, its header checked and every tensor's offset computed
 // as glm.c's runtime_open does (infer.c:357-744), and the tensors uploaded
 // through the library's own upload calls. Replaces runtime_open +
-// glm_backend_init (backend.c:88-101) for the cuda backend.
+// glm_backend_init (backend.c:73-86) for the cuda backend.
 //
 // Layout (format of glm47_flash_export.py:681-819, read by infer.c):
 //   256-byte header (RuntimeConfig, model.h:7-45)

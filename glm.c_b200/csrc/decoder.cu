@@ -381,12 +381,8 @@ size_t mla_heads_smem(const MlaArgs& a, int cache_cap) {
 cudaError_t launch_mla_heads(const MlaArgs& a, int n_heads, int cache_cap, cudaStream_t st) {
     const size_t smem = mla_heads_smem(a, cache_cap);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
-    static size_t cap = 0;
-    if (smem > 48 * 1024 && smem > cap) {
-        cudaError_t e = cudaFuncSetAttribute(mla_heads_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        cap = smem;
-    }
+    if (smem > 48 * 1024)
+        if (cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(mla_heads_kernel), (int)smem)) return e;
     return launch_pdl(mla_heads_kernel, n_heads, 512, smem, st, a);
 }
 

@@ -6,6 +6,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 #include <unordered_map>
@@ -15,6 +16,24 @@
 
 #include "glm_cuda.h"
 #include "glm_internal.h"
+
+namespace glmq {
+
+cudaError_t ensure_smem_attr(const void* fn, int bytes) {
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, int> set;
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err) return err;
+    std::lock_guard<std::mutex> lk(mu);
+    int& have = set[{fn, dev}];
+    if (have >= bytes) return cudaSuccess;
+    err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (!err) have = bytes;
+    return err;
+}
+
+}  // namespace glmq
 
 namespace {
 

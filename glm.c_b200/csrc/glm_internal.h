@@ -251,4 +251,10 @@ cudaError_t launch_moe_prefill(const MoeLayerDev& w, const MoeDims& d, unsigned 
 // Record the message glm_cuda_last_error() returns for this thread.
 void set_last_error(const char* msg);
 
+// Raise kernel `fn`'s dynamic shared-memory limit to at least `bytes` on the
+// current device. The attribute is per device, so the record is keyed on
+// (kernel, device) under a mutex; a later call for the same pair and size
+// makes no CUDA call (safe inside stream capture).
+cudaError_t ensure_smem_attr(const void* fn, int bytes);
+
 }  // namespace glmq

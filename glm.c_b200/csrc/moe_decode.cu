@@ -586,15 +586,13 @@ cudaError_t launch_moe_decode(const MoeLayerDev& w, const MoeDims& d, const MoeS
                               float* x_out, int routed_enabled, int num_sms, cudaStream_t stream,
                               cudaEvent_t* events) {
     if (d.K < 1 || d.K > kMaxTopK || d.K > d.E || d.gs != 32 || d.D % 128 || d.F % 64) return cudaErrorInvalidValue;
-    static bool attrs_set = false;
     const size_t sm1 = route_smem(d.D, d.E), sm2 = gate_up_smem(d.D), sm3 = down_smem(d.F, d.K + 1);
-    if (!attrs_set) {
-        cudaFuncSetAttribute(moe_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        cudaFuncSetAttribute(moe_gate_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        cudaFuncSetAttribute(moe_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        attrs_set = true;
-    }
     if (sm1 > 200 * 1024 || sm2 > 200 * 1024 || sm3 > 200 * 1024) return cudaErrorInvalidValue;
+    cudaError_t err;
+    if ((err = ensure_smem_attr(reinterpret_cast<const void*>(moe_route_kernel), (int)sm1)) ||
+        (err = ensure_smem_attr(reinterpret_cast<const void*>(moe_gate_up_kernel), (int)sm2)) ||
+        (err = ensure_smem_attr(reinterpret_cast<const void*>(moe_down_kernel), (int)sm3)))
+        return err;
 
     RouteArgs ra{x_in, w.ffn_norm, w.router, w.router_bias, s.xn, s.center, s.bound, s.topk_idx, s.topk_w,
                  s.counter, s.stats, d.D, d.E, d.K};

@@ -827,13 +827,7 @@ cudaError_t launch_moe_persistent(const MoeLayerDev* layers_dev, int first, int 
     size_t smem = 0;
     cudaError_t err = persistent_check(d, num_sms, &smem);
     if (err != cudaSuccess) return err;
-    static size_t cap = 0;
-    if (smem > cap) {
-        if ((err = cudaFuncSetAttribute(moe_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)smem)))
-            return err;
-        cap = smem;
-    }
+    if ((err = ensure_smem_attr(reinterpret_cast<const void*>(moe_persistent_kernel), (int)smem))) return err;
     PersistArgs a{layers_dev, first,    n_layers, x,           s.h,       s.center,
                   s.bound,    topk_out, topkw_out, s.grid_bar, s.grid_bar + 1, s.status, s.stats,
                   d.D,        d.F,      d.E,       d.K,        routed_enabled,

@@ -31,8 +31,6 @@
 // to the stage buffer's mbarrier. The accumulator (128 x 64 fp32) lives in
 // TMEM; four warps read it back with tcgen05.ld (thread = weight row).
 #include <cstdint>
-#include <map>
-#include <mutex>
 #include <utility>
 
 #include <cuda.h>
@@ -47,8 +45,6 @@
 namespace glmq {
 
 namespace {
-
-cudaError_t ensure_smem_attr(const void* fn, int bytes);
 
 constexpr int kMaxGroups = 257;  // routed experts + the shared expert
 constexpr int kTM = 128;     // weight rows per tile (MMA M)
@@ -1135,22 +1131,6 @@ __global__ void ep_combine_kernel(float* x, const float* __restrict__ Y, const i
         xv.w = __fadd_rn(xv.w, __fadd_rn(ys.w, acc.w));
         *xp = xv;
     }
-}
-
-// Raise a kernel's dynamic shared-memory limit once per device (so that
-// launches captured into a CUDA graph make no attribute calls).
-cudaError_t ensure_smem_attr(const void* fn, int bytes) {
-    static std::mutex mu;
-    static std::map<std::pair<const void*, int>, int> set;
-    int dev = 0;
-    cudaError_t err = cudaGetDevice(&dev);
-    if (err) return err;
-    std::lock_guard<std::mutex> lk(mu);
-    int& have = set[{fn, dev}];
-    if (have >= bytes) return cudaSuccess;
-    err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    if (!err) have = bytes;
-    return err;
 }
 
 // ------------------------------------------------------------ tensor maps

@@ -227,8 +227,7 @@ cudaError_t launch_q80_matvec(const int8_t* q, const float* s, const float* x, f
     if (gs == 16) {
         const size_t smem16 = (size_t)cols * 4;
         if (smem16 > 200 * 1024) return cudaErrorInvalidValue;
-        cudaError_t e = cudaFuncSetAttribute(q80_matvec_g16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem16);
+        cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(q80_matvec_g16_kernel), (int)smem16);
         if (e) return e;
         int grid = num_sms * 2;
         if (grid > (rows + kG16Warps - 1) / kG16Warps) grid = (rows + kG16Warps - 1) / kG16Warps;
@@ -237,11 +236,7 @@ cudaError_t launch_q80_matvec(const int8_t* q, const float* s, const float* x, f
     }
     const size_t smem = q80_matvec_smem_bytes(cols, norm != nullptr);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(q80_matvec_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        attr_set = true;
-    }
+    if (cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(q80_matvec_kernel), (int)smem)) return e;
     int grid = num_sms;
     if (grid > (rows + 15) / 16) grid = (rows + 15) / 16;
     MatvecArgs a{q, s, x, y, rows, cols, accumulate ? 1 : 0, norm};

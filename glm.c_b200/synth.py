@@ -135,10 +135,11 @@ def q8_matvec_bytes(rows: int, cols: int, gs: int) -> int:
     return rows * cols + rows * (cols // gs) * 4 + 4 * (rows + cols)
 
 
-def decoder_model(seed: int = 42, **dims) -> dict:
+def decoder_model(seed: int = 42, moe_layers: list | None = None, **dims) -> dict:
     """Weights of a full decoder with the given GlmCudaModelDims fields:
     Q8 linear layers as in config 0, all norms 1; layers 1.. are MoE layers
-    of moe_layer(seed, layer). Returns {"dims", "globals", "attn": [..],
+    of moe_layer(seed, layer), or the prebuilt `moe_layers` (one per layer
+    1..n_layers-1) when given. Returns {"dims", "globals", "attn": [..],
     "moe": [None, ..]}."""
     d = dict(dims)
     D, gs, H = d["dim"], d["group_size"], d["n_heads"]
@@ -161,9 +162,27 @@ def decoder_model(seed: int = 42, **dims) -> dict:
         for name, ((rows, cols), lead) in shapes.items():
             a[name + "_q"], a[name + "_s"] = q8_weights(_rng(seed, l, name + "_q"), rows, cols, gs, lead)
         attn.append(a)
-    moe = [None] + [moe_layer(seed, l, D, d["moe_ffn_dim"], d["n_routed_experts"], d["n_experts_used"], gs)
-                    for l in range(1, d["n_layers"])]
+    if moe_layers is not None:
+        assert len(moe_layers) == d["n_layers"] - 1
+        moe = [None] + list(moe_layers)
+    else:
+        moe = [None] + [moe_layer(seed, l, D, d["moe_ffn_dim"], d["n_routed_experts"], d["n_experts_used"], gs)
+                        for l in range(1, d["n_layers"])]
     return {"dims": d, "globals": g, "attn": attn, "moe": moe}
+
+
+def rolled_moe_layer(base: dict, shift: int) -> dict:
+    """A layer with distinct memory and different (still config-0
+    distributed) weights, made cheaply from `base`: the routed experts, the
+    router rows and the bias rotated by `shift` along the expert axis, and
+    the shared expert's rows rotated by `shift`. Used where many distinct
+    layers must sit in host memory and generating each one afresh would take
+    seconds (CPU baselines)."""
+    L = {k: v for k, v in base.items() if not isinstance(v, np.ndarray)}
+    for k, v in base.items():
+        if isinstance(v, np.ndarray):
+            L[k] = v.copy() if k == "ffn_norm" else np.roll(v, shift, axis=0)
+    return L
 
 
 def prompt_ids(seed: int, n: int, vocab: int) -> np.ndarray:

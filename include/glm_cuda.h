@@ -36,9 +36,9 @@ extern "C" {
 #define GLM_CUDA_ERR_NOMEM (-4)    /* device allocation failed */
 
 /* Device bring-up and per-process state for `n_layers` layer slots.
- * Replaces the device part of glm_backend_init (backend.h:7, backend.c:88-101;
+ * Replaces the device part of glm_backend_init (backend.h:7, backend.c:73-86;
  * Metal counterpart glm_metal_init, infer.m:847-929). The glm.c glue treats a
- * nonzero return the way backend.c:94-97 treats a Metal init failure. */
+ * nonzero return the way backend.c:79-82 treats a Metal init failure. */
 int glm_cuda_init(int device, int dim, int moe_ffn_dim, int n_routed_experts, int n_experts_used,
                   int group_size, int n_layers);
 
@@ -244,7 +244,7 @@ int glm_cuda_moe_layer_noalloc(const float *ffn_norm, const float *gate_inp, con
 
 /* y[rows] = Q8(qmat, smat) . x[dim], host pointers. Same signature and
  * return convention as glm_backend_try_metal_matvec (backend.h:13,
- * backend.c:82-86; called by matvec_rows at infer.c:793): 0 = handled,
+ * backend.c:67-71; called by matvec_rows at infer.c:793): 0 = handled,
  * nonzero = not handled. The weight matrix is copied to HBM on first use and
  * cached by its host address, as infer.m:307-322 caches Metal buffers. */
 int glm_cuda_matvec_q80(const int8_t *qmat, const float *smat, const float *x, float *y, int rows, int dim, int gs);
@@ -273,7 +273,7 @@ const char *glm_cuda_last_error(void);
 /* ------------------------------------------------------------------------
  * Full batch-1 decoder (GLM-4.7-Flash: MLA attention in every layer, a dense
  * SwiGLU FFN in layer 0, MoE FFN in layers 1..n_layers-1), the device side of
- * glm_backend_forward_token (backend.h:8, backend.c:88-101).
+ * glm_backend_forward_token (backend.h:8, backend.c:88-91).
  * ------------------------------------------------------------------------ */
 
 /* Shapes, named after RuntimeConfig (model.h:7-45). cache_cap = KV-cache
@@ -286,7 +286,7 @@ typedef struct GlmCudaModelDims {
 
 /* Device bring-up for the whole decoder; also does glm_cuda_init for the MoE
  * layers (then uploaded with glm_cuda_upload_moe_layer, layers 1..). Replaces
- * glm_backend_init's device part (backend.c:88-101). */
+ * glm_backend_init's device part (backend.c:73-86). */
 int glm_cuda_model_init(int device, const GlmCudaModelDims *dims);
 
 /* Runtime's model-wide weights (model.h:87-103): output_norm, token
@@ -334,13 +334,13 @@ int glm_cuda_forward_token(int token, int pos, float *logits);
 int glm_cuda_generate(const int32_t *prompt, int n_prompt, int n_gen, int32_t *out_ids, float *device_ms);
 
 /* Release all device memory and state. Replaces glm_backend_free's device
- * part (backend.c:108-110, glm_metal_free). Safe to call twice. */
+ * part (backend.c:93-95, glm_metal_free). Safe to call twice. */
 /* glm.c's runtime checkpoint (.bin, format version 4 with every layer's
  * attention, as glm47_flash_export.py writes it) to the device: maps the
  * file, checks the header and offsets as runtime_open does (infer.c:357-744),
  * then glm_cuda_model_init(device, dims from the header, cache_cap) and the
  * upload calls for the globals, every attention layer and every MoE layer.
- * Replaces runtime_open + glm_backend_init (backend.c:88-101) for the cuda
+ * Replaces runtime_open + glm_backend_init (backend.c:73-86) for the cuda
  * backend; glm_cuda_forward_token / glm_cuda_generate follow. A malformed
  * file is GLM_CUDA_ERR_ARG (glm.c exits instead). */
 int glm_cuda_load_checkpoint(const char *path, int device, int cache_cap);

@@ -29,9 +29,16 @@ MOE_FIELDS = (
 _libs: dict = {}
 
 
+def reference_dir() -> str:
+    """Where glm.c's sources are: $GLM_REFERENCE_DIR, else a `reference`
+    directory beside this repository ('' when neither holds infer.c)."""
+    cand = os.environ.get("GLM_REFERENCE_DIR") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+    return cand if os.path.isfile(os.path.join(cand, "infer.c")) else ""
+
+
 def build() -> None:
     """Compile liborc.so (and _ref/libglmref.so where the reference sources exist)."""
-    subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
+    subprocess.run(["make", "-s", "-C", HERE, "all", f"REF_DIR={reference_dir()}"], check=True)
 
 
 def ref_available() -> bool:
@@ -64,12 +71,16 @@ def lib(impl: str = "orc") -> ctypes.CDLL:
         L.ref_moe_layer.restype = I
         L.ref_time_moe_layer.argtypes = [I, I, I, I, I, P, I, P, I, I, ctypes.POINTER(ctypes.c_double)]
         L.ref_time_moe_layer.restype = I
+        L.ref_time_moe_stack.argtypes = [I, I, I, I, I, P, I, I, P, I, I, ctypes.POINTER(ctypes.c_double)]
+        L.ref_time_moe_stack.restype = I
         L.ref_matvec_q80.argtypes = [P, P, P, P, I, I, I]
         L.ref_matvec_q80.restype = None
         L.ref_time_matvec_q80.argtypes = [P, P, P, P, I, I, I, I, I, ctypes.POINTER(ctypes.c_double)]
         L.ref_time_matvec_q80.restype = I
         L.ref_rmsnorm.argtypes = [P, P, P, I]
         L.ref_omp_max_threads.restype = I
+        L.ref_set_omp_threads.argtypes = [I]
+        L.ref_set_omp_threads.restype = None
         if hasattr(L, "ref_decode"):
             L.ref_decode.argtypes = [P, P, P, P, P, I, I, P, P]
             L.ref_decode.restype = I
@@ -147,6 +158,28 @@ def time_moe_layer(layer: dict, x: np.ndarray, warmup: int, iters: int) -> float
     return out.value
 
 
+def time_moe_stack(layers: list, x: np.ndarray, warmup: int, steps: int) -> float:
+    """glm.c's MoE layer on one token per step through every layer of
+    `layers` in turn (distinct weights); total milliseconds of `steps` steps,
+    timed in C with the reference's own clock."""
+    L0 = layers[0]
+    x2 = np.array(x, dtype=np.float32, copy=True, order="C").reshape(-1, L0["dim"])
+    n = len(layers)
+    tab = (ctypes.c_void_p * (n * len(MOE_FIELDS)))()
+    keep = []
+    for l, layer in enumerate(layers):
+        t, k = _ptr_table(layer)
+        keep += k
+        for i in range(len(MOE_FIELDS)):
+            tab[l * len(MOE_FIELDS) + i] = t[i]
+    out = ctypes.c_double(0.0)
+    lib("ref").ref_time_moe_stack(L0["dim"], L0["ffn"], L0["n_experts"], L0["k_used"], L0["gs"],
+                                  ctypes.cast(tab, ctypes.c_void_p), n, x2.shape[0], _ptr(x2), warmup, steps,
+                                  ctypes.byref(out))
+    del keep
+    return out.value
+
+
 def matvec(q: np.ndarray, s: np.ndarray, x: np.ndarray, gs: int, impl: str = "orc") -> np.ndarray:
     q = np.ascontiguousarray(q, dtype=np.int8)
     s = np.ascontiguousarray(s, dtype=np.float32)
@@ -171,6 +204,10 @@ def time_matvec(q, s, x, gs: int, warmup: int, iters: int) -> float:
 
 def omp_threads() -> int:
     return int(lib("ref").ref_omp_max_threads())
+
+
+def set_omp_threads(n: int) -> None:
+    lib("ref").ref_set_omp_threads(int(n))
 
 
 # Table orders of ref_decode: Runtime globals (model.h:87-103) and

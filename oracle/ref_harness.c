@@ -14,6 +14,9 @@
  *   ref_rmsnorm      -> rmsnorm                      (infer.c:746-752)
  *   ref_time_moe_layer: wall-clock timing of the same call with the
  *                      reference's own clock (monotonic_ms, infer.c:1426)
+ *   ref_time_moe_stack: the same clock around one token passed through a
+ *                      stack of distinct MoE layers per step, as the
+ *                      decoder's layer loop calls them (infer.c:1819-1845)
  *   ref_decode       -> greedy generation with glm_cpu_forward_token
  *                      (infer.c:1903) and argmax (infer.c:1218), fed as
  *                      glm_app_main's loop feeds it (infer.c:2190-2228)
@@ -119,6 +122,48 @@ int ref_time_moe_layer(int dim, int moe_dim, int n_experts, int n_used, int gs,
     return 0;
 }
 
+/* Times `steps` steps after `warmup` untimed ones; a step takes the next
+ * token row of x (cycling) through layers 0..n_layers-1 of `tables`
+ * ([n_layers][RP_COUNT] weight pointers), each layer's output feeding the
+ * next, as glm_cpu_forward_token's layer loop does. *ms_total: the steps'
+ * total milliseconds. */
+int ref_time_moe_stack(int dim, int moe_dim, int n_experts, int n_used, int gs,
+                       const void *const *tables, int n_layers, int n_tokens, const float *x,
+                       int warmup, int steps, double *ms_total) {
+    RefMoeCtx c;
+    ref_ctx_build(&c, dim, moe_dim, n_experts, n_used, gs, tables);
+    double t0 = 0.0;
+    for (int i = 0; i < warmup + steps; i++) {
+        if (i == warmup) t0 = monotonic_ms();
+        int t = i % (n_tokens > 0 ? n_tokens : 1);
+        memcpy(c.st.x, x + (size_t)t * dim, (size_t)dim * sizeof(float));
+        for (int l = 0; l < n_layers; l++) {
+            const void *const *p = tables + (size_t)l * RP_COUNT;
+            LayerMoeShared *w = &c.shared[1];
+            LayerMoeRouted *r = &c.routed[1];
+            w->ffn_norm = (const float *)p[RP_FFN_NORM];
+            w->gate_inp = (const float *)p[RP_GATE_INP];
+            w->exp_probs_b = (const float *)p[RP_EXP_PROBS_B];
+            w->gate_sh_q = (const int8_t *)p[RP_GATE_SH_Q];
+            w->gate_sh_s = (const float *)p[RP_GATE_SH_S];
+            w->up_sh_q = (const int8_t *)p[RP_UP_SH_Q];
+            w->up_sh_s = (const float *)p[RP_UP_SH_S];
+            w->down_sh_q = (const int8_t *)p[RP_DOWN_SH_Q];
+            w->down_sh_s = (const float *)p[RP_DOWN_SH_S];
+            r->gate_q = (const int8_t *)p[RP_GATE_Q];
+            r->gate_s = (const float *)p[RP_GATE_S];
+            r->up_q = (const int8_t *)p[RP_UP_Q];
+            r->up_s = (const float *)p[RP_UP_S];
+            r->down_q = (const int8_t *)p[RP_DOWN_Q];
+            r->down_s = (const float *)p[RP_DOWN_S];
+            apply_moe_shared_ffn_layer(&c.rt, &c.st, gs, 1, 0, 0);
+        }
+    }
+    *ms_total = monotonic_ms() - t0;
+    runstate_free(&c.st);
+    return 0;
+}
+
 void ref_matvec_q80(const int8_t *q, const float *s, const float *x, float *y, int rows, int dim, int gs) {
     matvec_q80_rows(q, s, x, y, rows, dim, gs);
 }
@@ -136,6 +181,15 @@ int ref_time_matvec_q80(const int8_t *q, const float *s, const float *x, float *
 
 void ref_rmsnorm(float *o, const float *x, const float *w, int n) {
     rmsnorm(o, x, w, n);
+}
+
+/* OpenMP team size of later calls (the 1-thread baseline line). */
+void ref_set_omp_threads(int n) {
+#ifdef _OPENMP
+    omp_set_num_threads(n > 0 ? n : 1);
+#else
+    (void)n;
+#endif
 }
 
 int ref_omp_max_threads(void) {

@@ -21,7 +21,10 @@ def _check_line(line: dict, kind: str) -> None:
     assert line["cpu_baseline"]["kind"] == kind and line["cpu_baseline"]["cores"] >= 1
     assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}
-    assert line["config"]["workload"] == "moe_decode"
+    import bench
+
+    # the repo arm's exact workload dict (here with the small test stack)
+    assert line["config"] == bench.workload_config(1, 2)
 
 
 def test_reference_arm_json_line():
@@ -31,7 +34,7 @@ def test_reference_arm_json_line():
     if not oracle.ref_available():
         pytest.skip("oracle/_ref not built here")
     r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1",
-                        "--warmup", "3", "--ref-budget-s", "2"], capture_output=True, text=True, timeout=600,
+                        "--warmup", "3", "--layers", "2"], capture_output=True, text=True, timeout=600,
                        cwd=ROOT, env=dict(os.environ, OMP_NUM_THREADS="2"))
     assert r.returncode == 0, r.stderr[-2000:]
     _check_line(json.loads(r.stdout.strip().splitlines()[-1]), "reference")
@@ -46,10 +49,10 @@ def test_reference_arm_falls_back_to_the_oracle_port(monkeypatch):
     monkeypatch.setattr(oracle, "ref_available", lambda: False)
     out = io.StringIO()
     with contextlib.redirect_stdout(out):
-        bench.run_reference(argparse.Namespace(steps=1, warmup=3, ref_budget_s=1.0))
+        bench.run_reference(argparse.Namespace(steps=1, warmup=3, layers=2, seed=42))
     line = json.loads(out.getvalue().strip().splitlines()[-1])
     _check_line(line, "port")
-    assert line["cpu_baseline"]["cores"] == 1
+    assert line["cpu_baseline"]["cores"] == 1 and line["kind"] == "port" and "note" in line
 
 
 def test_cpu_baseline_port_fallback(monkeypatch):
@@ -63,7 +66,25 @@ def test_cpu_baseline_port_fallback(monkeypatch):
 
     synth = load_package().synth
     monkeypatch.setattr(oracle, "ref_available", lambda: False)
-    L = synth.moe_layer(seed=3, **synth.CONFIG0)
-    x = synth.tokens(3, 4, 2048)
-    cb = bench.cpu_baseline(L, x, 0.3)
-    assert cb["kind"] == "port" and cb["cores"] == 1 and cb["value"] > 0
+    cb = bench.cpu_baseline(argparse.Namespace(layers=2, seed=3, cpu_budget_s=0.3), synth)
+    assert cb["kind"] == "port" and cb["cores"] == 1 and cb["value"] > 0 and cb["cpu_model"]
+
+
+def test_cpu_baseline_every_config():
+    """With glm.c compiled: the config-0 line plus the 1-thread line, the
+    config-1 matvec shapes and the config-3/4 token loops (config 2's full
+    decoder is skipped here: it needs ~33 GB of host memory)."""
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import bench
+    import oracle
+    from __graft_entry__ import load_package
+
+    if not oracle.ref_available():
+        pytest.skip("oracle/_ref not built here")
+    synth = load_package().synth
+    args = argparse.Namespace(layers=2, seed=3, cpu_budget_s=0.3, prefill_tokens=16, ep_layers=2, no_decode=True)
+    cb = bench.cpu_baseline(args, synth)
+    assert cb["kind"] == "reference" and cb["value"] > 0 and cb["one_thread"]["value"] > 0
+    assert set(cb["matvec"]) == {f"{r}x{c}" for r, c in bench.MATVEC_SHAPES}
+    assert cb["prefill"]["tok_s"] > 0 and cb["ep_prefill"]["tok_s"] > 0
