@@ -260,8 +260,10 @@ int glm_cuda_synchronize(void);
 
 /* Router statistics since init: out[0] routed tokens, out[1] tokens whose
  * fast interval certification failed and took the exact recomputation,
- * out[2] ties that only libm's last bit of expf could decide (resolved with a
- * correctly rounded exp), out[3] rmsnorm means recomputed serially. */
+ * out[2] tokens still not certified after it: a tie that only libm's last
+ * bit of expf could decide (resolved with a correctly rounded exp), or
+ * experts with bit-identical exact logits (ordered by id, as glm.c orders
+ * them), out[3] rmsnorm means recomputed serially. */
 int glm_cuda_route_stats(uint64_t out[4]);
 
 /* Number of kernel launches the library has issued since init. */

@@ -32,6 +32,17 @@ def check_moe_outputs(x_in, x_out, x_out_ref, tol: float) -> float:
     return worst
 
 
+def assert_routing_exact(lib) -> None:
+    """Every routing since glm_cuda_init was certified even where its
+    intervals needed the exact recompute: glm_cuda_route_stats()[2] == 0. The
+    count is conservative (it also counts experts with bit-identical exact
+    logits, whose order the id settles exactly as glm.c's does), so it is
+    asserted on the benchmark configurations' random data, not on fixtures
+    built with exact ties."""
+    stats = lib.route_stats()
+    assert stats[2] == 0, f"{stats[2]} routings hinged on the last bit of expf (stats {stats})"
+
+
 @contextlib.contextmanager
 def routed_env(routed: bool):
     """Express 'routed experts off' the reference's way (GLM_DISABLE_MOE_ROUTED)."""

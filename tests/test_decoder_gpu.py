@@ -9,7 +9,7 @@ Bar (north star): greedy token ids identical; the logits of every step within
 import numpy as np
 import pytest
 
-from helpers import rel_l2
+from helpers import assert_routing_exact, rel_l2
 
 pytestmark = pytest.mark.gpu
 
@@ -53,6 +53,7 @@ def test_decoder_small_greedy_and_logits(path, lib, pkg, oracle_mod):
     lib.set_decode_path(path)
     ids, ms = lib.generate(prompt, n_gen)
     np.testing.assert_array_equal(ids, ids_ref)
+    assert_routing_exact(lib)
 
     # step by step through the host entry point: logits of every generated step
     tok = int(prompt[0])

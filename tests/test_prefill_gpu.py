@@ -9,7 +9,7 @@ within 1e-3 relative L2 of the reference (FFN delta x_out - x_in, per token).
 import numpy as np
 import pytest
 
-from helpers import check_moe_outputs, routed_env
+from helpers import assert_routing_exact, check_moe_outputs, routed_env
 
 pytestmark = pytest.mark.gpu
 
@@ -66,6 +66,7 @@ def test_prefill_config3_zipf_512_tokens(lib, pkg, oracle_mod):
     counts = np.bincount(ref[1].ravel(), minlength=64)
     print(f"config3: worst rel L2 {worst:.2e}; group sizes max {counts.max()} min {counts.min()}")
     assert counts.max() > 4 * max(counts.min(), 1)  # the groups really are uneven
+    assert_routing_exact(lib)
 
 
 @pytest.mark.parametrize("T", [1, 2, 63, 64, 65, 130])
