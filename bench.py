@@ -936,6 +936,21 @@ def run_ours(args) -> None:
                   "timing": "device time of glm_cuda_generate's step-graph replays (CUDA events); e2e: host "
                             "wall clock of the call (prompt H2D, graph build, ids D2H)",
                   "first_ids": ids[:8].tolist(), "api": "glm_cuda_generate"}
+        # How robust the greedy sequence is: the logits of every generated
+        # step (the same sequence replayed through glm_cuda_forward_token),
+        # their smallest top-1 minus top-2 margin, and whether each argmax is
+        # the id glm_cuda_generate produced.
+        feed = list(prompt) + ids.tolist()
+        gaps, agree = [], True
+        for pos in range(len(feed) - 1):
+            logits = lib.forward_token(int(feed[pos]), pos, dims["vocab_size"])
+            if pos >= len(prompt) - 1:
+                top2 = np.partition(logits, -2)[-2:]
+                gaps.append(float(top2[1] - top2[0]))
+                agree = agree and int(np.argmax(logits)) == int(feed[pos + 1])
+        g = int(np.argmin(gaps))
+        decode["greedy_margin"] = {"min_top1_minus_top2": round(gaps[g], 6), "at_step": g,
+                                   "median": round(float(np.median(gaps)), 5), "argmax_agrees": agree}
         del glob, attn
 
     route_stats = lib.route_stats()

@@ -19,6 +19,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORC_SO = os.path.join(HERE, "liborc.so")
 REF_SO = os.path.join(HERE, "_ref", "libglmref.so")
+REF_CUDA_SO = os.path.join(HERE, "_ref", "libglmref_cuda.so")  # glm.c patched with the cuda backend
 
 MOE_FIELDS = (
     "ffn_norm", "router", "router_bias",
@@ -37,8 +38,15 @@ def reference_dir() -> str:
 
 
 def build() -> None:
-    """Compile liborc.so (and _ref/libglmref.so where the reference sources exist)."""
-    subprocess.run(["make", "-s", "-C", HERE, "all", f"REF_DIR={reference_dir()}"], check=True)
+    """Compile liborc.so (and, where the reference sources exist, glm.c's own
+    code: _ref/libglmref.so, plus the cuda-patched glm.c of INTEGRATION.md
+    once the CUDA library is built)."""
+    ref = reference_dir()
+    subprocess.run(["make", "-s", "-C", HERE, "all", f"REF_DIR={ref}"], check=True)
+    import glm_cuda_patch
+
+    if ref and os.path.exists(os.path.join(glm_cuda_patch.CUDA_LIB_DIR, "libglm_cuda.so")):
+        glm_cuda_patch.build(ref)
 
 
 def ref_available() -> bool:
@@ -48,7 +56,7 @@ def ref_available() -> bool:
 def lib(impl: str = "orc") -> ctypes.CDLL:
     if impl in _libs:
         return _libs[impl]
-    path = ORC_SO if impl == "orc" else REF_SO
+    path = {"orc": ORC_SO, "ref": REF_SO, "refcuda": REF_CUDA_SO}[impl]
     if not os.path.exists(path):
         if impl == "orc":
             build()
@@ -221,11 +229,13 @@ DECODER_DIMS = ("dim", "hidden_dim", "n_layers", "n_heads", "vocab_size", "rope_
                 "group_size", "moe_ffn_dim", "cache_cap")
 
 
-def ref_decode(model: dict, prompt, n_gen: int, cache_cap: int, with_logits: bool = False):
+def ref_decode(model: dict, prompt, n_gen: int, cache_cap: int, with_logits: bool = False, impl: str = "ref"):
     """Greedy ids from glm.c's own forward pass (compiled from its sources):
     glm_cpu_forward_token per position, argmax at temperature 0, as
     glm_app_main feeds it (infer.c:2190-2228). model is synth.decoder_model's
-    dict; returns (ids [n_gen], logits [n_gen, vocab] or None)."""
+    dict; returns (ids [n_gen], logits [n_gen, vocab] or None). impl="refcuda"
+    runs glm.c patched with the cuda backend (oracle/glm_cuda_patch.py): the
+    same loop with every MoE layer and Q8 matvec in libglm_cuda.so."""
     d = dict(model["dims"], cache_cap=cache_cap)
     icfg = np.array([d[k] for k in DECODER_DIMS], dtype=np.int32)
     keep = []
@@ -245,7 +255,7 @@ def ref_decode(model: dict, prompt, n_gen: int, cache_cap: int, with_logits: boo
     p = np.ascontiguousarray(prompt, dtype=np.int32)
     out = np.zeros(n_gen, dtype=np.int32)
     logits = np.zeros((n_gen, d["vocab_size"]), dtype=np.float32) if with_logits else None
-    rc = lib("ref").ref_decode(icfg.ctypes.data, glob, attn, moe, p.ctypes.data, len(p), n_gen, out.ctypes.data,
+    rc = lib(impl).ref_decode(icfg.ctypes.data, glob, attn, moe, p.ctypes.data, len(p), n_gen, out.ctypes.data,
                                None if logits is None else logits.ctypes.data)
     del keep
     if rc != 0:

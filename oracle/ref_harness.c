@@ -213,7 +213,10 @@ int ref_omp_max_threads(void) {
  * The prompt ids are fed one per position; then n_gen tokens are picked
  * with argmax (temperature 0) and fed back. out_ids receives them; if
  * logits_out is not NULL it receives the logits of every generating step
- * ([n_gen][vocab]). Returns 0 or the failing forward's status. */
+ * ([n_gen][vocab]). Returns 0 or the failing forward's status. Built over
+ * the cuda-patched glm.c (GLM_ENABLE_CUDA, oracle/glm_cuda_patch.py), the
+ * loop runs with the cuda backend started, as glm_app_main starts it
+ * (infer.c:2174, 2258). */
 int ref_decode(const int32_t *icfg, const void *const *glob, const void *const *attn, const void *const *moe,
                const int32_t *prompt, int n_prompt, int n_gen, int32_t *out_ids, float *logits_out) {
     Runtime rt;
@@ -302,6 +305,9 @@ int ref_decode(const int32_t *icfg, const void *const *glob, const void *const *
 
     RunState st;
     runstate_build(&st, &rt, icfg[15]);
+#if defined(GLM_ENABLE_CUDA)
+    glm_backend_init(BACKEND_CUDA, &rt, &st);
+#endif
     int token = prompt[0];
     if (token < 0 || token >= c->vocab_size) token = 0;
     int prompt_index = 1, generated = 0, rc = 0;
@@ -321,6 +327,9 @@ int ref_decode(const int32_t *icfg, const void *const *glob, const void *const *
         }
         token = next;
     }
+#if defined(GLM_ENABLE_CUDA)
+    glm_backend_free(0);
+#endif
     runstate_free(&st);
     free(aw);
     free(ms);
