@@ -495,6 +495,82 @@ def run_matvec_leg(torch, lib, dev, world: int) -> dict:
             "api": "glm_cuda_matvec_q80_async (back-to-back launches over rotating weight copies)"}
 
 
+def run_gs16_leg(args, torch, pkg, lib, layers, dev, local, world) -> dict:
+    """The headline workload at gs = 16 (glm.c's own export): the same 46
+    layers' int8 weights with 16-column scale groups (fresh |N(0,0.02)|/127
+    scales), one token per step through the 46 per-layer persistent launches
+    of a CUDA graph, as the headline value; plus the 46 layers in one launch."""
+    import numpy as np
+
+    n = len(layers)
+    lib.init(local, D, F, E, K, 16, n)
+    g = torch.Generator(device=dev)
+    g.manual_seed(args.seed * 16 + 1)
+    layers16 = []
+    for li, L in enumerate(layers):
+        L16 = dict(L)
+        for k in [k for k in L if k.endswith("_s")]:
+            shp = tuple(L[k].shape[:-1]) + (L[k[:-2] + "_q"].shape[-1] // 16,)
+            L16[k] = torch.randn(shp, generator=g, device=dev).abs_().mul_(0.02 / 127.0)
+        layers16.append(L16)
+        lib.bind_moe_layer_device(li, L16)
+    path = lib.decode_path()
+    x0 = torch.randn(D, generator=g, device=dev)
+    x = torch.empty_like(x0)
+    st = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(st):
+        x.copy_(x0)
+        for li in range(n):
+            lib.moe_layer_async(li, x, 1, stream=st.cuda_stream)
+    torch.cuda.synchronize()
+    gph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gph, stream=st):
+        x.copy_(x0)
+        for li in range(n):
+            lib.moe_layer_async(li, x, 1, stream=torch.cuda.current_stream().cuda_stream)
+    for _ in range(args.warmup):
+        gph.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(st):
+        a.record(st)
+        for _ in range(args.steps):
+            gph.replay()
+        b.record(st)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    s_ms = []
+    for i in range(args.warmup + args.stack_steps):
+        with torch.cuda.stream(st):
+            x.copy_(x0)
+            a.record(st)
+            lib.moe_layers_async(0, n, x, stream=st.cuda_stream)
+            b.record(st)
+        torch.cuda.synchronize()
+        if i >= args.warmup:
+            s_ms.append(a.elapsed_time(b))
+    lib.synchronize()
+    del gph
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    lb16 = pkg.synth.moe_bytes(D, F, E, K, 16)
+    peak = measured_peaks()["hbm_gbs"]
+    gbps = world * n * lb16 / (ms / 1e3) / 1e9
+    out = {"metric": "MoE-layer HBM GB/s at gs = 16 (bs1 decode, 46 config-0 MoE layers per token)",
+           "value": round(gbps, 2), "unit": UNIT, "layer_us": round(ms / n * 1e3, 3),
+           "frac_of_hbm_peak": round(gbps / world / peak, 4), "bytes_per_layer": lb16,
+           "stacked_layer_us": round(float(np.mean(s_ms)) / n * 1e3, 3),
+           "decode_path": {1: "persistent", 2: "chain", 3: "batched"}.get(path, str(path)),
+           "route_stats": lib.route_stats()}
+    lib.free()
+    del layers16
+    return out
+
+
 def run_prefill_leg(args, torch, pkg, lib, layers, dev, local, rank, world) -> dict:
     """512 tokens (Zipf expert popularity) through one
     config-0 MoE layer with the batched prefill kernels."""
@@ -955,6 +1031,9 @@ def run_ours(args) -> None:
 
     route_stats = lib.route_stats()
     matvec = None if args.no_matvec else run_matvec_leg(torch, lib, dev, world)
+    gs16 = None
+    if not args.no_gs16 and N_MOE_LAYERS == 46:
+        gs16 = run_gs16_leg(args, torch, pkg, lib, layers, dev, local, world)
     prefill = None
     if not args.no_prefill:
         prefill = run_prefill_leg(args, torch, pkg, lib, layers, dev, local, rank, world)
@@ -995,6 +1074,8 @@ def run_ours(args) -> None:
             line["stacked"] = stacked
         if matvec is not None:
             line["matvec"] = matvec
+        if gs16 is not None:
+            line["gs16"] = gs16
         if decode is not None:
             line["decode"] = decode
         if cpu is not None:
@@ -1008,7 +1089,7 @@ def run_ours(args) -> None:
     del graphs
     # a routing that hinged on the last bit of expf may differ from glm.c's:
     # the line above stands as measured, but the run fails
-    unresolved = route_stats[2] + (prefill["route_stats"][2] if prefill else 0)
+    unresolved = route_stats[2] + (prefill["route_stats"][2] if prefill else 0) + (gs16["route_stats"][2] if gs16 else 0)
     if unresolved:
         print(f"[bench] {unresolved} routings were not certified exact (route_stats[2])", file=sys.stderr)
     if world > 1:
@@ -1044,6 +1125,7 @@ def main() -> None:
                     help="run only the config-3 prefill or the config-4 expert-parallel measurement")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 batched prefill measurement")
     ap.add_argument("--no-matvec", action="store_true", help="skip the config-1 matvec measurement")
+    ap.add_argument("--no-gs16", action="store_true", help="skip the gs = 16 decode measurement")
     ap.add_argument("--prefill-tokens", type=int, default=512)
     ap.add_argument("--prefill-steps", type=int, default=20)
     ap.add_argument("--no-ep", action="store_true", help="skip the config-4 expert-parallel measurement")

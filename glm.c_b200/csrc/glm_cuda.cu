@@ -339,9 +339,11 @@ int ensure_prefill_ws(int n_tokens) {
     return 0;
 }
 
-// The per-token decode kernels take gs = 32 only; other group sizes run every
-// call on the batched kernels.
-bool decode_kernels_ok() { return g.dims.gs == 32; }
+// Per-token decode kernels: the persistent kernel takes gs = 32 and 16, the
+// three-kernel chain gs = 32 only; where neither applies every call runs on
+// the batched kernels.
+bool chain_ok() { return g.dims.gs == 32; }
+bool decode_kernels_ok() { return use_persistent() || chain_ok(); }
 
 bool use_prefill(int n_tokens) {
     if (!g.prefill_ok) return false;
@@ -436,10 +438,10 @@ int init_locked(int device, int dim, int moe_ffn_dim, int n_routed_experts, int 
     *g.status_host = 0;
     g.persistent_ok = glmq::persistent_check(g.dims, g.num_sms, nullptr) == cudaSuccess;
     g.prefill_ok = glmq::prefill_check(g.dims) == cudaSuccess;
-    if (group_size != 32 && !g.prefill_ok) {
+    if (group_size != 32 && !g.prefill_ok && !g.persistent_ok) {
         release_all();
-        return fail(GLM_CUDA_ERR_ARG, "group size %d needs the batched kernels: dim and moe_ffn_dim multiples of 128",
-                    group_size);
+        return fail(GLM_CUDA_ERR_ARG,
+                    "group size %d needs the persistent or the batched kernels, and these sizes fit neither", group_size);
     }
     g.layers.assign(n_layers, LayerSlot{});
     g.launches = 0;
@@ -588,6 +590,8 @@ int glm_cuda_set_decode_path(int path) {
         return fail(GLM_CUDA_ERR_ARG, "unknown decode path %d", path);
     if (path == GLM_CUDA_PATH_PERSISTENT && !g.persistent_ok)
         return fail(GLM_CUDA_ERR_ARG, "these model sizes do not fit the persistent decode kernel on this device");
+    if (path == GLM_CUDA_PATH_CHAIN && !chain_ok())
+        return fail(GLM_CUDA_ERR_ARG, "the three-kernel decode chain takes gs = 32 only");
     g.decode_path = path;
     return 0;
 }
@@ -855,7 +859,7 @@ int glm_cuda_moe_layer_profile(int layer, float* x_dev, float ms_out[3]) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (int rc = check_layer(layer)) return rc;
     if (!x_dev || !ms_out) return fail(GLM_CUDA_ERR_ARG, "x_dev and ms_out must be non-NULL");
-    if (!decode_kernels_ok()) return fail(GLM_CUDA_ERR_ARG, "the per-token decode kernels take gs = 32 only");
+    if (!chain_ok()) return fail(GLM_CUDA_ERR_ARG, "the three-kernel decode chain takes gs = 32 only");
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
     for (auto& e : ev) CUDA_TRY(cudaEventCreate(&e));
     const int routed = routed_disabled_by_env() ? 0 : 1;

@@ -104,7 +104,7 @@ cudaError_t launch_argmax(const float* x, int n, float2* part, unsigned* counter
 cudaError_t launch_decode_advance(int* pos, int* token, const int* argmax, const int* prompt, int n_prompt,
                                   int* out_ids, int vocab, cudaStream_t st);
 
-size_t q80_matvec_smem_bytes(int cols, bool norm = false);
+size_t q80_matvec_smem_bytes(int cols, bool norm = false, int gs = 32);
 
 // ---- batched prefill (moe_prefill.cu)
 

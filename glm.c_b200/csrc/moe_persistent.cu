@@ -50,20 +50,32 @@
 
 namespace glmq {
 
-constexpr int kPCons = 15;                     // consumer warps (+1 producer: 512 threads, 128 regs)
 constexpr int kPGroupWarps = 3;                // consumer warps per group; group g owns ring slot g
-constexpr int kPGroups = kPCons / kPGroupWarps;
-constexpr int kPConsThreads = kPCons * 32;
-constexpr int kPThreads = kPConsThreads + 32;
-constexpr int kPSlots = 5;
 #ifndef GLM_P_INFLIGHT
 #define GLM_P_INFLIGHT 5
 #endif
-// At most this many ring items in flight (issued, not landed); below kPSlots
-// it trades ring throughput for shorter queues behind the kernel's small
-// critical-path loads (measured best: no limit, with the L2 prefetches).
+// At most this many ring items in flight (issued, not landed); below the
+// slot count it trades ring throughput for shorter queues behind the
+// kernel's small critical-path loads (measured best: no limit, with the L2
+// prefetches).
 constexpr int kPInflight = GLM_P_INFLIGHT;
-static_assert(kPGroups == kPSlots, "one consumer group per ring slot");
+
+// Shape of the CTA for a weight group size. gs = 32: a 5-slot ring and 5
+// consumer groups of 3 warps (+1 producer: 512 threads, 128 registers).
+// gs = 16 doubles the scale bytes of every tile (16 rows of D = 2048 take
+// 40 KB instead of 36 KB), so 5 slots no longer fit shared memory beside the
+// activation planes: 4 slots and 4 groups (416 threads); its engine reads
+// the x-group scales directly (no epilogue table).
+template <int kGS>
+struct PCfg {
+    static constexpr int kSlots = kGS == 32 ? 5 : 4;
+    static constexpr int kGroups = kSlots;  // one consumer group per ring slot
+    static constexpr int kCons = kGroups * kPGroupWarps;
+    static constexpr int kConsThreads = kCons * 32;
+    static constexpr int kThreads = kConsThreads + 32;
+    static constexpr int kTab = kGS == 32 ? kChunkTab : 0;  // epilogue-table floats per 64-column chunk
+};
+constexpr int kPMaxCons = PCfg<32>::kCons;
 constexpr int kPTile = 16;                     // rows per ring item
 constexpr int kPHRows = 8;                     // h rows per gate/up item (8 gate rows + their 8 up rows)
 constexpr unsigned kStatBarrier = 4u, kStatFull = 8u, kStatEmpty = 16u, kStatRoute = 32u;
@@ -84,6 +96,9 @@ struct PersistArgs {
     unsigned long long* stats;
     int D, F, E, K, routed_enabled, slot_bytes;
     int next_layer;     // table index whose shared weights to pull into L2 during the last layer, or -1
+    int gs;             // weight scale group (32 or 16)
+    int sdiv;           // weight bytes per scale byte (gs / 4): a row of n weights has n / sdiv scale bytes
+    int slots;          // ring slots
 };
 
 __host__ __device__ inline size_t p_take(size_t& o, size_t n) {
@@ -95,38 +110,40 @@ __host__ __device__ inline size_t p_take(size_t& o, size_t n) {
 // Dynamic shared memory layout (offsets in bytes).
 struct PSmem {
     size_t bars, ring, xs, ph, px, tx, gx, th, gh, part, ys, bias, cen, bnd, sel, rscr, misc, total;
-    __host__ __device__ PSmem(int D, int F, int E, int K, int slot_bytes) {
+    // slots: ring slots (= consumer groups), tab: epilogue floats per chunk
+    __host__ __device__ PSmem(int D, int F, int E, int K, int slot_bytes, int slots, int tab) {
         size_t o = 0;
         const int NS = K + 1, nchD = D >> 6, nchF = F >> 6;
         bars = p_take(o, 128);
-        ring = p_take(o, (size_t)kPSlots * slot_bytes);
+        ring = p_take(o, (size_t)slots * slot_bytes);
         // xn (until routing is decided) and the h digit planes (after that)
         // are never live together.
         const size_t hpl = (size_t)NS * nchF * kChunkBytes;
         xs = p_take(o, hpl > (size_t)D * 4 ? hpl : (size_t)D * 4);
         ph = xs;
         px = p_take(o, (size_t)nchD * kChunkBytes);
-        tx = p_take(o, (size_t)nchD * kChunkTab * 4);
+        tx = p_take(o, (size_t)nchD * tab * 4);
         gx = p_take(o, (size_t)(D >> 5) * 4);
-        th = p_take(o, (size_t)NS * nchF * kChunkTab * 4);
+        th = p_take(o, (size_t)NS * nchF * tab * 4);
         gh = p_take(o, (size_t)NS * (F >> 5) * 4);
-        part = p_take(o, (size_t)kPGroups * 2 * kPGroupWarps * kPTile * 4);
+        part = p_take(o, (size_t)slots * 2 * kPGroupWarps * kPTile * 4);
         ys = p_take(o, (size_t)NS * kPTile * 4);
         bias = p_take(o, (size_t)E * 4);
         cen = p_take(o, (size_t)E * 8);
         bnd = p_take(o, (size_t)E * 8);
         sel = p_take(o, (size_t)E * 20);
-        rscr = p_take(o, (size_t)(64 + 5 * kPCons) * 4);
+        rscr = p_take(o, (size_t)(64 + 5 * kPMaxCons) * 4);
         misc = p_take(o, 512);
         total = o;
     }
 };
 
 // Ring slot: the largest of a gate/up tile (16 rows of D), a down tile (16
-// rows of F) and the layer constants (norm + bias).
-__host__ __device__ inline int p_slot_bytes(int D, int F, int E) {
-    int b = kPTile * (D + D / 8);
-    const int bf = kPTile * (F + F / 8);
+// rows of F) and the layer constants (norm + bias); weights plus their
+// gs-group scales (4 bytes per gs weights).
+__host__ __device__ inline int p_slot_bytes(int D, int F, int E, int gs) {
+    int b = kPTile * (D + 4 * D / gs);
+    const int bf = kPTile * (F + 4 * F / gs);
     if (bf > b) b = bf;
     if (D * 4 + E * 4 > b) b = D * 4 + E * 4;
     return (b + 127) & ~127;
@@ -134,7 +151,11 @@ __host__ __device__ inline int p_slot_bytes(int D, int F, int E) {
 
 // ------------------------------------------------------------ primitives
 
-__device__ __forceinline__ void cons_sync() { asm volatile("bar.sync 1, %0;\n" ::"n"(kPConsThreads) : "memory"); }
+// Barrier 1 among the kN consumer threads (the producer warp never joins it).
+template <int kN>
+__device__ __forceinline__ void cons_sync() {
+    asm volatile("bar.sync 1, %0;\n" ::"n"(kN) : "memory");
+}
 
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
     unsigned v;
@@ -179,7 +200,7 @@ struct GRow {
 __device__ __forceinline__ GRow gate_row(const MoeLayerDev& W, const PersistArgs& a, const PRows& m, bool routed,
                                          int t, int j, const int* topk) {
     GRow r;
-    const size_t D = (size_t)a.D, sgrp = D >> 5;
+    const size_t D = (size_t)a.D, sgrp = D / a.gs;
     const int i = t * kPHRows + (j & (kPHRows - 1)), mat = j >= kPHRows;
     if (!routed) {
         if (i >= m.nsh) return r;
@@ -209,7 +230,7 @@ __device__ void produce_gate_item(const MoeLayerDev& W, const PersistArgs& a, co
                                   const int* topk, unsigned char* buf, uint64_t* bar) {
     const unsigned full = 0xffffffffu;
     const int lane = threadIdx.x & 31;
-    const size_t D = (size_t)a.D, sgrp = D >> 5;
+    const size_t D = (size_t)a.D, sgrp = D / a.gs, sbytes = D / a.sdiv;
     GRow r;
     if (lane < kPTile) r = gate_row(W, a, m, routed, t, lane, topk);
     const bool take = lane < kPTile && r.q != nullptr;
@@ -218,7 +239,7 @@ __device__ void produce_gate_item(const MoeLayerDev& W, const PersistArgs& a, co
     const auto ps = reinterpret_cast<const float*>(__shfl_up_sync(full, reinterpret_cast<unsigned long long>(r.s), 1));
     const bool cont = take && lane > 0 && ((tmask >> (lane - 1)) & 1u) && pq + D == r.q && ps + sgrp == r.s;
     const unsigned cmask = __ballot_sync(full, cont);
-    const uint32_t bytes = (uint32_t)__popc(tmask) * (uint32_t)(D + (D >> 3));
+    const uint32_t bytes = (uint32_t)__popc(tmask) * (uint32_t)(D + sbytes);
     if (lane == 0) {
         if (bytes)
             mbar_arrive_expect_tx(bar, bytes);
@@ -230,7 +251,7 @@ __device__ void produce_gate_item(const MoeLayerDev& W, const PersistArgs& a, co
         // run length: this lane plus the following lanes that continue it
         const int n = __ffs(~(cmask >> (lane + 1)));
         bulk_copy_g2s(buf + (size_t)lane * D, r.q, (uint32_t)(n * D), bar);
-        bulk_copy_g2s(buf + kPTile * D + (size_t)lane * (D >> 3), r.s, (uint32_t)(n * (D >> 3)), bar);
+        bulk_copy_g2s(buf + kPTile * D + (size_t)lane * sbytes, r.s, (uint32_t)(n * sbytes), bar);
     }
 }
 
@@ -239,7 +260,7 @@ __device__ void produce_down(const MoeLayerDev& W, const PersistArgs& a, const P
                              unsigned char* buf, uint64_t* bar) {
     const int lane = threadIdx.x & 31;
     const int n = m.re - m.rb;
-    const size_t F = (size_t)a.F, fgrp = F >> 5;
+    const size_t F = (size_t)a.F, fgrp = F / a.gs, sbytes = F / a.sdiv;
     const int8_t* q = nullptr;
     const float* s = nullptr;
     if (n > 0) {
@@ -254,9 +275,9 @@ __device__ void produce_down(const MoeLayerDev& W, const PersistArgs& a, const P
     }
     if (lane == 0) {
         if (q) {
-            mbar_arrive_expect_tx(bar, (uint32_t)(n * (F + (F >> 3))));
+            mbar_arrive_expect_tx(bar, (uint32_t)(n * (F + sbytes)));
             bulk_copy_g2s(buf, q, (uint32_t)(n * F), bar);
-            bulk_copy_g2s(buf + kPTile * F, s, (uint32_t)(n * (F >> 3)), bar);
+            bulk_copy_g2s(buf + kPTile * F, s, (uint32_t)(n * sbytes), bar);
         } else {
             mbar_arrive(bar);
         }
@@ -287,9 +308,9 @@ __device__ void prefetch_routed_gate_up(const MoeLayerDev& W, const PersistArgs&
         const size_t row = (size_t)e * F + r0, n = (size_t)(r1 - r0);
         const int base = 4 * (sl - s_first);
         if (lane == base) prefetch_l2(W.gate_q + row * D, (uint32_t)(n * D));
-        if (lane == base + 1) prefetch_l2(W.gate_s + row * (D >> 5), (uint32_t)(n * (D >> 3)));
+        if (lane == base + 1) prefetch_l2(W.gate_s + row * (D / a.gs), (uint32_t)(n * (D / a.sdiv)));
         if (lane == base + 2) prefetch_l2(W.up_q + row * D, (uint32_t)(n * D));
-        if (lane == base + 3) prefetch_l2(W.up_s + row * (D >> 5), (uint32_t)(n * (D >> 3)));
+        if (lane == base + 3) prefetch_l2(W.up_s + row * (D / a.gs), (uint32_t)(n * (D / a.sdiv)));
     }
 }
 
@@ -305,7 +326,7 @@ __device__ void prefetch_routed_down(const MoeLayerDev& W, const PersistArgs& a,
     if ((lane & 1) == 0)
         prefetch_l2(W.down_q + row * F, (uint32_t)(n * F));
     else
-        prefetch_l2(W.down_s + row * (F >> 5), (uint32_t)(n * (F >> 3)));
+        prefetch_l2(W.down_s + row * (F / a.gs), (uint32_t)(n * (F / a.sdiv)));
 }
 
 // Producer lanes: the routing-independent weights this CTA needs of layer W
@@ -318,11 +339,11 @@ __device__ void prefetch_shared(const MoeLayerDev& W, const PersistArgs& a, cons
     switch (lane) {
         case 0: if (W.router && c < a.E) prefetch_l2(W.router + (size_t)c * D, (uint32_t)(D * 4)); break;
         case 1: if (W.gate_sh_q && m.nsh > 0) prefetch_l2(W.gate_sh_q + (size_t)m.sh0 * D, (uint32_t)(m.nsh * D)); break;
-        case 2: if (W.gate_sh_s && m.nsh > 0) prefetch_l2(W.gate_sh_s + (size_t)m.sh0 * (D >> 5), (uint32_t)(m.nsh * (D >> 3))); break;
+        case 2: if (W.gate_sh_s && m.nsh > 0) prefetch_l2(W.gate_sh_s + (size_t)m.sh0 * (D / a.gs), (uint32_t)(m.nsh * (D / a.sdiv))); break;
         case 3: if (W.up_sh_q && m.nsh > 0) prefetch_l2(W.up_sh_q + (size_t)m.sh0 * D, (uint32_t)(m.nsh * D)); break;
-        case 4: if (W.up_sh_s && m.nsh > 0) prefetch_l2(W.up_sh_s + (size_t)m.sh0 * (D >> 5), (uint32_t)(m.nsh * (D >> 3))); break;
+        case 4: if (W.up_sh_s && m.nsh > 0) prefetch_l2(W.up_sh_s + (size_t)m.sh0 * (D / a.gs), (uint32_t)(m.nsh * (D / a.sdiv))); break;
         case 5: if (W.down_sh_q && n > 0) prefetch_l2(W.down_sh_q + (size_t)m.rb * F, (uint32_t)(n * F)); break;
-        case 6: if (W.down_sh_s && n > 0) prefetch_l2(W.down_sh_s + (size_t)m.rb * (F >> 5), (uint32_t)(n * (F >> 3))); break;
+        case 6: if (W.down_sh_s && n > 0) prefetch_l2(W.down_sh_s + (size_t)m.rb * (F / a.gs), (uint32_t)(n * (F / a.sdiv))); break;
         case 7: if (c == 0) prefetch_l2(W.ffn_norm, (uint32_t)(D * 4)); break;
         case 8: if (c == 0) prefetch_l2(W.router_bias, (uint32_t)(a.E * 4)); break;
         default: break;
@@ -336,12 +357,13 @@ struct PCtx {
     uint64_t* full;
     uint64_t* empty;
     int slot_bytes;
+    int slots;
     volatile int* abort_flag;
     unsigned* status;
 };
 
 __device__ __forceinline__ unsigned char* slot_buf(const PCtx& P, uint32_t it) {
-    return P.ring + (size_t)(it % kPSlots) * P.slot_bytes;
+    return P.ring + (size_t)(it % P.slots) * P.slot_bytes;
 }
 
 // Every consumer thread waits for ring item `it` itself. A wait that gives up
@@ -349,7 +371,7 @@ __device__ __forceinline__ unsigned char* slot_buf(const PCtx& P, uint32_t it) {
 // with whatever the slot holds (no block-wide agreement per item), and the
 // CTA leaves at its next grid barrier, which checks the flag.
 __device__ __forceinline__ void cons_wait(const PCtx& P, uint32_t it) {
-    if (!mbar_wait_bounded(&P.full[it % kPSlots], (it / kPSlots) & 1u)) {
+    if (!mbar_wait_bounded(&P.full[it % P.slots], (it / P.slots) & 1u)) {
         atomicOr(P.status, kStatFull);
         *P.abort_flag = 1;
     }
@@ -359,13 +381,14 @@ __device__ __forceinline__ void cons_wait(const PCtx& P, uint32_t it) {
 // per warp hands the slot back once the group's kPGroupWarps warps are done.
 __device__ __forceinline__ void cons_release(const PCtx& P, uint32_t it) {
     __syncwarp();
-    if ((threadIdx.x & 31) == 0) mbar_arrive(&P.empty[it % kPSlots]);
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&P.empty[it % P.slots]);
 }
 
 // Grid-wide barrier among the consumer warps of all CTAs; false when this
 // CTA or another one has given up (every CTA then leaves).
+template <int kN>
 __device__ bool grid_sync(const PersistArgs& a, const PCtx& P, unsigned& nbar, int tid, volatile int* s_ok) {
-    cons_sync();
+    cons_sync<kN>();
     ++nbar;
     if (tid == 0) {
         int ok = 0;
@@ -387,14 +410,15 @@ __device__ bool grid_sync(const PersistArgs& a, const PCtx& P, unsigned& nbar, i
         __threadfence();
         *s_ok = ok;
     }
-    cons_sync();
+    cons_sync<kN>();
     return *s_ok != 0;
 }
 
 // grid_sync in two halves: grid_arrive (after this CTA's writes) and
 // grid_wait (before reading the other CTAs'), with work in between.
+template <int kN>
 __device__ void grid_arrive(const PersistArgs& a, const PCtx& P, unsigned& nbar, int tid) {
-    cons_sync();
+    cons_sync<kN>();
     ++nbar;
     if (tid == 0) {
         __threadfence();
@@ -402,8 +426,9 @@ __device__ void grid_arrive(const PersistArgs& a, const PCtx& P, unsigned& nbar,
     }
 }
 
+template <int kN>
 __device__ bool grid_wait(const PersistArgs& a, const PCtx& P, unsigned nbar, int tid, volatile int* s_ok) {
-    cons_sync();
+    cons_sync<kN>();
     if (tid == 0) {
         int ok = 0;
         const unsigned target = nbar * gridDim.x;
@@ -422,17 +447,21 @@ __device__ bool grid_wait(const PersistArgs& a, const PCtx& P, unsigned nbar, in
         __threadfence();
         *s_ok = ok;
     }
-    cons_sync();
+    cons_sync<kN>();
     return *s_ok != 0;
 }
 
 __device__ __forceinline__ float silu_p(float v) { return v / (1.0f + expf(-v)); }
 
-__global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArgs a) {
+template <int kGS>
+__global__ void __launch_bounds__(PCfg<kGS>::kThreads, 1) moe_persistent_kernel(PersistArgs a) {
+    using Cfg = PCfg<kGS>;
+    constexpr int kPSlots = Cfg::kSlots, kPCons = Cfg::kCons, kPConsThreads = Cfg::kConsThreads, kTab = Cfg::kTab;
+    auto cons_sync = []() { glmq::cons_sync<kPConsThreads>(); };
     extern __shared__ __align__(128) unsigned char sm[];
     const int D = a.D, F = a.F, E = a.E, K = a.K;
     const int nchF = F >> 6;
-    const PSmem L(D, F, E, K, a.slot_bytes);
+    const PSmem L(D, F, E, K, a.slot_bytes, kPSlots, kTab);
     uint64_t* full = reinterpret_cast<uint64_t*>(sm + L.bars);
     uint64_t* empty = full + kPSlots;
     uint64_t* route_ready = empty + kPSlots;
@@ -457,7 +486,7 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
     float* s_inv = reinterpret_cast<float*>(misc + 64);
     volatile int* s_ok = misc + 65;
     volatile int* s_abort = misc + 66;
-    double* red = reinterpret_cast<double*>(misc + 72);   // [kPCons]
+    double* red = reinterpret_cast<double*>(misc + 72);   // [kPCons] (<= kPMaxCons)
     SelectScratch S;
     S.sel_c = reinterpret_cast<float*>(sm + L.sel);
     S.sel_lo = S.sel_c + E;
@@ -470,7 +499,7 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int c = blockIdx.x, G = gridDim.x;
     const PRows m(c, G, D, F, K);
-    const PCtx P{sm + L.ring, full, empty, a.slot_bytes, s_abort, a.status};
+    const PCtx P{sm + L.ring, full, empty, a.slot_bytes, kPSlots, s_abort, a.status};
 
     if (tid == 0) {
         for (int i = 0; i < kPSlots; ++i) {
@@ -586,6 +615,7 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
     const int gid = lane >> 2, t4 = lane & 3;
     const int grp = warp / kPGroupWarps, gw = warp % kPGroupWarps;
     const int boff = b_frag_offset(lane);
+    const G16Lane gl = g16_lane(lane);
     const int4 z4 = make_int4(0, 0, 0, 0);
     const float2 z2 = make_float2(0.f, 0.f);
     constexpr int kPart = kPGroupWarps * kPTile;
@@ -593,7 +623,7 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
     uint32_t it = 0;
     unsigned nbar = 0;
     int nlocal = 0;  // items this group has processed (parity picks the partial buffer)
-    auto sync = []() { cons_sync(); };
+    auto sync = []() { glmq::cons_sync<kPConsThreads>(); };
     auto grp_sync = [&]() { asm volatile("bar.sync %0, %1;\n" ::"r"(2 + grp), "n"(kPGroupWarps * 32) : "memory"); };
 
     // Items that every consumer reads (layer constants, router row): after
@@ -605,22 +635,34 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
     // A weight item is processed by the group that owns its ring slot: each
     // of the group's warps dots its third of the 64-column chunks of the 16
     // rows with the activation planes and hands the slot back; after the
-    // group barrier one warp adds the three partials of every row.
+    // group barrier one warp adds the three partials of every row. tab: the
+    // planes' epilogue table (gs = 32) or x-group scales (gs = 16).
     auto group_rows = [&](uint32_t item, const int8_t* planes, const float* tab, int cols, bool v0, bool v1) {
         cons_wait(P, item);
         const int nch = cols >> 6;
         const int8_t* qb = reinterpret_cast<const int8_t*>(slot_buf(P, item));
         const unsigned char* sb = slot_buf(P, item) + kPTile * cols;
+        const int srow = cols * 4 / kGS;  // scale bytes per row
         float acc0 = 0.f, acc1 = 0.f;
         for (int j = gw * nch / kPGroupWarps; j < (gw + 1) * nch / kPGroupWarps; ++j) {
             const int off = j * kChunkCols + 16 * t4;
-            const int4 b4 = boff >= 0 ? lds16(planes + j * kChunkBytes + boff) : z4;
-            const float2 tb = *reinterpret_cast<const float2*>(tab + j * kChunkTab + 2 * t4);
             const int4 q0 = v0 ? lds16(qb + gid * cols + off) : z4;
             const int4 q1 = v1 ? lds16(qb + (gid + 8) * cols + off) : z4;
-            const float2 s0 = v0 ? *reinterpret_cast<const float2*>(sb + gid * (cols >> 3) + 8 * j) : z2;
-            const float2 s1 = v1 ? *reinterpret_cast<const float2*>(sb + (gid + 8) * (cols >> 3) + 8 * j) : z2;
-            chunk_mma_accumulate(q0, q1, s0, s1, b4, tb, t4, acc0, acc1);
+            if constexpr (kGS == 32) {
+                const int4 b4 = boff >= 0 ? lds16(planes + j * kChunkBytes + boff) : z4;
+                const float2 tb = *reinterpret_cast<const float2*>(tab + j * kTab + 2 * t4);
+                const float2 s0 = v0 ? *reinterpret_cast<const float2*>(sb + gid * srow + 8 * j) : z2;
+                const float2 s1 = v1 ? *reinterpret_cast<const float2*>(sb + (gid + 8) * srow + 8 * j) : z2;
+                chunk_mma_accumulate(q0, q1, s0, s1, b4, tb, t4, acc0, acc1);
+            } else {  // tab: the x-group scales
+                const int8_t* pl = planes + j * kChunkBytes;
+                const int4 bx = gl.offX >= 0 ? lds16(pl + gl.offX) : z4;
+                const int4 by = gl.offY >= 0 ? lds16(pl + gl.offY) : z4;
+                const float sx = tab[2 * j + (t4 >> 1)];
+                const float s0 = v0 ? *reinterpret_cast<const float*>(sb + gid * srow + 16 * j + 4 * t4) : 0.f;
+                const float s1 = v1 ? *reinterpret_cast<const float*>(sb + (gid + 8) * srow + 16 * j + 4 * t4) : 0.f;
+                chunk_mma_accumulate_g16(q0, q1, s0, s1, bx, by, sx, acc0, acc1);
+            }
         }
         cons_release(P, item);
         acc0 = quad_sum(acc0);
@@ -645,7 +687,7 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
     // (infer.c:1184-1188, 1197-1201).
     auto gate_item = [&](const MoeLayerDev& W, bool routed, int t, uint32_t item) {
         const int* tk = routed ? s_topk : nullptr;
-        const float* pt = group_rows(item, px, tx, D, gate_row(W, a, m, routed, t, gid, tk).q != nullptr,
+        const float* pt = group_rows(item, px, kGS == 32 ? tx : gx, D, gate_row(W, a, m, routed, t, gid, tk).q != nullptr,
                                      gate_row(W, a, m, routed, t, gid + 8, tk).q != nullptr);
         if (gw == 0 && lane < kPHRows) {
             const int hidx = gate_row(W, a, m, routed, t, lane, tk).hidx;
@@ -657,8 +699,9 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
     auto down_item = [&](const MoeLayerDev& W, int slot, uint32_t item) {
         const int n = m.re - m.rb;
         const bool live = slot == K || (a.routed_enabled && W.down_q && s_topk[slot] >= 0);
-        const float* pt = group_rows(item, ph + (size_t)slot * nchF * kChunkBytes, th + (size_t)slot * nchF * kChunkTab,
-                                     F, live && gid < n, live && gid + 8 < n);
+        const float* tb = kGS == 32 ? th + (size_t)slot * nchF * kTab : gh + (size_t)slot * (F >> 5);
+        const float* pt = group_rows(item, ph + (size_t)slot * nchF * kChunkBytes, tb, F, live && gid < n,
+                                     live && gid + 8 < n);
         if (gw == 0 && lane < kPTile) ys[slot * kPTile + lane] = row_total(pt, lane);
     };
 
@@ -755,9 +798,9 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
         // arrive as soon as this CTA's router results are out, then turn xn
         // into digit planes for the gate/up products while the other CTAs'
         // results come in, then wait
-        grid_arrive(a, P, nbar, tid);
-        quantize_planes_part<false>(xs, D, px, gx, tx, tid, kPConsThreads, sync);
-        if (!grid_wait(a, P, nbar, tid, s_ok)) return leave();
+        grid_arrive<kPConsThreads>(a, P, nbar, tid);
+        quantize_planes_part<false, kGS == 16>(xs, D, px, gx, tx, tid, kPConsThreads, sync);
+        if (!grid_wait<kPConsThreads>(a, P, nbar, tid, s_ok)) return leave();
 
         // ---- P2: routing (every CTA, identical); shared and routed gate/up
         for (int i = tid; i < E; i += kPConsThreads) {
@@ -780,10 +823,10 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
             gate_item(W, u >= nsh, u >= nsh ? u - nsh : u, item);
         }
         it += (uint32_t)nitems;
-        if (!grid_sync(a, P, nbar, tid, s_ok)) return leave();
+        if (!grid_sync<kPConsThreads>(a, P, nbar, tid, s_ok)) return leave();
 
         // ---- P3: h -> digit planes (xs is dead); down rows; combine
-        quantize_planes_part<true>(a.h, (K + 1) * F, ph, gh, th, tid, kPConsThreads, sync);
+        quantize_planes_part<true, kGS == 16>(a.h, (K + 1) * F, ph, gh, th, tid, kPConsThreads, sync);
         // down items in the order shared, routed 0 .. K-1; each group takes its own
         for (uint32_t item = first_mine(it); item < it + (uint32_t)(K + 1); item += kPSlots) {
             const int q = (int)(item - it);
@@ -803,7 +846,7 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
             }
             a.x[r] = __fadd_rn(__ldcg(a.x + r), __fadd_rn(ys[K * kPTile + tid], acc));
         }
-        if (li + 1 < a.n_layers && !grid_sync(a, P, nbar, tid, s_ok)) return leave();
+        if (li + 1 < a.n_layers && !grid_sync<kPConsThreads>(a, P, nbar, tid, s_ok)) return leave();
     }
     leave();
 }
@@ -811,11 +854,12 @@ __global__ void __launch_bounds__(kPThreads, 1) moe_persistent_kernel(PersistArg
 // ------------------------------------------------------------- launcher
 
 cudaError_t persistent_check(const MoeDims& d, int num_sms, size_t* smem_out) {
-    if (d.K < 1 || d.K > kMaxTopK || d.K > d.E || d.E > num_sms || d.E % 4 || d.gs != 32 || d.D % 128 ||
-        d.D > 2048 || d.F % 128 || (d.D + kPTile - 1) / kPTile > num_sms)
+    if (d.K < 1 || d.K > kMaxTopK || d.K > d.E || d.E > num_sms || d.E % 4 || (d.gs != 32 && d.gs != 16) ||
+        d.D % 128 || d.D > 2048 || d.F % 128 || (d.D + kPTile - 1) / kPTile > num_sms)
         return cudaErrorInvalidValue;
-    const int slot = p_slot_bytes(d.D, d.F, d.E);
-    const size_t smem = PSmem(d.D, d.F, d.E, d.K, slot).total;
+    const int slot = p_slot_bytes(d.D, d.F, d.E, d.gs);
+    const size_t smem = d.gs == 32 ? PSmem(d.D, d.F, d.E, d.K, slot, PCfg<32>::kSlots, PCfg<32>::kTab).total
+                                   : PSmem(d.D, d.F, d.E, d.K, slot, PCfg<16>::kSlots, PCfg<16>::kTab).total;
     if (smem > 227 * 1024 - 1024) return cudaErrorInvalidValue;
     if (smem_out) *smem_out = smem;
     return cudaSuccess;
@@ -827,14 +871,17 @@ cudaError_t launch_moe_persistent(const MoeLayerDev* layers_dev, int first, int 
     size_t smem = 0;
     cudaError_t err = persistent_check(d, num_sms, &smem);
     if (err != cudaSuccess) return err;
-    if ((err = ensure_smem_attr(reinterpret_cast<const void*>(moe_persistent_kernel), (int)smem))) return err;
+    const bool g16 = d.gs == 16;
+    auto kernel = g16 ? moe_persistent_kernel<16> : moe_persistent_kernel<32>;
+    if ((err = ensure_smem_attr(reinterpret_cast<const void*>(kernel), (int)smem))) return err;
     PersistArgs a{layers_dev, first,    n_layers, x,           s.h,       s.center,
                   s.bound,    topk_out, topkw_out, s.grid_bar, s.grid_bar + 1, s.status, s.stats,
                   d.D,        d.F,      d.E,       d.K,        routed_enabled,
-                  p_slot_bytes(d.D, d.F, d.E), next_layer};
+                  p_slot_bytes(d.D, d.F, d.E, d.gs), next_layer, d.gs, d.gs / 4,
+                  g16 ? PCfg<16>::kSlots : PCfg<32>::kSlots};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(num_sms);
-    cfg.blockDim = dim3(kPThreads);
+    cfg.blockDim = dim3(g16 ? PCfg<16>::kThreads : PCfg<32>::kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
@@ -844,7 +891,7 @@ cudaError_t launch_moe_persistent(const MoeLayerDev* layers_dev, int first, int 
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, moe_persistent_kernel, a);
+    return cudaLaunchKernelEx(&cfg, kernel, a);
 }
 
 }  // namespace glmq

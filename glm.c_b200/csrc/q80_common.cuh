@@ -148,6 +148,62 @@ __device__ __forceinline__ void chunk_mma_accumulate(const int4& q0, const int4&
     acc1 = fmaf(i2f_exact22(d[3]), swB1 * tab.y, acc1);
 }
 
+// ------------------------------------------------- gs = 16 weight scales
+//
+// glm.c's own export uses 16-column weight groups (glm47_flash_export.py:36),
+// so one MMA column may not sum a whole 32-column x group. Lane t of a quad
+// holds exactly the k-slots of chunk columns [16t, 16t+16) in its A fragment
+// (its 16 weight bytes), i.e. of weight group w = t. Each B column carries
+// one (weight group w, digit plane p) and is zero outside group w, and the
+// columns are placed so that accumulator lane t (which holds columns 2t and
+// 2t+1) receives the three plane sums of its own group w = t:
+//   set X: column n = (w = n/2, p = n%2)              (hi, mid planes)
+//   set Y: column n = (w = n/2, p = 2) for even n,   (lo plane)
+//          zero for odd n
+// Each set takes both 8-byte halves of the lanes' weight bytes, so a chunk
+// costs 4 MMAs; the lane then scales its group's value
+// 65536 hi + 256 mid + lo by its own weight scale s[row][4j + t] and by the
+// scale of x group 2j + t/2 (columns 0-31 or 32-63 of chunk j). No per-lane
+// table or selection is involved.
+struct G16Lane {
+    int offX, offY;  // byte offsets of the lane's B fragments in a chunk's planes, -1 = zero
+};
+
+__device__ __forceinline__ G16Lane g16_lane(int lane) {
+    const int n = lane >> 2, t = lane & 3;  // B column n, k-slots of group t
+    G16Lane L;
+    L.offX = (n >> 1) == t ? (n & 1) * 64 + 16 * t : -1;
+    L.offY = ((n >> 1) == t && (n & 1) == 0) ? 128 + 16 * t : -1;
+    return L;
+}
+
+// Accumulate one 16-row x 64-column chunk with gs = 16 weight scales into the
+// lane's partial sums for rows gid (acc0) and gid+8 (acc1).
+//   q0/q1: this lane's 16 weight bytes of row gid / gid+8
+//   s0/s1: weight scale of group t (lane-in-quad) of row gid / gid+8
+//   bX/bY: this lane's B fragments (zero where G16Lane offX / offY < 0)
+//   sx:    scale of the x group that holds weight group t
+__device__ __forceinline__ void chunk_mma_accumulate_g16(const int4& q0, const int4& q1, float s0, float s1,
+                                                         const int4& bX, const int4& bY, float sx, float& acc0,
+                                                         float& acc1) {
+    int dx[4] = {0, 0, 0, 0}, dy[4] = {0, 0, 0, 0};
+    mma_s8(dx, (uint32_t)q0.x, (uint32_t)q1.x, (uint32_t)q0.y, (uint32_t)q1.y, (uint32_t)bX.x, (uint32_t)bX.y);
+    mma_s8(dx, (uint32_t)q0.z, (uint32_t)q1.z, (uint32_t)q0.w, (uint32_t)q1.w, (uint32_t)bX.z, (uint32_t)bX.w);
+    mma_s8(dy, (uint32_t)q0.x, (uint32_t)q1.x, (uint32_t)q0.y, (uint32_t)q1.y, (uint32_t)bY.x, (uint32_t)bY.y);
+    mma_s8(dy, (uint32_t)q0.z, (uint32_t)q1.z, (uint32_t)q0.w, (uint32_t)q1.w, (uint32_t)bY.z, (uint32_t)bY.w);
+    // columns 2t (hi), 2t+1 (mid) of X and 2t (lo) of Y; dy[1], dy[3] are the zero columns
+    const float v0 = fmaf(i2f_exact22(dx[0]), 65536.0f, fmaf(i2f_exact22(dx[1]), 256.0f, i2f_exact22(dy[0])));
+    const float v1 = fmaf(i2f_exact22(dx[2]), 65536.0f, fmaf(i2f_exact22(dx[3]), 256.0f, i2f_exact22(dy[2])));
+    acc0 = fmaf(v0, s0 * sx, acc0);
+    acc1 = fmaf(v1, s1 * sx, acc1);
+}
+
+__device__ __forceinline__ float ld_scale1(const float* p) {
+    float v;
+    asm volatile("ld.global.nc.f32 %0, [%1];\n" : "=f"(v) : "l"(p));
+    return v;
+}
+
 __device__ __forceinline__ float quad_sum(float v) {
     v += __shfl_xor_sync(0xffffffffu, v, 1);
     v += __shfl_xor_sync(0xffffffffu, v, 2);
@@ -277,8 +333,9 @@ __device__ __forceinline__ void fill_sxtab(const float* sxg, float* sxtab, int c
 // Quantise src[0, n) (n % 64 == 0) into planes/sxg/sxtab, run by threads
 // [0, nthreads) of a block that synchronise with `sync()` (e.g. the consumer
 // warps of a warp-specialised kernel). kGlobal: src is global memory written
-// by other CTAs; otherwise shared memory. Ends with sync().
-template <bool kGlobal, typename Sync>
+// by other CTAs; otherwise shared memory. kG16: no sxtab (the gs = 16 engine
+// reads sxg). Ends with sync().
+template <bool kGlobal, bool kG16 = false, typename Sync>
 __device__ __forceinline__ void quantize_planes_part(const float* src, int n, int8_t* planes, float* sxg,
                                                      float* sxtab, int tid, int nthreads, Sync sync) {
     constexpr int kB = 4;
@@ -289,8 +346,10 @@ __device__ __forceinline__ void quantize_planes_part(const float* src, int n, in
         q4_store<kB>(v, groups, s0, nwarps, lane, planes, sxg);
     }
     sync();
-    fill_sxtab(sxg, sxtab, n >> 6, tid, nthreads);
-    sync();
+    if constexpr (!kG16) {  // gs = 16 reads the group scales sxg directly
+        fill_sxtab(sxg, sxtab, n >> 6, tid, nthreads);
+        sync();
+    }
 }
 
 // ------------------------------------------------------- TMA and mbarriers

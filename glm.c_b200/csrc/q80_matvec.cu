@@ -1,5 +1,5 @@
 // Batch-1 planar Q8 matvec on sm_100a: y[r] = sum_g s[r,g] * sum_k q[r,gs*g+k] x[gs*g+k]
-// (gs = 32: integer tensor-core kernel; gs = 16: CUDA-core kernel below)
+// (gs = 32 or 16, both on the integer tensor core; see q80_common.cuh)
 // Replaces matvec_q80_rows (infer.c:765-786) behind matvec_rows (infer.c:792-797).
 //
 // One persistent CTA per SM owns an equal contiguous slice of the rows; its
@@ -30,7 +30,13 @@ struct MatvecArgs {
     const float* norm;   // if set: x is first replaced by rmsnorm(x) * norm (infer.c:746-752)
 };
 
+// Group-scale floats of x, rounded up to a multiple of 4 so that the table
+// after them starts on a 16-byte boundary.
+__host__ __device__ constexpr int sxg_floats(int cols) { return ((cols >> 5) + 3) & ~3; }
+
+template <int kGS>
 __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a) {
+    constexpr int kTab = kChunkTab;  // the gs = 32 table (gs = 16 reads sxg directly)
     {
         // Before waiting for the previous kernel (which writes x, never the
         // weights' values this kernel reads afterwards): pull the first
@@ -39,12 +45,13 @@ __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a)
         // only: the loads below come after the wait.
         const long long r0 = (long long)blockIdx.x * a.rows / gridDim.x;
         const long long r1 = (long long)(blockIdx.x + 1) * a.rows / gridDim.x;
-        const size_t qb = (size_t)(r1 - r0) * a.cols, sb = qb / 8;  // gs = 32: 4 bytes of scale per 32 weights
+        constexpr int kSDiv = kGS / 4;  // weight bytes per scale byte
+        const size_t qb = (size_t)(r1 - r0) * a.cols, sb = qb / kSDiv;
         const char* qp = reinterpret_cast<const char*>(a.q) + (size_t)r0 * a.cols;
-        const char* sp = reinterpret_cast<const char*>(a.s) + (size_t)r0 * (a.cols / 8);
+        const char* sp = reinterpret_cast<const char*>(a.s) + (size_t)r0 * (a.cols / kSDiv);
         for (size_t o = (size_t)threadIdx.x * 128; o < qb && o < kMvPrefetch; o += (size_t)kMvThreads * 128)
             asm volatile("prefetch.global.L2 [%0];\n" ::"l"(qp + o));
-        for (size_t o = (size_t)threadIdx.x * 128; o < sb && o < kMvPrefetch / 8; o += (size_t)kMvThreads * 128)
+        for (size_t o = (size_t)threadIdx.x * 128; o < sb && o < kMvPrefetch / kSDiv; o += (size_t)kMvThreads * 128)
             asm volatile("prefetch.global.L2 [%0];\n" ::"l"(sp + o));
     }
     pdl_enter();
@@ -52,8 +59,8 @@ __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a)
     const int nch = a.cols >> 6;
     int8_t* planes = reinterpret_cast<int8_t*>(sm);
     float* sxg = reinterpret_cast<float*>(sm + (size_t)nch * kChunkBytes);
-    float* sxtab = sxg + (a.cols >> 5);
-    float* part = sxtab + (size_t)nch * kChunkTab;  // [kMvWarps][16]
+    float* sxtab = sxg + sxg_floats(a.cols);  // 16-byte aligned: the gs = 16 table is read as float4
+    float* part = sxtab + (size_t)nch * kTab;       // [kMvWarps][16]
     float* xs = part + kMvWarps * 16;                 // [cols] normalised x (with a.norm)
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, t = lane & 3;
@@ -86,9 +93,10 @@ __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a)
     }
 
     const int boff = b_frag_offset(lane);
+    const G16Lane gl = g16_lane(lane);
     const int kq = warp % ks, tw = warp / ks;
     const int jb = kq * nch / ks, je = (kq + 1) * nch / ks;
-    const size_t sgrp = (size_t)(a.cols >> 5);
+    const size_t sgrp = (size_t)(a.cols / kGS);
 
     for (int tile0 = 0; tile0 < ntiles; tile0 += tiles_per_pass) {
         const int tile = tile0 + tw;
@@ -99,27 +107,41 @@ __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a)
             const int8_t* q1 = r1 < re ? a.q + (size_t)r1 * a.cols : nullptr;
             const float* s0 = r0 < re ? a.s + (size_t)r0 * sgrp : nullptr;
             const float* s1 = r1 < re ? a.s + (size_t)r1 * sgrp : nullptr;
+            const int4 z4 = make_int4(0, 0, 0, 0);
             for (int j = jb; j < je; j += kMvUnroll) {
                 int4 qa[kMvUnroll], qb[kMvUnroll];
-                float2 sa[kMvUnroll], sb[kMvUnroll];
+                float2 sa[kMvUnroll], sb[kMvUnroll];  // gs 16: .x, the scale of the lane's group
 #pragma unroll
                 for (int u = 0; u < kMvUnroll; ++u) {
                     const int jj = j + u;
                     const bool in = jj < je;
                     const int off = jj * kChunkCols + 16 * t;
-                    qa[u] = (in && q0) ? ld_weights16(q0 + off) : make_int4(0, 0, 0, 0);
-                    qb[u] = (in && q1) ? ld_weights16(q1 + off) : make_int4(0, 0, 0, 0);
-                    sa[u] = (in && s0) ? ld_scales2(s0 + 2 * jj) : make_float2(0.f, 0.f);
-                    sb[u] = (in && s1) ? ld_scales2(s1 + 2 * jj) : make_float2(0.f, 0.f);
+                    qa[u] = (in && q0) ? ld_weights16(q0 + off) : z4;
+                    qb[u] = (in && q1) ? ld_weights16(q1 + off) : z4;
+                    sa[u] = sb[u] = make_float2(0.f, 0.f);
+                    if constexpr (kGS == 32) {
+                        if (in && s0) sa[u] = ld_scales2(s0 + 2 * jj);
+                        if (in && s1) sb[u] = ld_scales2(s1 + 2 * jj);
+                    } else {
+                        if (in && s0) sa[u].x = ld_scale1(s0 + 4 * jj + t);
+                        if (in && s1) sb[u].x = ld_scale1(s1 + 4 * jj + t);
+                    }
                 }
 #pragma unroll
                 for (int u = 0; u < kMvUnroll; ++u) {
                     const int jj = j + u;
                     if (jj < je) {
-                        const int4 b = boff >= 0 ? *reinterpret_cast<const int4*>(planes + jj * kChunkBytes + boff)
-                                                 : make_int4(0, 0, 0, 0);
-                        const float2 tab = *reinterpret_cast<const float2*>(sxtab + jj * kChunkTab + 2 * t);
-                        chunk_mma_accumulate(qa[u], qb[u], sa[u], sb[u], b, tab, t, acc0, acc1);
+                        const int8_t* pl = planes + jj * kChunkBytes;
+                        if constexpr (kGS == 32) {
+                            const int4 b = boff >= 0 ? *reinterpret_cast<const int4*>(pl + boff) : z4;
+                            const float2 tab = *reinterpret_cast<const float2*>(sxtab + jj * kChunkTab + 2 * t);
+                            chunk_mma_accumulate(qa[u], qb[u], sa[u], sb[u], b, tab, t, acc0, acc1);
+                        } else {
+                            const int4 bx = gl.offX >= 0 ? *reinterpret_cast<const int4*>(pl + gl.offX) : z4;
+                            const int4 by = gl.offY >= 0 ? *reinterpret_cast<const int4*>(pl + gl.offY) : z4;
+                            chunk_mma_accumulate_g16(qa[u], qb[u], sa[u].x, sb[u].x, bx, by, sxg[2 * jj + (t >> 1)],
+                                                     acc0, acc1);
+                        }
                     }
                 }
             }
@@ -152,95 +174,27 @@ __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a)
     }
 }
 
-// gs = 16 (glm.c's own export, glm47_flash_export.py:36): the int8 MMA of
-// the kernel above sums 32 columns under one weight scale, so 16-column
-// groups take this CUDA-core kernel instead. Lane = one 16-byte group per
-// step (coalesced 512-byte warp loads), int8 -> fp32 by the exponent trick,
-// per-group dot, then s[row][group] * dot accumulated as in glm.c's
-// matvec_q80_rows (infer.c:765-786); one warp per row, rows strided over
-// the persistent CTAs.
-constexpr int kG16Warps = 16;
-
-__global__ void __launch_bounds__(kG16Warps * 32) q80_matvec_g16_kernel(MatvecArgs a) {
-    pdl_enter();
-    extern __shared__ __align__(16) unsigned char sm16[];
-    float* xs = reinterpret_cast<float*>(sm16);  // [cols]
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (a.norm) {
-        __shared__ double red[kG16Warps];
-        double ss = 0.0;
-        for (int i = threadIdx.x; i < a.cols; i += blockDim.x) ss += (double)a.x[i] * (double)a.x[i];
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-        if (lane == 0) red[warp] = ss;
-        __syncthreads();
-        double tot = 0.0;
-        for (int w = 0; w < kG16Warps; ++w) tot += red[w];
-        const float mean = (float)(tot / (double)a.cols);
-        const float inv = 1.0f / sqrtf(mean + 1e-5f);
-        for (int i = threadIdx.x; i < a.cols; i += blockDim.x) xs[i] = a.x[i] * inv * a.norm[i];
-    } else {
-        for (int i = threadIdx.x; i < a.cols; i += blockDim.x) xs[i] = a.x[i];
-    }
-    __syncthreads();
-    const int ng = a.cols >> 4;
-    for (int r = blockIdx.x * kG16Warps + warp; r < a.rows; r += gridDim.x * kG16Warps) {
-        const int8_t* qr = a.q + (size_t)r * a.cols;
-        const float* sr = a.s + (size_t)r * ng;
-        float acc = 0.0f;
-        for (int g = lane; g < ng; g += 32) {
-            const int4 q = ld_weights16(qr + 16 * g);
-            const float sc = __ldg(sr + g);
-            const float4* xv = reinterpret_cast<const float4*>(xs + 16 * g);
-            const uint32_t w4[4] = {(uint32_t)q.x, (uint32_t)q.y, (uint32_t)q.z, (uint32_t)q.w};
-            float dot = 0.0f;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float4 x4 = xv[j];
-                const uint32_t u = w4[j] ^ 0x80808080u;  // bytes q + 128
-                const float q0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650)) - 8388736.0f;
-                const float q1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7651)) - 8388736.0f;
-                const float q2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7652)) - 8388736.0f;
-                const float q3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7653)) - 8388736.0f;
-                dot = fmaf(q0, x4.x, dot);
-                dot = fmaf(q1, x4.y, dot);
-                dot = fmaf(q2, x4.z, dot);
-                dot = fmaf(q3, x4.w, dot);
-            }
-            acc = fmaf(sc, dot, acc);
-        }
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-        if (lane == 0) a.y[r] = a.accumulate ? a.y[r] + acc : acc;
-    }
-}
-
-size_t q80_matvec_smem_bytes(int cols, bool norm) {
+size_t q80_matvec_smem_bytes(int cols, bool norm, int gs) {
     const int nch = cols >> 6;
-    return (size_t)nch * kChunkBytes + (size_t)(cols >> 5) * 4 + (size_t)nch * kChunkTab * 4 + kMvWarps * 16 * 4 +
-           (norm ? (size_t)cols * 4 : 0);
+    (void)gs;  // both group sizes share the layout
+    return (size_t)nch * kChunkBytes + (size_t)sxg_floats(cols) * 4 + (size_t)nch * kChunkTab * 4 +
+           kMvWarps * 16 * 4 + (norm ? (size_t)cols * 4 : 0);
 }
 
 cudaError_t launch_q80_matvec(const int8_t* q, const float* s, const float* x, float* y, int rows, int cols,
                               int gs, int num_sms, cudaStream_t stream, bool accumulate, const float* norm) {
     if ((gs != 32 && gs != 16) || cols % 64 || rows <= 0) return cudaErrorInvalidValue;
-    if (gs == 16) {
-        const size_t smem16 = (size_t)cols * 4;
-        if (smem16 > 200 * 1024) return cudaErrorInvalidValue;
-        cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(q80_matvec_g16_kernel), (int)smem16);
-        if (e) return e;
-        int grid = num_sms * 2;
-        if (grid > (rows + kG16Warps - 1) / kG16Warps) grid = (rows + kG16Warps - 1) / kG16Warps;
-        MatvecArgs a{q, s, x, y, rows, cols, accumulate ? 1 : 0, norm};
-        return launch_pdl(q80_matvec_g16_kernel, grid, kG16Warps * 32, smem16, stream, a);
-    }
-    const size_t smem = q80_matvec_smem_bytes(cols, norm != nullptr);
+    // weight rows are read 16 bytes at a time, scales 2 floats (gs 32) or 1 (gs 16) at a time
+    if ((reinterpret_cast<uintptr_t>(q) & 15u) || (reinterpret_cast<uintptr_t>(s) & (gs == 16 ? 3u : 7u)))
+        return cudaErrorMisalignedAddress;
+    const size_t smem = q80_matvec_smem_bytes(cols, norm != nullptr, gs);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
-    if (cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(q80_matvec_kernel), (int)smem)) return e;
+    auto kernel = gs == 16 ? q80_matvec_kernel<16> : q80_matvec_kernel<32>;
+    if (cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kernel), (int)smem)) return e;
     int grid = num_sms;
     if (grid > (rows + 15) / 16) grid = (rows + 15) / 16;
     MatvecArgs a{q, s, x, y, rows, cols, accumulate ? 1 : 0, norm};
-    return launch_pdl(q80_matvec_kernel, grid, kMvThreads, smem, stream, a);
+    return launch_pdl(kernel, grid, kMvThreads, smem, stream, a);
 }
 
 }  // namespace glmq

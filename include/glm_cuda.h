@@ -13,8 +13,9 @@
  * experts stored expert-major (infer.c:697-742). Supported: gs == 32 or 16
  * (glm.c's own export uses 16, glm47_flash_export.py:36), dim % 128 == 0,
  * moe_ffn_dim % 64 == 0 (% 128 for gs == 16), 1 <= n_experts_used <= 8.
- * With gs == 16 every MoE call runs the batched kernels (the per-token
- * decode kernels take gs == 32 only) and the Q8 matvec a CUDA-core kernel.
+ * Both group sizes run on the integer tensor cores; per-token MoE calls take
+ * the persistent kernel at either size (the three-kernel chain, which the
+ * allocation-free entry point uses, takes gs == 32 only).
  *
  * Threading: like glm.c's backends (one instance per process, infer.m:18-37)
  * the library keeps one global device context; calls are serialised by an
@@ -89,7 +90,7 @@ int glm_cuda_moe_layer_async(int layer, float *x_dev, int n_tokens, int32_t *top
 #define GLM_CUDA_PATH_AUTO 0
 #define GLM_CUDA_PATH_PERSISTENT 1
 #define GLM_CUDA_PATH_CHAIN 2
-#define GLM_CUDA_PATH_BATCHED 3  /* group_size 16: every call runs the batched kernels */
+#define GLM_CUDA_PATH_BATCHED 3  /* sizes outside the per-token kernels: every call runs the batched kernels */
 
 /* Select the decode kernels (GLM_CUDA_PATH_*). No counterpart in glm.c. */
 int glm_cuda_set_decode_path(int path);
@@ -249,7 +250,9 @@ int glm_cuda_moe_layer_noalloc(const float *ffn_norm, const float *gate_inp, con
  * cached by its host address, as infer.m:307-322 caches Metal buffers. */
 int glm_cuda_matvec_q80(const int8_t *qmat, const float *smat, const float *x, float *y, int rows, int dim, int gs);
 
-/* Stream-ordered matvec on device pointers. */
+/* Stream-ordered matvec on device pointers. q_dev must be 16-byte aligned,
+ * s_dev 8-byte (gs 32) or 4-byte (gs 16) aligned, dim a multiple of 64;
+ * GLM_CUDA_ERR_CUDA (misaligned address) otherwise, before any launch. */
 int glm_cuda_matvec_q80_async(const int8_t *q_dev, const float *s_dev, const float *x_dev, float *y_dev, int rows,
                               int dim, int gs, void *stream);
 

@@ -1,7 +1,8 @@
 """Group size 16 (glm.c's own checkpoint export, glm47_flash_export.py:36)
-on the GPU: the MoE layer through the batched kernels, the Q8 matvec
-through the CUDA-core kernel and the full decoder, against glm.c's CPU path
-at gs = 16 (same bars as gs = 32: ids bit-exact, MoE output within 1e-3,
+on the GPU: the MoE layer through the persistent kernel (per-token calls)
+and the batched kernels (64 tokens), the Q8 matvec on the integer MMA with
+16-column scale groups, and the full decoder, against glm.c's CPU path at
+gs = 16 (same bars as gs = 32: ids bit-exact, MoE output within 1e-3,
 matvec within 1e-5, greedy ids identical and logits within 1e-3)."""
 import numpy as np
 import pytest
@@ -29,6 +30,7 @@ def test_gs16_config0_shape(T, lib, pkg, oracle_mod):
     x = synth.tokens(1600 + T, T, cfg["dim"])
     lib.init(0, cfg["dim"], cfg["ffn"], cfg["n_experts"], cfg["k_used"], 16, 1)
     lib.upload_moe_layer(0, L)
+    assert lib.decode_path() == lib.PATH_PERSISTENT  # T < 32: per-token calls; T = 64 batched
     x_out, idx, w = lib.moe_layer(0, x, cfg["k_used"])
     ref, ref_idx, ref_w = oracle_mod.moe_layer(L, x, impl="orc")
     np.testing.assert_array_equal(idx, ref_idx)
@@ -37,7 +39,7 @@ def test_gs16_config0_shape(T, lib, pkg, oracle_mod):
     print(f"gs16 T={T}: worst rel L2 {worst:.2e}")
 
 
-@pytest.mark.parametrize("rows,cols", [(1536, 2048), (2048, 1536), (4608, 2048), (37, 192), (1, 64)])
+@pytest.mark.parametrize("rows,cols", [(1536, 2048), (2048, 1536), (4608, 2048), (37, 192), (1, 64), (5000, 10240)])
 def test_gs16_matvec(rows, cols, lib, pkg, oracle_mod):
     q, s, x = pkg.synth.matvec_case(rows + 16 * cols, rows, cols, 16)
     lib.init(0, 256, 128, 8, 2, 16, 1)
@@ -90,12 +92,13 @@ def test_checkpoint_file_decodes_like_glm(gs, lib, pkg, oracle_mod, tmp_path):
     np.testing.assert_array_equal(ids, ids_ref)
 
 
-def test_checkpoint_config2_shapes(lib, pkg, oracle_mod, tmp_path):
+@pytest.mark.parametrize("gs", [32, 16])
+def test_checkpoint_config2_shapes(gs, lib, pkg, oracle_mod, tmp_path):
     """GLM-4.7-Flash shapes (3 layers, vocab 154880) through the .bin path."""
     from bin_writer import write_runtime_bin
 
     synth = pkg.synth
-    dims = dict(synth.CONFIG2, n_layers=3)
+    dims = dict(synth.CONFIG2, n_layers=3, group_size=gs)
     model = synth.decoder_model(24, **dims)
     prompt = synth.prompt_ids(24, 8, dims["vocab_size"])
     path = str(tmp_path / "model.bin")

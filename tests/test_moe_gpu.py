@@ -53,17 +53,31 @@ def test_moe_decode_matches_golden(name, path, lib, golden):
     print(f"{name}: worst FFN-delta rel L2 {worst:.2e}")
 
 
-def test_moe_gs16_runs_batched(lib, golden):
-    """gs = 16 (glm.c's own export): the per-token decode kernels take gs = 32
-    only, so every call runs the batched kernels; results as the reference's."""
+@pytest.mark.parametrize("batched", [False, True])
+def test_moe_gs16_golden(batched, lib, golden):
+    """gs = 16 (glm.c's own export): per-token calls take the persistent
+    kernel (16-column scale groups on the integer MMA); with the prefill
+    threshold at 1 every call takes the batched kernels. Both as glm.c's."""
     L, x, routed, exp = golden.load_case("moe_tiny_gs16")
     lib.init(0, L["dim"], L["ffn"], L["n_experts"], L["k_used"], L["gs"], 1)
     lib.upload_moe_layer(0, L)
-    assert lib.decode_path() == 3  # GLM_CUDA_PATH_BATCHED
+    assert lib.decode_path() == lib.PATH_PERSISTENT
+    lib.set_prefill_tokens(1 if batched else 0)
     with routed_env(routed):
         x_out, idx, w = lib.moe_layer(0, x, L["k_used"])
     np.testing.assert_array_equal(idx, exp["topk_idx"])
+    valid = exp["topk_idx"] >= 0
+    np.testing.assert_allclose(w[valid], exp["topk_w"][valid], rtol=0, atol=TOL_W)
     check_moe_outputs(x, x_out, exp["x_out"], TOL)
+
+
+def test_moe_gs16_refuses_the_chain(lib, golden):
+    import glm_c_b200.glm_cuda as gc
+
+    L, _, _, _ = golden.load_case("moe_tiny_gs16")
+    lib.init(0, L["dim"], L["ffn"], L["n_experts"], L["k_used"], L["gs"], 1)
+    with pytest.raises(gc.GlmCudaError):
+        lib.set_decode_path(PATHS["chain"])
 
 
 def test_auto_path_is_persistent_at_config0(lib, pkg):
