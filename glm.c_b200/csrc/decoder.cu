@@ -14,6 +14,8 @@
 #include <cmath>
 #include <cstdint>
 
+#include <cooperative_groups.h>
+
 #include "glm_internal.h"
 #include "q80_common.cuh"
 
@@ -73,31 +75,6 @@ __global__ void embed_kernel(const int8_t* tok_q, const float* tok_s, const int*
     for (int i = threadIdx.x; i < D; i += blockDim.x) x[i] = (float)q[i] * s[i / gs];
 }
 
-// kv_a[0:kv_lora] <- rmsnorm * kv_a_norm, stored as this position's
-// compressed key; kv_a[kv_lora:] roped, stored as its rope key
-// (infer.c:1003-1016).
-__global__ void kv_cache_write_kernel(float* kv_a, const float* kv_norm, float* cache_comp, float* cache_pe,
-                                      const int* pos_dev, int kv_lora, int rope) {
-    pdl_enter();
-    __shared__ double red[32];
-    const int pos = *pos_dev;
-    const float inv = rms_inv(kv_a, kv_lora, red);
-    __syncthreads();
-    float* comp = cache_comp + (size_t)pos * kv_lora;
-    for (int i = threadIdx.x; i < kv_lora; i += blockDim.x) {
-        const float v = kv_a[i] * inv * kv_norm[i];
-        kv_a[i] = v;
-        comp[i] = v;
-    }
-    float* pe = cache_pe + (size_t)pos * rope;
-    for (int i = 2 * threadIdx.x; i + 1 < rope; i += 2 * blockDim.x) {
-        float x0 = kv_a[kv_lora + i], x1 = kv_a[kv_lora + i + 1];
-        rope_pair(x0, x1, i, rope, pos);
-        pe[i] = x0;
-        pe[i + 1] = x1;
-    }
-}
-
 // kR rows of a planar Q8 matrix dotted with x (shared memory) by one warp,
 // all rows' loads issued together: lane l covers the kBytes-wide pieces
 // l, l + 32, ... of every row (cols a multiple of kBytes and of gs).
@@ -148,81 +125,153 @@ __device__ __forceinline__ void q8_rows_dot(const int8_t* q, const float* s, con
         for (int off = 16; off > 0; off >>= 1) out[j] += __shfl_xor_sync(0xffffffffu, out[j], off);
 }
 
-// MLA attention of one head per CTA (infer.c:1018-1058): q_pe roped,
-// q_abs = k_b_h . q_nope, scores over the cache, softmax, context, and
-// att_concat[h] = v_b_h . context. Every stage keeps many independent loads
-// in flight (rows in groups of 8 per warp; cache rows split over the warps).
-__global__ void __launch_bounds__(512) mla_heads_kernel(MlaArgs a) {
-    pdl_enter();
+// kR rows of q8_rows_dot as lane kR-1 .. 0 hold them: row r0 + lane's value in
+// lanes [0, kR).
+template <int kR>
+__device__ __forceinline__ float pick_row(const float (&v)[kR], int lane) {
+    float mine = v[0];
+#pragma unroll
+    for (int j = 1; j < kR; ++j)
+        if (lane == j) mine = v[j];
+    return mine;
+}
+
+// MLA attention (infer.c:1003-1058) for every head, one thread-block cluster
+// of kMlaCluster CTAs per head; the CTAs of a head split every stage and
+// exchange through distributed shared memory:
+//   0. every CTA forms this position's key from kv_a: the latent part
+//      rmsnorm * kv_a_norm, the rope part roped (infer.c:1003-1016); rank 0
+//      of head 0 stores it in the cache, every CTA uses its own copy for
+//      position pos;
+//   1. q_abs = k_b_h . q_nope: each CTA computes 1/S of the rows and stores
+//      them into every CTA of the cluster;
+//   2. scores over 1/S of the positions, with the CTA's own max m and sum l
+//      of exp(score - m), and its context partial sum_t exp(score_t - m) kc[t];
+//   3. each CTA combines 1/S of the context columns over the cluster
+//      (ctx = sum_r e^(m_r - M) part_r / sum_r e^(m_r - M) l_r, M the
+//      largest m_r) and stores them into every CTA;
+//   4. att_concat[h] = v_b_h . ctx: each CTA computes 1/S of the rows.
+__global__ void __cluster_dims__(kMlaCluster, 1, 1) __launch_bounds__(kMlaThreads)
+    mla_cluster_kernel(MlaArgs a) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cl = cg::this_cluster();
+    constexpr int S = kMlaCluster, nw = kMlaThreads / 32;
     extern __shared__ __align__(16) float smf[];
-    constexpr int kR = 8;
-    const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-    const int pos = *a.pos;
-    float* q_nope = smf;                   // [qk_nope]
-    float* q_pe = q_nope + a.qk_nope;      // [rope]
-    float* q_abs = q_pe + a.rope;          // [kv_lora]
-    float* ctx = q_abs + a.kv_lora;        // [kv_lora]
-    float* scores = ctx + a.kv_lora;       // [cache_cap]
-    float* cpart = scores + a.cache_cap;   // [nw][kv_lora] per-warp context partials
-    __shared__ float red[32];
-
-    const float* qh = a.q_full + (size_t)h * a.head_k;
-    for (int i = tid; i < a.qk_nope; i += blockDim.x) q_nope[i] = qh[i];
-    for (int i = 2 * tid; i + 1 < a.rope; i += 2 * blockDim.x) {
-        float x0 = qh[a.qk_nope + i], x1 = qh[a.qk_nope + i + 1];
-        rope_pair(x0, x1, i, a.rope, pos);
-        q_pe[i] = x0;
-        q_pe[i + 1] = x1;
-    }
-    __syncthreads();
-
-    // q_abs[r] = k_b_h[r] . q_nope  (k_b: [heads][kv_lora][qk_nope])
+    const int rank = (int)cl.block_rank(), h = blockIdx.x / S;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int r_lo = rank * a.kv_lora / S, r_hi = (rank + 1) * a.kv_lora / S;  // q_abs rows
+    const int o_lo = rank * a.v_head / S, o_hi = (rank + 1) * a.v_head / S;    // output rows
     const int8_t* kbq = a.k_b_q + (size_t)h * a.kv_lora * a.qk_nope;
     const float* kbs = a.k_b_s + (size_t)h * a.kv_lora * (a.qk_nope / a.gs);
-    for (int r0 = warp * kR; r0 < a.kv_lora; r0 += nw * kR) {
-        float v[kR];
-        q8_rows_dot<8, kR>(kbq, kbs, q_nope, a.qk_nope, a.gs, r0, a.kv_lora, v);
-        if (lane < kR && r0 + lane < a.kv_lora) {
-            float mine = v[0];
+    const int8_t* vbq = a.v_b_q + (size_t)h * a.v_head * a.kv_lora;
+    const float* vbs = a.v_b_s + (size_t)h * a.v_head * (a.kv_lora / a.gs);
+    {
+        // Weights no kernel writes: pull this CTA's slices into L2 before
+        // waiting for the previous kernel.
+        auto pf = [&](const void* p, size_t bytes) {
+            for (size_t o = (size_t)tid * 128; o < bytes; o += (size_t)kMlaThreads * 128)
+                asm volatile("prefetch.global.L2 [%0];\n" ::"l"(reinterpret_cast<const char*>(p) + o));
+        };
+        pf(kbq + (size_t)r_lo * a.qk_nope, (size_t)(r_hi - r_lo) * a.qk_nope);
+        pf(kbs + (size_t)r_lo * (a.qk_nope / a.gs), (size_t)(r_hi - r_lo) * (a.qk_nope / a.gs) * 4);
+        pf(vbq + (size_t)o_lo * a.kv_lora, (size_t)(o_hi - o_lo) * a.kv_lora);
+        pf(vbs + (size_t)o_lo * (a.kv_lora / a.gs), (size_t)(o_hi - o_lo) * (a.kv_lora / a.gs) * 4);
+        pf(a.kv_norm, (size_t)a.kv_lora * 4);
+    }
+    float* q_nope = smf;                      // [qk_nope]
+    float* q_pe = q_nope + a.qk_nope;         // [rope]
+    float* key = q_pe + a.rope;               // [kv_lora + rope] this position's cache entry
+    float* q_abs = key + a.kv_lora + a.rope;  // [kv_lora]
+    float* ctx = q_abs + a.kv_lora;           // [kv_lora]
+    float* part = ctx + a.kv_lora;            // [kv_lora] this CTA's context partial
+    float* stat = part + a.kv_lora;           // [2] m, l  (+2 pad)
+    float* scores = stat + 4;                 // [ceil(cap / S)]
+    __shared__ double red_d[32];
+    __shared__ float red[32];
+
+    pdl_enter();
+    const int pos = *a.pos;
+    // this head's query and the kv_a projection, every load in flight at once
+    {
+        const float* qh = a.q_full + (size_t)h * a.head_k;
+        const int nkv = a.kv_lora + a.rope;
+        float vq[kMlaStage], vk[kMlaStage];
 #pragma unroll
-            for (int j = 1; j < kR; ++j)
-                if (lane == j) mine = v[j];
-            q_abs[r0 + lane] = mine;
+        for (int u = 0; u < kMlaStage; ++u) {
+            const int i = tid + u * kMlaThreads;
+            vq[u] = i < a.head_k ? qh[i] : 0.f;
+            vk[u] = i < nkv ? a.kv_a[i] : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < kMlaStage; ++u) {
+            const int i = tid + u * kMlaThreads;
+            if (i < a.head_k) q_nope[i] = vq[u];  // q_nope then q_pe: contiguous like q_full
+            if (i < nkv) key[i] = vk[u];
         }
     }
     __syncthreads();
+    // q_pe roped; this position's key: the latent part rmsnorm * kv_a_norm,
+    // the rope part roped (infer.c:1003-1016)
+    for (int i = 2 * tid; i + 1 < a.rope; i += 2 * kMlaThreads) {
+        rope_pair(q_pe[i], q_pe[i + 1], i, a.rope, pos);
+        rope_pair(key[a.kv_lora + i], key[a.kv_lora + i + 1], i, a.rope, pos);
+    }
+    const float inv = rms_inv(key, a.kv_lora, red_d);  // starts and ends with block barriers
+    for (int i = tid; i < a.kv_lora; i += kMlaThreads) key[i] = key[i] * inv * a.kv_norm[i];
+    __syncthreads();
+    if (h == 0 && rank == 0) {
+        for (int i = tid; i < a.kv_lora; i += kMlaThreads) a.cache_comp[(size_t)pos * a.kv_lora + i] = key[i];
+        for (int i = tid; i < a.rope; i += kMlaThreads) a.cache_pe[(size_t)pos * a.rope + i] = key[a.kv_lora + i];
+    }
 
-    // scores[t] = (q_abs . kc[t] + q_pe . kp[t]) * kq_scale, two rows per warp step
-    const float* cc = a.cache_comp;
-    const float* cp = a.cache_pe;
-    for (int t = warp; t <= pos; t += 2 * nw) {
-        const int t2 = t + nw;
-        const float* kc = cc + (size_t)t * a.kv_lora;
-        const float* kc2 = cc + (size_t)(t2 <= pos ? t2 : t) * a.kv_lora;
-        float d = 0.f, d2 = 0.f;
-        for (int i = lane; i < a.kv_lora; i += 32) {
-            d += q_abs[i] * kc[i];
-            d2 += q_abs[i] * kc2[i];
-        }
-        for (int i = lane; i < a.rope; i += 32) {
-            d += q_pe[i] * cp[(size_t)t * a.rope + i];
-            d2 += q_pe[i] * cp[(size_t)(t2 <= pos ? t2 : t) * a.rope + i];
-        }
+    // 1. q_abs[r] = k_b_h[r] . q_nope (k_b: [heads][kv_lora][qk_nope]), rows [r_lo, r_hi)
+    {
+        constexpr int kR = 8;
+        for (int r0 = r_lo + warp * kR; r0 < r_hi; r0 += nw * kR) {
+            float v[kR];
+            q8_rows_dot<8, kR>(kbq, kbs, q_nope, a.qk_nope, a.gs, r0, r_hi, v);
+            const float mine = pick_row(v, lane);
+            if (lane < kR && r0 + lane < r_hi)
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) {
-            d += __shfl_xor_sync(0xffffffffu, d, off);
-            d2 += __shfl_xor_sync(0xffffffffu, d2, off);
-        }
-        if (lane == 0) {
-            scores[t] = d * a.kq_scale;
-            if (t2 <= pos) scores[t2] = d2 * a.kq_scale;
+                for (int d = 0; d < S; ++d) *cl.map_shared_rank(q_abs + r0 + lane, d) = mine;
         }
     }
-    __syncthreads();
+    cl.sync();
 
-    // softmax (infer.c:951-962)
-    float mx = -FLT_MAX;
-    for (int t = tid; t <= pos; t += blockDim.x) mx = fmaxf(mx, scores[t]);
+    // 2. scores[t] = (q_abs . kc[t] + q_pe . kp[t]) * kq_scale over positions
+    // [t_lo, t_hi): a warp per position, each lane 4 consecutive floats per
+    // 128-float block, every load of the row in flight at once
+    const int np = pos + 1, t_lo = rank * np / S, t_hi = (rank + 1) * np / S, nloc = t_hi - t_lo;
+    for (int t = t_lo + warp; t < t_hi; t += nw) {
+        const float* kc = t == pos ? key : a.cache_comp + (size_t)t * a.kv_lora;
+        const float* kp = t == pos ? key + a.kv_lora : a.cache_pe + (size_t)t * a.rope;
+        float4 c4[kMlaRowBlocks], p4;
+#pragma unroll
+        for (int u = 0; u < kMlaRowBlocks; ++u) {
+            const int i = 4 * lane + 128 * u;
+            c4[u] = i < a.kv_lora ? *reinterpret_cast<const float4*>(kc + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        p4 = 4 * lane < a.rope ? *reinterpret_cast<const float4*>(kp + 4 * lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+        float d = 0.f;
+#pragma unroll
+        for (int u = 0; u < kMlaRowBlocks; ++u) {
+            const int i = 4 * lane + 128 * u;
+            if (i < a.kv_lora) {
+                const float4 qa = *reinterpret_cast<const float4*>(q_abs + i);
+                d += qa.x * c4[u].x + qa.y * c4[u].y + qa.z * c4[u].z + qa.w * c4[u].w;
+            }
+        }
+        if (4 * lane < a.rope) {
+            const float4 qp = *reinterpret_cast<const float4*>(q_pe + 4 * lane);
+            d += qp.x * p4.x + qp.y * p4.y + qp.z * p4.z + qp.w * p4.w;
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+        if (lane == 0) scores[t - t_lo] = d * a.kq_scale;
+    }
+    __syncthreads();
+    float mx = -FLT_MAX;  // a CTA without positions keeps -FLT_MAX and l = 0
+    for (int t = tid; t < nloc; t += kMlaThreads) mx = fmaxf(mx, scores[t]);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
     if (lane == 0) red[warp] = mx;
@@ -231,43 +280,80 @@ __global__ void __launch_bounds__(512) mla_heads_kernel(MlaArgs a) {
     for (int w = 1; w < nw; ++w) mx = fmaxf(mx, red[w]);
     __syncthreads();
     float sum = 0.f;
-    for (int t = tid; t <= pos; t += blockDim.x) {
+    for (int t = tid; t < nloc; t += kMlaThreads) {
         const float e = expf(scores[t] - mx);
         scores[t] = e;
         sum += e;
     }
-    sum = block_sum_f(sum, red);
-    const float inv = sum > 0.f ? 1.0f / sum : 1.0f;
-    __syncthreads();
-
-    // ctx = sum_t p[t] kc[t]: warp w takes positions w, w + nw, ... (lanes
-    // over the row), then the warps' partials are added in warp order.
-    for (int i = lane; i < a.kv_lora; i += 32) {
-        float acc = 0.f;
-        for (int t = warp; t <= pos; t += nw) acc += scores[t] * inv * cc[(size_t)t * a.kv_lora + i];
-        cpart[warp * a.kv_lora + i] = acc;
-    }
-    __syncthreads();
-    for (int i = tid; i < a.kv_lora; i += blockDim.x) {
-        float acc = 0.f;
-        for (int w = 0; w < nw; ++w) acc += cpart[w * a.kv_lora + i];
-        ctx[i] = acc;
-    }
-    __syncthreads();
-
-    // att_concat[h][r] = v_b_h[r] . ctx  (v_b: [heads][v_head][kv_lora])
-    const int8_t* vbq = a.v_b_q + (size_t)h * a.v_head * a.kv_lora;
-    const float* vbs = a.v_b_s + (size_t)h * a.v_head * (a.kv_lora / a.gs);
-    float* out = a.att_concat + (size_t)h * a.v_head;
-    for (int r0 = warp * kR; r0 < a.v_head; r0 += nw * kR) {
-        float v[kR];
-        q8_rows_dot<16, kR>(vbq, vbs, ctx, a.kv_lora, a.gs, r0, a.v_head, v);
-        if (lane < kR && r0 + lane < a.v_head) {
-            float mine = v[0];
+    sum = block_sum_f(sum, red);  // ends with a block barrier: every exp is stored
+    // context partial: thread pairs of columns, 8 positions' loads in flight
+    for (int i = 2 * tid; i < a.kv_lora; i += 2 * kMlaThreads) {
+        float2 acc = make_float2(0.f, 0.f);
+        for (int t0 = t_lo; t0 < t_hi; t0 += 8) {
+            float2 v[8];
 #pragma unroll
-            for (int j = 1; j < kR; ++j)
-                if (lane == j) mine = v[j];
-            out[r0 + lane] = mine;
+            for (int u = 0; u < 8; ++u) {
+                const int t = t0 + u;
+                v[u] = t >= t_hi ? make_float2(0.f, 0.f)
+                       : t == pos ? make_float2(key[i], key[i + 1])
+                                  : *reinterpret_cast<const float2*>(a.cache_comp + (size_t)t * a.kv_lora + i);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const float e = t0 + u < t_hi ? scores[t0 + u - t_lo] : 0.f;
+                acc.x += e * v[u].x;
+                acc.y += e * v[u].y;
+            }
+        }
+        part[i] = acc.x;
+        part[i + 1] = acc.y;
+    }
+    if (tid == 0) {
+        stat[0] = mx;
+        stat[1] = sum;
+    }
+    cl.sync();
+
+    // 3. ctx columns [c_lo, c_hi), combined over the cluster
+    {
+        float m_r[S], w_r[S];
+        float M = -FLT_MAX;
+#pragma unroll
+        for (int r = 0; r < S; ++r) {
+            m_r[r] = *cl.map_shared_rank(stat, r);
+            M = fmaxf(M, m_r[r]);
+        }
+        float L = 0.f;
+#pragma unroll
+        for (int r = 0; r < S; ++r) {
+            w_r[r] = expf(m_r[r] - M);
+            L += *cl.map_shared_rank(stat + 1, r) * w_r[r];
+        }
+        const float invL = L > 0.f ? 1.0f / L : 1.0f;
+        const int c_lo = rank * a.kv_lora / S, c_hi = (rank + 1) * a.kv_lora / S;
+        for (int i = c_lo + tid; i < c_hi; i += kMlaThreads) {
+            float pr[S];
+#pragma unroll
+            for (int r = 0; r < S; ++r) pr[r] = *cl.map_shared_rank(part + i, r);
+            float acc = 0.f;
+#pragma unroll
+            for (int r = 0; r < S; ++r) acc += pr[r] * w_r[r];
+            acc *= invL;
+#pragma unroll
+            for (int d = 0; d < S; ++d) *cl.map_shared_rank(ctx + i, d) = acc;
+        }
+    }
+    cl.sync();  // last cluster-wide access: after it every CTA reads only its own memory
+
+    // 4. att_concat[h][r] = v_b_h[r] . ctx (v_b: [heads][v_head][kv_lora]), rows [o_lo, o_hi)
+    {
+        constexpr int kR = 4;
+        float* out = a.att_concat + (size_t)h * a.v_head;
+        for (int r0 = o_lo + warp * kR; r0 < o_hi; r0 += nw * kR) {
+            float v[kR];
+            q8_rows_dot<16, kR>(vbq, vbs, ctx, a.kv_lora, a.gs, r0, o_hi, v);
+            const float mine = pick_row(v, lane);
+            if (lane < kR && r0 + lane < o_hi) out[r0 + lane] = mine;
         }
     }
 }
@@ -369,21 +455,21 @@ cudaError_t launch_embed(const int8_t* tok_q, const float* tok_s, const int* tok
     return launch_pdl(embed_kernel, 1, 512, 0, st, tok_q, tok_s, token, x, D, gs);
 }
 
-cudaError_t launch_kv_cache_write(float* kv_a, const float* kv_norm, float* cache_comp, float* cache_pe,
-                                  const int* pos, int kv_lora, int rope, cudaStream_t st) {
-    return launch_pdl(kv_cache_write_kernel, 1, 512, 0, st, kv_a, kv_norm, cache_comp, cache_pe, pos, kv_lora, rope);
+size_t mla_smem(const MlaArgs& a) {
+    const size_t per = ((size_t)a.cache_cap + kMlaCluster - 1) / kMlaCluster;
+    return sizeof(float) * ((size_t)a.qk_nope + 2 * (size_t)a.rope + 4 * (size_t)a.kv_lora + 4 + per);
 }
 
-size_t mla_heads_smem(const MlaArgs& a, int cache_cap) {
-    return sizeof(float) * ((size_t)a.qk_nope + a.rope + 2 * (size_t)a.kv_lora + cache_cap + 16 * (size_t)a.kv_lora);
-}
-
-cudaError_t launch_mla_heads(const MlaArgs& a, int n_heads, int cache_cap, cudaStream_t st) {
-    const size_t smem = mla_heads_smem(a, cache_cap);
+cudaError_t launch_mla(const MlaArgs& a, int n_heads, cudaStream_t st) {
+    // q8_rows_dot widths, float4 rows, register staging and row blocks
+    if (a.qk_nope % 8 || a.kv_lora % 16 || a.qk_nope % a.gs || a.kv_lora % a.gs || a.rope % 4 || a.rope > 128 ||
+        a.head_k != a.qk_nope + a.rope || a.head_k > kMlaStage * kMlaThreads ||
+        a.kv_lora + a.rope > kMlaStage * kMlaThreads || a.kv_lora > 128 * kMlaRowBlocks)
+        return cudaErrorInvalidValue;
+    const size_t smem = mla_smem(a);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
-    if (smem > 48 * 1024)
-        if (cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(mla_heads_kernel), (int)smem)) return e;
-    return launch_pdl(mla_heads_kernel, n_heads, 512, smem, st, a);
+    if (cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(mla_cluster_kernel), (int)smem)) return e;
+    return launch_pdl(mla_cluster_kernel, n_heads * kMlaCluster, kMlaThreads, smem, st, a);
 }
 
 cudaError_t launch_silu_mul(float* g, const float* u, int n, int num_sms, cudaStream_t st) {

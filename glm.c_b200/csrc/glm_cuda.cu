@@ -1028,20 +1028,18 @@ int enqueue_step(cudaStream_t st) {
         const AttnLayer& A = m.attn[l];
         // MLA attention (infer.c:978-1065)
         // (the rmsnorms of x and q_a run fused into the matvecs that read them)
-        LAUNCH_TRY(glmq::launch_q80_matvec(A.q_a_q, A.q_a_s, m.x, m.q_a, d.q_lora_rank, D, gs, ns, st, false,
-                                           A.attn_norm));
+        // q_a and kv_a both read rmsnorm(x) * attn_norm: one launch
+        LAUNCH_TRY(glmq::launch_q80_matvec2(A.q_a_q, A.q_a_s, m.q_a, d.q_lora_rank, A.kv_a_q, A.kv_a_s, m.kv_a,
+                                            d.kv_lora_rank + d.rope_dim, m.x, D, gs, ns, st, A.attn_norm));
         LAUNCH_TRY(glmq::launch_q80_matvec(A.q_b_q, A.q_b_s, m.q_a, m.q_full, d.n_heads * d.head_k_dim, d.q_lora_rank,
                                            gs, ns, st, false, A.q_a_norm));
-        LAUNCH_TRY(glmq::launch_q80_matvec(A.kv_a_q, A.kv_a_s, m.x, m.kv_a, d.kv_lora_rank + d.rope_dim, D, gs, ns, st,
-                                           false, A.attn_norm));
         float* comp = m.cache_comp + (size_t)l * d.cache_cap * d.kv_lora_rank;
         float* pe = m.cache_pe + (size_t)l * d.cache_cap * d.rope_dim;
-        LAUNCH_TRY(glmq::launch_kv_cache_write(m.kv_a, A.kv_a_norm, comp, pe, m.pos, d.kv_lora_rank, d.rope_dim, st));
-        glmq::MlaArgs ma{m.q_full,        comp,          pe,           A.k_b_q,         A.k_b_s,
-                         A.v_b_q,         A.v_b_s,       m.att,        m.pos,           d.qk_nope_dim,
-                         d.rope_dim,      d.head_k_dim,  d.kv_lora_rank, d.v_head_dim,  gs,
-                         d.cache_cap,     kq_scale};
-        LAUNCH_TRY(glmq::launch_mla_heads(ma, d.n_heads, d.cache_cap, st));
+        glmq::MlaArgs ma{m.q_full,       m.kv_a,        A.kv_a_norm,  comp,          pe,
+                         A.k_b_q,        A.k_b_s,       A.v_b_q,      A.v_b_s,       m.att,
+                         m.pos,          d.qk_nope_dim, d.rope_dim,   d.head_k_dim,  d.kv_lora_rank,
+                         d.v_head_dim,   gs,            d.cache_cap,  kq_scale};
+        LAUNCH_TRY(glmq::launch_mla(ma, d.n_heads, st));
         LAUNCH_TRY(glmq::launch_q80_matvec(A.attn_out_q, A.attn_out_s, m.att, m.x, D, d.n_heads * d.v_head_dim, gs,
                                            ns, st, true));
         if (l == 0) {
@@ -1067,7 +1065,7 @@ int enqueue_step(cudaStream_t st) {
             LAUNCH_TRY(glmq::launch_moe_decode(g.layers[l].w, g.dims, g.scratch, m.x, m.x, routed, ns, st));
             g.launches += 3;
         }
-        g.launches += 6;
+        g.launches += 4;  // q_a + kv_a, q_b, MLA, attention output
     }
     // final norm (fused), LM head, argmax (infer.c:1888-1893, 1218-1228)
     LAUNCH_TRY(glmq::launch_q80_matvec(m.out_q, m.out_s, m.x, m.logits, d.vocab_size, D, gs, ns, st, false,

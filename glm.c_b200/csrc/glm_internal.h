@@ -75,12 +75,20 @@ cudaError_t launch_q80_matvec(const int8_t* q, const float* s, const float* x, f
                               int gs, int num_sms, cudaStream_t stream, bool accumulate = false,
                               const float* norm = nullptr);
 
+// Two matrices with the same column count on the same (normed) x in one
+// launch: y = Q8(q, s) . x (rows rows), y2 = Q8(q2, s2) . x (rows2 rows).
+cudaError_t launch_q80_matvec2(const int8_t* q, const float* s, float* y, int rows, const int8_t* q2,
+                               const float* s2, float* y2, int rows2, const float* x, int cols, int gs, int num_sms,
+                               cudaStream_t stream, const float* norm);
+
 // ---- decoder around the MoE layers (decoder.cu)
 
 struct MlaArgs {
     const float* q_full;      // [n_heads][head_k]
-    const float* cache_comp;  // this layer's [cap][kv_lora]
-    const float* cache_pe;    // this layer's [cap][rope]
+    const float* kv_a;        // [kv_lora + rope] this position's kv_a projection
+    const float* kv_norm;     // [kv_lora] kv_a_norm
+    float* cache_comp;        // this layer's [cap][kv_lora]; position pos is written
+    float* cache_pe;          // this layer's [cap][rope]
     const int8_t* k_b_q;      // [n_heads][kv_lora][qk_nope]
     const float* k_b_s;
     const int8_t* v_b_q;      // [n_heads][v_head][kv_lora]
@@ -93,10 +101,14 @@ struct MlaArgs {
 
 cudaError_t launch_embed(const int8_t* tok_q, const float* tok_s, const int* token, float* x, int D, int gs,
                          cudaStream_t st);
-cudaError_t launch_kv_cache_write(float* kv_a, const float* kv_norm, float* cache_comp, float* cache_pe,
-                                  const int* pos, int kv_lora, int rope, cudaStream_t st);
-size_t mla_heads_smem(const MlaArgs& a, int cache_cap);
-cudaError_t launch_mla_heads(const MlaArgs& a, int n_heads, int cache_cap, cudaStream_t st);
+// MLA attention of every head with this position's cache write, one
+// thread-block cluster of kMlaCluster CTAs per head (decoder.cu).
+constexpr int kMlaCluster = 8;
+constexpr int kMlaThreads = 256;
+constexpr int kMlaStage = 4;      // staged q / kv_a floats per thread: head_k, kv_lora + rope <= 1024
+constexpr int kMlaRowBlocks = 8;  // 128-float blocks of a cache row: kv_lora <= 1024
+size_t mla_smem(const MlaArgs& a);
+cudaError_t launch_mla(const MlaArgs& a, int n_heads, cudaStream_t st);
 cudaError_t launch_silu_mul(float* g, const float* u, int n, int num_sms, cudaStream_t st);
 // part: nblocks float2 scratch; counter: one word, zero between calls.
 cudaError_t launch_argmax(const float* x, int n, float2* part, unsigned* counter, int nblocks, int* out,

@@ -644,6 +644,7 @@ __global__ void __launch_bounds__(PCfg<kGS>::kThreads, 1) moe_persistent_kernel(
         const unsigned char* sb = slot_buf(P, item) + kPTile * cols;
         const int srow = cols * 4 / kGS;  // scale bytes per row
         float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll(kGS == 32 ? 2 : 1)
         for (int j = gw * nch / kPGroupWarps; j < (gw + 1) * nch / kPGroupWarps; ++j) {
             const int off = j * kChunkCols + 16 * t4;
             const int4 q0 = v0 ? lds16(qb + gid * cols + off) : z4;

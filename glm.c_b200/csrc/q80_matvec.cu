@@ -28,6 +28,20 @@ struct MatvecArgs {
     int rows, cols;
     int accumulate;      // y += result instead of y = result
     const float* norm;   // if set: x is first replaced by rmsnorm(x) * norm (infer.c:746-752)
+    // optional second matrix on the same x (rows2 = 0: none): its rows follow
+    // the first matrix's in the row split and land in y2
+    const int8_t* q2;
+    const float* s2;
+    float* y2;
+    int rows2;
+
+    __device__ __forceinline__ const int8_t* qrow(int r) const {
+        return r < rows ? q + (size_t)r * cols : q2 + (size_t)(r - rows) * cols;
+    }
+    __device__ __forceinline__ const float* srow(int r, int groups) const {
+        return r < rows ? s + (size_t)r * groups : s2 + (size_t)(r - rows) * groups;
+    }
+    __device__ __forceinline__ float* yrow(int r) const { return r < rows ? y + r : y2 + (r - rows); }
 };
 
 // Group-scale floats of x, rounded up to a multiple of 4 so that the table
@@ -43,16 +57,24 @@ __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a)
         // kMvPrefetch bytes of this CTA's weight rows and their scales into
         // L2, so the stream starts while the previous kernel drains. A hint
         // only: the loads below come after the wait.
-        const long long r0 = (long long)blockIdx.x * a.rows / gridDim.x;
-        const long long r1 = (long long)(blockIdx.x + 1) * a.rows / gridDim.x;
+        const int total = a.rows + a.rows2;
+        const int r0 = (int)((long long)blockIdx.x * total / gridDim.x);
+        const int r1 = (int)((long long)(blockIdx.x + 1) * total / gridDim.x);
         constexpr int kSDiv = kGS / 4;  // weight bytes per scale byte
-        const size_t qb = (size_t)(r1 - r0) * a.cols, sb = qb / kSDiv;
-        const char* qp = reinterpret_cast<const char*>(a.q) + (size_t)r0 * a.cols;
-        const char* sp = reinterpret_cast<const char*>(a.s) + (size_t)r0 * (a.cols / kSDiv);
-        for (size_t o = (size_t)threadIdx.x * 128; o < qb && o < kMvPrefetch; o += (size_t)kMvThreads * 128)
-            asm volatile("prefetch.global.L2 [%0];\n" ::"l"(qp + o));
-        for (size_t o = (size_t)threadIdx.x * 128; o < sb && o < kMvPrefetch / kSDiv; o += (size_t)kMvThreads * 128)
-            asm volatile("prefetch.global.L2 [%0];\n" ::"l"(sp + o));
+        // the slice's rows of each matrix are contiguous: [r0, r1) split at a.rows
+        const int ra[2] = {r0, r0 > a.rows ? r0 : a.rows}, rz[2] = {r1 < a.rows ? r1 : a.rows, r1};
+        size_t budget = kMvPrefetch;
+        for (int part = 0; part < 2; ++part) {
+            if (rz[part] <= ra[part]) continue;
+            const size_t qb = (size_t)(rz[part] - ra[part]) * a.cols, sb = qb / kSDiv;
+            const char* qp = reinterpret_cast<const char*>(a.qrow(ra[part]));
+            const char* sp = reinterpret_cast<const char*>(a.srow(ra[part], a.cols / kGS));
+            for (size_t o = (size_t)threadIdx.x * 128; o < qb && o < budget; o += (size_t)kMvThreads * 128)
+                asm volatile("prefetch.global.L2 [%0];\n" ::"l"(qp + o));
+            for (size_t o = (size_t)threadIdx.x * 128; o < sb && o < budget / kSDiv; o += (size_t)kMvThreads * 128)
+                asm volatile("prefetch.global.L2 [%0];\n" ::"l"(sp + o));
+            budget -= qb < budget ? qb : budget;
+        }
     }
     pdl_enter();
     extern __shared__ __align__(16) unsigned char sm[];
@@ -64,8 +86,8 @@ __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a)
     float* xs = part + kMvWarps * 16;                 // [cols] normalised x (with a.norm)
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gid = lane >> 2, t = lane & 3;
-    const int rb = (int)((long long)blockIdx.x * a.rows / gridDim.x);
-    const int re = (int)((long long)(blockIdx.x + 1) * a.rows / gridDim.x);
+    const int rb = (int)((long long)blockIdx.x * (a.rows + a.rows2) / gridDim.x);
+    const int re = (int)((long long)(blockIdx.x + 1) * (a.rows + a.rows2) / gridDim.x);
     const int ntiles = (re - rb + 15) >> 4;
     int ks = kMvWarps / (ntiles > 0 ? ntiles : 1);
     ks = ks < 1 ? 1 : (ks > nch ? nch : ks);
@@ -103,10 +125,10 @@ __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a)
         float acc0 = 0.f, acc1 = 0.f;
         if (tw < tiles_per_pass && tile < ntiles) {
             const int r0 = rb + tile * 16 + gid, r1 = r0 + 8;
-            const int8_t* q0 = r0 < re ? a.q + (size_t)r0 * a.cols : nullptr;
-            const int8_t* q1 = r1 < re ? a.q + (size_t)r1 * a.cols : nullptr;
-            const float* s0 = r0 < re ? a.s + (size_t)r0 * sgrp : nullptr;
-            const float* s1 = r1 < re ? a.s + (size_t)r1 * sgrp : nullptr;
+            const int8_t* q0 = r0 < re ? a.qrow(r0) : nullptr;
+            const int8_t* q1 = r1 < re ? a.qrow(r1) : nullptr;
+            const float* s0 = r0 < re ? a.srow(r0, (int)sgrp) : nullptr;
+            const float* s1 = r1 < re ? a.srow(r1, (int)sgrp) : nullptr;
             const int4 z4 = make_int4(0, 0, 0, 0);
             for (int j = jb; j < je; j += kMvUnroll) {
                 int4 qa[kMvUnroll], qb[kMvUnroll];
@@ -151,8 +173,14 @@ __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a)
         if (ks == 1) {
             if (t == 0 && tw < tiles_per_pass && tile < ntiles) {
                 const int r0 = rb + tile * 16 + gid;
-                if (r0 < re) a.y[r0] = a.accumulate ? a.y[r0] + acc0 : acc0;
-                if (r0 + 8 < re) a.y[r0 + 8] = a.accumulate ? a.y[r0 + 8] + acc1 : acc1;
+                if (r0 < re) {
+                    float* y = a.yrow(r0);
+                    *y = a.accumulate ? *y + acc0 : acc0;
+                }
+                if (r0 + 8 < re) {
+                    float* y = a.yrow(r0 + 8);
+                    *y = a.accumulate ? *y + acc1 : acc1;
+                }
             }
             continue;  // uniform across the CTA: ks is
         }
@@ -167,7 +195,8 @@ __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a)
             if (tile0 + tl < ntiles && r < re) {
                 float sum = 0.f;
                 for (int k = 0; k < ks; ++k) sum += part[(tl * ks + k) * 16 + rr];
-                a.y[r] = a.accumulate ? a.y[r] + sum : sum;
+                float* y = a.yrow(r);
+                *y = a.accumulate ? *y + sum : sum;
             }
         }
         __syncthreads();
@@ -181,20 +210,40 @@ size_t q80_matvec_smem_bytes(int cols, bool norm, int gs) {
            kMvWarps * 16 * 4 + (norm ? (size_t)cols * 4 : 0);
 }
 
-cudaError_t launch_q80_matvec(const int8_t* q, const float* s, const float* x, float* y, int rows, int cols,
-                              int gs, int num_sms, cudaStream_t stream, bool accumulate, const float* norm) {
-    if ((gs != 32 && gs != 16) || cols % 64 || rows <= 0) return cudaErrorInvalidValue;
+namespace {
+
+bool matvec_aligned(const int8_t* q, const float* s, int gs) {
     // weight rows are read 16 bytes at a time, scales 2 floats (gs 32) or 1 (gs 16) at a time
-    if ((reinterpret_cast<uintptr_t>(q) & 15u) || (reinterpret_cast<uintptr_t>(s) & (gs == 16 ? 3u : 7u)))
+    return !(reinterpret_cast<uintptr_t>(q) & 15u) && !(reinterpret_cast<uintptr_t>(s) & (gs == 16 ? 3u : 7u));
+}
+
+cudaError_t launch_matvec(const MatvecArgs& a, int gs, int num_sms, cudaStream_t stream) {
+    if ((gs != 32 && gs != 16) || a.cols % 64 || a.rows <= 0 || a.rows2 < 0) return cudaErrorInvalidValue;
+    if (!matvec_aligned(a.q, a.s, gs) || (a.rows2 > 0 && !matvec_aligned(a.q2, a.s2, gs)))
         return cudaErrorMisalignedAddress;
-    const size_t smem = q80_matvec_smem_bytes(cols, norm != nullptr, gs);
+    const size_t smem = q80_matvec_smem_bytes(a.cols, a.norm != nullptr, gs);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
     auto kernel = gs == 16 ? q80_matvec_kernel<16> : q80_matvec_kernel<32>;
     if (cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kernel), (int)smem)) return e;
     int grid = num_sms;
-    if (grid > (rows + 15) / 16) grid = (rows + 15) / 16;
-    MatvecArgs a{q, s, x, y, rows, cols, accumulate ? 1 : 0, norm};
+    if (grid > (a.rows + a.rows2 + 15) / 16) grid = (a.rows + a.rows2 + 15) / 16;
     return launch_pdl(kernel, grid, kMvThreads, smem, stream, a);
+}
+
+}  // namespace
+
+cudaError_t launch_q80_matvec(const int8_t* q, const float* s, const float* x, float* y, int rows, int cols,
+                              int gs, int num_sms, cudaStream_t stream, bool accumulate, const float* norm) {
+    MatvecArgs a{q, s, x, y, rows, cols, accumulate ? 1 : 0, norm, nullptr, nullptr, nullptr, 0};
+    return launch_matvec(a, gs, num_sms, stream);
+}
+
+cudaError_t launch_q80_matvec2(const int8_t* q, const float* s, float* y, int rows, const int8_t* q2,
+                               const float* s2, float* y2, int rows2, const float* x, int cols, int gs, int num_sms,
+                               cudaStream_t stream, const float* norm) {
+    if (rows2 <= 0) return cudaErrorInvalidValue;
+    MatvecArgs a{q, s, x, y, rows, cols, 0, norm, q2, s2, y2, rows2};
+    return launch_matvec(a, gs, num_sms, stream);
 }
 
 }  // namespace glmq
