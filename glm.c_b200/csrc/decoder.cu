@@ -75,58 +75,91 @@ __global__ void embed_kernel(const int8_t* tok_q, const float* tok_s, const int*
     for (int i = threadIdx.x; i < D; i += blockDim.x) x[i] = (float)q[i] * s[i / gs];
 }
 
-// kR rows of a planar Q8 matrix dotted with x (shared memory) by one warp,
-// all rows' loads issued together: lane l covers the kBytes-wide pieces
-// l, l + 32, ... of every row (cols a multiple of kBytes and of gs).
+// One lane's piece of kR rows of a planar Q8 matrix: kBytes weights of each
+// row from column c0, and each row's scale of that piece (zero past nrows or
+// past cols).
 template <int kBytes, int kR>
-__device__ __forceinline__ void q8_rows_dot(const int8_t* q, const float* s, const float* x, int cols, int gs,
-                                            int r0, int nrows, float (&out)[kR]) {
-    const int lane = threadIdx.x & 31;
+struct Q8Frag {
+    int w[kR][kBytes / 4];
+    float sc[kR];
+};
+
+template <int kBytes, int kR>
+__device__ __forceinline__ void q8_frag_load(const int8_t* q, const float* s, int cols, int gs, int r0, int nrows,
+                                             int c0, Q8Frag<kBytes, kR>& f) {
     const int ng = cols / gs;
 #pragma unroll
-    for (int j = 0; j < kR; ++j) out[j] = 0.f;
-    for (int c0 = lane * kBytes; c0 < cols; c0 += 32 * kBytes) {
-        int w[kR][kBytes / 4];
-        float sc[kR];
-#pragma unroll
-        for (int j = 0; j < kR; ++j) {
-            const int r = r0 + j;
-            if (r < nrows) {
-                const int8_t* p = q + (size_t)r * cols + c0;
-                if constexpr (kBytes == 16) {
-                    const int4 v = *reinterpret_cast<const int4*>(p);
-                    w[j][0] = v.x;
-                    w[j][1] = v.y;
-                    w[j][2] = v.z;
-                    w[j][3] = v.w;
-                } else {
-                    const int2 v = *reinterpret_cast<const int2*>(p);
-                    w[j][0] = v.x;
-                    w[j][1] = v.y;
-                }
-                sc[j] = s[(size_t)r * ng + c0 / gs];
+    for (int j = 0; j < kR; ++j) {
+        const int r = r0 + j;
+        if (r < nrows && c0 < cols) {
+            const int8_t* p = q + (size_t)r * cols + c0;
+            if constexpr (kBytes == 16) {
+                const int4 v = *reinterpret_cast<const int4*>(p);
+                f.w[j][0] = v.x;
+                f.w[j][1] = v.y;
+                f.w[j][2] = v.z;
+                f.w[j][3] = v.w;
             } else {
-#pragma unroll
-                for (int k = 0; k < kBytes / 4; ++k) w[j][k] = 0;
-                sc[j] = 0.f;
+                const int2 v = *reinterpret_cast<const int2*>(p);
+                f.w[j][0] = v.x;
+                f.w[j][1] = v.y;
             }
-        }
+            f.sc[j] = s[(size_t)r * ng + c0 / gs];
+        } else {
 #pragma unroll
-        for (int j = 0; j < kR; ++j) {
-            float d = 0.f;
-#pragma unroll
-            for (int k = 0; k < kBytes; ++k) d += (float)(int8_t)(w[j][k >> 2] >> (8 * (k & 3))) * x[c0 + k];
-            out[j] += sc[j] * d;
+            for (int k = 0; k < kBytes / 4; ++k) f.w[j][k] = 0;
+            f.sc[j] = 0.f;
         }
     }
+}
+
+// out[j] += scale * (piece of row j) . x[c0 : c0 + kBytes] (x in shared memory)
+template <int kBytes, int kR>
+__device__ __forceinline__ void q8_frag_fma(const Q8Frag<kBytes, kR>& f, const float* x, int c0, int cols,
+                                            float (&out)[kR]) {
+    if (c0 >= cols) return;
+#pragma unroll
+    for (int j = 0; j < kR; ++j) {
+        float d = 0.f;
+#pragma unroll
+        for (int k = 0; k < kBytes; ++k) d += (float)(int8_t)(f.w[j][k >> 2] >> (8 * (k & 3))) * x[c0 + k];
+        out[j] += f.sc[j] * d;
+    }
+}
+
+template <int kR>
+__device__ __forceinline__ void warp_sum_rows(float (&out)[kR]) {
 #pragma unroll
     for (int j = 0; j < kR; ++j)
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) out[j] += __shfl_xor_sync(0xffffffffu, out[j], off);
 }
 
-// kR rows of q8_rows_dot as lane kR-1 .. 0 hold them: row r0 + lane's value in
-// lanes [0, kR).
+// kR rows of a planar Q8 matrix dotted with x (shared memory) by one warp,
+// all rows' loads issued together: lane l covers the kBytes-wide pieces
+// l, l + 32, ... of every row (cols a multiple of kBytes and of gs). When
+// `first` holds the lane's first piece (loaded earlier), it is used instead
+// of loading it.
+template <int kBytes, int kR>
+__device__ __forceinline__ void q8_rows_dot(const int8_t* q, const float* s, const float* x, int cols, int gs,
+                                            int r0, int nrows, float (&out)[kR],
+                                            const Q8Frag<kBytes, kR>* first = nullptr) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int j = 0; j < kR; ++j) out[j] = 0.f;
+    for (int c0 = lane * kBytes; c0 < cols; c0 += 32 * kBytes) {
+        Q8Frag<kBytes, kR> f;
+        if (first && c0 == lane * kBytes)
+            f = *first;
+        else
+            q8_frag_load(q, s, cols, gs, r0, nrows, c0, f);
+        q8_frag_fma(f, x, c0, cols, out);
+    }
+    warp_sum_rows(out);
+}
+
+// Row r0 + lane's sum from q8_rows_dot's kR row sums (which every lane
+// holds), for lanes [0, kR).
 template <int kR>
 __device__ __forceinline__ float pick_row(const float (&v)[kR], int lane) {
     float mine = v[0];
@@ -165,18 +198,19 @@ __global__ void __cluster_dims__(kMlaCluster, 1, 1) __launch_bounds__(kMlaThread
     const float* kbs = a.k_b_s + (size_t)h * a.kv_lora * (a.qk_nope / a.gs);
     const int8_t* vbq = a.v_b_q + (size_t)h * a.v_head * a.kv_lora;
     const float* vbs = a.v_b_s + (size_t)h * a.v_head * (a.kv_lora / a.gs);
-    {
-        // Weights no kernel writes: pull this CTA's slices into L2 before
-        // waiting for the previous kernel.
-        auto pf = [&](const void* p, size_t bytes) {
-            for (size_t o = (size_t)tid * 128; o < bytes; o += (size_t)kMlaThreads * 128)
-                asm volatile("prefetch.global.L2 [%0];\n" ::"l"(reinterpret_cast<const char*>(p) + o));
-        };
-        pf(kbq + (size_t)r_lo * a.qk_nope, (size_t)(r_hi - r_lo) * a.qk_nope);
-        pf(kbs + (size_t)r_lo * (a.qk_nope / a.gs), (size_t)(r_hi - r_lo) * (a.qk_nope / a.gs) * 4);
-        pf(vbq + (size_t)o_lo * a.kv_lora, (size_t)(o_hi - o_lo) * a.kv_lora);
-        pf(vbs + (size_t)o_lo * (a.kv_lora / a.gs), (size_t)(o_hi - o_lo) * (a.kv_lora / a.gs) * 4);
-        pf(a.kv_norm, (size_t)a.kv_lora * 4);
+    // Weights no kernel writes, loaded before waiting for the previous
+    // kernel: each warp's first k_b and v_b pieces (for GLM-4.7-Flash's
+    // shapes, all of this CTA's slices) and the kv_a_norm weights.
+    constexpr int kRq = 8, kRo = 4;  // rows per warp step: q_abs, output
+    Q8Frag<8, kRq> kf;
+    Q8Frag<16, kRo> vf;
+    q8_frag_load(kbq, kbs, a.qk_nope, a.gs, r_lo + warp * kRq, r_hi, lane * 8, kf);
+    q8_frag_load(vbq, vbs, a.kv_lora, a.gs, o_lo + warp * kRo, o_hi, lane * 16, vf);
+    float kn[kMlaStage];
+#pragma unroll
+    for (int u = 0; u < kMlaStage; ++u) {
+        const int i = tid + u * kMlaThreads;
+        kn[u] = i < a.kv_lora ? __ldg(a.kv_norm + i) : 0.f;
     }
     float* q_nope = smf;                      // [qk_nope]
     float* q_pe = q_nope + a.qk_nope;         // [rope]
@@ -216,8 +250,12 @@ __global__ void __cluster_dims__(kMlaCluster, 1, 1) __launch_bounds__(kMlaThread
         rope_pair(q_pe[i], q_pe[i + 1], i, a.rope, pos);
         rope_pair(key[a.kv_lora + i], key[a.kv_lora + i + 1], i, a.rope, pos);
     }
-    const float inv = rms_inv(key, a.kv_lora, red_d);  // starts and ends with block barriers
-    for (int i = tid; i < a.kv_lora; i += kMlaThreads) key[i] = key[i] * inv * a.kv_norm[i];
+    const float inv = rms_inv(key, a.kv_lora, red_d);  // every read of key precedes its barriers
+#pragma unroll
+    for (int u = 0; u < kMlaStage; ++u) {
+        const int i = tid + u * kMlaThreads;
+        if (i < a.kv_lora) key[i] = key[i] * inv * kn[u];
+    }
     __syncthreads();
     if (h == 0 && rank == 0) {
         for (int i = tid; i < a.kv_lora; i += kMlaThreads) a.cache_comp[(size_t)pos * a.kv_lora + i] = key[i];
@@ -226,10 +264,10 @@ __global__ void __cluster_dims__(kMlaCluster, 1, 1) __launch_bounds__(kMlaThread
 
     // 1. q_abs[r] = k_b_h[r] . q_nope (k_b: [heads][kv_lora][qk_nope]), rows [r_lo, r_hi)
     {
-        constexpr int kR = 8;
+        constexpr int kR = kRq;
         for (int r0 = r_lo + warp * kR; r0 < r_hi; r0 += nw * kR) {
             float v[kR];
-            q8_rows_dot<8, kR>(kbq, kbs, q_nope, a.qk_nope, a.gs, r0, r_hi, v);
+            q8_rows_dot<8, kR>(kbq, kbs, q_nope, a.qk_nope, a.gs, r0, r_hi, v, r0 == r_lo + warp * kR ? &kf : nullptr);
             const float mine = pick_row(v, lane);
             if (lane < kR && r0 + lane < r_hi)
 #pragma unroll
@@ -347,11 +385,11 @@ __global__ void __cluster_dims__(kMlaCluster, 1, 1) __launch_bounds__(kMlaThread
 
     // 4. att_concat[h][r] = v_b_h[r] . ctx (v_b: [heads][v_head][kv_lora]), rows [o_lo, o_hi)
     {
-        constexpr int kR = 4;
+        constexpr int kR = kRo;
         float* out = a.att_concat + (size_t)h * a.v_head;
         for (int r0 = o_lo + warp * kR; r0 < o_hi; r0 += nw * kR) {
             float v[kR];
-            q8_rows_dot<16, kR>(vbq, vbs, ctx, a.kv_lora, a.gs, r0, o_hi, v);
+            q8_rows_dot<16, kR>(vbq, vbs, ctx, a.kv_lora, a.gs, r0, o_hi, v, r0 == o_lo + warp * kR ? &vf : nullptr);
             const float mine = pick_row(v, lane);
             if (lane < kR && r0 + lane < o_hi) out[r0 + lane] = mine;
         }

@@ -77,57 +77,6 @@ __device__ __forceinline__ int b_frag_offset(int lane) {
     return plane * 64 + 16 * t;
 }
 
-// Quantize `n` fp32 values (n % 64 == 0) into digit planes + scale table in
-// shared memory. planes: [n/64][3][64] int8, sxg: [n/32] scratch,
-// sxtab: [n/64][4][2]. Must be called by all threads of the block; ends with
-// __syncthreads(). A group with a non-finite element gets a NaN scale so the
-// rows it feeds come out non-finite, as the fp32 reference's would.
-__device__ __forceinline__ void quantize_to_planes(const float* __restrict__ src, int n, int8_t* planes,
-                                                   float* sxg, float* sxtab) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-    const int groups = n >> 5;
-    for (int g = warp; g < groups; g += nwarps) {
-        const float v = src[g * 32 + lane];
-        float a = fabsf(v);
-        const bool bad = __any_sync(0xffffffffu, !isfinite(v));
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, off));
-        int X = 0;
-        float sx = 0.0f;
-        if (bad) {
-            sx = __int_as_float(0x7fc00000);
-        } else if (a > 0.0f) {
-            int e = ilogbf(a) - 22;  // a * 2^-e in [2^22, 2^23)
-            if (ldexpf(a, -e) > kDigitMax) e += 1;
-            sx = ldexpf(1.0f, e);
-            X = __float2int_rn(ldexpf(v, -e));
-        }
-        const int lo = ((X + 128) & 255) - 128;
-        const int x1 = (X - lo) >> 8;
-        const int mid = ((x1 + 128) & 255) - 128;
-        const int hi = (x1 - mid) >> 8;
-        int8_t* c = planes + (g >> 1) * kChunkBytes + (g & 1) * 32 + lane;
-        c[0] = (int8_t)hi;
-        c[64] = (int8_t)mid;
-        c[128] = (int8_t)lo;
-        if (lane == 0) sxg[g] = sx;
-    }
-    __syncthreads();
-    const int chunks = n >> 6;
-    for (int i = threadIdx.x; i < chunks * 4; i += blockDim.x) {
-        const int c = i >> 2, t = i & 3;
-        const float s0 = sxg[2 * c], s1 = sxg[2 * c + 1];
-        float A, B;
-        if (t == 0) { A = 65536.0f * s0; B = 256.0f * s0; }
-        else if (t == 1) { A = 65536.0f * s1; B = 256.0f * s1; }
-        else if (t == 2) { A = s0; B = s1; }
-        else { A = 0.0f; B = 0.0f; }
-        sxtab[c * kChunkTab + 2 * t] = A;
-        sxtab[c * kChunkTab + 2 * t + 1] = B;
-    }
-    __syncthreads();
-}
-
 // Accumulate one 16-row x 64-column chunk of a Q8 matrix into the lane's
 // partial sums for rows gid (acc0) and gid+8 (acc1).
 //   q0/q1: this lane's 16 weight bytes of row gid / gid+8
@@ -238,8 +187,13 @@ __device__ __forceinline__ float4 ldcg_f4(const float* p) {
 
 // ------------------------------------------------ vectorised quantisation
 //
-// The same group quantisation as quantize_to_planes, laid out for
-// throughput: 8 lanes per 32-element group, 4 consecutive elements per lane,
+// Group quantisation of the activations: each 32-element group with
+// maximum |x| = a gets the scale 2^e, e = ilogb(a) - 22, so that every
+// X = rn(x * 2^-e) fits 24 bits and splits exactly into three balanced
+// signed bytes hi, mid, lo (X = 65536 hi + 256 mid + lo); a group with a
+// non-finite element gets a NaN scale and zero digits, an all-zero group
+// scale 0. Laid out for throughput: 8 lanes per group, 4 consecutive
+// elements per lane,
 // so a warp step covers 4 groups with one 16-byte load and three 4-byte digit
 // stores per lane. Step s covers groups 4s .. 4s+3; warp w of nwarps takes
 // steps w, w + nwarps, ... q4_load fetches kB such steps (global memory
@@ -352,7 +306,31 @@ __device__ __forceinline__ void quantize_planes_part(const float* src, int n, in
     }
 }
 
+// Quantize n fp32 values (n % 64 == 0; src 16-byte aligned, global or
+// shared memory) into digit planes + scale table in shared memory with every
+// thread of the block: planes [n/64][3][64] int8, sxg [n/32], sxtab
+// [n/64][4][2]. All of a warp's loads are in flight at once. Ends with
+// __syncthreads(). A group with a non-finite element gets a NaN scale so the
+// rows it feeds come out non-finite, as the fp32 reference's would.
+__device__ __forceinline__ void quantize_to_planes(const float* src, int n, int8_t* planes, float* sxg,
+                                                   float* sxtab) {
+    quantize_planes_part<false>(src, n, planes, sxg, sxtab, (int)threadIdx.x, (int)blockDim.x,
+                                [] { __syncthreads(); });
+}
+
 // ------------------------------------------------------- TMA and mbarriers
+
+// L2 prefetch hint for the 16-byte-aligned part of [p, p + bytes) (the
+// unaligned ends are left out), one bulk request per MiB.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, size_t bytes) {
+    uintptr_t a = (reinterpret_cast<uintptr_t>(p) + 15) & ~(uintptr_t)15;
+    const uintptr_t e = (reinterpret_cast<uintptr_t>(p) + bytes) & ~(uintptr_t)15;
+    while (a < e) {
+        const uint32_t n = (uint32_t)(e - a < ((uintptr_t)1 << 20) ? e - a : ((uintptr_t)1 << 20));
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(a), "r"(n) : "memory");
+        a += n;
+    }
+}
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

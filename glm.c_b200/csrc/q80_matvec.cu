@@ -18,7 +18,8 @@ namespace glmq {
 constexpr int kMvWarps = 16;
 constexpr int kMvThreads = kMvWarps * 32;
 constexpr int kMvUnroll = 4;
-constexpr size_t kMvPrefetch = 32768;  // weight bytes per CTA pulled into L2 before the launch wait
+constexpr size_t kMvPrefetch = 262144;  // weight bytes per CTA pulled into L2 before the launch wait
+constexpr int kMvStage = 8;            // x / norm floats per thread loaded at once (all in flight)
 
 struct MatvecArgs {
     const int8_t* q;
@@ -55,8 +56,9 @@ __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a)
         // Before waiting for the previous kernel (which writes x, never the
         // weights' values this kernel reads afterwards): pull the first
         // kMvPrefetch bytes of this CTA's weight rows and their scales into
-        // L2, so the stream starts while the previous kernel drains. A hint
-        // only: the loads below come after the wait.
+        // L2 (one bulk request per contiguous range), so the stream runs
+        // while the previous kernel works. A hint only: the loads below come
+        // after the wait.
         const int total = a.rows + a.rows2;
         const int r0 = (int)((long long)blockIdx.x * total / gridDim.x);
         const int r1 = (int)((long long)(blockIdx.x + 1) * total / gridDim.x);
@@ -64,16 +66,22 @@ __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a)
         // the slice's rows of each matrix are contiguous: [r0, r1) split at a.rows
         const int ra[2] = {r0, r0 > a.rows ? r0 : a.rows}, rz[2] = {r1 < a.rows ? r1 : a.rows, r1};
         size_t budget = kMvPrefetch;
-        for (int part = 0; part < 2; ++part) {
-            if (rz[part] <= ra[part]) continue;
-            const size_t qb = (size_t)(rz[part] - ra[part]) * a.cols, sb = qb / kSDiv;
-            const char* qp = reinterpret_cast<const char*>(a.qrow(ra[part]));
-            const char* sp = reinterpret_cast<const char*>(a.srow(ra[part], a.cols / kGS));
-            for (size_t o = (size_t)threadIdx.x * 128; o < qb && o < budget; o += (size_t)kMvThreads * 128)
-                asm volatile("prefetch.global.L2 [%0];\n" ::"l"(qp + o));
-            for (size_t o = (size_t)threadIdx.x * 128; o < sb && o < budget / kSDiv; o += (size_t)kMvThreads * 128)
-                asm volatile("prefetch.global.L2 [%0];\n" ::"l"(sp + o));
-            budget -= qb < budget ? qb : budget;
+        for (int part = 0; part < 2 && threadIdx.x == 0; ++part) {
+            if (rz[part] <= ra[part] || budget == 0) continue;
+            size_t qb = (size_t)(rz[part] - ra[part]) * a.cols;
+            qb = qb < budget ? qb : budget;
+            bulk_prefetch_l2(a.qrow(ra[part]), qb);
+            bulk_prefetch_l2(a.srow(ra[part], a.cols / kGS), qb / kSDiv);
+            budget -= qb;
+        }
+    }
+    // the first kMvStage * kMvThreads norm weights (no kernel writes them)
+    float nv[kMvStage];
+    if (a.norm) {
+#pragma unroll
+        for (int u = 0; u < kMvStage; ++u) {
+            const int i = threadIdx.x + u * kMvThreads;
+            nv[u] = i < a.cols ? __ldg(a.norm + i) : 0.f;
         }
     }
     pdl_enter();
@@ -98,7 +106,22 @@ __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a)
         // xn = x * (1/sqrtf(mean(x^2) + 1e-5)) * w (sum of squares in fp64).
         __shared__ double red[kMvWarps];
         double ss = 0.0;
-        for (int i = threadIdx.x; i < a.cols; i += kMvThreads) ss += (double)a.x[i] * (double)a.x[i];
+        for (int base = threadIdx.x; base < a.cols; base += kMvThreads * kMvStage) {
+            float v[kMvStage];
+#pragma unroll
+            for (int u = 0; u < kMvStage; ++u) {
+                const int i = base + u * kMvThreads;
+                v[u] = i < a.cols ? a.x[i] : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < kMvStage; ++u) {
+                const int i = base + u * kMvThreads;
+                if (i < a.cols) {
+                    ss += (double)v[u] * (double)v[u];
+                    xs[i] = v[u];
+                }
+            }
+        }
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
         if (lane == 0) red[warp] = ss;
@@ -107,7 +130,19 @@ __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a)
         for (int w = 0; w < kMvWarps; ++w) tot += red[w];
         const float mean = (float)(tot / (double)a.cols);
         const float inv = 1.0f / sqrtf(mean + 1e-5f);
-        for (int i = threadIdx.x; i < a.cols; i += kMvThreads) xs[i] = a.x[i] * inv * a.norm[i];
+        for (int base = threadIdx.x, c = 0; base < a.cols; base += kMvThreads * kMvStage, ++c) {
+            float w[kMvStage];
+#pragma unroll
+            for (int u = 0; u < kMvStage; ++u) {
+                const int i = base + u * kMvThreads;
+                w[u] = c == 0 ? nv[u] : (i < a.cols ? a.norm[i] : 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < kMvStage; ++u) {
+                const int i = base + u * kMvThreads;
+                if (i < a.cols) xs[i] = xs[i] * inv * w[u];  // each thread rescales the xs it stored
+            }
+        }
         __syncthreads();
         quantize_to_planes(xs, a.cols, planes, sxg, sxtab);
     } else {

@@ -237,21 +237,6 @@ __device__ __forceinline__ void warp_logit_bound_contig(const float* __restrict_
     B = 1.01 * 0x1p-24 * sabs + 0x1p-40 * sum_abs_p;
 }
 
-// Rank of expert i by (sel desc, id asc) among the experts with sel > -inf
-// (NaN and -inf never rank, infer.c:1118-1124): the number of such experts
-// that beat it; E for an expert that does not rank.
-__device__ __forceinline__ int rank_of(const float* sel, int E, int i) {
-    const float v = sel[i];
-    if (!(v > -INFINITY)) return E;
-    int r = 0;
-#pragma unroll 8
-    for (int j = 0; j < E; ++j) {
-        const float u = sel[j];
-        r += (u > v || (u == v && j < i)) ? 1 : 0;
-    }
-    return r;
-}
-
 // Shared-memory scratch of block_select.
 struct SelectScratch {
     float* sel_c;
@@ -266,28 +251,56 @@ struct SelectScratch {
 // Ranks every expert into S.taken and the first R into S.rank (preset to -1
 // and *S.cert to 1 by the caller), then clears *S.cert unless the top K are
 // present and provably ordered: each winner's [lo, hi] sel interval lies
-// strictly above the interval of every expert ranked after it. Two sync()s.
+// strictly above the interval of every expert ranked after it. Two sync()s;
+// nthreads a multiple of 32.
 template <typename Sync>
 __device__ __forceinline__ void rank_and_certify(const SelectScratch& S, int E, int K, int R, int tid, int nthreads,
                                                  Sync sync) {
-    for (int i = tid; i < E; i += nthreads) {
-        const int r = rank_of(S.sel_c, E, i);
-        S.taken[i] = r;
-        if (r < R) S.rank[r] = i;
-    }
-    sync();
-    bool ok = tid != 0 || S.rank[K - 1] >= 0;
-    for (int i = tid; i < E; i += nthreads) {
-        const int r = S.taken[i];
-        if (r < K) {
-            float hm = -INFINITY;
-#pragma unroll 8
-            for (int j = 0; j < E; ++j)
-                if (S.taken[j] > r) hm = fmaxf(hm, S.sel_hi[j]);
-            ok = ok && S.sel_lo[i] > hm;
+    // rank_of with P threads per expert (a power of two <= 8 that fits the
+    // block): thread sub of expert i counts the experts j = sub, sub + P, ...
+    // that beat it, the P counts are added by shuffles within aligned lanes
+    int P = 1;
+    while (P < 8 && 2 * P * E <= nthreads) P <<= 1;
+    for (int t = tid; t - (tid & 31) < P * E; t += nthreads) {  // warp-uniform: the warp's first t
+        const int i = t / P, sub = t % P;
+        int r = 0;
+        bool ranks = false;
+        if (i < E) {
+            const float v = S.sel_c[i];
+            ranks = v > -INFINITY;  // NaN and -inf never rank (infer.c:1118-1124)
+            if (ranks)
+                for (int j = sub; j < E; j += P) {
+                    const float u = S.sel_c[j];
+                    r += (u > v || (u == v && j < i)) ? 1 : 0;
+                }
+        }
+        for (int off = 1; off < P; off <<= 1) r += __shfl_xor_sync(0xffffffffu, r, off);
+        if (i < E && sub == 0) {
+            if (!ranks) r = E;
+            S.taken[i] = r;
+            if (r < R) S.rank[r] = i;
         }
     }
-    if (!ok) *S.cert = 0;
+    sync();
+    if (tid < 32) {
+        // the largest upper end among the experts ranked K or later (NaN and
+        // -inf ends take no part in fmaxf), then the winners from the last
+        // up, each against that and the upper ends of the winners after it
+        float hm = -INFINITY;
+        for (int i = tid; i < E; i += 32)
+            if (S.taken[i] >= K) hm = fmaxf(hm, S.sel_hi[i]);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) hm = fmaxf(hm, __shfl_xor_sync(0xffffffffu, hm, off));
+        if (tid == 0) {
+            bool ok = S.rank[K - 1] >= 0;
+            for (int k = K - 1; k >= 0 && ok; --k) {
+                const int w = S.rank[k];
+                ok = S.sel_lo[w] > hm;
+                hm = fmaxf(hm, S.sel_hi[w]);
+            }
+            if (!ok) *S.cert = 0;
+        }
+    }
     sync();
 }
 
@@ -303,16 +316,20 @@ __device__ void block_select(const double* center, const double* bound, const fl
                              const float* router, const float* xs, int D, int tid, int nthreads,
                              const SelectScratch& S, int* idx, float* w, unsigned long long* stats, Sync sync,
                              float* rowbuf = nullptr, int nbuf = 0) {
-    for (int i = tid; i < E; i += nthreads) {
+    // the centre, lower and upper sel of every expert, each on its own thread
+    for (int t = tid; t < 3 * E; t += nthreads) {
+        const int i = t % E, which = t / E;
         const double C = center[i], B = bound[i];
         const float b = bias[i];
-        const float lc = __double2float_rn(C);
-        const float llo = __double2float_rd(C - B), lhi = __double2float_ru(C + B);
-        const float pc = sigmoid_of_exp(expf(-lc));
-        S.p_c[i] = pc;
-        S.sel_c[i] = __fadd_rn(pc, b);
-        S.sel_lo[i] = __fadd_rn(sigmoid_of_exp(ulp_up(expf(-llo), 3)), b);
-        S.sel_hi[i] = __fadd_rn(sigmoid_of_exp(ulp_down(expf(-lhi), 3)), b);
+        if (which == 0) {
+            const float pc = sigmoid_of_exp(expf(-__double2float_rn(C)));
+            S.p_c[i] = pc;
+            S.sel_c[i] = __fadd_rn(pc, b);
+        } else if (which == 1) {
+            S.sel_lo[i] = __fadd_rn(sigmoid_of_exp(ulp_up(expf(-__double2float_rd(C - B)), 3)), b);
+        } else {
+            S.sel_hi[i] = __fadd_rn(sigmoid_of_exp(ulp_down(expf(-__double2float_ru(C + B)), 3)), b);
+        }
     }
     const int R = (K + 1 < E) ? K + 1 : E;
     if (tid < R) S.rank[tid] = -1;
