@@ -751,6 +751,29 @@ def run_ep_leg(args, torch, pkg, lib, layers, dev, local, rank, world) -> dict:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_a2a, ms_p2p, comm_a, tot_a = (float(v) for v in t.tolist()[:4])
         same = t.tolist()[4] == 0.0
+    # every rank's rows and phase times (one all_gather, on every rank)
+    rows = counts or a2a.last or {}
+    mine = [float(rows.get("n_recv", 0)), float(rows.get("n_send", 0))] + [float(v) for v in ph_p] + \
+           [float(v) for v in ph_a]
+    if world > 1:
+        v = torch.tensor(mine, device=dev, dtype=torch.float64)
+        got = [torch.zeros_like(v) for _ in range(world)]
+        dist.all_gather(got, v)
+        table = [g.tolist() for g in got]
+    else:
+        table = [mine]
+    recv = [r[0] for r in table]
+    mean_recv = sum(recv) / len(recv)
+    per_rank = {"recv_rows_last_layer": [int(r[0]) for r in table],
+                "send_rows_last_layer": [int(r[1]) for r in table],
+                "recv_imbalance_max_over_mean": round(max(recv) / mean_recv, 4) if mean_recv > 0 else None,
+                "p2p_phase_ms": [[round(v, 3) for v in r[2:5]] for r in table],
+                "nccl_phase_ms": [[round(v, 3) for v in r[5:10]] for r in table]}
+    # the peer-memory step against the compute phases of the same kernels on
+    # the same rows (the NCCL form's dispatch, experts and combine, which run
+    # after its exchange has finished), on the slowest rank
+    compute_ms = max(r[5] + r[7] + r[9] for r in table)
+    p2p_total = max(r[2] + r[3] + r[4] for r in table)
     use_p2p = ok and args.ep_exchange == "p2p"
     ms = ms_p2p if use_p2p else ms_a2a
     out = {"metric": f"EP prefill tok/s (config 4: {args.ep_tokens} tokens x {n_layers} config-0 MoE layers, "
@@ -766,7 +789,12 @@ def run_ep_leg(args, torch, pkg, lib, layers, dev, local, rank, world) -> dict:
                           "no collective, no host round trip",
                    "phase_ms_rank0": {"route_pack_push": round(float(ph_p[0]), 3),
                                       "wait_rows_experts_push_back": round(float(ph_p[1]), 3),
-                                      "wait_outputs_combine": round(float(ph_p[2]), 3)}},
+                                      "wait_outputs_combine": round(float(ph_p[2]), 3)},
+                   "exposed_fraction": round(max(0.0, 1.0 - compute_ms / p2p_total), 4) if p2p_total > 0 else None,
+                   "exposed_how": "1 - (slowest rank's dispatch + experts + combine time of the NCCL form, i.e. "
+                                  "the same kernels on the same rows with the exchange excluded) / (slowest "
+                                  "rank's peer-memory step): exchange time not hidden behind compute, plus "
+                                  "waits for slower ranks"},
            "nccl": {"value": round(args.ep_tokens / (ms_a2a / 1e3), 1), "ms_per_step": round(ms_a2a, 3),
                     "how": "torch.distributed all_to_all_single (NCCL) of per-rank row counts (host copy of the "
                            "splits), rows and expert ids; rows back the same way",
@@ -776,7 +804,8 @@ def run_ep_leg(args, torch, pkg, lib, layers, dev, local, rank, world) -> dict:
                                        "exchange_back": round(float(ph_a[3]), 3),
                                        "combine": round(float(ph_a[4]), 3)}},
            "p2p_equals_nccl_bitwise": same if ok else None,
-           "last_layer_rows": counts or a2a.last}
+           "last_layer_rows": counts or a2a.last,
+           "per_rank": per_rank}
     if world > 1:
         dist.barrier()  # no rank frees its peer region while another may still store into it
     lib.free()
