@@ -495,23 +495,24 @@ def run_matvec_leg(torch, lib, dev, world: int) -> dict:
             "api": "glm_cuda_matvec_q80_async (back-to-back launches over rotating weight copies)"}
 
 
-def run_gs16_leg(args, torch, pkg, lib, layers, dev, local, world) -> dict:
-    """The headline workload at gs = 16 (glm.c's own export): the same 46
-    layers' int8 weights with 16-column scale groups (fresh |N(0,0.02)|/127
-    scales), one token per step through the 46 per-layer persistent launches
-    of a CUDA graph, as the headline value; plus the 46 layers in one launch."""
+def run_moe_leg(args, torch, pkg, lib, layers, dev, local, world, gs=16) -> dict:
+    """One token per step through the given config-0 layers' per-layer
+    persistent launches in a CUDA graph (the headline measurement), plus the
+    layers in one launch. gs = 16 (glm.c's own export): the same int8
+    weights with 16-column scale groups (fresh |N(0,0.02)|/127 scales)."""
     import numpy as np
 
     n = len(layers)
-    lib.init(local, D, F, E, K, 16, n)
+    lib.init(local, D, F, E, K, gs, n)
     g = torch.Generator(device=dev)
     g.manual_seed(args.seed * 16 + 1)
     layers16 = []
     for li, L in enumerate(layers):
         L16 = dict(L)
-        for k in [k for k in L if k.endswith("_s")]:
-            shp = tuple(L[k].shape[:-1]) + (L[k[:-2] + "_q"].shape[-1] // 16,)
-            L16[k] = torch.randn(shp, generator=g, device=dev).abs_().mul_(0.02 / 127.0)
+        if gs != GS:
+            for k in [k for k in L if k.endswith("_s")]:
+                shp = tuple(L[k].shape[:-1]) + (L[k[:-2] + "_q"].shape[-1] // gs,)
+                L16[k] = torch.randn(shp, generator=g, device=dev).abs_().mul_(0.02 / 127.0)
         layers16.append(L16)
         lib.bind_moe_layer_device(li, L16)
     path = lib.decode_path()
@@ -557,10 +558,10 @@ def run_gs16_leg(args, torch, pkg, lib, layers, dev, local, world) -> dict:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    lb16 = pkg.synth.moe_bytes(D, F, E, K, 16)
+    lb16 = pkg.synth.moe_bytes(D, F, E, K, gs)
     peak = measured_peaks()["hbm_gbs"]
     gbps = world * n * lb16 / (ms / 1e3) / 1e9
-    out = {"metric": "MoE-layer HBM GB/s at gs = 16 (bs1 decode, 46 config-0 MoE layers per token)",
+    out = {"metric": f"MoE-layer HBM GB/s at gs = {gs} (bs1 decode, {n} config-0 MoE layers per token)",
            "value": round(gbps, 2), "unit": UNIT, "layer_us": round(ms / n * 1e3, 3),
            "frac_of_hbm_peak": round(gbps / world / peak, 4), "bytes_per_layer": lb16,
            "stacked_layer_us": round(float(np.mean(s_ms)) / n * 1e3, 3),
@@ -569,6 +570,71 @@ def run_gs16_leg(args, torch, pkg, lib, layers, dev, local, world) -> dict:
     lib.free()
     del layers16
     return out
+
+
+def run_decode_leg(args, torch, pkg, lib, layers, dev, local, rank, world) -> dict:
+    """The config-2 decoder (GLM-4.7-Flash: layer 0 dense, one MoE layer per
+    given config-0 layer) greedy through glm_cuda_generate, with
+    device-generated attention, embedding and LM-head weights; tok/s from
+    the device time of the step-graph replays."""
+    import numpy as np
+    import torch.distributed as dist
+
+    synth = pkg.synth
+    dims = dict(synth.CONFIG2, n_layers=len(layers) + 1, cache_cap=args.decode_prompt + args.decode_gen + 8)
+    glob, attn = make_device_decoder(torch, dims, args.seed + rank, dev)
+    lib.model_init(local, dims)
+    lib.set_decode_path({"auto": 0, "persistent": 1, "chain": 2}[args.path])
+    lib.upload_model_globals(glob, device=True)
+    for l, a in enumerate(attn):
+        lib.upload_attn_layer(l, a, device=True)
+    for l in range(1, dims["n_layers"]):
+        lib.bind_moe_layer_device(l, layers[l - 1])
+    torch.cuda.synchronize()
+    prompt = synth.prompt_ids(args.seed, args.decode_prompt, dims["vocab_size"])
+    lib.generate(prompt, args.decode_gen)  # warm-up
+    runs, walls = [], []
+    for _ in range(args.decode_reps):
+        t0 = time.perf_counter()
+        ids, ms_dec = lib.generate(prompt, args.decode_gen)
+        walls.append(time.perf_counter() - t0)
+        runs.append(ms_dec)
+    steps = args.decode_prompt + args.decode_gen - 1
+    ms_tok = statistics.median(runs) / steps
+    step_bytes = sum(decoder_bytes(dims, p) for p in range(steps)) / steps
+    if world > 1:
+        t = torch.tensor([ms_tok], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_tok = float(t.item())
+    decode = {"metric": f"decode tok/s @bs1 (greedy, GLM-4.7-Flash config 2: {dims['n_layers']} layers, "
+                        f"vocab {dims['vocab_size']})",
+              "value": round(world * 1000.0 / ms_tok, 2), "unit": "tok/s", "ms_per_token": round(ms_tok, 4),
+              "prompt": args.decode_prompt, "generated": args.decode_gen, "reps": len(runs),
+              "bytes_per_token": int(step_bytes),
+              "achieved_gbs": round(step_bytes / (ms_tok / 1e3) / 1e9, 1),
+              "frac_of_hbm_peak": round(step_bytes / (ms_tok / 1e3) / 1e9 / measured_peaks()["hbm_gbs"], 4),
+              "e2e_tok_s": round(world * steps / statistics.median(walls), 2),
+              "timing": "device time of glm_cuda_generate's step-graph replays (CUDA events); e2e: host "
+                        "wall clock of the call (prompt H2D, graph build, ids D2H)",
+              "first_ids": ids[:8].tolist(), "api": "glm_cuda_generate"}
+    # How robust the greedy sequence is: the logits of every generated
+    # step (the same sequence replayed through glm_cuda_forward_token),
+    # their smallest top-1 minus top-2 margin, and whether each argmax is
+    # the id glm_cuda_generate produced.
+    feed = list(prompt) + ids.tolist()
+    gaps, agree = [], True
+    for pos in range(len(feed) - 1):
+        logits = lib.forward_token(int(feed[pos]), pos, dims["vocab_size"])
+        if pos >= len(prompt) - 1:
+            top2 = np.partition(logits, -2)[-2:]
+            gaps.append(float(top2[1] - top2[0]))
+            agree = agree and int(np.argmax(logits)) == int(feed[pos + 1])
+    g = int(np.argmin(gaps))
+    decode["greedy_margin"] = {"min_top1_minus_top2": round(gaps[g], 6), "at_step": g,
+                               "median": round(float(np.median(gaps)), 5), "argmax_agrees": agree}
+    del glob, attn
+
+    return decode
 
 
 def run_prefill_leg(args, torch, pkg, lib, layers, dev, local, rank, world) -> dict:
@@ -813,8 +879,9 @@ def run_ep_leg(args, torch, pkg, lib, layers, dev, local, rank, world) -> dict:
 
 
 def run_only(args) -> None:
-    """One leg alone (--only prefill | ep), e.g. for a profiler capture: the
-    same measurement as in the full run, on freshly generated layers."""
+    """One leg alone (--only prefill | ep | moe | model), e.g. for a profiler
+    capture: the same measurement as in the full run, on freshly generated
+    layers (moe and model: --layers of them, 46 for the full model)."""
     import torch
     import torch.distributed as dist
 
@@ -829,13 +896,17 @@ def run_only(args) -> None:
 
     pkg = load_package()
     lib = pkg.glm_cuda.GlmCuda()
-    n = 1 if args.only == "prefill" else args.ep_layers
+    n = {"prefill": 1, "ep": args.ep_layers}.get(args.only, args.layers)
     layers = make_device_layers(torch, n, args.seed + rank, dev)
     torch.cuda.synchronize()
     if args.only == "prefill":
         out = run_prefill_leg(args, torch, pkg, lib, layers, dev, local, rank, world)
-    else:
+    elif args.only == "ep":
         out = run_ep_leg(args, torch, pkg, lib, layers, dev, local, rank, world)
+    elif args.only == "moe":
+        out = run_moe_leg(args, torch, pkg, lib, layers, dev, local, world, gs=args.gs)
+    else:
+        out = run_decode_leg(args, torch, pkg, lib, layers, dev, local, rank, world)
     if rank == 0:
         print(json.dumps(out))
     if world > 1:
@@ -1005,64 +1076,13 @@ def run_ours(args) -> None:
     # layers plus device-generated attention / embedding / LM head weights.
     decode = None
     if N_MOE_LAYERS == 46 and not args.no_decode:
-        synth = pkg.synth
-        dims = dict(synth.CONFIG2, cache_cap=args.decode_prompt + args.decode_gen + 8)
-        glob, attn = make_device_decoder(torch, dims, args.seed + rank, dev)
-        lib.model_init(local, dims)
-        lib.set_decode_path({"auto": 0, "persistent": 1, "chain": 2}[args.path])
-        lib.upload_model_globals(glob, device=True)
-        for l, a in enumerate(attn):
-            lib.upload_attn_layer(l, a, device=True)
-        for l in range(1, dims["n_layers"]):
-            lib.bind_moe_layer_device(l, layers[l - 1])
-        torch.cuda.synchronize()
-        prompt = synth.prompt_ids(args.seed, args.decode_prompt, dims["vocab_size"])
-        lib.generate(prompt, args.decode_gen)  # warm-up
-        runs, walls = [], []
-        for _ in range(args.decode_reps):
-            t0 = time.perf_counter()
-            ids, ms_dec = lib.generate(prompt, args.decode_gen)
-            walls.append(time.perf_counter() - t0)
-            runs.append(ms_dec)
-        steps = args.decode_prompt + args.decode_gen - 1
-        ms_tok = statistics.median(runs) / steps
-        step_bytes = sum(decoder_bytes(dims, p) for p in range(steps)) / steps
-        if world > 1:
-            t = torch.tensor([ms_tok], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms_tok = float(t.item())
-        decode = {"metric": "decode tok/s @bs1 (greedy, GLM-4.7-Flash config 2: 47 layers, vocab 154880)",
-                  "value": round(world * 1000.0 / ms_tok, 2), "unit": "tok/s", "ms_per_token": round(ms_tok, 4),
-                  "prompt": args.decode_prompt, "generated": args.decode_gen, "reps": len(runs),
-                  "bytes_per_token": int(step_bytes),
-                  "achieved_gbs": round(step_bytes / (ms_tok / 1e3) / 1e9, 1),
-                  "frac_of_hbm_peak": round(step_bytes / (ms_tok / 1e3) / 1e9 / measured_peaks()["hbm_gbs"], 4),
-                  "e2e_tok_s": round(world * steps / statistics.median(walls), 2),
-                  "timing": "device time of glm_cuda_generate's step-graph replays (CUDA events); e2e: host "
-                            "wall clock of the call (prompt H2D, graph build, ids D2H)",
-                  "first_ids": ids[:8].tolist(), "api": "glm_cuda_generate"}
-        # How robust the greedy sequence is: the logits of every generated
-        # step (the same sequence replayed through glm_cuda_forward_token),
-        # their smallest top-1 minus top-2 margin, and whether each argmax is
-        # the id glm_cuda_generate produced.
-        feed = list(prompt) + ids.tolist()
-        gaps, agree = [], True
-        for pos in range(len(feed) - 1):
-            logits = lib.forward_token(int(feed[pos]), pos, dims["vocab_size"])
-            if pos >= len(prompt) - 1:
-                top2 = np.partition(logits, -2)[-2:]
-                gaps.append(float(top2[1] - top2[0]))
-                agree = agree and int(np.argmax(logits)) == int(feed[pos + 1])
-        g = int(np.argmin(gaps))
-        decode["greedy_margin"] = {"min_top1_minus_top2": round(gaps[g], 6), "at_step": g,
-                                   "median": round(float(np.median(gaps)), 5), "argmax_agrees": agree}
-        del glob, attn
+        decode = run_decode_leg(args, torch, pkg, lib, layers, dev, local, rank, world)
 
     route_stats = lib.route_stats()
     matvec = None if args.no_matvec else run_matvec_leg(torch, lib, dev, world)
     gs16 = None
     if not args.no_gs16 and N_MOE_LAYERS == 46:
-        gs16 = run_gs16_leg(args, torch, pkg, lib, layers, dev, local, world)
+        gs16 = run_moe_leg(args, torch, pkg, lib, layers, dev, local, world, gs=16)
     prefill = None
     if not args.no_prefill:
         prefill = run_prefill_leg(args, torch, pkg, lib, layers, dev, local, rank, world)
@@ -1150,8 +1170,11 @@ def main() -> None:
     ap.add_argument("--ref-budget-s", type=float, default=90.0,
                     help="total CPU seconds of the reference arm; each step is an equal bounded sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["prefill", "ep"], default=None,
-                    help="run only the config-3 prefill or the config-4 expert-parallel measurement")
+    ap.add_argument("--only", choices=["prefill", "ep", "moe", "model"], default=None,
+                    help="run one measurement alone: the config-3 prefill, the config-4 expert-parallel prefill, "
+                         "the per-layer MoE decode (--layers layers, --gs) or the config-2 decoder "
+                         "(--layers MoE layers)")
+    ap.add_argument("--gs", type=int, choices=[32, 16], default=32, help="weight scale group of --only moe")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-3 batched prefill measurement")
     ap.add_argument("--no-matvec", action="store_true", help="skip the config-1 matvec measurement")
     ap.add_argument("--no-gs16", action="store_true", help="skip the gs = 16 decode measurement")
