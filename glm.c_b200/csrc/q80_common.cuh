@@ -85,9 +85,13 @@ __device__ __forceinline__ int b_frag_offset(int lane) {
 __device__ __forceinline__ void chunk_mma_accumulate(const int4& q0, const int4& q1, const float2& s0,
                                                      const float2& s1, const int4& b, const float2& tab,
                                                      int t, float& acc0, float& acc1) {
-    int d[4] = {0, 0, 0, 0};
+    // two independent MMAs (one per 8-byte half) so they issue back to back;
+    // the int32 sum below is exact, as chaining them through C would be
+    int d[4] = {0, 0, 0, 0}, e[4] = {0, 0, 0, 0};
     mma_s8(d, (uint32_t)q0.x, (uint32_t)q1.x, (uint32_t)q0.y, (uint32_t)q1.y, (uint32_t)b.x, (uint32_t)b.y);
-    mma_s8(d, (uint32_t)q0.z, (uint32_t)q1.z, (uint32_t)q0.w, (uint32_t)q1.w, (uint32_t)b.z, (uint32_t)b.w);
+    mma_s8(e, (uint32_t)q0.z, (uint32_t)q1.z, (uint32_t)q0.w, (uint32_t)q1.w, (uint32_t)b.z, (uint32_t)b.w);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d[i] += e[i];
     // Column A of lane t belongs to group g1 only for t==1; column B for t==1,2.
     const float swA0 = (t == 1) ? s0.y : s0.x, swB0 = (t == 1 || t == 2) ? s0.y : s0.x;
     const float swA1 = (t == 1) ? s1.y : s1.x, swB1 = (t == 1 || t == 2) ? s1.y : s1.x;
@@ -135,11 +139,17 @@ __device__ __forceinline__ G16Lane g16_lane(int lane) {
 __device__ __forceinline__ void chunk_mma_accumulate_g16(const int4& q0, const int4& q1, float s0, float s1,
                                                          const int4& bX, const int4& bY, float sx, float& acc0,
                                                          float& acc1) {
-    int dx[4] = {0, 0, 0, 0}, dy[4] = {0, 0, 0, 0};
+    // four independent MMAs (set x half), summed exactly in int32 after
+    int dx[4] = {0, 0, 0, 0}, dy[4] = {0, 0, 0, 0}, ex[4] = {0, 0, 0, 0}, ey[4] = {0, 0, 0, 0};
     mma_s8(dx, (uint32_t)q0.x, (uint32_t)q1.x, (uint32_t)q0.y, (uint32_t)q1.y, (uint32_t)bX.x, (uint32_t)bX.y);
-    mma_s8(dx, (uint32_t)q0.z, (uint32_t)q1.z, (uint32_t)q0.w, (uint32_t)q1.w, (uint32_t)bX.z, (uint32_t)bX.w);
     mma_s8(dy, (uint32_t)q0.x, (uint32_t)q1.x, (uint32_t)q0.y, (uint32_t)q1.y, (uint32_t)bY.x, (uint32_t)bY.y);
-    mma_s8(dy, (uint32_t)q0.z, (uint32_t)q1.z, (uint32_t)q0.w, (uint32_t)q1.w, (uint32_t)bY.z, (uint32_t)bY.w);
+    mma_s8(ex, (uint32_t)q0.z, (uint32_t)q1.z, (uint32_t)q0.w, (uint32_t)q1.w, (uint32_t)bX.z, (uint32_t)bX.w);
+    mma_s8(ey, (uint32_t)q0.z, (uint32_t)q1.z, (uint32_t)q0.w, (uint32_t)q1.w, (uint32_t)bY.z, (uint32_t)bY.w);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        dx[i] += ex[i];
+        dy[i] += ey[i];
+    }
     // columns 2t (hi), 2t+1 (mid) of X and 2t (lo) of Y; dy[1], dy[3] are the zero columns
     const float v0 = fmaf(i2f_exact22(dx[0]), 65536.0f, fmaf(i2f_exact22(dx[1]), 256.0f, i2f_exact22(dy[0])));
     const float v1 = fmaf(i2f_exact22(dx[2]), 65536.0f, fmaf(i2f_exact22(dx[3]), 256.0f, i2f_exact22(dy[2])));
