@@ -228,6 +228,22 @@ __device__ __forceinline__ unsigned pack_digit_bytes(int a, int b, int c, int d)
     return (unsigned)(a & 255) | ((unsigned)(b & 255) << 8) | ((unsigned)(c & 255) << 16) | ((unsigned)d << 24);
 }
 
+// A group whose maximum |x| is below 2^-100 (a rare case, kept out of line so
+// that the quantiser's hot code stays small): its scale and integers with
+// the library's exponent functions.
+struct TinyGroupQ {
+    int x0, x1, x2, x3;
+    float sx;
+};
+
+static __device__ __noinline__ TinyGroupQ tiny_group_q(float x0, float x1, float x2, float x3, unsigned am) {
+    const float a = __uint_as_float(am);
+    int e = ilogbf(a) - 22;
+    if (ldexpf(a, -e) > kDigitMax) e += 1;
+    return TinyGroupQ{__float2int_rn(ldexpf(x0, -e)), __float2int_rn(ldexpf(x1, -e)), __float2int_rn(ldexpf(x2, -e)),
+                      __float2int_rn(ldexpf(x3, -e)), ldexpf(1.0f, e)};
+}
+
 template <int kB>
 __device__ __forceinline__ void q4_store(const float4 (&v)[kB], int groups, int s0, int nwarps, int lane,
                                          int8_t* planes, float* sxg) {
@@ -251,13 +267,13 @@ __device__ __forceinline__ void q4_store(const float4 (&v)[kB], int groups, int 
             const float inv = __uint_as_float((unsigned)(127 - e) << 23);
 #pragma unroll
             for (int j = 0; j < 4; ++j) X[j] = __float2int_rn(__fmul_rn(x[j], inv));
-        } else if (am != 0u) {  // tiny group: library scaling
-            const float a = __uint_as_float(am);
-            int e = ilogbf(a) - 22;
-            if (ldexpf(a, -e) > kDigitMax) e += 1;
-            sx = ldexpf(1.0f, e);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) X[j] = __float2int_rn(ldexpf(x[j], -e));
+        } else if (am != 0u) {  // tiny group: library scaling, out of line
+            const TinyGroupQ t = tiny_group_q(x[0], x[1], x[2], x[3], am);
+            X[0] = t.x0;
+            X[1] = t.x1;
+            X[2] = t.x2;
+            X[3] = t.x3;
+            sx = t.sx;
         }
         int hi[4], mid[4], lo[4];
 #pragma unroll

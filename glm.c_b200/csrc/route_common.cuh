@@ -107,7 +107,6 @@ __device__ __forceinline__ float serial_logit(const float* wrow, const float* xs
 template <typename Sync>
 __device__ __forceinline__ void block_logit_bound_rows(const float* wr, const float* xs, int D, int tid, int nthreads,
                                                        float* scratch, Sync sync, double& C, double& B) {
-    constexpr int kMaxRowsPerWarp = 8;
     const int lane = tid & 31, warp = tid >> 5, nwarps = nthreads >> 5;
     const int rows = D >> 5;
     float* rowtot = scratch;  // [64]
@@ -116,25 +115,26 @@ __device__ __forceinline__ void block_logit_bound_rows(const float* wr, const fl
     float* w_sabs = w_lo + nwarps;
     float* w_abs = w_sabs + nwarps;
     float* w_absT = w_abs + nwarps;
-    float q[kMaxRowsPerWarp];
-    float s = 0.0f, cmp = 0.0f, abs_p = 0.0f;
+    // A row's product and its inclusive fp32 warp scan Q_{k,l} (recomputed
+    // where needed again rather than kept: runtime loops keep this code short).
+    auto row_scan = [&](int k, float& p) {
+        p = __fmul_rn(wr[32 * k + lane], xs[32 * k + lane]);
+        float v = p;
 #pragma unroll
-    for (int j = 0; j < kMaxRowsPerWarp; ++j) {
-        const int k = warp + j * nwarps;
-        float v = 0.0f;
-        if (k < rows) {  // warp-uniform
-            const float p = __fmul_rn(wr[32 * k + lane], xs[32 * k + lane]);
-            two_sum_acc(s, cmp, p);
-            abs_p += fabsf(p);
-            v = p;
-#pragma unroll
-            for (int off = 1; off < 32; off <<= 1) {
-                const float y = __shfl_up_sync(0xffffffffu, v, off);
-                if (lane >= off) v = __fadd_rn(v, y);
-            }
-            if (lane == 31) rowtot[k] = v;
+        for (int off = 1; off < 32; off <<= 1) {
+            const float y = __shfl_up_sync(0xffffffffu, v, off);
+            if (lane >= off) v = __fadd_rn(v, y);
         }
-        q[j] = v;
+        return v;
+    };
+    float s = 0.0f, cmp = 0.0f, abs_p = 0.0f;
+#pragma unroll 1
+    for (int k = warp; k < rows; k += nwarps) {  // warp-uniform; rows ascending, as before
+        float p;
+        const float v = row_scan(k, p);
+        two_sum_acc(s, cmp, p);
+        abs_p += fabsf(p);
+        if (lane == 31) rowtot[k] = v;
     }
     sync();
     // Every warp scans the row totals itself: lane l holds rows 2l and 2l+1.
@@ -150,13 +150,12 @@ __device__ __forceinline__ void block_logit_bound_rows(const float* wr, const fl
     if (lane == 0) r_even = 0.0f;
     const float r_odd = __fadd_rn(r_even, t0);
     float sabs = 0.0f;
-#pragma unroll
-    for (int j = 0; j < kMaxRowsPerWarp; ++j) {
-        const int k = warp + j * nwarps;
-        if (k < rows) {  // warp-uniform
-            const float R = __shfl_sync(0xffffffffu, (k & 1) ? r_odd : r_even, k >> 1);
-            sabs = __fadd_rn(sabs, fabsf(__fadd_rn(R, q[j])));
-        }
+#pragma unroll 1
+    for (int k = warp; k < rows; k += nwarps) {  // warp-uniform
+        float p;
+        const float q = row_scan(k, p);
+        const float R = __shfl_sync(0xffffffffu, (k & 1) ? r_odd : r_even, k >> 1);
+        sabs = __fadd_rn(sabs, fabsf(__fadd_rn(R, q)));
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
