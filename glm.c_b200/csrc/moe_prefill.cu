@@ -3,16 +3,17 @@
 // with the expert products as grouped GEMMs on the 5th-generation tensor
 // cores (tcgen05, accumulators in TMEM).
 //
-//   1 prefill_route_kernel   one CTA per token: certified rmsnorm, router
-//                            logit centre/bound per expert (one warp each),
-//                            exact top-k (route_common.cuh) -> ids, weights
-//   2 prefill_dispatch_kernel rows = (token, slot) pairs grouped by expert
+//   1 route_logits_kernel    certified rmsnorm; glm.c's router logits to
+//                            the bit (serial fp32 chains, one per pair)
+//   2 route_select_kernel    top-k (route_common.cuh) -> ids, weights
+//   3 route_exact_kernel     the rare token whose ranking expf's last bits
+//                            could decide, with the exact fallback
+//   4 prefill_dispatch_kernel rows = (token, slot) pairs grouped by expert
 //                            (+ the shared expert: every token), tile lists
-//   3 gather_split_kernel    activation rows as bf16 hi + lo
-//   4 q8_group_gemm_kernel   gate and up: G/U[row][f] = xn . W[f]
-//   5 swiglu_split_kernel    h = silu(G) * U as bf16 hi + lo
-//   6 q8_group_gemm_kernel   down: Y[row][d] = h . Wd[d]
-//   7 prefill_combine_kernel x += y_shared + sum_k (1.8 w_k) y_k, rank order
+//   5 gather_split_kernel    activation rows as bf16 hi + lo
+//   6 q8_group_gemm_kernel   gate and up + SwiGLU: h = silu(xn . Wg) * (xn . Wu)
+//   7 q8_group_gemm_kernel   down: Y[row][d] = h . Wd[d]
+//   8 prefill_combine_kernel x += y_shared + sum_k (1.8 w_k) y_k, rank order
 //
 // Precision. The Q8 weights are dequantised in shared memory to bf16 pairs
 // w = w_hi + w_lo (w_hi = bf16(q*s), w_lo = bf16(q*s - w_hi)) and the
@@ -90,226 +91,185 @@ __device__ __forceinline__ void split_bf16(float v, __nv_bfloat16& hi, __nv_bflo
 
 // ------------------------------------------------------------------ routing
 
-__global__ void __launch_bounds__(512) prefill_route_kernel(PrefillRouteArgs a) {
-    extern __shared__ __align__(16) unsigned char smr[];
-    const int D = a.D, E = a.E, K = a.K, t = blockIdx.x;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-    float* xsp = reinterpret_cast<float*>(smr);                  // padded xn [pad64(D)]
-    float* xs = xsp + ((pad64(D) + 3) & ~3);                      // flat xn [D]
-    double* cen = reinterpret_cast<double*>(xs + D);              // [E]
-    double* bnd = cen + E;                                        // [E]
-    float* sel = reinterpret_cast<float*>(bnd + E);               // 4E floats + E ints
-    int* misc = reinterpret_cast<int*>(sel + 5 * E);
-    __shared__ double red[16];
-    __shared__ float s_inv;
-    SelectScratch S;
-    S.sel_c = sel;
-    S.sel_lo = sel + E;
-    S.sel_hi = sel + 2 * E;
-    S.p_c = sel + 3 * E;
-    S.taken = reinterpret_cast<int*>(sel + 4 * E);
-    S.rank = misc;            // [kMaxTopK + 1]
-    S.cert = misc + 16;
-    int* s_idx = misc + 32;   // [kMaxTopK]
-    float* s_w = reinterpret_cast<float*>(misc + 48);
-
-    const float* x = a.x + (size_t)t * D;
-    double ss = 0.0;
-    for (int i = tid; i < D; i += blockDim.x) ss += (double)x[i] * (double)x[i];
-    ss = warp_sum_d(ss);
-    if (lane == 0) red[warp] = ss;
-    __syncthreads();
-    if (tid == 0) {
-        double tot = 0.0;
-        for (int w = 0; w < nw; ++w) tot += red[w];
-        s_inv = rms_inv_certified(tot, x, D, a.stats ? &a.stats[3] : nullptr);
-    }
-    __syncthreads();
-    const float inv = s_inv;
-    for (int i = tid; i < D; i += blockDim.x) {
-        const float v = __fmul_rn(__fmul_rn(x[i], inv), a.norm[i]);  // infer.c:751
-        xs[i] = v;
-        xsp[pad64(i)] = v;
-        a.xn[(size_t)t * D + i] = v;
-    }
-    __syncthreads();
-    for (int e = warp; e < E; e += nw) {
-        double C, B;
-        warp_logit_bound_contig(a.router + (size_t)e * D, xsp, D, C, B);
-        if (lane == 0) {
-            cen[e] = C;
-            bnd[e] = B;
-        }
-    }
-    __syncthreads();
-    block_select(cen, bnd, a.bias, E, K, a.router, xs, D, tid, (int)blockDim.x, S, s_idx, s_w, a.stats,
-                 []() { __syncthreads(); });
-    if (tid < K) {
-        a.topk_idx[(size_t)t * K + tid] = s_idx[tid];
-        a.topk_w[(size_t)t * K + tid] = s_w[tid];
-    }
-}
-
-// Batched form, two kernels.
+// Batched form, three kernels.
 //
-// route_logits_kernel<PER>: CTA (token block, expert block) = kLT tokens (one
-// warp each) x kLE experts whose router rows sit in shared memory (padded
-// layout pad68, so the lanes' float4 reads are conflict-free). Lane l of a
-// warp holds its token's xn elements [l*PER, (l+1)*PER) in registers (rmsnorm
-// recomputed per expert block: certified mean as everywhere else). Per
-// expert, in one pass over the lane's elements taken as sub-chunks of 16:
-// the fp32 products p (as glm.c forms them), each sub-chunk's running sum q
-// and sum |q|, sum |p|, and the products summed as fp32 fours whose totals go
-// into fp64 sub-chunk totals. Bound: glm.c's serial sum is within
-// u * sum_i |P_i| of the exact sum, P_i its prefixes. With R_c the exact sum
-// before sub-chunk c (fp64 warp scan of the lane totals plus the lane's
-// earlier sub-chunks) and Q_{c,j} the exact in-chunk prefix,
-// |P_i| <= |R_c| + |Q_{c,j}|, so sum_i |P_i| <= sum_c (16 |R_c| + sum_j |Q_{c,j}|);
-// the fp32 q_j are within 16 u A_c (A_c = the sub-chunk's sum |p|) of Q_{c,j},
-// and the fp32 sum of |q_j| within (1 - 16 u)^-1. Hence
-//   B = 1.01 u sum_c [16 |R_c| + (1 + 2^-15) sabs_c + 256 u A_c]
-//       + (2.0001 u + 2^-40) sum |p|,
-// the second term covering the centre's own error (fours: 2u of their
-// magnitude each; fp64 sums: < 2^-40). C and B go to global memory.
+// route_logits_kernel<NT, NE>: glm.c's router logits themselves, to the bit
+// (dot_f32, infer.c:916-938: s = 0; s = s + w[i] * xn[i], each product and
+// sum rounded to fp32, left to right). A CTA of 128 threads takes 8*NT tokens
+// x 16*NE experts; thread (ty, tx) carries the serial chains of its NT x NE
+// (token, expert) pairs, tokens ty + 8k and experts tx + 16j. The serial
+// order costs nothing here: with T tokens there are T x E independent chains
+// and each one is two fp32 instructions per element, fewer than any
+// reassociated sum with a rigorous error bound needs. D streams through a
+// double-buffered shared-memory tile in chunks of kLD elements: the router
+// rows by cp.async, xn computed on the way in (phase 1 takes each token's
+// certified rmsnorm scale; x * inv * ffn_norm as infer.c:751; the CTAs of
+// expert block 0 also store xn for the GEMM gather). Rows are padded by 4
+// floats, so the 8 router rows a quarter-warp reads fall in distinct bank
+// groups, and a token row is a broadcast. Rows past the end are zero: s + 0
+// is s for every s the chain can hold (it starts at +0, so it is never -0).
+// The select kernel receives each logit as a centre with bound 0.
 //
 // route_select_kernel: kRT tokens per CTA, 64 threads each on a named
-// barrier: the same certified top-k / exact fallback as the decode path
-// (route_common.cuh).
-constexpr int kLE = 8;                 // experts (router rows) per CTA
-constexpr int kLT = 8;                 // tokens (warps) per CTA
+// barrier: the same certified top-k as the decode path (route_common.cuh),
+// without the exact fallback, so a CTA needs ~2.6 KB of shared memory and a
+// whole batch of tokens is resident at once. With exact logits a ranking
+// fails to certify only where expf's last bits could reorder two experts;
+// such a token gets kRouteRedo as its first id and is routed again by
+// route_exact_kernel.
+constexpr int kRouteRedo = -2;         // never a routing result (ids are -1 .. E-1)
+constexpr int kExactCtas = 296;        // route_exact_kernel CTAs (two per SM)
+constexpr int kSelRows = 8;            // router rows staged at a time by the exact fallback
+constexpr int kLTx = 16;               // logit CTA: threads along the experts
+constexpr int kLTy = 8;                // logit CTA: threads along the tokens
+constexpr int kLThreads = kLTx * kLTy;
+constexpr int kLD = 128;               // D elements per staged chunk
+constexpr int kLRow = kLD + 4;         // padded row, floats
 constexpr int kRT = 1;                 // tokens per select CTA
-constexpr int kSelRows = 8;            // router rows staged at a time for the exact fallback
 constexpr int kRThreads = 64 * kRT;
-
-__host__ __device__ __forceinline__ int pad68(int i) { return i + 4 * (i >> 6); }
 
 __device__ __forceinline__ void token_bar(int tb) {
     asm volatile("bar.sync %0, 64;\n" ::"r"(1 + tb) : "memory");
 }
 
-template <int PER>
-__global__ void __launch_bounds__(kLT * 32) route_logits_kernel(PrefillRouteArgs a) {
+// 16-byte global -> shared copy; src_bytes 0 writes zeros (src not read).
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_addr(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+constexpr size_t route_logits_smem(int NT, int NE) {
+    return sizeof(float) * 2 * (size_t)(kLTy * NT + kLTx * NE) * kLRow;
+}
+
+template <int NT, int NE>
+__global__ void __launch_bounds__(kLThreads) route_logits_kernel(PrefillRouteArgs a) {
+    constexpr int TT = kLTy * NT, TE = kLTx * NE;
+    constexpr int XI = TT * (kLD / 4) / kLThreads;  // float4 of x per thread per chunk
+    constexpr int WI = TE * (kLD / 4) / kLThreads;  // float4 of router rows per thread per chunk
+    static_assert(XI >= 1 && WI >= 1, "tile smaller than one float4 per thread");
     extern __shared__ __align__(16) unsigned char smr[];
-    const int D = PER * 32, E = a.E;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int e0 = blockIdx.y * kLE, ne = min(kLE, E - e0);
-    const int rowf4 = ((pad68(D - 1) + 1) + 3) & ~3;
-    float* rows = reinterpret_cast<float*>(smr);  // phase 1: x of each warp's token; phase 2: kLE router rows
-    float* nrm = rows + kLE * rowf4;              // ffn_norm, padded layout
-    const int t = blockIdx.x * kLT + warp;
-    const bool live = t < a.T;
-    const int base = lane * PER;
-    // phase 1: coalesced loads into the padded layout, lane-contiguous reads back
-    for (int c = threadIdx.x; c < D / 4; c += blockDim.x)
-        *reinterpret_cast<float4*>(nrm + pad68(4 * c)) = __ldg(reinterpret_cast<const float4*>(a.norm) + c);
-    float* xw = rows + warp * rowf4;
-    if (live)
-        for (int c = lane; c < D / 4; c += 32)
-            *reinterpret_cast<float4*>(xw + pad68(4 * c)) = *(reinterpret_cast<const float4*>(a.x + (size_t)t * D) + c);
-    __syncthreads();
-    float xr[PER];
-    if (live) {
+    float* xs = reinterpret_cast<float*>(smr);  // [2][TT][kLRow]
+    float* ws = xs + 2 * TT * kLRow;            // [2][TE][kLRow]
+    __shared__ float inv_s[TT];
+    const int D = a.D, E = a.E, T = a.T;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int ty = tid / kLTx, tx = tid % kLTx;
+    const int t0 = blockIdx.x * TT, e0 = blockIdx.y * TE;
+    const bool first = blockIdx.y == 0;
+    const int nch = D / kLD;
+
+    auto stage_w = [&](int c, int buf) {
+        float* dst = ws + buf * TE * kLRow;
 #pragma unroll
-        for (int j = 0; j < PER; j += 4) {
-            const float4 v = *reinterpret_cast<const float4*>(xw + pad68(base + j));
-            xr[j] = v.x;
-            xr[j + 1] = v.y;
-            xr[j + 2] = v.z;
-            xr[j + 3] = v.w;
+        for (int k = 0; k < WI; ++k) {
+            const int q = tid + k * kLThreads, r = q >> 5, c4 = q & 31, e = e0 + r;
+            cp_async16(dst + r * kLRow + 4 * c4, a.router + (size_t)(e < E ? e : 0) * D + c * kLD + 4 * c4,
+                       e < E ? 16 : 0);
         }
-        double ss = 0.0;
+        cp_async_commit();
+    };
+    float4 xv[XI];
+    auto load_x = [&](int c) {
 #pragma unroll
-        for (int j = 0; j < PER; ++j) ss += (double)xr[j] * (double)xr[j];
-        ss = warp_sum_d(ss);
+        for (int k = 0; k < XI; ++k) {
+            const int q = tid + k * kLThreads, r = q >> 5, c4 = q & 31, t = t0 + r;
+            xv[k] = t < T ? *reinterpret_cast<const float4*>(a.x + (size_t)t * D + c * kLD + 4 * c4)
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    };
+    auto store_x = [&](int c, int buf) {
+        float* dst = xs + buf * TT * kLRow;
+#pragma unroll
+        for (int k = 0; k < XI; ++k) {
+            const int q = tid + k * kLThreads, r = q >> 5, c4 = q & 31, t = t0 + r;
+            const float inv = inv_s[r];
+            const float4 nv = __ldg(reinterpret_cast<const float4*>(a.norm + c * kLD) + c4);
+            float4 v;  // infer.c:751: (x * inv) * w
+            v.x = __fmul_rn(__fmul_rn(xv[k].x, inv), nv.x);
+            v.y = __fmul_rn(__fmul_rn(xv[k].y, inv), nv.y);
+            v.z = __fmul_rn(__fmul_rn(xv[k].z, inv), nv.z);
+            v.w = __fmul_rn(__fmul_rn(xv[k].w, inv), nv.w);
+            if (t >= T) v = make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4*>(dst + r * kLRow + 4 * c4) = v;
+            if (first && t < T) *reinterpret_cast<float4*>(a.xn + (size_t)t * D + c * kLD + 4 * c4) = v;
+        }
+    };
+
+    stage_w(0, 0);  // the router rows do not depend on phase 1
+    load_x(0);
+    // phase 1: each token's rmsnorm scale (fp64 sum of squares, certified)
+    for (int r = warp; r < TT; r += kLThreads / 32) {
+        const int t = t0 + r;
         float inv = 0.0f;
-        if (lane == 0) inv = rms_inv_certified_padded(ss, xw, D, (a.stats && blockIdx.y == 0) ? &a.stats[3] : nullptr);
-        inv = __shfl_sync(0xffffffffu, inv, 0);
-#pragma unroll
-        for (int j = 0; j < PER; j += 4) {
-            const float4 w4 = *reinterpret_cast<const float4*>(nrm + pad68(base + j));
-            xr[j] = __fmul_rn(__fmul_rn(xr[j], inv), w4.x);  // infer.c:751
-            xr[j + 1] = __fmul_rn(__fmul_rn(xr[j + 1], inv), w4.y);
-            xr[j + 2] = __fmul_rn(__fmul_rn(xr[j + 2], inv), w4.z);
-            xr[j + 3] = __fmul_rn(__fmul_rn(xr[j + 3], inv), w4.w);
+        if (t < T) {
+            const float4* xr = reinterpret_cast<const float4*>(a.x + (size_t)t * D);
+            double ss = 0.0;
+            for (int c = lane; c < D / 4; c += 32) {
+                const float4 v = xr[c];
+                ss += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+            }
+            ss = warp_sum_d(ss);
+            if (lane == 0)
+                inv = rms_inv_certified(ss, a.x + (size_t)t * D, D, (a.stats && first) ? &a.stats[3] : nullptr);
         }
-    }
-    __syncthreads();  // x staging is dead: the same space takes the router rows
-    {
-        const int chunks = D / 4;
-        for (int c = threadIdx.x; c < kLE * chunks; c += blockDim.x) {
-            const int r = c / chunks, q = c - r * chunks;
-            const float4 v = r < ne ? __ldg(reinterpret_cast<const float4*>(a.router + (size_t)(e0 + r) * D) + q)
-                                    : make_float4(0.f, 0.f, 0.f, 0.f);
-            *reinterpret_cast<float4*>(rows + r * rowf4 + pad68(4 * q)) = v;
-        }
-    }
-    if (live && blockIdx.y == 0) {  // xn rows for the GEMM gather and the exact fallback
-        float* xo = a.xn + (size_t)t * D + base;
-#pragma unroll
-        for (int j = 0; j < PER; j += 4)
-            *reinterpret_cast<float4*>(xo + j) = make_float4(xr[j], xr[j + 1], xr[j + 2], xr[j + 3]);
+        if (lane == 0) inv_s[r] = inv;
     }
     __syncthreads();
-    if (!live) return;  // no block barrier follows
-    // Per expert, the lane's PER elements as NSUB sub-chunks of 16 with
-    // their own running sums (independent chains in flight); the bound uses
-    // |P_i| <= |prefix before the sub-chunk| + |in-chunk prefix|.
-    constexpr int NSUB = PER / 16;
-    for (int r = 0; r < ne; ++r) {
-        const float* wr = rows + r * rowf4;
-        double Ls[NSUB];
-        float qs[NSUB], sa[NSUB], sap = 0.0f;
+    store_x(0, 0);
+
+    float acc[NT][NE];
 #pragma unroll
-        for (int k = 0; k < NSUB; ++k) {
-            Ls[k] = 0.0;
-            qs[k] = sa[k] = 0.0f;
+    for (int k = 0; k < NT; ++k)
+#pragma unroll
+        for (int j = 0; j < NE; ++j) acc[k][j] = 0.0f;
+    for (int c = 0; c < nch; ++c) {
+        const int buf = c & 1;
+        if (c + 1 < nch) {
+            stage_w(c + 1, buf ^ 1);
+            load_x(c + 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
         }
+        __syncthreads();  // chunk c's rows are in shared memory
+        const float* xb = xs + (buf * TT + ty) * kLRow;
+        const float* wb = ws + (buf * TE + tx) * kLRow;
+#pragma unroll 4
+        for (int i = 0; i < kLD; i += 4) {
+            float4 xq[NT], wq[NE];
 #pragma unroll
-        for (int j = 0; j < 16; j += 4) {
+            for (int k = 0; k < NT; ++k) xq[k] = *reinterpret_cast<const float4*>(xb + k * kLTy * kLRow + i);
 #pragma unroll
-            for (int k = 0; k < NSUB; ++k) {
-                const int jj = 16 * k + j;
-                const float4 w4 = *reinterpret_cast<const float4*>(wr + pad68(base + jj));
-                const float p0 = __fmul_rn(w4.x, xr[jj]), p1 = __fmul_rn(w4.y, xr[jj + 1]);
-                const float p2 = __fmul_rn(w4.z, xr[jj + 2]), p3 = __fmul_rn(w4.w, xr[jj + 3]);
-                Ls[k] += (double)__fadd_rn(__fadd_rn(p0, p1), __fadd_rn(p2, p3));
-                qs[k] = __fadd_rn(qs[k], p0);
-                sa[k] = __fadd_rn(sa[k], fabsf(qs[k]));
-                qs[k] = __fadd_rn(qs[k], p1);
-                sa[k] = __fadd_rn(sa[k], fabsf(qs[k]));
-                qs[k] = __fadd_rn(qs[k], p2);
-                sa[k] = __fadd_rn(sa[k], fabsf(qs[k]));
-                qs[k] = __fadd_rn(qs[k], p3);
-                sa[k] = __fadd_rn(sa[k], fabsf(qs[k]));
-                sap = __fadd_rn(__fadd_rn(sap, fabsf(p0)), __fadd_rn(fabsf(p1), __fadd_rn(fabsf(p2), fabsf(p3))));
+            for (int j = 0; j < NE; ++j) wq[j] = *reinterpret_cast<const float4*>(wb + j * kLTx * kLRow + i);
+#pragma unroll
+            for (int k = 0; k < NT; ++k)
+#pragma unroll
+                for (int j = 0; j < NE; ++j) {
+                    acc[k][j] = __fadd_rn(acc[k][j], __fmul_rn(wq[j].x, xq[k].x));
+                    acc[k][j] = __fadd_rn(acc[k][j], __fmul_rn(wq[j].y, xq[k].y));
+                    acc[k][j] = __fadd_rn(acc[k][j], __fmul_rn(wq[j].z, xq[k].z));
+                    acc[k][j] = __fadd_rn(acc[k][j], __fmul_rn(wq[j].w, xq[k].w));
+                }
+        }
+        if (c + 1 < nch) store_x(c + 1, buf ^ 1);
+        __syncthreads();  // chunk c's buffer is free for chunk c + 2
+    }
+#pragma unroll
+    for (int k = 0; k < NT; ++k)
+#pragma unroll
+        for (int j = 0; j < NE; ++j) {
+            const int t = t0 + ty + k * kLTy, e = e0 + tx + j * kLTx;
+            if (t < T && e < E) {
+                a.cen[(size_t)t * E + e] = (double)acc[k][j];
+                a.bnd[(size_t)t * E + e] = 0.0;
             }
         }
-        double L = 0.0;
-#pragma unroll
-        for (int k = 0; k < NSUB; ++k) L += Ls[k];
-        double inc = L;
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-            const double y = __shfl_up_sync(0xffffffffu, inc, off);
-            if (lane >= off) inc += y;
-        }
-        const double C = __shfl_sync(0xffffffffu, inc, 31);
-        double pre = inc - L, tl = 0.0;
-#pragma unroll
-        for (int k = 0; k < NSUB; ++k) {
-            tl += 16.0 * fabs(pre) + (double)sa[k] * (1.0 + 0x1p-15);
-            pre += Ls[k];
-        }
-        const double A = (double)sap * 1.0001;
-        tl += 256.0 * 0x1p-24 * A;
-        double ap = A;
-        tl = warp_sum_d(tl);
-        ap = warp_sum_d(ap);
-        if (lane == 0) {
-            a.cen[(size_t)t * E + e0 + r] = C;
-            a.bnd[(size_t)t * E + e0 + r] = 1.01 * 0x1p-24 * tl + (2.0001 * 0x1p-24 + 0x1p-40) * ap;
-        }
-    }
 }
 
 __global__ void __launch_bounds__(kRThreads) route_select_kernel(PrefillRouteArgs a) {
@@ -323,15 +283,14 @@ __global__ void __launch_bounds__(kRThreads) route_select_kernel(PrefillRouteArg
     float* sel = reinterpret_cast<float*>(reinterpret_cast<double*>(smr) + (size_t)kRT * 2 * E) + (size_t)tb * 5 * E;
     int* misc = reinterpret_cast<int*>(reinterpret_cast<float*>(reinterpret_cast<double*>(smr) + (size_t)kRT * 2 * E) +
                                        (size_t)kRT * 5 * E) + tb * 64;
-    float* xs = reinterpret_cast<float*>(reinterpret_cast<int*>(reinterpret_cast<float*>(reinterpret_cast<double*>(smr) +
-                                                                                         (size_t)kRT * 2 * E) +
-                                                                (size_t)kRT * 5 * E) + kRT * 64) + (size_t)tb * D;
+    // xn and the router rows stay in global memory (L2): only the rare exact
+    // fallback reads them, so the CTA keeps ~2.6 KB of shared memory and a
+    // whole batch of tokens is resident at once
+    const float* xs = a.xn + (size_t)t * D;
     for (int i = ltid; i < E; i += 64) {
         cen[i] = a.cen[(size_t)t * E + i];
         bnd[i] = a.bnd[(size_t)t * E + i];
     }
-    for (int i = ltid * 4; i < D; i += 256)  // xn for the exact fallback (serial_logit reads it D times)
-        *reinterpret_cast<float4*>(xs + i) = *reinterpret_cast<const float4*>(a.xn + (size_t)t * D + i);
     SelectScratch S;
     S.sel_c = sel;
     S.sel_lo = sel + E;
@@ -343,30 +302,89 @@ __global__ void __launch_bounds__(kRThreads) route_select_kernel(PrefillRouteArg
     int* s_idx = misc + 32;
     float* s_w = reinterpret_cast<float*>(misc + 48);
     token_bar(tb);
-    float* rowbuf = reinterpret_cast<float*>(reinterpret_cast<int*>(reinterpret_cast<float*>(
-                        reinterpret_cast<double*>(smr) + (size_t)kRT * 2 * E) + (size_t)kRT * 5 * E) + kRT * 64) +
-                    (size_t)kRT * D + (size_t)tb * kSelRows * D;
     block_select(cen, bnd, a.bias, E, K, a.router, xs, D, ltid, 64, S, s_idx, s_w,
-                 (warp & 1) == 0 ? a.stats : nullptr, [tb]() { token_bar(tb); }, rowbuf, kSelRows);
-    if (ltid < K) {
+                 (warp & 1) == 0 ? a.stats : nullptr, [tb]() { token_bar(tb); }, nullptr, 0, false);
+    if (!*S.cert) {
+        if (ltid == 0) a.topk_idx[(size_t)t * K] = kRouteRedo;  // route_exact_kernel takes it
+    } else if (ltid < K) {
         a.topk_idx[(size_t)t * K + ltid] = s_idx[ltid];
         a.topk_w[(size_t)t * K + ltid] = s_w[ltid];
     }
 }
 
-template <int PER>
-cudaError_t launch_route_batched(const PrefillRouteArgs& ra, cudaStream_t st) {
-    const int D = PER * 32;
-    const size_t rowf4 = (size_t)((((D - 1) + 4 * ((D - 1) >> 6) + 1) + 3) & ~3);
-    static_assert(kLT <= kLE, "the x staging of phase 1 reuses the router-row space");
-    const size_t smem1 = sizeof(float) * (kLE + 1) * rowf4;
-    cudaError_t err = ensure_smem_attr(reinterpret_cast<const void*>(route_logits_kernel<PER>), (int)smem1);
+// Byte offset of route_exact_kernel's staged xn: after the centres, bounds,
+// sel arrays and 64 ints, rounded up to 16 bytes.
+__host__ __device__ __forceinline__ size_t exact_xs_offset(int E) {
+    return ((size_t)E * (2 * sizeof(double) + 5 * sizeof(float)) + 64 * sizeof(int) + 15) & ~(size_t)15;
+}
+
+// The tokens route_select_kernel marked kRouteRedo, each by a whole CTA of
+// 64 threads in turn: block_select with the exact fallback, xn and the
+// candidates' router rows staged in shared memory (serial chains on on-chip
+// data). CTAs step over the unmarked tokens.
+__global__ void __launch_bounds__(64) route_exact_kernel(PrefillRouteArgs a) {
+    extern __shared__ __align__(16) unsigned char smr[];
+    const int E = a.E, K = a.K, D = a.D, tid = threadIdx.x;
+    double* cen = reinterpret_cast<double*>(smr);
+    double* bnd = cen + E;
+    float* sel = reinterpret_cast<float*>(bnd + E);
+    int* misc = reinterpret_cast<int*>(sel + 5 * E);
+    float* xs = reinterpret_cast<float*>(smr + exact_xs_offset(E));  // 16-byte aligned: float4 staging
+    float* rowbuf = xs + D;
+    SelectScratch S;
+    S.sel_c = sel;
+    S.sel_lo = sel + E;
+    S.sel_hi = sel + 2 * E;
+    S.p_c = sel + 3 * E;
+    S.taken = reinterpret_cast<int*>(sel + 4 * E);
+    S.rank = misc;
+    S.cert = misc + 16;
+    int* s_idx = misc + 32;
+    float* s_w = reinterpret_cast<float*>(misc + 48);
+    for (int t = blockIdx.x; t < a.T; t += gridDim.x) {
+        if (a.topk_idx[(size_t)t * K] != kRouteRedo) continue;  // the same in every thread
+        for (int i = tid; i < E; i += 64) {
+            cen[i] = a.cen[(size_t)t * E + i];
+            bnd[i] = a.bnd[(size_t)t * E + i];
+        }
+        for (int i = tid * 4; i < D; i += 256)
+            *reinterpret_cast<float4*>(xs + i) = *reinterpret_cast<const float4*>(a.xn + (size_t)t * D + i);
+        __syncthreads();
+        block_select(cen, bnd, a.bias, E, K, a.router, xs, D, tid, 64, S, s_idx, s_w, a.stats,
+                     []() { __syncthreads(); }, rowbuf, kSelRows);
+        if (tid < K) {
+            a.topk_idx[(size_t)t * K + tid] = s_idx[tid];
+            a.topk_w[(size_t)t * K + tid] = s_w[tid];
+        }
+        __syncthreads();  // the shared arrays are refilled for the next token
+    }
+}
+
+// The logit tile: 16 tokens x 32 experts per CTA (four chains a thread) when
+// that still gives two CTAs per SM, else 8 x 16 (one chain a thread) for more
+// CTAs on a small batch.
+template <int NT, int NE>
+cudaError_t launch_route_logits(const PrefillRouteArgs& ra, int num_sms, cudaStream_t st) {
+    const size_t smem = route_logits_smem(NT, NE);
+    cudaError_t err = ensure_smem_attr(reinterpret_cast<const void*>(route_logits_kernel<NT, NE>), (int)smem);
     if (err) return err;
-    route_logits_kernel<PER><<<dim3((ra.T + kLT - 1) / kLT, (ra.E + kLE - 1) / kLE), kLT * 32, smem1, st>>>(ra);
-    const size_t smem2 = (size_t)kRT * (2 * ra.E * sizeof(double) + 5 * ra.E * sizeof(float) + 64 * sizeof(int) +
-                                        (1 + kSelRows) * D * sizeof(float));
+    const dim3 grid((ra.T + kLTy * NT - 1) / (kLTy * NT), (ra.E + kLTx * NE - 1) / (kLTx * NE));
+    route_logits_kernel<NT, NE><<<grid, kLThreads, smem, st>>>(ra);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_route_batched(const PrefillRouteArgs& ra, int num_sms, cudaStream_t st) {
+    if (ra.D % kLD) return cudaErrorInvalidValue;
+    const long big = (long)((ra.T + 15) / 16) * ((ra.E + 31) / 32);
+    cudaError_t err = big >= 2L * num_sms ? launch_route_logits<2, 2>(ra, num_sms, st)
+                                          : launch_route_logits<1, 1>(ra, num_sms, st);
+    if (err) return err;
+    const size_t smem2 = (size_t)kRT * (2 * ra.E * sizeof(double) + 5 * ra.E * sizeof(float) + 64 * sizeof(int));
     if ((err = ensure_smem_attr(reinterpret_cast<const void*>(route_select_kernel), (int)smem2))) return err;
     route_select_kernel<<<(ra.T + kRT - 1) / kRT, kRThreads, smem2, st>>>(ra);
+    const size_t smem3 = exact_xs_offset(ra.E) + (1 + kSelRows) * (size_t)ra.D * sizeof(float);
+    if ((err = ensure_smem_attr(reinterpret_cast<const void*>(route_exact_kernel), (int)smem3))) return err;
+    route_exact_kernel<<<ra.T < kExactCtas ? ra.T : kExactCtas, 64, smem3, st>>>(ra);
     return cudaGetLastError();
 }
 
@@ -1220,20 +1238,8 @@ size_t prefill_workspace_bytes(const MoeDims& d, int T) { return carve(nullptr, 
 
 namespace {
 
-cudaError_t launch_route(const PrefillRouteArgs& ra, cudaStream_t st) {
-    switch (ra.D / 32) {
-        case 16: return launch_route_batched<16>(ra, st);
-        case 32: return launch_route_batched<32>(ra, st);
-        case 48: return launch_route_batched<48>(ra, st);
-        case 64: return launch_route_batched<64>(ra, st);
-        default: break;
-    }
-    const size_t rsmem = sizeof(float) * ((pad64(ra.D) + 3) & ~3) + sizeof(float) * ra.D + 16 * (size_t)ra.E +
-                         20 * (size_t)ra.E + 256;
-    cudaError_t err = ensure_smem_attr(reinterpret_cast<const void*>(prefill_route_kernel), (int)rsmem);
-    if (err) return err;
-    prefill_route_kernel<<<ra.T, 512, rsmem, st>>>(ra);
-    return cudaGetLastError();
+cudaError_t launch_route(const PrefillRouteArgs& ra, int num_sms, cudaStream_t st) {
+    return launch_route_batched(ra, num_sms, st);
 }
 
 // Gate/up + SwiGLU and down for grouped rows already split into xhi / xlo
@@ -1321,7 +1327,7 @@ cudaError_t launch_moe_prefill(const MoeLayerDev& w, const MoeDims& d, unsigned 
     // 1 routing
     PrefillRouteArgs ra{x, w.ffn_norm, w.router, w.router_bias, p.xn, p.ids, p.wts, stats, T, d.D, d.E, d.K,
                         p.cen, p.bnd};
-    if ((err = launch_route(ra, st))) return err;
+    if ((err = launch_route(ra, num_sms, st))) return err;
     // 2 dispatch
     PrefillDispatchArgs da{p.ids, T, d.K, d.E, use_routed ? 1 : 0, mt1, mt2, p.counts, p.row_tok, p.tok_row,
                            p.items1, p.items2};
@@ -1524,7 +1530,7 @@ cudaError_t launch_ep_dispatch(const MoeLayerDev& w, const MoeDims& d, const EpS
     const EpWs p = ep_carve(ws, s);
     PrefillRouteArgs ra{x, w.ffn_norm, w.router, w.router_bias, p.xn, p.ids, p.wts, stats, T, d.D, d.E, d.K,
                         p.cen, p.bnd};
-    cudaError_t err = launch_route(ra, st);
+    cudaError_t err = launch_route(ra, num_sms, st);
     if (err) return err;
     ep_pack_kernel<<<1, 1024, 0, st>>>(p.ids, T, d.K, s.e_local, s.n_shards, routed && w.gate_q ? 1 : 0, p.send_pos,
                                        send_counts, send_expert);
@@ -1588,7 +1594,7 @@ cudaError_t launch_ep_p2p_dispatch(const MoeLayerDev& w, const MoeDims& d, const
     const EpRegion R = ep_region_layout(s);
     PrefillRouteArgs ra{x, w.ffn_norm, w.router, w.router_bias, p.xn, p.ids, p.wts, stats, T, d.D, d.E, d.K,
                         p.cen, p.bnd};
-    cudaError_t err = launch_route(ra, st);
+    cudaError_t err = launch_route(ra, num_sms, st);
     if (err) return err;
     ep_pack_kernel<<<1, 1024, 0, st>>>(p.ids, T, d.K, s.e_local, s.n_shards, routed && w.gate_q ? 1 : 0, p.send_pos,
                                        p.send_counts, p.send_expert);

@@ -197,45 +197,6 @@ __device__ __forceinline__ void block_logit_bound_rows(const float* wr, const fl
     }
 }
 
-// Centre and bound of one router logit by one warp, lane-contiguous form:
-// lane l takes elements [l*per, (l+1)*per) (per = D/32) of the router row
-// (global memory) and of xn (`xsp`, shared memory in the padded layout
-// pad64, so the lanes' strided reads hit distinct banks). The products are
-// summed in fp64 and the reference's prefixes come from an fp64 warp scan
-// plus a per-lane running sum, so their own error is negligible next to the
-// fp32 rounding of the serial sum: B = 1.01 * 2^-24 * sum_i |P_i| +
-// 2^-40 * sum_i |p_i|. Returned in lane 0.
-__device__ __forceinline__ void warp_logit_bound_contig(const float* __restrict__ wrow, const float* xsp, int D,
-                                                        double& C, double& B) {
-    const int lane = threadIdx.x & 31, per = D >> 5, base = lane * per;
-    const float* wr = wrow + base;
-    double L = 0.0, sum_abs_p = 0.0;
-    for (int j = 0; j < per; j += 4) {
-        const float4 w4 = __ldg(reinterpret_cast<const float4*>(wr + j));
-        const float p0 = __fmul_rn(w4.x, xsp[pad64(base + j)]);
-        const float p1 = __fmul_rn(w4.y, xsp[pad64(base + j + 1)]);
-        const float p2 = __fmul_rn(w4.z, xsp[pad64(base + j + 2)]);
-        const float p3 = __fmul_rn(w4.w, xsp[pad64(base + j + 3)]);
-        L += (double)p0 + (double)p1 + (double)p2 + (double)p3;
-        sum_abs_p += fabs((double)p0) + fabs((double)p1) + fabs((double)p2) + fabs((double)p3);
-    }
-    double inc = L;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-        const double y = __shfl_up_sync(0xffffffffu, inc, off);
-        if (lane >= off) inc += y;
-    }
-    C = __shfl_sync(0xffffffffu, inc, 31);
-    double run = inc - L, sabs = 0.0;
-    for (int j = 0; j < per; ++j) {
-        run += (double)__fmul_rn(__ldg(wr + j), xsp[pad64(base + j)]);
-        sabs += fabs(run);
-    }
-    sabs = warp_sum_d(sabs);
-    sum_abs_p = warp_sum_d(sum_abs_p);
-    B = 1.01 * 0x1p-24 * sabs + 0x1p-40 * sum_abs_p;
-}
-
 // Shared-memory scratch of block_select.
 struct SelectScratch {
     float* sel_c;
@@ -309,12 +270,14 @@ __device__ __forceinline__ void rank_and_certify(const SelectScratch& S, int E, 
 // weights to w[K] (shared memory) exactly as infer.c:1110-1145 would. `xs`
 // (xn in shared memory) and the router rows in global memory serve the exact
 // fallback. stats (may be null): [0] calls, [1] fallbacks, [2] ties only
-// libm's last bit could decide.
+// libm's last bit could decide. With exact_fallback false, a ranking that
+// does not certify returns with *S.cert == 0 and idx / w untouched (and
+// counts nothing): the caller routes that token again with the fallback.
 template <typename Sync>
 __device__ void block_select(const double* center, const double* bound, const float* bias, int E, int K,
                              const float* router, const float* xs, int D, int tid, int nthreads,
                              const SelectScratch& S, int* idx, float* w, unsigned long long* stats, Sync sync,
-                             float* rowbuf = nullptr, int nbuf = 0) {
+                             float* rowbuf = nullptr, int nbuf = 0, bool exact_fallback = true) {
     // the centre, lower and upper sel of every expert, each on its own thread
     for (int t = tid; t < 3 * E; t += nthreads) {
         const int i = t % E, which = t / E;
@@ -335,6 +298,9 @@ __device__ void block_select(const double* center, const double* bound, const fl
     if (tid == 0) *S.cert = 1;
     sync();
     rank_and_certify(S, E, K, R, tid, nthreads, sync);
+    // without the fallback an uncertified ranking leaves idx / w untouched
+    // and *S.cert == 0 (identical in every thread: read after a barrier)
+    if (!exact_fallback && !*S.cert) return;
 
     if (!*S.cert) {
         // Every expert whose interval reaches the weakest winner's lower end
