@@ -705,7 +705,7 @@ def run_prefill_leg(args, torch, pkg, lib, layers, dev, local, rank, world) -> d
            "e2e": {"value": round(world * T / (e2e_ms / 1e3), 1), "unit": "tok/s", "ms": round(e2e_ms, 4),
                    "h2d_bytes_per_step": T * D * 4, "d2h_bytes_per_step": T * D * 4,
                    "api": "glm_cuda_moe_layer (host pointers, synchronous)"},
-           "gpu_launches_per_layer": 8,
+           "gpu_launches_per_layer": 9,
            "api": "glm_cuda_moe_layer_async (n_tokens >= glm_cuda_set_prefill_tokens threshold)"}
     out["route_stats"] = lib.route_stats()  # calls, interval fallbacks, unresolved ties, mean fallbacks
     prof = prefill_ncu()

@@ -358,7 +358,7 @@ int moe_enqueue(int layer, float* x_dev, int n_tokens, int32_t* idx_dev, float* 
         if (int rc = ensure_prefill_ws(n_tokens)) return rc;
         cudaError_t e = glmq::launch_moe_prefill(L.w, d, g.pf_ws, x_dev, n_tokens, idx_dev, w_dev, routed, g.num_sms,
                                                  g.scratch.status, g.scratch.stats, st);
-        g.launches += 8;
+        g.launches += 9;
         if (e != cudaSuccess) return fail(GLM_CUDA_ERR_CUDA, "moe prefill launch: %s", cudaGetErrorString(e));
         return 0;
     }
@@ -650,7 +650,7 @@ int glm_cuda_ep_dispatch(int layer, const float* x_dev, int n_tokens, float* sen
     cudaError_t e = glmq::launch_ep_dispatch(g.layers[layer].w, g.dims, g.ep, g.ep_ws, x_dev, n_tokens, send_rows_dev,
                                              send_expert_dev, send_counts_dev, routed_disabled_by_env() ? 0 : 1,
                                              g.num_sms, g.scratch.stats, st);
-    g.launches += 4;
+    g.launches += 5;
     if (e != cudaSuccess) return fail(GLM_CUDA_ERR_CUDA, "ep dispatch launch: %s", cudaGetErrorString(e));
     g.ep_layer = layer;
     g.ep_T = n_tokens;
@@ -786,7 +786,7 @@ int glm_cuda_ep_p2p_dispatch(int layer, const float* x_dev, int n_tokens, void* 
     cudaError_t e = glmq::launch_ep_p2p_dispatch(g.layers[layer].w, g.dims, g.ep, g.ep_ws, x_dev, n_tokens,
                                                  routed_disabled_by_env() ? 0 : 1, g.num_sms, g.scratch.stats,
                                                  g.ep_peers, g.ep_shard, epoch, st);
-    g.launches += 5;
+    g.launches += 6;
     if (e != cudaSuccess) return fail(GLM_CUDA_ERR_CUDA, "ep p2p dispatch launch: %s", cudaGetErrorString(e));
     g.ep_epoch = epoch;
     g.ep_layer = layer;
@@ -1056,7 +1056,7 @@ int enqueue_step(cudaStream_t st) {
             // gs = 16: the batched kernels with one token (workspace sized at model init)
             LAUNCH_TRY(glmq::launch_moe_prefill(g.layers[l].w, g.dims, g.pf_ws, m.x, 1, nullptr, nullptr, routed, ns,
                                                 g.scratch.status, g.scratch.stats, st));
-            g.launches += 8;
+            g.launches += 9;
         } else if (use_persistent()) {
             LAUNCH_TRY(glmq::launch_moe_persistent(g.layers_dev, l, 1, g.dims, g.scratch, m.x, nullptr, nullptr,
                                                    routed, ns, st, l + 1 < d.n_layers ? l + 1 : -1));

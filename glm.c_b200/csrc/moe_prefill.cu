@@ -91,24 +91,29 @@ __device__ __forceinline__ void split_bf16(float v, __nv_bfloat16& hi, __nv_bflo
 
 // ------------------------------------------------------------------ routing
 
-// Batched form, three kernels.
+// Batched form, four kernels.
+//
+// route_norm_kernel: one warp per token. The row stays in registers between
+// the fp64 sum of squares (certified rmsnorm scale, infer.c:746-752) and
+// xn = (x * inv) * ffn_norm (infer.c:751), written to a.xn for the router and
+// the GEMM gather.
 //
 // route_logits_kernel<NT, NE>: glm.c's router logits themselves, to the bit
 // (dot_f32, infer.c:916-938: s = 0; s = s + w[i] * xn[i], each product and
-// sum rounded to fp32, left to right). A CTA of 128 threads takes 8*NT tokens
-// x 16*NE experts; thread (ty, tx) carries the serial chains of its NT x NE
-// (token, expert) pairs, tokens ty + 8k and experts tx + 16j. The serial
-// order costs nothing here: with T tokens there are T x E independent chains
-// and each one is two fp32 instructions per element, fewer than any
-// reassociated sum with a rigorous error bound needs. D streams through a
-// double-buffered shared-memory tile in chunks of kLD elements: the router
-// rows by cp.async, xn computed on the way in (phase 1 takes each token's
-// certified rmsnorm scale; x * inv * ffn_norm as infer.c:751; the CTAs of
-// expert block 0 also store xn for the GEMM gather). Rows are padded by 4
-// floats, so the 8 router rows a quarter-warp reads fall in distinct bank
-// groups, and a token row is a broadcast. Rows past the end are zero: s + 0
-// is s for every s the chain can hold (it starts at +0, so it is never -0).
-// The select kernel receives each logit as a centre with bound 0.
+// sum rounded to fp32, left to right). Every (token, expert) pair is one
+// serial chain of two fp32 instructions per element -- fewer than any
+// reassociated sum with a rigorous error bound needs -- and with T tokens
+// there are T x E independent chains. A lane holds NT x NE chains (tokens
+// ty + 4k, experts tx + 8j of its warp's tile; ty = lane / 8, tx = lane % 8),
+// so one float4 of a token row and one of a router row feed NE and NT
+// chains: shared-memory traffic per instruction falls as NT x NE grows. Two
+// warps (stacked along the tokens) share the router rows. D streams through
+// a ring of kLD-element chunks (as many as ~100 KB holds), xn rows and router
+// rows both by cp.async. Rows are padded by 4 floats, so the 8 router rows a quarter-warp
+// reads fall in distinct bank groups; a token row is a broadcast. Rows past
+// the end are zero: s + 0 is s for every s the chain can hold (it starts at
+// +0, so it is never -0). The select kernel receives each logit as a centre
+// with bound 0.
 //
 // route_select_kernel: kRT tokens per CTA, 64 threads each on a named
 // barrier: the same certified top-k as the decode path (route_common.cuh),
@@ -120,11 +125,13 @@ __device__ __forceinline__ void split_bf16(float v, __nv_bfloat16& hi, __nv_bflo
 constexpr int kRouteRedo = -2;         // never a routing result (ids are -1 .. E-1)
 constexpr int kExactCtas = 296;        // route_exact_kernel CTAs (two per SM)
 constexpr int kSelRows = 8;            // router rows staged at a time by the exact fallback
-constexpr int kLTx = 16;               // logit CTA: threads along the experts
-constexpr int kLTy = 8;                // logit CTA: threads along the tokens
-constexpr int kLThreads = kLTx * kLTy;
+constexpr int kNormRegs = 16;          // float4 of a row a lane keeps (D <= 2048); longer rows are read twice
+constexpr int kLWarps = 2;             // logit CTA: warps, stacked along the tokens
+constexpr int kLThreads = 32 * kLWarps;
 constexpr int kLD = 128;               // D elements per staged chunk
+constexpr int kLPrefetch = 3;          // short tiles: steps between an operand load and its use
 constexpr int kLRow = kLD + 4;         // padded row, floats
+constexpr size_t kLRingBytes = 104 * 1024;  // logit CTA's chunk ring: two CTAs per SM
 constexpr int kRT = 1;                 // tokens per select CTA
 constexpr int kRThreads = 64 * kRT;
 
@@ -143,85 +150,115 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
-constexpr size_t route_logits_smem(int NT, int NE) {
-    return sizeof(float) * 2 * (size_t)(kLTy * NT + kLTx * NE) * kLRow;
+__global__ void __launch_bounds__(256) route_norm_kernel(PrefillRouteArgs a) {
+    const int lane = threadIdx.x & 31, t = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (t >= a.T) return;  // per-warp work only: no block barrier
+    const int D = a.D, n4 = D / 4;
+    const float4* xr = reinterpret_cast<const float4*>(a.x + (size_t)t * D);
+    const float4* nr = reinterpret_cast<const float4*>(a.norm);
+    float4* xo = reinterpret_cast<float4*>(a.xn + (size_t)t * D);
+    const bool in_regs = n4 <= 32 * kNormRegs;
+    float4 v[kNormRegs];
+    double ss = 0.0;
+    if (in_regs) {
+#pragma unroll
+        for (int k = 0; k < kNormRegs; ++k) {
+            const int c = lane + 32 * k;
+            v[k] = c < n4 ? xr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int k = 0; k < kNormRegs; ++k)
+            ss += (double)v[k].x * v[k].x + (double)v[k].y * v[k].y + (double)v[k].z * v[k].z +
+                  (double)v[k].w * v[k].w;
+    } else {
+        for (int c = lane; c < n4; c += 32) {
+            const float4 u = xr[c];
+            ss += (double)u.x * u.x + (double)u.y * u.y + (double)u.z * u.z + (double)u.w * u.w;
+        }
+    }
+    ss = warp_sum_d(ss);
+    float inv = 0.0f;
+    if (lane == 0) inv = rms_inv_certified(ss, a.x + (size_t)t * D, D, a.stats ? &a.stats[3] : nullptr);
+    inv = __shfl_sync(0xffffffffu, inv, 0);
+    auto out = [&](int c, float4 u) {
+        const float4 w = __ldg(nr + c);
+        float4 o;  // infer.c:751: (x * inv) * w
+        o.x = __fmul_rn(__fmul_rn(u.x, inv), w.x);
+        o.y = __fmul_rn(__fmul_rn(u.y, inv), w.y);
+        o.z = __fmul_rn(__fmul_rn(u.z, inv), w.z);
+        o.w = __fmul_rn(__fmul_rn(u.w, inv), w.w);
+        xo[c] = o;
+    };
+    if (in_regs) {
+#pragma unroll
+        for (int k = 0; k < kNormRegs; ++k)
+            if (lane + 32 * k < n4) out(lane + 32 * k, v[k]);
+    } else {
+        for (int c = lane; c < n4; c += 32) out(c, xr[c]);
+    }
+}
+
+// Chunks in flight: as many as kLRingBytes holds. A short tile computes a
+// chunk in a fraction of the L2 latency, so it needs the deeper ring.
+__host__ __device__ constexpr int route_logits_stages(int NT, int NE) {
+    return (int)(kLRingBytes / (sizeof(float) * (size_t)(kLWarps * 4 * NT + 8 * NE) * kLRow));
+}
+__host__ __device__ constexpr size_t route_logits_smem(int NT, int NE) {
+    return sizeof(float) * route_logits_stages(NT, NE) * (size_t)(kLWarps * 4 * NT + 8 * NE) * kLRow;
+}
+
+// Four elements of every chain of a lane: s = s + w * x, rounded per step
+// (infer.c:920-926).
+template <int NT, int NE>
+__device__ __forceinline__ void logit_step(float (&acc)[NT][NE], const float4 (&xq)[NT], const float4 (&wq)[NE]) {
+#pragma unroll
+    for (int k = 0; k < NT; ++k)
+#pragma unroll
+        for (int j = 0; j < NE; ++j) {
+            acc[k][j] = __fadd_rn(acc[k][j], __fmul_rn(wq[j].x, xq[k].x));
+            acc[k][j] = __fadd_rn(acc[k][j], __fmul_rn(wq[j].y, xq[k].y));
+            acc[k][j] = __fadd_rn(acc[k][j], __fmul_rn(wq[j].z, xq[k].z));
+            acc[k][j] = __fadd_rn(acc[k][j], __fmul_rn(wq[j].w, xq[k].w));
+        }
 }
 
 template <int NT, int NE>
-__global__ void __launch_bounds__(kLThreads) route_logits_kernel(PrefillRouteArgs a) {
-    constexpr int TT = kLTy * NT, TE = kLTx * NE;
-    constexpr int XI = TT * (kLD / 4) / kLThreads;  // float4 of x per thread per chunk
-    constexpr int WI = TE * (kLD / 4) / kLThreads;  // float4 of router rows per thread per chunk
-    static_assert(XI >= 1 && WI >= 1, "tile smaller than one float4 per thread");
+__global__ void __launch_bounds__(kLThreads, 1) route_logits_kernel(PrefillRouteArgs a) {
+    constexpr int TT = kLWarps * 4 * NT, TE = 8 * NE, ROWS = TT + TE;
+    constexpr int CP = ROWS * (kLD / 4) / kLThreads;  // cp.async per thread per chunk
+    constexpr int kLStages = route_logits_stages(NT, NE);
+    static_assert(kLStages >= 3, "the ring holds at least three chunks");
+    static_assert(ROWS * (kLD / 4) % kLThreads == 0, "chunk copies split evenly over the threads");
     extern __shared__ __align__(16) unsigned char smr[];
-    float* xs = reinterpret_cast<float*>(smr);  // [2][TT][kLRow]
-    float* ws = xs + 2 * TT * kLRow;            // [2][TE][kLRow]
-    __shared__ float inv_s[TT];
+    float* ring = reinterpret_cast<float*>(smr);  // [kLStages][ROWS][kLRow]: TT xn rows, then TE router rows
     const int D = a.D, E = a.E, T = a.T;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int ty = tid / kLTx, tx = tid % kLTx;
+    const int ty = lane >> 3, tx = lane & 7;
     const int t0 = blockIdx.x * TT, e0 = blockIdx.y * TE;
-    const bool first = blockIdx.y == 0;
     const int nch = D / kLD;
 
-    auto stage_w = [&](int c, int buf) {
-        float* dst = ws + buf * TE * kLRow;
+    auto stage = [&](int c, int slot) {
+        float* dst = ring + (size_t)slot * ROWS * kLRow;
 #pragma unroll
-        for (int k = 0; k < WI; ++k) {
-            const int q = tid + k * kLThreads, r = q >> 5, c4 = q & 31, e = e0 + r;
-            cp_async16(dst + r * kLRow + 4 * c4, a.router + (size_t)(e < E ? e : 0) * D + c * kLD + 4 * c4,
-                       e < E ? 16 : 0);
-        }
-        cp_async_commit();
-    };
-    float4 xv[XI];
-    auto load_x = [&](int c) {
-#pragma unroll
-        for (int k = 0; k < XI; ++k) {
-            const int q = tid + k * kLThreads, r = q >> 5, c4 = q & 31, t = t0 + r;
-            xv[k] = t < T ? *reinterpret_cast<const float4*>(a.x + (size_t)t * D + c * kLD + 4 * c4)
-                          : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-    };
-    auto store_x = [&](int c, int buf) {
-        float* dst = xs + buf * TT * kLRow;
-#pragma unroll
-        for (int k = 0; k < XI; ++k) {
-            const int q = tid + k * kLThreads, r = q >> 5, c4 = q & 31, t = t0 + r;
-            const float inv = inv_s[r];
-            const float4 nv = __ldg(reinterpret_cast<const float4*>(a.norm + c * kLD) + c4);
-            float4 v;  // infer.c:751: (x * inv) * w
-            v.x = __fmul_rn(__fmul_rn(xv[k].x, inv), nv.x);
-            v.y = __fmul_rn(__fmul_rn(xv[k].y, inv), nv.y);
-            v.z = __fmul_rn(__fmul_rn(xv[k].z, inv), nv.z);
-            v.w = __fmul_rn(__fmul_rn(xv[k].w, inv), nv.w);
-            if (t >= T) v = make_float4(0.f, 0.f, 0.f, 0.f);
-            *reinterpret_cast<float4*>(dst + r * kLRow + 4 * c4) = v;
-            if (first && t < T) *reinterpret_cast<float4*>(a.xn + (size_t)t * D + c * kLD + 4 * c4) = v;
-        }
-    };
-
-    stage_w(0, 0);  // the router rows do not depend on phase 1
-    load_x(0);
-    // phase 1: each token's rmsnorm scale (fp64 sum of squares, certified)
-    for (int r = warp; r < TT; r += kLThreads / 32) {
-        const int t = t0 + r;
-        float inv = 0.0f;
-        if (t < T) {
-            const float4* xr = reinterpret_cast<const float4*>(a.x + (size_t)t * D);
-            double ss = 0.0;
-            for (int c = lane; c < D / 4; c += 32) {
-                const float4 v = xr[c];
-                ss += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+        for (int k = 0; k < CP; ++k) {
+            const int q = tid + k * kLThreads, r = q >> 5, c4 = q & 31;
+            const float* src;
+            bool ok;
+            if (r < TT) {
+                ok = t0 + r < T;
+                src = a.xn + (size_t)(ok ? t0 + r : 0) * D;
+            } else {
+                ok = e0 + r - TT < E;
+                src = a.router + (size_t)(ok ? e0 + r - TT : 0) * D;
             }
-            ss = warp_sum_d(ss);
-            if (lane == 0)
-                inv = rms_inv_certified(ss, a.x + (size_t)t * D, D, (a.stats && first) ? &a.stats[3] : nullptr);
+            cp_async16(dst + r * kLRow + 4 * c4, src + c * kLD + 4 * c4, ok ? 16 : 0);
         }
-        if (lane == 0) inv_s[r] = inv;
+    };
+#pragma unroll
+    for (int s = 0; s < kLStages - 1; ++s) {
+        if (s < nch) stage(s, s);
+        cp_async_commit();  // one group per chunk, empty past the end
     }
-    __syncthreads();
-    store_x(0, 0);
 
     float acc[NT][NE];
 #pragma unroll
@@ -229,42 +266,48 @@ __global__ void __launch_bounds__(kLThreads) route_logits_kernel(PrefillRouteArg
 #pragma unroll
         for (int j = 0; j < NE; ++j) acc[k][j] = 0.0f;
     for (int c = 0; c < nch; ++c) {
-        const int buf = c & 1;
-        if (c + 1 < nch) {
-            stage_w(c + 1, buf ^ 1);
-            load_x(c + 1);
-            cp_async_wait<1>();
+        cp_async_wait<kLStages - 2>();  // this thread's copies of chunk c have landed
+        __syncthreads();                // everyone's have; chunk c - 1's slot is free
+        if (c + kLStages - 1 < nch) stage(c + kLStages - 1, (c + kLStages - 1) % kLStages);
+        cp_async_commit();
+        const float* base = ring + (size_t)(c % kLStages) * ROWS * kLRow;
+        const float* xb = base + (warp * 4 * NT + ty) * kLRow;
+        const float* wb = base + (TT + tx) * kLRow;
+        if constexpr (NT * NE >= 16) {
+            // enough independent chains per lane to cover the shared-memory latency
+#pragma unroll 2
+            for (int i = 0; i < kLD; i += 4) {
+                float4 xq[NT], wq[NE];
+#pragma unroll
+                for (int k = 0; k < NT; ++k) xq[k] = *reinterpret_cast<const float4*>(xb + 4 * k * kLRow + i);
+#pragma unroll
+                for (int j = 0; j < NE; ++j) wq[j] = *reinterpret_cast<const float4*>(wb + 8 * j * kLRow + i);
+                logit_step<NT, NE>(acc, xq, wq);
+            }
         } else {
-            cp_async_wait<0>();
-        }
-        __syncthreads();  // chunk c's rows are in shared memory
-        const float* xb = xs + (buf * TT + ty) * kLRow;
-        const float* wb = ws + (buf * TE + tx) * kLRow;
-#pragma unroll 4
-        for (int i = 0; i < kLD; i += 4) {
-            float4 xq[NT], wq[NE];
+            // few chains: each step's operands are loaded kLPrefetch steps ahead (a
+            // step's dependent adds take less time than a shared-memory load)
+            float4 xq[kLPrefetch][NT], wq[kLPrefetch][NE];
 #pragma unroll
-            for (int k = 0; k < NT; ++k) xq[k] = *reinterpret_cast<const float4*>(xb + k * kLTy * kLRow + i);
+            for (int st = 0; st < kLD / 4 + kLPrefetch; ++st) {
+                if (st >= kLPrefetch) logit_step<NT, NE>(acc, xq[st % kLPrefetch], wq[st % kLPrefetch]);
+                if (st < kLD / 4) {
 #pragma unroll
-            for (int j = 0; j < NE; ++j) wq[j] = *reinterpret_cast<const float4*>(wb + j * kLTx * kLRow + i);
+                    for (int k = 0; k < NT; ++k)
+                        xq[st % kLPrefetch][k] = *reinterpret_cast<const float4*>(xb + 4 * k * kLRow + 4 * st);
 #pragma unroll
-            for (int k = 0; k < NT; ++k)
-#pragma unroll
-                for (int j = 0; j < NE; ++j) {
-                    acc[k][j] = __fadd_rn(acc[k][j], __fmul_rn(wq[j].x, xq[k].x));
-                    acc[k][j] = __fadd_rn(acc[k][j], __fmul_rn(wq[j].y, xq[k].y));
-                    acc[k][j] = __fadd_rn(acc[k][j], __fmul_rn(wq[j].z, xq[k].z));
-                    acc[k][j] = __fadd_rn(acc[k][j], __fmul_rn(wq[j].w, xq[k].w));
+                    for (int j = 0; j < NE; ++j)
+                        wq[st % kLPrefetch][j] = *reinterpret_cast<const float4*>(wb + 8 * j * kLRow + 4 * st);
                 }
+            }
         }
-        if (c + 1 < nch) store_x(c + 1, buf ^ 1);
-        __syncthreads();  // chunk c's buffer is free for chunk c + 2
     }
+    cp_async_wait<0>();  // no copy outlives the CTA (the trailing groups are empty)
 #pragma unroll
     for (int k = 0; k < NT; ++k)
 #pragma unroll
         for (int j = 0; j < NE; ++j) {
-            const int t = t0 + ty + k * kLTy, e = e0 + tx + j * kLTx;
+            const int t = t0 + warp * 4 * NT + ty + 4 * k, e = e0 + tx + 8 * j;
             if (t < T && e < E) {
                 a.cen[(size_t)t * E + e] = (double)acc[k][j];
                 a.bnd[(size_t)t * E + e] = 0.0;
@@ -360,24 +403,32 @@ __global__ void __launch_bounds__(64) route_exact_kernel(PrefillRouteArgs a) {
     }
 }
 
-// The logit tile: 16 tokens x 32 experts per CTA (four chains a thread) when
-// that still gives two CTAs per SM, else 8 x 16 (one chain a thread) for more
-// CTAs on a small batch.
 template <int NT, int NE>
-cudaError_t launch_route_logits(const PrefillRouteArgs& ra, int num_sms, cudaStream_t st) {
+cudaError_t launch_route_logits(const PrefillRouteArgs& ra, cudaStream_t st) {
     const size_t smem = route_logits_smem(NT, NE);
     cudaError_t err = ensure_smem_attr(reinterpret_cast<const void*>(route_logits_kernel<NT, NE>), (int)smem);
     if (err) return err;
-    const dim3 grid((ra.T + kLTy * NT - 1) / (kLTy * NT), (ra.E + kLTx * NE - 1) / (kLTx * NE));
-    route_logits_kernel<NT, NE><<<grid, kLThreads, smem, st>>>(ra);
+    const int tt = kLWarps * 4 * NT, te = 8 * NE;
+    route_logits_kernel<NT, NE><<<dim3((ra.T + tt - 1) / tt, (ra.E + te - 1) / te), kLThreads, smem, st>>>(ra);
     return cudaGetLastError();
+}
+
+// The largest per-lane chain tile (shared-memory traffic per instruction
+// falls with it) that still gives every SM a CTA; a small batch takes short
+// tiles, since a lane's chains run one after another.
+cudaError_t launch_route_logit_tiles(const PrefillRouteArgs& ra, int num_sms, cudaStream_t st) {
+    auto ctas = [&](int nt, int ne) {
+        return (long)((ra.T + kLWarps * 4 * nt - 1) / (kLWarps * 4 * nt)) * ((ra.E + 8 * ne - 1) / (8 * ne));
+    };
+    if (ctas(4, 4) >= num_sms) return launch_route_logits<4, 4>(ra, st);
+    if (ctas(2, 2) >= num_sms) return launch_route_logits<2, 2>(ra, st);
+    return launch_route_logits<1, 2>(ra, st);
 }
 
 cudaError_t launch_route_batched(const PrefillRouteArgs& ra, int num_sms, cudaStream_t st) {
     if (ra.D % kLD) return cudaErrorInvalidValue;
-    const long big = (long)((ra.T + 15) / 16) * ((ra.E + 31) / 32);
-    cudaError_t err = big >= 2L * num_sms ? launch_route_logits<2, 2>(ra, num_sms, st)
-                                          : launch_route_logits<1, 1>(ra, num_sms, st);
+    route_norm_kernel<<<(ra.T + 7) / 8, 256, 0, st>>>(ra);
+    cudaError_t err = launch_route_logit_tiles(ra, num_sms, st);
     if (err) return err;
     const size_t smem2 = (size_t)kRT * (2 * ra.E * sizeof(double) + 5 * ra.E * sizeof(float) + 64 * sizeof(int));
     if ((err = ensure_smem_attr(reinterpret_cast<const void*>(route_select_kernel), (int)smem2))) return err;
