@@ -97,6 +97,12 @@ struct Model {
     unsigned* amax_count = nullptr;   // argmax last-CTA counter
     int prompt_cap = 0, out_cap = 0;
     int* io_host = nullptr;  // pinned [2]: token, pos
+    // batched prompt pass (glm_cuda_prefill)
+    float* pf_x = nullptr;    // [pf_cap][dim] the batch's residual rows
+    int* pf_pos = nullptr;    // [pf_cap] their positions
+    int* pf_tok = nullptr;    // [pf_cap] their token ids (clamped as infer.c:2219)
+    int* pf_host = nullptr;   // pinned [2 * pf_cap]: ids, then positions
+    int pf_cap = 0;
 };
 
 struct State {
@@ -124,6 +130,7 @@ struct State {
     // batched prefill (calls with n_tokens >= prefill_min_tokens)
     bool prefill_ok = false;   // sizes fit the prefill kernels
     int prefill_min_tokens = 32;
+    int model_prefill_min = 0; // glm_cuda_generate: batched prompt pass from this many prompt tokens (0 = off)
     unsigned char* pf_ws = nullptr;
     size_t pf_ws_cap = 0;
     // expert parallelism (glm_cuda_ep_setup): routed weights hold this shard's experts
@@ -186,10 +193,11 @@ void release_model() {
     for (void* p : m.owned_globals) cudaFree(p);
     void* bufs[] = {m.x,     m.xn,        m.q_a,      m.q_full, m.kv_a,   m.att,    m.ff_gate, m.ff_up,
                     m.logits, m.cache_comp, m.cache_pe, m.pos,    m.token,  m.argmax, m.prompt,  m.out_ids,
-                    m.amax_part, m.amax_count};
+                    m.amax_part, m.amax_count, m.pf_x, m.pf_pos, m.pf_tok};
     for (void* p : bufs)
         if (p) cudaFree(p);
     if (m.io_host) cudaFreeHost(m.io_host);
+    if (m.pf_host) cudaFreeHost(m.pf_host);
     g.m = Model{};
 }
 
@@ -231,6 +239,7 @@ void release_all() {
     g.pf_ws_cap = 0;
     g.prefill_ok = false;
     g.prefill_min_tokens = 32;
+    g.model_prefill_min = 0;
     g.scratch = glmq::MoeScratch{};
     g.x_dev = nullptr;
     g.idx_dev = nullptr;
@@ -1075,6 +1084,96 @@ int enqueue_step(cudaStream_t st) {
     return 0;
 }
 
+// Positions pf_pos[0 .. T) (consecutive, ids in pf_tok) through every layer
+// as one batch, layer by layer: per layer each token's attention in position
+// order -- the causal order of infer.c's token loop (infer.c:2190-2233), so
+// token t reads the cache rows that this pass wrote for the tokens before it
+// -- then the FFN of all T tokens at once: the batched MoE kernels read each
+// touched expert's weights once per layer instead of once per token. The
+// attention kernels are the decode step's, so the cache rows are the ones
+// token-by-token decoding writes. Leaves the batch's residual rows in pf_x.
+int enqueue_prefill(int T, cudaStream_t st) {
+    Model& m = g.m;
+    const GlmCudaModelDims& d = m.d;
+    const int D = d.dim, gs = d.group_size, ns = g.num_sms;
+    const int routed = routed_disabled_by_env() ? 0 : 1;
+    const float kq_scale = 1.0f / sqrtf((float)d.head_k_dim);
+    for (int t = 0; t < T; ++t)
+        LAUNCH_TRY(glmq::launch_embed(m.tok_q, m.tok_s, m.pf_tok + t, m.pf_x + (size_t)t * D, D, gs, st));
+    g.launches += (unsigned long long)T;
+    for (int l = 0; l < d.n_layers; ++l) {
+        const AttnLayer& A = m.attn[l];
+        float* comp = m.cache_comp + (size_t)l * d.cache_cap * d.kv_lora_rank;
+        float* pe = m.cache_pe + (size_t)l * d.cache_cap * d.rope_dim;
+        for (int t = 0; t < T; ++t) {
+            float* xt = m.pf_x + (size_t)t * D;
+            LAUNCH_TRY(glmq::launch_q80_matvec2(A.q_a_q, A.q_a_s, m.q_a, d.q_lora_rank, A.kv_a_q, A.kv_a_s, m.kv_a,
+                                                d.kv_lora_rank + d.rope_dim, xt, D, gs, ns, st, A.attn_norm));
+            LAUNCH_TRY(glmq::launch_q80_matvec(A.q_b_q, A.q_b_s, m.q_a, m.q_full, d.n_heads * d.head_k_dim,
+                                               d.q_lora_rank, gs, ns, st, false, A.q_a_norm));
+            glmq::MlaArgs ma{m.q_full,       m.kv_a,        A.kv_a_norm,  comp,          pe,
+                             A.k_b_q,        A.k_b_s,       A.v_b_q,      A.v_b_s,       m.att,
+                             m.pf_pos + t,   d.qk_nope_dim, d.rope_dim,   d.head_k_dim,  d.kv_lora_rank,
+                             d.v_head_dim,   gs,            d.cache_cap,  kq_scale};
+            LAUNCH_TRY(glmq::launch_mla(ma, d.n_heads, st));
+            LAUNCH_TRY(glmq::launch_q80_matvec(A.attn_out_q, A.attn_out_s, m.att, xt, D, d.n_heads * d.v_head_dim,
+                                               gs, ns, st, true));
+            if (l == 0) {  // dense SwiGLU FFN (infer.c:1067-1085), token by token
+                LAUNCH_TRY(glmq::launch_q80_matvec(m.l0_gate_q, m.l0_gate_s, xt, m.ff_gate, d.hidden_dim, D, gs, ns,
+                                                   st, false, m.l0_norm));
+                LAUNCH_TRY(glmq::launch_q80_matvec(m.l0_up_q, m.l0_up_s, xt, m.ff_up, d.hidden_dim, D, gs, ns, st,
+                                                   false, m.l0_norm));
+                LAUNCH_TRY(glmq::launch_silu_mul(m.ff_gate, m.ff_up, d.hidden_dim, ns, st));
+                LAUNCH_TRY(glmq::launch_q80_matvec(m.l0_down_q, m.l0_down_s, m.ff_gate, xt, D, d.hidden_dim, gs, ns,
+                                                   st, true));
+                g.launches += 4;
+            }
+        }
+        g.launches += 4ull * (unsigned long long)T;  // q_a + kv_a, q_b, MLA, attention output
+        if (l > 0) {
+            LAUNCH_TRY(glmq::launch_moe_prefill(g.layers[l].w, g.dims, g.pf_ws, m.pf_x, T, nullptr, nullptr, routed,
+                                                ns, g.scratch.status, g.scratch.stats, st));
+            g.launches += 9;
+        }
+    }
+    return 0;
+}
+
+// Room for a batch of T prompt tokens and its positions / ids.
+int ensure_model_prefill(int T) {
+    Model& m = g.m;
+    if (!g.prefill_ok) return fail(GLM_CUDA_ERR_STATE, "the batched prompt pass needs the prefill kernels (unsupported dims)");
+    if (int rc = ensure_prefill_ws(T)) return rc;
+    if (T <= m.pf_cap) return 0;
+    if (m.pf_x) cudaFree(m.pf_x);
+    if (m.pf_pos) cudaFree(m.pf_pos);
+    if (m.pf_tok) cudaFree(m.pf_tok);
+    if (m.pf_host) cudaFreeHost(m.pf_host);
+    m.pf_x = nullptr;
+    m.pf_pos = m.pf_tok = m.pf_host = nullptr;
+    m.pf_cap = 0;
+    if (int rc = dev_alloc(&m.pf_x, (size_t)T * m.d.dim)) return rc;
+    if (int rc = dev_alloc(&m.pf_pos, T)) return rc;
+    if (int rc = dev_alloc(&m.pf_tok, T)) return rc;
+    CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&m.pf_host), 2 * sizeof(int) * (size_t)T, cudaHostAllocDefault));
+    m.pf_cap = T;
+    return 0;
+}
+
+// Stage the ids (clamped to the vocabulary as infer.c:2219) and positions
+// start_pos .. start_pos + T - 1 of a batch.
+int stage_prefill_batch(const int32_t* tokens, int T, int start_pos, cudaStream_t st) {
+    Model& m = g.m;
+    for (int t = 0; t < T; ++t) {
+        const int id = tokens[t];
+        m.pf_host[t] = (id < 0 || id >= m.d.vocab_size) ? 0 : id;
+        m.pf_host[m.pf_cap + t] = start_pos + t;
+    }
+    CUDA_TRY(cudaMemcpyAsync(m.pf_tok, m.pf_host, sizeof(int) * (size_t)T, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(m.pf_pos, m.pf_host + m.pf_cap, sizeof(int) * (size_t)T, cudaMemcpyHostToDevice, st));
+    return 0;
+}
+
 int status_check_sync() {
     CUDA_TRY(cudaMemcpyAsync(g.status_host, g.scratch.status, sizeof(unsigned int), cudaMemcpyDeviceToHost, g.stream));
     CUDA_TRY(cudaStreamSynchronize(g.stream));
@@ -1241,6 +1340,37 @@ int glm_cuda_forward_token(int token, int pos, float* logits) {
     return status_check_sync();
 }
 
+int glm_cuda_prefill(const int32_t* tokens, int n_tokens, int start_pos, float* logits) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (int rc = check_model()) return rc;
+    Model& m = g.m;
+    if (!tokens || n_tokens < 1) return fail(GLM_CUDA_ERR_ARG, "prefill: tokens must be non-NULL and n_tokens >= 1");
+    if (start_pos < 0 || start_pos + n_tokens > m.d.cache_cap)
+        return fail(GLM_CUDA_ERR_ARG, "prefill: positions [%d,%d) outside the cache [0,%d)", start_pos,
+                    start_pos + n_tokens, m.d.cache_cap);
+    if (int rc = ensure_model_prefill(n_tokens)) return rc;
+    cudaStream_t st = g.stream;
+    if (int rc = stage_prefill_batch(tokens, n_tokens, start_pos, st)) return rc;
+    if (int rc = enqueue_prefill(n_tokens, st)) return rc;
+    if (logits) {
+        // the last token's logits: final norm (fused) and LM head (infer.c:1888-1893)
+        LAUNCH_TRY(glmq::launch_q80_matvec(m.out_q, m.out_s, m.pf_x + (size_t)(n_tokens - 1) * m.d.dim, m.logits,
+                                           m.d.vocab_size, m.d.dim, m.d.group_size, g.num_sms, st, false,
+                                           m.output_norm));
+        g.launches += 1;
+        CUDA_TRY(cudaMemcpyAsync(logits, m.logits, sizeof(float) * m.d.vocab_size, cudaMemcpyDeviceToHost, st));
+    }
+    return status_check_sync();
+}
+
+int glm_cuda_set_model_prefill(int min_tokens) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.inited) return fail(GLM_CUDA_ERR_STATE, "glm_cuda_init has not been called");
+    if (min_tokens < 0) return fail(GLM_CUDA_ERR_ARG, "min_tokens must be >= 0");
+    g.model_prefill_min = min_tokens;
+    return 0;
+}
+
 int glm_cuda_generate(const int32_t* prompt, int n_prompt, int n_gen, int32_t* out_ids, float* device_ms) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (int rc = check_model()) return rc;
@@ -1264,11 +1394,17 @@ int glm_cuda_generate(const int32_t* prompt, int n_prompt, int n_gen, int32_t* o
         m.out_cap = n_gen;
     }
     cudaStream_t st = g.stream;
+    // positions [0, n_batch) as one batched pass, the rest step by step
+    const int n_batch = (g.model_prefill_min > 0 && n_prompt - 1 >= g.model_prefill_min) ? n_prompt - 1 : 0;
+    if (n_batch) {
+        if (int rc = ensure_model_prefill(n_batch)) return rc;
+        if (int rc = stage_prefill_batch(prompt, n_batch, 0, st)) return rc;
+    }
     CUDA_TRY(cudaMemcpyAsync(m.prompt, prompt, sizeof(int32_t) * n_prompt, cudaMemcpyHostToDevice, st));
-    int first = prompt[0];
+    int first = prompt[n_batch];
     if (first < 0 || first >= m.d.vocab_size) first = 0;
     m.io_host[0] = first;
-    m.io_host[1] = 0;
+    m.io_host[1] = n_batch;
     CUDA_TRY(cudaMemcpyAsync(m.token, &m.io_host[0], sizeof(int), cudaMemcpyHostToDevice, st));
     CUDA_TRY(cudaMemcpyAsync(m.pos, &m.io_host[1], sizeof(int), cudaMemcpyHostToDevice, st));
     // One decode step (+ picking the next token) captured once, replayed
@@ -1297,7 +1433,16 @@ int glm_cuda_generate(const int32_t* prompt, int n_prompt, int n_gen, int32_t* o
         cudaEventCreate(&ev[1]);
         cudaEventRecord(ev[0], st);
     }
-    const int steps = n_prompt + n_gen - 1;
+    if (n_batch) {
+        if (int prc = enqueue_prefill(n_batch, st)) {
+            cudaStreamSynchronize(st);
+            for (auto e : ev)
+                if (e) cudaEventDestroy(e);
+            cudaGraphExecDestroy(exec);
+            return prc;
+        }
+    }
+    const int steps = n_prompt - n_batch + n_gen - 1;
     for (int i = 0; i < steps && ec == cudaSuccess; ++i) ec = cudaGraphLaunch(exec, st);
     if (device_ms) cudaEventRecord(ev[1], st);
     g.launches += (unsigned long long)steps;

@@ -57,6 +57,8 @@ def _signatures(L: ctypes.CDLL) -> None:
     L.glm_cuda_bind_attn_layer_device.argtypes = [_I] + [_P] * 15
     L.glm_cuda_forward_token.argtypes = [_I, _I, _P]
     L.glm_cuda_generate.argtypes = [_P, _I, _I, _P, _P]
+    L.glm_cuda_prefill.argtypes = [_P, _I, _I, _P]
+    L.glm_cuda_set_model_prefill.argtypes = [_I]
     L.glm_cuda_set_decode_path.argtypes = [_I]
     L.glm_cuda_decode_path.argtypes = []
     L.glm_cuda_set_prefill_tokens.argtypes = [_I]
@@ -95,7 +97,7 @@ def _signatures(L: ctypes.CDLL) -> None:
                  "glm_cuda_ep_p2p_counts",
                  "glm_cuda_model_init", "glm_cuda_upload_model_globals", "glm_cuda_bind_model_globals_device",
                  "glm_cuda_upload_attn_layer", "glm_cuda_bind_attn_layer_device", "glm_cuda_forward_token",
-                 "glm_cuda_generate",
+                 "glm_cuda_generate", "glm_cuda_prefill", "glm_cuda_set_model_prefill",
                  "glm_cuda_matvec_q80",
                  "glm_cuda_matvec_q80_async", "glm_cuda_synchronize", "glm_cuda_route_stats"):
         getattr(L, name).restype = _I
@@ -212,6 +214,17 @@ class GlmCuda:
         self._check("glm_cuda_generate", self.L.glm_cuda_generate(_ptr(p), len(p), n_gen, _ptr(out),
                                                                    ctypes.addressof(ms)))
         return out, float(ms.value)
+
+    def prefill(self, tokens, start_pos: int = 0, vocab: int | None = None):
+        """The batched prompt pass over positions start_pos .. + len(tokens) - 1;
+        the last token's logits when vocab is given."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        logits = np.zeros(vocab, dtype=np.float32) if vocab else None
+        self._check("glm_cuda_prefill", self.L.glm_cuda_prefill(_ptr(t), len(t), start_pos, _ptr(logits)))
+        return logits
+
+    def set_model_prefill(self, min_tokens: int) -> None:
+        self._check("glm_cuda_set_model_prefill", self.L.glm_cuda_set_model_prefill(min_tokens))
 
     def set_decode_path(self, path: int) -> None:
         self._check("glm_cuda_set_decode_path", self.L.glm_cuda_set_decode_path(path))

@@ -338,6 +338,28 @@ int glm_cuda_forward_token(int token, int pos, float *logits);
  * device time of the n_prompt + n_gen - 1 steps. */
 int glm_cuda_generate(const int32_t *prompt, int n_prompt, int n_gen, int32_t *out_ids, float *device_ms);
 
+/* Batched prompt pass: positions start_pos .. start_pos + n_tokens - 1 with
+ * ids tokens[0 .. n_tokens) (clamped to the vocabulary as infer.c:2219)
+ * through every layer as one batch, writing their KV-cache rows: what
+ * n_tokens calls of glm_backend_forward_token in glm.c's prompt loop
+ * (infer.c:2190-2233) leave behind, with the layers taken one at a time.
+ * Per layer, each token's attention runs in position order on the decode
+ * kernels (the causal order: token t reads the rows written for the tokens
+ * before it). Then the FFN of the whole batch runs at once on the batched
+ * MoE kernels, which read each touched expert's weights once per layer.
+ * Expert ids are glm.c's.
+ * The residual rows agree with token-by-token decoding to ~1e-5 relative
+ * (the grouped GEMMs' bf16-pair products). logits (host, vocab_size
+ * floats, may be NULL) receive the last token's LM-head output. Needs the
+ * batched MoE kernels (dim and moe_ffn_dim multiples of 128). */
+int glm_cuda_prefill(const int32_t *tokens, int n_tokens, int start_pos, float *logits);
+
+/* glm_cuda_generate runs prompts of n_prompt - 1 >= min_tokens through
+ * glm_cuda_prefill's batched pass for positions 0 .. n_prompt - 2, then
+ * decodes step by step from position n_prompt - 1. 0 (the default) keeps
+ * the token-by-token prompt loop. */
+int glm_cuda_set_model_prefill(int min_tokens);
+
 /* Release all device memory and state. Replaces glm_backend_free's device
  * part (backend.c:93-95, glm_metal_free). Safe to call twice. */
 /* glm.c's runtime checkpoint (.bin, format version 4 with every layer's

@@ -70,6 +70,38 @@ def test_decoder_small_greedy_and_logits(path, lib, pkg, oracle_mod):
     assert worst <= TOL_LOGITS
 
 
+def test_model_prefill_small(lib, pkg, oracle_mod):
+    """The batched prompt pass (glm_cuda_prefill): the prompt through every
+    layer as one batch leaves the cache that token-by-token decoding leaves.
+    Its last-token logits match the reference's first generating step, and
+    decoding continues from that cache with the reference's greedy ids, both
+    step by step and through glm_cuda_generate."""
+    synth = pkg.synth
+    model = synth.decoder_model(12, **SMALL)
+    prompt = synth.prompt_ids(12, 8, SMALL["vocab_size"])
+    n_gen, cap = 12, 8 + 12 + 8
+    ids_ref, logits_ref = oracle_mod.ref_decode(model, prompt, n_gen, cap, with_logits=True)
+    load_model(lib, model, cap)
+    logits = lib.prefill(prompt, 0, SMALL["vocab_size"])
+    err = rel_l2(logits, logits_ref[0], logits_ref[0])
+    assert err <= TOL_LOGITS, err
+    assert int(np.argmax(logits)) == ids_ref[0]
+    worst = err
+    for g in range(1, n_gen):  # decode from the batch's cache
+        logits = lib.forward_token(int(ids_ref[g - 1]), len(prompt) + g - 1, SMALL["vocab_size"])
+        worst = max(worst, rel_l2(logits, logits_ref[g], logits_ref[g]))
+        assert int(np.argmax(logits)) == ids_ref[g]
+    assert worst <= TOL_LOGITS
+    lib.set_model_prefill(1)
+    try:
+        ids, ms = lib.generate(prompt, n_gen)
+    finally:
+        lib.set_model_prefill(0)
+    np.testing.assert_array_equal(ids, ids_ref)
+    assert_routing_exact(lib)
+    print(f"batched prompt pass: last-token logits rel L2 {err:.2e}, worst {worst:.2e}; generate {ms:.2f} ms")
+
+
 def test_decoder_config2_shapes_greedy(lib, pkg, oracle_mod):
     """GLM-4.7-Flash shapes (20 heads, q_lora 768, kv_lora 512, rope 64, vocab
     154880, dense 10240, config-0 MoE) with 3 layers: 16 prompt ids, greedy."""
@@ -83,6 +115,13 @@ def test_decoder_config2_shapes_greedy(lib, pkg, oracle_mod):
     ids, ms = lib.generate(prompt, n_gen)
     print(f"config-2 shapes x3 layers: {ids.tolist()} ({ms:.2f} ms)")
     np.testing.assert_array_equal(ids, ids_ref)
+    lib.set_model_prefill(1)  # the 16-token prompt as one batch, then decode
+    try:
+        ids2, ms2 = lib.generate(prompt, n_gen)
+    finally:
+        lib.set_model_prefill(0)
+    print(f"  with the batched prompt pass: {ids2.tolist()} ({ms2:.2f} ms)")
+    np.testing.assert_array_equal(ids2, ids_ref)
 
 
 def test_decoder_config2_full_greedy_100(lib, pkg, oracle_mod):
@@ -105,3 +144,11 @@ def test_decoder_config2_full_greedy_100(lib, pkg, oracle_mod):
     steps = len(prompt) + n_gen - 1
     print(f"config 2 full: {steps} steps in {ms:.1f} ms ({1000.0 * steps / ms:.1f} tok/s); first ids {ids[:8].tolist()}")
     np.testing.assert_array_equal(ids, ids_ref)
+    # the 16-token prompt through all 47 layers as one batch, then 100 greedy steps
+    lib.set_model_prefill(1)
+    try:
+        ids2, ms2 = lib.generate(prompt, n_gen)
+    finally:
+        lib.set_model_prefill(0)
+    print(f"config 2 full, batched prompt pass: {ms2:.1f} ms; first ids {ids2[:8].tolist()}")
+    np.testing.assert_array_equal(ids2, ids_ref)
