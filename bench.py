@@ -632,6 +632,21 @@ def run_decode_leg(args, torch, pkg, lib, layers, dev, local, rank, world) -> di
     g = int(np.argmin(gaps))
     decode["greedy_margin"] = {"min_top1_minus_top2": round(gaps[g], 6), "at_step": g,
                                "median": round(float(np.median(gaps)), 5), "argmax_agrees": agree}
+    # The same generation with the prompt positions as one batched pass
+    # (glm_cuda_prefill through every layer), then step by step.
+    lib.set_model_prefill(1)
+    try:
+        lib.generate(prompt, args.decode_gen)  # warm-up (workspace)
+        runs2 = []
+        for _ in range(args.decode_reps):
+            ids2, ms2 = lib.generate(prompt, args.decode_gen)
+            runs2.append(ms2)
+    finally:
+        lib.set_model_prefill(0)
+    decode["batched_prompt"] = {
+        "generate_ms": round(statistics.median(runs2), 3), "token_loop_generate_ms": round(statistics.median(runs), 3),
+        "prompt_positions": args.decode_prompt - 1, "ids_identical": bool((ids2 == ids).all()),
+        "api": "glm_cuda_set_model_prefill(1) + glm_cuda_generate (glm_cuda_prefill for positions 0 .. prompt-2)"}
     del glob, attn
 
     return decode
