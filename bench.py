@@ -647,6 +647,10 @@ def run_decode_leg(args, torch, pkg, lib, layers, dev, local, rank, world) -> di
         "generate_ms": round(statistics.median(runs2), 3), "token_loop_generate_ms": round(statistics.median(runs), 3),
         "prompt_positions": args.decode_prompt - 1, "ids_identical": bool((ids2 == ids).all()),
         "api": "glm_cuda_set_model_prefill(1) + glm_cuda_generate (glm_cuda_prefill for positions 0 .. prompt-2)"}
+    # the decoder's own per-token routings over this leg (model_init starts
+    # the counters at zero): calls, interval fallbacks, expf-last-bit ties,
+    # rmsnorm fallbacks
+    decode["route_stats"] = lib.route_stats()
     del glob, attn
 
     return decode
@@ -1089,11 +1093,12 @@ def run_ours(args) -> None:
 
     # Full config-2 decoder (greedy, glm_cuda_generate) on the same 46 MoE
     # layers plus device-generated attention / embedding / LM head weights.
+    # the headline workload's routing statistics, before the decoder leg adds
+    # its own routings to the same counters
+    route_stats = lib.route_stats()
     decode = None
     if N_MOE_LAYERS == 46 and not args.no_decode:
         decode = run_decode_leg(args, torch, pkg, lib, layers, dev, local, rank, world)
-
-    route_stats = lib.route_stats()
     matvec = None if args.no_matvec else run_matvec_leg(torch, lib, dev, world)
     gs16 = None
     if not args.no_gs16 and N_MOE_LAYERS == 46:
@@ -1151,8 +1156,12 @@ def run_ours(args) -> None:
         print(json.dumps(line))
     lib.free()
     del graphs
-    # a routing that hinged on the last bit of expf may differ from glm.c's:
-    # the line above stands as measured, but the run fails
+    # A routing that hinged on the last bit of expf may differ from glm.c's
+    # on the same layer input: the line above stands as measured, but the
+    # run fails. The decoder's count is reported in its own object and does
+    # not fail the run: its layer inputs already differ from glm.c's by fp32
+    # reassociation (attention, matvecs), so its parity with glm.c is judged
+    # by the greedy ids (tests/test_decoder_gpu.py), not per routing.
     unresolved = route_stats[2] + (prefill["route_stats"][2] if prefill else 0) + (gs16["route_stats"][2] if gs16 else 0)
     if unresolved:
         print(f"[bench] {unresolved} routings were not certified exact (route_stats[2])", file=sys.stderr)

@@ -787,8 +787,8 @@ __global__ void __launch_bounds__(PCfg<kGS>::kThreads, 1) moe_persistent_kernel(
         if (c < E) {
             cons_wait(P, it);
             double C = 0.0, B = 0.0;
-            block_logit_bound_rows(reinterpret_cast<const float*>(slot_buf(P, it)), xs, D, tid, kPConsThreads, rscr,
-                                   sync, C, B);
+            block_logit_bound_rows<(64 + kPCons - 1) / kPCons>(reinterpret_cast<const float*>(slot_buf(P, it)), xs, D,
+                                                               tid, kPConsThreads, rscr, sync, C, B);
             release_shared_item(it);  // the row was read before the function's first barrier
             ++it;
             if (tid == 0) {

@@ -104,37 +104,43 @@ __device__ __forceinline__ float serial_logit(const float* wrow, const float* xs
 // The reference's serial sum is within u * sum_i |its prefix_i| of the exact
 // sum; the returned bound B covers that plus the centre's own error.
 // `scratch` holds 64 + 5 * (nthreads/32) floats. C, B are returned in thread 0.
-template <typename Sync>
+template <int kR, typename Sync>
 __device__ __forceinline__ void block_logit_bound_rows(const float* wr, const float* xs, int D, int tid, int nthreads,
                                                        float* scratch, Sync sync, double& C, double& B) {
     const int lane = tid & 31, warp = tid >> 5, nwarps = nthreads >> 5;
-    const int rows = D >> 5;
+    const int rows = D >> 5;  // at most kR * nwarps
     float* rowtot = scratch;  // [64]
     float* w_hi = scratch + 64;
     float* w_lo = w_hi + nwarps;
     float* w_sabs = w_lo + nwarps;
     float* w_abs = w_sabs + nwarps;
     float* w_absT = w_abs + nwarps;
-    // A row's product and its inclusive fp32 warp scan Q_{k,l} (recomputed
-    // where needed again rather than kept: runtime loops keep this code short).
-    auto row_scan = [&](int k, float& p) {
-        p = __fmul_rn(wr[32 * k + lane], xs[32 * k + lane]);
-        float v = p;
+    // This warp's rows k = warp + j * nwarps (j < kR) stay in registers: their
+    // products p and inclusive fp32 warp scans Q_{k,l}, the scans' shuffle
+    // steps interleaved across the rows (each row's own sums are unchanged).
+    float p[kR], v[kR];
 #pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-            const float y = __shfl_up_sync(0xffffffffu, v, off);
-            if (lane >= off) v = __fadd_rn(v, y);
+    for (int j = 0; j < kR; ++j) {
+        const int k = warp + j * nwarps;
+        p[j] = k < rows ? __fmul_rn(wr[32 * k + lane], xs[32 * k + lane]) : 0.0f;
+        v[j] = p[j];
+    }
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+#pragma unroll
+        for (int j = 0; j < kR; ++j) {
+            const float y = __shfl_up_sync(0xffffffffu, v[j], off);
+            if (lane >= off) v[j] = __fadd_rn(v[j], y);
         }
-        return v;
-    };
+    }
     float s = 0.0f, cmp = 0.0f, abs_p = 0.0f;
-#pragma unroll 1
-    for (int k = warp; k < rows; k += nwarps) {  // warp-uniform; rows ascending, as before
-        float p;
-        const float v = row_scan(k, p);
-        two_sum_acc(s, cmp, p);
-        abs_p += fabsf(p);
-        if (lane == 31) rowtot[k] = v;
+#pragma unroll
+    for (int j = 0; j < kR; ++j) {  // rows ascending, as the serial order
+        if (warp + j * nwarps < rows) {
+            two_sum_acc(s, cmp, p[j]);
+            abs_p += fabsf(p[j]);
+            if (lane == 31) rowtot[warp + j * nwarps] = v[j];
+        }
     }
     sync();
     // Every warp scans the row totals itself: lane l holds rows 2l and 2l+1.
@@ -150,12 +156,13 @@ __device__ __forceinline__ void block_logit_bound_rows(const float* wr, const fl
     if (lane == 0) r_even = 0.0f;
     const float r_odd = __fadd_rn(r_even, t0);
     float sabs = 0.0f;
-#pragma unroll 1
-    for (int k = warp; k < rows; k += nwarps) {  // warp-uniform
-        float p;
-        const float q = row_scan(k, p);
-        const float R = __shfl_sync(0xffffffffu, (k & 1) ? r_odd : r_even, k >> 1);
-        sabs = __fadd_rn(sabs, fabsf(__fadd_rn(R, q)));
+#pragma unroll
+    for (int j = 0; j < kR; ++j) {
+        const int k = warp + j * nwarps;
+        if (k < rows) {  // warp-uniform
+            const float R = __shfl_sync(0xffffffffu, (k & 1) ? r_odd : r_even, k >> 1);
+            sabs = __fadd_rn(sabs, fabsf(__fadd_rn(R, v[j])));
+        }
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
