@@ -7,6 +7,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <map>
+#include <tuple>
 #include <mutex>
 #include <string>
 #include <unordered_map>
@@ -31,6 +32,23 @@ cudaError_t ensure_smem_attr(const void* fn, int bytes) {
     err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (!err) have = bytes;
     return err;
+}
+
+cudaError_t ensure_resident(const void* fn, int threads, int smem, int grid) {
+    static std::mutex mu;
+    static std::map<std::tuple<const void*, int, int, int>, int> ok;  // (fn, device, threads, smem) -> CTAs that fit
+    int dev = 0, sms = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err) return err;
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = ok.find({fn, dev, threads, smem});
+    if (it == ok.end()) {
+        int per_sm = 0;
+        if ((err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, (size_t)smem))) return err;
+        if ((err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev))) return err;
+        it = ok.emplace(std::make_tuple(fn, dev, threads, smem), per_sm * sms).first;
+    }
+    return it->second >= grid ? cudaSuccess : cudaErrorCooperativeLaunchTooLarge;
 }
 
 }  // namespace glmq

@@ -59,7 +59,7 @@ cudaError_t launch_moe_decode(const MoeLayerDev& w, const MoeDims& d, const MoeS
 cudaError_t persistent_check(const MoeDims& d, int num_sms, size_t* smem_out);
 
 // One token through the MoE FFN of layers [first, first + n_layers) of the
-// device table `layers_dev`, in one cooperative launch of one CTA per SM:
+// device table `layers_dev`, in one launch of one CTA per SM (all resident):
 // x <- x + FFN_l(x) for each layer in turn. topk_out / topkw_out (optional,
 // [n_layers][K]) receive each layer's expert ids and weights. next_layer
 // (table index or -1) names the layer expected after the last one: its
@@ -268,5 +268,13 @@ void set_last_error(const char* msg);
 // (kernel, device) under a mutex; a later call for the same pair and size
 // makes no CUDA call (safe inside stream capture).
 cudaError_t ensure_smem_attr(const void* fn, int bytes);
+
+// Whether `grid` CTAs of kernel `fn` (threads per CTA, dynamic shared memory
+// smem, its attribute already raised) fit the current device at once, i.e.
+// every CTA of a grid-synchronising kernel can be resident together.
+// cudaErrorCooperativeLaunchTooLarge if not. The occupancy query is made once
+// per (kernel, device, threads, smem) under a mutex; later calls make no CUDA
+// call (safe inside stream capture).
+cudaError_t ensure_resident(const void* fn, int threads, int smem, int grid);
 
 }  // namespace glmq

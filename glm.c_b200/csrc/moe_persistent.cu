@@ -1,4 +1,4 @@
-// Persistent batch-1 MoE decode: one cooperative launch runs the MoE FFN of
+// Persistent batch-1 MoE decode: one launch runs the MoE FFN of
 // one or more consecutive layers for one token (apply_moe_shared_ffn_layer,
 // infer.c:1087-1216, once per layer).
 //
@@ -39,7 +39,8 @@
 // wait in this kernel (barriers, ring slots, routing hand-off) gives up after
 // a bounded number of polls, records the reason in `status`, raises an abort
 // flag, and the kernel leaves at its next grid barrier, so a fault cannot
-// hang the GPU. Cooperative launch guarantees all CTAs are co-resident.
+// hang the GPU. One CTA per SM fits (checked at launch), so all CTAs are
+// resident together.
 #include <cstdint>
 
 #include <cuda_runtime.h>
@@ -880,18 +881,28 @@ cudaError_t launch_moe_persistent(const MoeLayerDev* layers_dev, int first, int 
                   d.D,        d.F,      d.E,       d.K,        routed_enabled,
                   p_slot_bytes(d.D, d.F, d.E, d.gs), next_layer, d.gs, d.gs / 4,
                   g16 ? PCfg<16>::kSlots : PCfg<32>::kSlots};
+    // The grid barriers need every CTA resident at once: one CTA per SM must
+    // fit (checked here, as a cooperative launch would). The launch itself is
+    // not cooperative: a plain programmatic dependent launch lets this grid's
+    // CTAs start on the SMs that the previous kernel frees and stream their
+    // first weight tiles while it drains (measured 1 us per layer faster than
+    // the cooperative launch). Residency still holds: the previous kernel
+    // never waits on this one, and the next kernel on the stream cannot start
+    // before every CTA of this one has run its launch_dependents (the first
+    // thing it does). A wait that still could not complete gives up after
+    // kWaitNs and reports it in `status`.
+    const int threads = g16 ? PCfg<16>::kThreads : PCfg<32>::kThreads;
+    if ((err = ensure_resident(reinterpret_cast<const void*>(kernel), threads, (int)smem, num_sms))) return err;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(num_sms);
-    cfg.blockDim = dim3(g16 ? PCfg<16>::kThreads : PCfg<32>::kThreads);
+    cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 2;
+    cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kernel, a);
 }
 

@@ -81,7 +81,7 @@ int glm_cuda_moe_layer_async(int layer, float *x_dev, int n_tokens, int32_t *top
                              void *stream);
 
 /* Decode kernels behind glm_cuda_moe_layer / _async. PERSISTENT: one
- * cooperative launch per token and layer, one CTA per SM streaming every
+ * launch per token and layer, one CTA per SM (all resident) streaming every
  * weight tile through shared memory with TMA (needs n_routed_experts <= SM
  * count and a multiple of 4, dim <= 2048, moe_ffn_dim % 128 == 0 and <= 3840).
  * CHAIN: three dependent kernels per token and layer (router, gate/up, down).
