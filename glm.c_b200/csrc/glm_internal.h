@@ -70,16 +70,20 @@ cudaError_t launch_moe_persistent(const MoeLayerDev* layers_dev, int first, int 
 
 // y = Q8(q, s) . x for a rows x cols planar Q8 matrix (gs = 32, cols % 64 == 0);
 // with `accumulate`, y += Q8(q, s) . x; with `norm`, x is first replaced by
-// rmsnorm(x) * norm (glm.c's rmsnorm, infer.c:746-752).
+// rmsnorm(x) * norm (glm.c's rmsnorm, infer.c:746-752). With `stage`, each
+// CTA copies its weight rows into shared memory before the launch wait when
+// they fit (~200 KB): faster when the launch follows a long kernel whose SMs
+// free up one by one (the decoder), slower back to back with no work in
+// between (each CTA then waits for its whole slice before computing).
 cudaError_t launch_q80_matvec(const int8_t* q, const float* s, const float* x, float* y, int rows, int cols,
                               int gs, int num_sms, cudaStream_t stream, bool accumulate = false,
-                              const float* norm = nullptr);
+                              const float* norm = nullptr, bool stage = false);
 
 // Two matrices with the same column count on the same (normed) x in one
 // launch: y = Q8(q, s) . x (rows rows), y2 = Q8(q2, s2) . x (rows2 rows).
 cudaError_t launch_q80_matvec2(const int8_t* q, const float* s, float* y, int rows, const int8_t* q2,
                                const float* s2, float* y2, int rows2, const float* x, int cols, int gs, int num_sms,
-                               cudaStream_t stream, const float* norm);
+                               cudaStream_t stream, const float* norm, bool stage = false);
 
 // ---- decoder around the MoE layers (decoder.cu)
 

@@ -35,7 +35,10 @@
 // layer's routing-independent weights (router row, shared expert rows) into
 // L2.
 //
-// Grid barriers are a global arrival counter polled with acquire loads. Every
+// Grid barriers are a global arrival counter: after a block barrier one
+// thread adds its arrival with a gpu-scope release (covering the CTA's
+// writes ordered before it by that barrier) and polls with acquire loads;
+// a block barrier then passes the others on. Every
 // wait in this kernel (barriers, ring slots, routing hand-off) gives up after
 // a bounded number of polls, records the reason in `status`, raises an abort
 // flag, and the kernel leaves at its next grid barrier, so a fault cannot
@@ -162,6 +165,10 @@ __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
     unsigned v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
     return v;
+}
+
+__device__ __forceinline__ void red_release_gpu_add(unsigned* p, unsigned v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ unsigned ld_relaxed_gpu(const unsigned* p) {
@@ -385,6 +392,21 @@ __device__ __forceinline__ void cons_release(const PCtx& P, uint32_t it) {
     if ((threadIdx.x & 31) == 0) mbar_arrive(&P.empty[it % P.slots]);
 }
 
+// Thread 0: wait until the arrival count reaches target (acquire), polling
+// 32 times between looks at the clock, the abort flag and the status word.
+__device__ __forceinline__ int poll_barrier(const PersistArgs& a, const PCtx& P, unsigned target) {
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 0; !*P.abort_flag && global_ns() - t0 < kWaitNs; ++i) {
+#pragma unroll 1
+        for (int j = 0; j < 32; ++j)
+            if (ld_acquire_gpu(a.bar) >= target) return 1;
+        if ((i & 7u) == 7u && (ld_relaxed_gpu(a.status) & kStatAbort)) break;
+    }
+    atomicOr(a.status, kStatBarrier);
+    *P.abort_flag = 1;
+    return 0;
+}
+
 // Grid-wide barrier among the consumer warps of all CTAs; false when this
 // CTA or another one has given up (every CTA then leaves).
 template <int kN>
@@ -392,23 +414,8 @@ __device__ bool grid_sync(const PersistArgs& a, const PCtx& P, unsigned& nbar, i
     cons_sync<kN>();
     ++nbar;
     if (tid == 0) {
-        int ok = 0;
-        __threadfence();
-        if (!*P.abort_flag) atomicAdd(a.bar, 1u);
-        const unsigned target = nbar * gridDim.x;
-        const uint64_t t0 = global_ns();
-        for (uint32_t i = 0; !*P.abort_flag && global_ns() - t0 < kWaitNs; ++i) {
-            if (ld_acquire_gpu(a.bar) >= target) {
-                ok = 1;
-                break;
-            }
-            if ((i & 255u) == 255u && (ld_relaxed_gpu(a.status) & kStatAbort)) break;
-        }
-        if (!ok) {
-            atomicOr(a.status, kStatBarrier);
-            *P.abort_flag = 1;
-        }
-        __threadfence();
+        if (!*P.abort_flag) red_release_gpu_add(a.bar, 1u);
+        const int ok = poll_barrier(a, P, nbar * gridDim.x);
         *s_ok = ok;
     }
     cons_sync<kN>();
@@ -421,33 +428,13 @@ template <int kN>
 __device__ void grid_arrive(const PersistArgs& a, const PCtx& P, unsigned& nbar, int tid) {
     cons_sync<kN>();
     ++nbar;
-    if (tid == 0) {
-        __threadfence();
-        if (!*P.abort_flag) atomicAdd(a.bar, 1u);
-    }
+    if (tid == 0 && !*P.abort_flag) red_release_gpu_add(a.bar, 1u);
 }
 
 template <int kN>
 __device__ bool grid_wait(const PersistArgs& a, const PCtx& P, unsigned nbar, int tid, volatile int* s_ok) {
     cons_sync<kN>();
-    if (tid == 0) {
-        int ok = 0;
-        const unsigned target = nbar * gridDim.x;
-        const uint64_t t0 = global_ns();
-        for (uint32_t i = 0; !*P.abort_flag && global_ns() - t0 < kWaitNs; ++i) {
-            if (ld_acquire_gpu(a.bar) >= target) {
-                ok = 1;
-                break;
-            }
-            if ((i & 255u) == 255u && (ld_relaxed_gpu(a.status) & kStatAbort)) break;
-        }
-        if (!ok) {
-            atomicOr(a.status, kStatBarrier);
-            *P.abort_flag = 1;
-        }
-        __threadfence();
-        *s_ok = ok;
-    }
+    if (tid == 0) *s_ok = poll_barrier(a, P, nbar * gridDim.x);
     cons_sync<kN>();
     return *s_ok != 0;
 }
@@ -717,11 +704,14 @@ __global__ void __launch_bounds__(PCfg<kGS>::kThreads, 1) moe_persistent_kernel(
     // barrier words for the next launch (no memset between launches).
     auto leave = [&]() {
         if (tid == 0) {
-            __threadfence();
-            if (atomicAdd(a.done, 1u) == (unsigned)G - 1u) {
+            // every CTA counted here has passed its last grid barrier: the
+            // last one resets the words (the next launch reads them only
+            // after this grid has completed)
+            unsigned prev;
+            asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;\n" : "=r"(prev) : "l"(a.done) : "memory");
+            if (prev == (unsigned)G - 1u) {
                 *reinterpret_cast<volatile unsigned*>(a.bar) = 0u;
                 *reinterpret_cast<volatile unsigned*>(a.done) = 0u;
-                __threadfence();
             }
         }
     };
