@@ -27,8 +27,9 @@
 //         CTA's routed rows into L2; the shared gate/up items (already in
 //         the ring) then the routed ones -> h
 //     --  grid barrier B
-//     P3  h quantised; this CTA's output rows of the shared and the K routed
-//         down matrices; weighted combine in rank order + residual -> x
+//     P3  this CTA's output rows of the shared and the K routed down
+//         matrices, each group quantising its slot's h first (group
+//         barrier only); weighted combine in rank order + residual -> x
 //     --  grid barrier C (between layers)
 //
 // While a layer's routing is decided, the producer also pulls the next
@@ -684,13 +685,18 @@ __global__ void __launch_bounds__(PCfg<kGS>::kThreads, 1) moe_persistent_kernel(
         }
     };
 
-    // This CTA's output rows of down matrix `slot` (K = shared) -> ys[slot].
+    // This CTA's output rows of down matrix `slot` (K = shared) -> ys[slot]:
+    // the group quantises that slot's h itself (its group barrier, no block
+    // barrier), then dots the down tile with it.
     auto down_item = [&](const MoeLayerDev& W, int slot, uint32_t item) {
         const int n = m.re - m.rb;
         const bool live = slot == K || (a.routed_enabled && W.down_q && s_topk[slot] >= 0);
-        const float* tb = kGS == 32 ? th + (size_t)slot * nchF * kTab : gh + (size_t)slot * (F >> 5);
-        const float* pt = group_rows(item, ph + (size_t)slot * nchF * kChunkBytes, tb, F, live && gid < n,
-                                     live && gid + 8 < n);
+        int8_t* pl = ph + (size_t)slot * nchF * kChunkBytes;
+        float* sg = gh + (size_t)slot * (F >> 5);
+        float* tb = th + (size_t)slot * nchF * kTab;
+        quantize_planes_part<true, kGS == 16>(a.h + (size_t)slot * F, F, pl, sg, tb, gw * 32 + lane,
+                                              kPGroupWarps * 32, grp_sync);
+        const float* pt = group_rows(item, pl, kGS == 32 ? tb : sg, F, live && gid < n, live && gid + 8 < n);
         if (gw == 0 && lane < kPTile) ys[slot * kPTile + lane] = row_total(pt, lane);
     };
 
@@ -817,8 +823,7 @@ __global__ void __launch_bounds__(PCfg<kGS>::kThreads, 1) moe_persistent_kernel(
         it += (uint32_t)nitems;
         if (!grid_sync<kPConsThreads>(a, P, nbar, tid, s_ok)) return leave();
 
-        // ---- P3: h -> digit planes (xs is dead); down rows; combine
-        quantize_planes_part<true, kGS == 16>(a.h, (K + 1) * F, ph, gh, th, tid, kPConsThreads, sync);
+        // ---- P3: down rows (each group quantises its slots' h: xs is dead); combine
         // down items in the order shared, routed 0 .. K-1; each group takes its own
         for (uint32_t item = first_mine(it); item < it + (uint32_t)(K + 1); item += kPSlots) {
             const int q = (int)(item - it);
