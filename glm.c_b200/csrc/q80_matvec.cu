@@ -74,7 +74,9 @@ __host__ __device__ inline size_t mv_stage_bytes(int nrows, int cols, int gs) {
     return (size_t)nrows * (size_t)(mv_qpitch(cols) + mv_spitch(cols, gs));
 }
 
-template <int kGS>
+// kStage (a.stage set): the weight rows staged in shared memory; a separate
+// instantiation, so that the streaming kernel keeps its own register budget.
+template <int kGS, bool kStage>
 __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a) {
     constexpr int kTab = kChunkTab;  // the gs = 32 table (gs = 16 reads sxg directly)
     extern __shared__ __align__(16) unsigned char sm[];
@@ -84,7 +86,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a)
     const int qpitch = mv_qpitch(a.cols), spitch = mv_spitch(a.cols, kGS), sbytes = a.cols * 4 / kGS;
     int8_t* wq = reinterpret_cast<int8_t*>(sm + mv_base_bytes(a.cols, a.norm != nullptr));
     unsigned char* ws = reinterpret_cast<unsigned char*>(wq) + (size_t)(re - rb) * qpitch;
-    if (a.stage) {
+    if constexpr (kStage) {
         // Before waiting for the previous kernel (which writes x, never the
         // weights): copy this CTA's weight rows and scales into shared
         // memory, one bulk copy per row and part, so that the dot loop after
@@ -203,7 +205,8 @@ __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a)
 
     // the staged rows (normally landed long before): a copy that never lands
     // leaves this CTA on the global loads instead
-    const bool staged = a.stage && mbar_wait_bounded(&stage_bar, 0);
+    bool staged = false;
+    if constexpr (kStage) staged = mbar_wait_bounded(&stage_bar, 0);
     auto run_tiles = [&](auto staged_tag) {
         constexpr bool kSt = decltype(staged_tag)::value;
         for (int tile0 = 0; tile0 < ntiles; tile0 += tiles_per_pass) {
@@ -302,10 +305,13 @@ __global__ void __launch_bounds__(kMvThreads, 1) q80_matvec_kernel(MatvecArgs a)
             __syncthreads();
         }
     };
-    if (staged)
-        run_tiles(std::true_type{});
-    else
-        run_tiles(std::false_type{});
+    if constexpr (kStage) {
+        if (staged) {
+            run_tiles(std::true_type{});
+            return;
+        }
+    }
+    run_tiles(std::false_type{});
 }
 
 size_t q80_matvec_smem_bytes(int cols, bool norm, int gs) {
@@ -341,7 +347,8 @@ cudaError_t launch_matvec(MatvecArgs a, int gs, int num_sms, cudaStream_t stream
                        (a.rows2 == 0 || !((reinterpret_cast<uintptr_t>(a.q2) | reinterpret_cast<uintptr_t>(a.s2)) & 15u));
     a.stage = allow_stage && src16 && (gs == 16 || a.cols % 128 == 0) && staged <= kMvStagedSmemMax ? 1 : 0;
     if (a.stage) smem = staged;
-    auto kernel = gs == 16 ? q80_matvec_kernel<16> : q80_matvec_kernel<32>;
+    auto kernel = gs == 16 ? (a.stage ? q80_matvec_kernel<16, true> : q80_matvec_kernel<16, false>)
+                           : (a.stage ? q80_matvec_kernel<32, true> : q80_matvec_kernel<32, false>);
     if (cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kernel), (int)smem)) return e;
     return launch_pdl(kernel, grid, kMvThreads, smem, stream, a);
 }
